@@ -1,0 +1,1036 @@
+// engine.cu -- host side of the B200 resident decode-epoch engine and its C ABI
+// (include/cruise_epoch.h): device memory, seeded weight synthesis, weight
+// loading, the one-launch epoch, and the reference-compatible bridge
+// resident_epoch_create / _execute / _destroy.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <mutex>
+#include <string>
+#include <time.h>
+#include <vector>
+
+#include "../../include/cruise_epoch.h"
+#include "epoch_kernel.cuh"
+
+namespace cruise {
+namespace {
+
+constexpr int kLayerTensors = 12;  // per-layer checkpoint tensors, in id order
+const char *const kLayerKeys[kLayerTensors] = {
+    "input_layernorm.weight", "post_attention_layernorm.weight",
+    "self_attn.q_proj.weight", "self_attn.q_proj.bias",
+    "self_attn.k_proj.weight", "self_attn.k_proj.bias",
+    "self_attn.v_proj.weight", "self_attn.v_proj.bias",
+    "self_attn.o_proj.weight", "mlp.gate_proj.weight",
+    "mlp.up_proj.weight",      "mlp.down_proj.weight"};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---- seeded weight synthesis (splitmix64 -> Irwin-Hall(4) -> bf16) -------------
+constexpr uint64_t kGamma = 0x9E3779B97F4A7C15ull;
+constexpr uint64_t kKeyMul = 0xD1B54A32D192ED03ull;
+
+__host__ __device__ inline uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+enum SynthMode : int32_t { kPlain = 0, kQkvRows = 1, kGateUp = 2, kDownPad = 3, kRowsPad = 4 };
+
+struct SynthMap {
+  int32_t mode;
+  int32_t ids[3];       // tensor ids (q,k,v for kQkvRows; gate,up for kGateUp)
+  int64_t cols;         // row length of the canonical tensor(s)
+  int64_t rows0, rows1; // q rows / k rows (kQkvRows); valid rows (kRowsPad)
+  int64_t dst_cols;     // packed row length (kDownPad)
+};
+
+__device__ __forceinline__ uint16_t synth_value(uint64_t key, int64_t index, float scale) {
+  const uint64_t h = mix64(key + static_cast<uint64_t>(index + 1) * kGamma);
+  const int32_t sum = static_cast<int32_t>((h & 0xFFFF) + ((h >> 16) & 0xFFFF) + ((h >> 32) & 0xFFFF) +
+                                           (h >> 48));
+  const float centred = static_cast<float>(2 * sum - 262140);
+  const float v = __fmul_rn(centred, scale);
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+__global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_t seed, float scale) {
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < count;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int32_t id = map.ids[0];
+    int64_t idx = e;
+    bool zero = false;
+    switch (map.mode) {
+      case kQkvRows: {
+        const int64_t r = e / map.cols, c = e % map.cols;
+        if (r < map.rows0) { id = map.ids[0]; idx = r * map.cols + c; }
+        else if (r < map.rows0 + map.rows1) { id = map.ids[1]; idx = (r - map.rows0) * map.cols + c; }
+        else { id = map.ids[2]; idx = (r - map.rows0 - map.rows1) * map.cols + c; }
+        break;
+      }
+      case kGateUp: {
+        const int64_t R = e / map.cols, c = e % map.cols;
+        const int64_t blk = R / 16, rr = R % 16;
+        id = rr < 8 ? map.ids[0] : map.ids[1];
+        idx = (blk * 8 + (rr & 7)) * map.cols + c;
+        break;
+      }
+      case kDownPad: {
+        const int64_t r = e / map.dst_cols, c = e % map.dst_cols;
+        zero = c >= map.cols;
+        idx = r * map.cols + c;
+        break;
+      }
+      case kRowsPad: {
+        zero = e / map.cols >= map.rows0;
+        break;
+      }
+      default:
+        break;
+    }
+    const uint64_t key = mix64(seed * kGamma + static_cast<uint64_t>(id + 1) * kKeyMul);
+    dst[e] = zero ? 0 : synth_value(key, idx, scale);
+  }
+}
+
+struct Region {
+  uint16_t *ptr = nullptr;   // packed device buffer
+  int64_t elems = 0;
+};
+
+struct Engine {
+  CruiseModelConfig cfg{};
+  ModelDims m{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  int sms = 0;
+  int stages = 0;
+  int xs_stride = 0;
+  size_t smem = 0;
+  // device memory
+  void *weights = nullptr;   // one allocation for every weight tensor
+  size_t weight_bytes = 0;
+  std::vector<LayerWeights> layers;
+  LayerWeights *d_layers = nullptr;
+  bf16 *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
+  void *state = nullptr;     // caches, activations, control blocks
+  bf16 *key_cache = nullptr, *value_cache = nullptr;
+  bf16 *rope_cos = nullptr, *rope_sin = nullptr;
+  bf16 *h = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr;
+  float *partials = nullptr, *arg_val = nullptr, *logits = nullptr;
+  int32_t *arg_idx = nullptr, *arg_bad = nullptr;
+  EpochIO *d_io = nullptr;
+  ResidentState *d_res = nullptr;
+  EpochWork *d_work = nullptr;
+  SyncState *d_sync = nullptr;
+  uint8_t *d_payload = nullptr;   // import staging, allocated on first import
+  size_t payload_bytes = 0;
+  EpochIO *h_io = nullptr;        // pinned staging
+  float last_ms = 0.f;
+  int32_t last_launches = 0;
+  std::string last_error;
+  std::mutex execute_mutex;
+  std::array<uint8_t, kTilingBytes> tiling{};
+};
+
+int32_t set_err(Engine *e, cudaError_t err, const char *what) {
+  if (err != cudaSuccess && e != nullptr) {
+    e->last_error = std::string(what) + ": " + cudaGetErrorString(err);
+  }
+  return static_cast<int32_t>(err);
+}
+
+bool valid_config(const CruiseModelConfig &c) {
+  if (c.num_layers < 1 || c.num_layers > 64 || c.hidden < 64 || c.hidden % 64 != 0) return false;
+  if (c.num_heads < 1 || c.num_kv_heads < 1 || c.num_heads % c.num_kv_heads != 0) return false;
+  if (c.head_dim != 64 && c.head_dim != 128) return false;
+  if (c.num_heads * c.head_dim != c.hidden) return false;
+  if (c.intermediate < 8 || c.intermediate % 8 != 0) return false;
+  if (c.vocab < 2) return false;
+  if (c.block_size < 1 || c.blocks_per_row < 1 || c.blocks_per_row > kMaxBlocksPerRow) return false;
+  if (c.num_blocks < kBatch * c.blocks_per_row || c.num_blocks > 256) return false;
+  if (((2 * c.num_kv_heads * c.head_dim) % kRows) != 0) return false;
+  // Adler-32 splits a block over 256 threads in 16-byte pieces
+  if ((static_cast<int64_t>(c.block_size) * c.num_kv_heads * c.head_dim * 2) % (256 * 16) != 0) return false;
+  if (c.configured_eos < 0 || c.configured_eos >= c.vocab) return false;
+  return true;
+}
+
+void fill_dims(Engine *e) {
+  const CruiseModelConfig &c = e->cfg;
+  ModelDims &m = e->m;
+  m.L = c.num_layers;
+  m.H = c.hidden;
+  m.nq = c.num_heads;
+  m.nkv = c.num_kv_heads;
+  m.d = c.head_dim;
+  m.I = c.intermediate;
+  m.I_pad = static_cast<int32_t>(align_up(c.intermediate, 64));
+  m.V = c.vocab;
+  m.V_pad = static_cast<int32_t>(align_up(c.vocab, kRows));
+  m.Nqkv = c.hidden + 2 * c.num_kv_heads * c.head_dim;
+  m.eps = c.rms_eps;
+  m.sqrt_d = static_cast<float>(std::sqrt(static_cast<double>(c.head_dim)));
+  m.bs = c.block_size;
+  m.bpr = c.blocks_per_row;
+  m.NB = c.num_blocks;
+  m.C = c.block_size * c.blocks_per_row;
+}
+
+// Default RoPE tables: inv_freq = 1 / theta^(2i/d) and cos/sin of pos*inv_freq
+// in fp32, rounded to bf16, following batched_decoder_step.py:212-216,235-240.
+void default_rope(const Engine *e, std::vector<uint16_t> &cos_t, std::vector<uint16_t> &sin_t) {
+  const int d = e->m.d, C = e->m.C;
+  cos_t.resize(static_cast<size_t>(C) * d);
+  sin_t.resize(static_cast<size_t>(C) * d);
+  auto to_bf16 = [](float v) {
+    uint32_t bits;
+    std::memcpy(&bits, &v, 4);
+    bits += 0x7FFFu + ((bits >> 16) & 1u);
+    return static_cast<uint16_t>(bits >> 16);
+  };
+  for (int pos = 0; pos < C; ++pos) {
+    for (int i = 0; i < d / 2; ++i) {
+      const float expo = static_cast<float>(2 * i) / static_cast<float>(d);
+      const float inv = 1.0f / std::pow(e->cfg.rope_theta, expo);
+      const float f = static_cast<float>(pos) * inv;
+      const uint16_t cv = to_bf16(static_cast<float>(std::cos(static_cast<double>(f))));
+      const uint16_t sv = to_bf16(static_cast<float>(std::sin(static_cast<double>(f))));
+      cos_t[static_cast<size_t>(pos) * d + i] = cos_t[static_cast<size_t>(pos) * d + i + d / 2] = cv;
+      sin_t[static_cast<size_t>(pos) * d + i] = sin_t[static_cast<size_t>(pos) * d + i + d / 2] = sv;
+    }
+  }
+}
+
+void destroy_engine(Engine *e) {
+  if (e == nullptr) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  cudaFree(e->weights);
+  cudaFree(e->state);
+  cudaFree(e->d_layers);
+  cudaFree(e->d_payload);
+  if (e->h_io) cudaFreeHost(e->h_io);
+  if (e->ev0) cudaEventDestroy(e->ev0);
+  if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status) {
+  *status = 5;
+  if (!valid_config(cfg)) return nullptr;
+  Engine *e = new Engine();
+  e->cfg = cfg;
+  e->device = device;
+  fill_dims(e);
+  const ModelDims &m = e->m;
+  *status = 3;
+  if (cudaSetDevice(device) != cudaSuccess) { delete e; return nullptr; }
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) {
+    delete e;
+    return nullptr;
+  }
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+  if (!coop) { delete e; return nullptr; }
+  e->sms = std::min(prop.multiProcessorCount, kMaxCtas);
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&e->ev0) != cudaSuccess || cudaEventCreate(&e->ev1) != cudaSuccess) {
+    destroy_engine(e);
+    return nullptr;
+  }
+  // shared memory geometry: activation rows sized for the widest projection input
+  const int kmax = std::max(m.H, m.I_pad);
+  e->xs_stride = kmax + 8;
+  const size_t limit = prop.sharedMemPerBlockOptin;
+  int stages = kMaxStages;
+  while (stages > 2 && smem_bytes(stages, e->xs_stride) > limit) --stages;
+  e->stages = stages;
+  e->smem = smem_bytes(stages, e->xs_stride);
+  if (e->smem > limit) { *status = 5; destroy_engine(e); return nullptr; }
+  if (cudaFuncSetAttribute(resident_epoch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(e->smem)) != cudaSuccess) {
+    destroy_engine(e);
+    return nullptr;
+  }
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, resident_epoch_kernel, kThreads, e->smem);
+  if (per_sm < 1) { destroy_engine(e); return nullptr; }
+
+  // ---- weights: one allocation ----
+  *status = 6;
+  const int64_t H = m.H, kv = static_cast<int64_t>(m.nkv) * m.d;
+  std::vector<size_t> offs;
+  size_t total = 0;
+  auto take = [&](int64_t elems) {
+    const size_t off = total;
+    total = align_up(total + static_cast<size_t>(elems) * 2, 256);
+    return off;
+  };
+  const size_t off_embed = take(static_cast<int64_t>(m.V) * H);
+  struct LayerOff { size_t w_in, w_post, qkv_w, qkv_b, o_w, gu_w, down_w; };
+  std::vector<LayerOff> lo(m.L);
+  for (int l = 0; l < m.L; ++l) {
+    lo[l].w_in = take(H);
+    lo[l].w_post = take(H);
+    lo[l].qkv_w = take(static_cast<int64_t>(m.Nqkv) * H);
+    lo[l].qkv_b = take(m.Nqkv);
+    lo[l].o_w = take(H * H);
+    lo[l].gu_w = take(2LL * m.I * H);
+    lo[l].down_w = take(H * m.I_pad);
+  }
+  const size_t off_norm = take(H);
+  const size_t off_lm = take(static_cast<int64_t>(m.V_pad) * H);
+  (void)kv;
+  e->weight_bytes = total;
+  if (cudaMalloc(&e->weights, total) != cudaSuccess) { destroy_engine(e); return nullptr; }
+  cudaMemsetAsync(e->weights, 0, total, e->stream);
+  uint8_t *wb = static_cast<uint8_t *>(e->weights);
+  auto wp = [&](size_t off) { return reinterpret_cast<bf16 *>(wb + off); };
+  e->embed = wp(off_embed);
+  e->final_norm = wp(off_norm);
+  e->lm_head = wp(off_lm);
+  e->layers.resize(m.L);
+  for (int l = 0; l < m.L; ++l) {
+    e->layers[l] = LayerWeights{wp(lo[l].w_in), wp(lo[l].w_post), wp(lo[l].qkv_w), wp(lo[l].qkv_b),
+                                wp(lo[l].o_w),  wp(lo[l].gu_w),   wp(lo[l].down_w)};
+  }
+  if (cudaMalloc(&e->d_layers, sizeof(LayerWeights) * m.L) != cudaSuccess) { destroy_engine(e); return nullptr; }
+  cudaMemcpyAsync(e->d_layers, e->layers.data(), sizeof(LayerWeights) * m.L, cudaMemcpyHostToDevice, e->stream);
+
+  // ---- caches, activations, control blocks: one allocation ----
+  const size_t cache_elems = static_cast<size_t>(m.L) * m.NB * m.bs * m.nkv * m.d;
+  size_t st = 0;
+  auto take2 = [&](size_t bytes) {
+    const size_t off = st;
+    st = align_up(st + bytes, 256);
+    return off;
+  };
+  const size_t o_k = take2(cache_elems * 2), o_v = take2(cache_elems * 2);
+  const size_t o_cos = take2(static_cast<size_t>(m.C) * m.d * 2), o_sin = take2(static_cast<size_t>(m.C) * m.d * 2);
+  const size_t o_h = take2(kBatch * H * 2), o_qkv = take2(static_cast<size_t>(kBatch) * m.Nqkv * 2);
+  const size_t o_attn = take2(kBatch * H * 2), o_act = take2(static_cast<size_t>(kBatch) * m.I_pad * 2);
+  const size_t o_part = take2(static_cast<size_t>(e->sms) * 64 * 4);
+  const size_t o_av = take2(static_cast<size_t>(e->sms) * kBatch * 4);
+  const size_t o_ai = take2(static_cast<size_t>(e->sms) * kBatch * 4);
+  const size_t o_ab = take2(static_cast<size_t>(e->sms) * kBatch * 4);
+  const size_t o_lg = take2(static_cast<size_t>(kMaxSteps) * kBatch * m.V * 4);
+  const size_t o_io = take2(sizeof(EpochIO)), o_res = take2(sizeof(ResidentState));
+  const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sizeof(SyncState));
+  if (cudaMalloc(&e->state, st) != cudaSuccess) { destroy_engine(e); return nullptr; }
+  cudaMemsetAsync(e->state, 0, st, e->stream);
+  uint8_t *sb = static_cast<uint8_t *>(e->state);
+  e->key_cache = reinterpret_cast<bf16 *>(sb + o_k);
+  e->value_cache = reinterpret_cast<bf16 *>(sb + o_v);
+  e->rope_cos = reinterpret_cast<bf16 *>(sb + o_cos);
+  e->rope_sin = reinterpret_cast<bf16 *>(sb + o_sin);
+  e->h = reinterpret_cast<bf16 *>(sb + o_h);
+  e->qkv = reinterpret_cast<bf16 *>(sb + o_qkv);
+  e->attn = reinterpret_cast<bf16 *>(sb + o_attn);
+  e->act = reinterpret_cast<bf16 *>(sb + o_act);
+  e->partials = reinterpret_cast<float *>(sb + o_part);
+  e->arg_val = reinterpret_cast<float *>(sb + o_av);
+  e->arg_idx = reinterpret_cast<int32_t *>(sb + o_ai);
+  e->arg_bad = reinterpret_cast<int32_t *>(sb + o_ab);
+  e->logits = reinterpret_cast<float *>(sb + o_lg);
+  e->d_io = reinterpret_cast<EpochIO *>(sb + o_io);
+  e->d_res = reinterpret_cast<ResidentState *>(sb + o_res);
+  e->d_work = reinterpret_cast<EpochWork *>(sb + o_work);
+  e->d_sync = reinterpret_cast<SyncState *>(sb + o_sync);
+  if (cudaHostAlloc(reinterpret_cast<void **>(&e->h_io), sizeof(EpochIO), cudaHostAllocDefault) != cudaSuccess) {
+    destroy_engine(e);
+    return nullptr;
+  }
+  std::vector<uint16_t> cos_t, sin_t;
+  default_rope(e, cos_t, sin_t);
+  cudaMemcpyAsync(e->rope_cos, cos_t.data(), cos_t.size() * 2, cudaMemcpyHostToDevice, e->stream);
+  cudaMemcpyAsync(e->rope_sin, sin_t.data(), sin_t.size() * 2, cudaMemcpyHostToDevice, e->stream);
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) { *status = 3; destroy_engine(e); return nullptr; }
+  *status = 0;
+  return e;
+}
+
+// ---- weight tensors by checkpoint name ---------------------------------------------------
+struct TensorPlace {
+  enum Kind { kFlat, kRowsAt, kGate, kUp, kDownCols } kind = kFlat;
+  bf16 *base = nullptr;
+  int64_t rows = 0, cols = 0;  // canonical shape
+  int64_t row_offset = 0;      // kRowsAt: destination row offset
+  int64_t dst_cols = 0;        // packed row pitch (elements)
+};
+
+bool locate(Engine *e, const std::string &name, TensorPlace &tp) {
+  const ModelDims &m = e->m;
+  const int64_t H = m.H, kv = static_cast<int64_t>(m.nkv) * m.d;
+  if (name == "model.embed_tokens.weight") { tp = {TensorPlace::kFlat, e->embed, m.V, H, 0, H}; return true; }
+  if (name == "model.norm.weight") { tp = {TensorPlace::kFlat, e->final_norm, 1, H, 0, H}; return true; }
+  if (name == "lm_head.weight") { tp = {TensorPlace::kFlat, e->lm_head, m.V, H, 0, H}; return true; }
+  const std::string prefix = "model.layers.";
+  if (name.compare(0, prefix.size(), prefix) != 0) return false;
+  const size_t dot = name.find('.', prefix.size());
+  if (dot == std::string::npos) return false;
+  const int layer = std::atoi(name.substr(prefix.size(), dot - prefix.size()).c_str());
+  if (layer < 0 || layer >= m.L) return false;
+  const std::string key = name.substr(dot + 1);
+  const LayerWeights &lw = e->layers[layer];
+  auto mut = [](const bf16 *p) { return const_cast<bf16 *>(p); };
+  if (key == "input_layernorm.weight") { tp = {TensorPlace::kFlat, mut(lw.w_in), 1, H, 0, H}; return true; }
+  if (key == "post_attention_layernorm.weight") { tp = {TensorPlace::kFlat, mut(lw.w_post), 1, H, 0, H}; return true; }
+  if (key == "self_attn.q_proj.weight") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_w), H, H, 0, H}; return true; }
+  if (key == "self_attn.k_proj.weight") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_w), kv, H, H, H}; return true; }
+  if (key == "self_attn.v_proj.weight") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_w), kv, H, H + kv, H}; return true; }
+  if (key == "self_attn.q_proj.bias") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_b), H, 1, 0, 1}; return true; }
+  if (key == "self_attn.k_proj.bias") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_b), kv, 1, H, 1}; return true; }
+  if (key == "self_attn.v_proj.bias") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_b), kv, 1, H + kv, 1}; return true; }
+  if (key == "self_attn.o_proj.weight") { tp = {TensorPlace::kFlat, mut(lw.o_w), H, H, 0, H}; return true; }
+  if (key == "mlp.gate_proj.weight") { tp = {TensorPlace::kGate, mut(lw.gu_w), m.I, H, 0, H}; return true; }
+  if (key == "mlp.up_proj.weight") { tp = {TensorPlace::kUp, mut(lw.gu_w), m.I, H, 0, H}; return true; }
+  if (key == "mlp.down_proj.weight") { tp = {TensorPlace::kDownCols, mut(lw.down_w), H, m.I, 0, m.I_pad}; return true; }
+  return false;
+}
+
+int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t bytes, bool to_device) {
+  TensorPlace tp;
+  if (!locate(e, name, tp)) return -1;
+  if (bytes != static_cast<uint64_t>(tp.rows * tp.cols * 2)) return -1;
+  const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+  cudaError_t err = cudaSuccess;
+  const size_t row_bytes = static_cast<size_t>(tp.cols) * 2;
+  switch (tp.kind) {
+    case TensorPlace::kFlat:
+    case TensorPlace::kRowsAt: {
+      bf16 *dev = tp.base + tp.row_offset * tp.cols;
+      err = to_device ? cudaMemcpy(dev, host, bytes, kind) : cudaMemcpy(host, dev, bytes, kind);
+      break;
+    }
+    case TensorPlace::kGate:
+    case TensorPlace::kUp: {
+      // packed [I/8][16][H]: gate rows at 0..7, up rows at 8..15 of each group
+      bf16 *dev = tp.base + (tp.kind == TensorPlace::kUp ? 8 : 0) * tp.cols;
+      const size_t dpitch = 16 * row_bytes, spitch = 8 * row_bytes;
+      const size_t height = static_cast<size_t>(tp.rows / 8);
+      err = to_device ? cudaMemcpy2D(dev, dpitch, host, spitch, spitch, height, kind)
+                      : cudaMemcpy2D(host, spitch, dev, dpitch, spitch, height, kind);
+      break;
+    }
+    case TensorPlace::kDownCols: {
+      const size_t dpitch = static_cast<size_t>(tp.dst_cols) * 2;
+      err = to_device ? cudaMemcpy2D(tp.base, dpitch, host, row_bytes, row_bytes, tp.rows, kind)
+                      : cudaMemcpy2D(host, row_bytes, tp.base, dpitch, row_bytes, tp.rows, kind);
+      break;
+    }
+  }
+  return set_err(e, err, name.c_str());
+}
+
+int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
+  const ModelDims &m = e->m;
+  const double sigma = 2.0 * std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  const float scale = static_cast<float>(stddev / sigma);
+  const int64_t H = m.H, kv = static_cast<int64_t>(m.nkv) * m.d;
+  auto launch = [&](bf16 *dst, int64_t count, SynthMap map) {
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((count + threads - 1) / threads, 148LL * 64);
+    synth_kernel<<<static_cast<unsigned>(blocks), threads, 0, e->stream>>>(
+        reinterpret_cast<uint16_t *>(dst), count, map, seed, scale);
+  };
+  auto plain = [&](int id) { SynthMap s{}; s.mode = kPlain; s.ids[0] = id; return s; };
+  const int L = m.L;
+  launch(e->embed, static_cast<int64_t>(m.V) * H, plain(0));
+  for (int l = 0; l < L; ++l) {
+    const int base = 1 + kLayerTensors * l;
+    const LayerWeights &lw = e->layers[l];
+    launch(const_cast<bf16 *>(lw.w_in), H, plain(base + 0));
+    launch(const_cast<bf16 *>(lw.w_post), H, plain(base + 1));
+    SynthMap q{};
+    q.mode = kQkvRows; q.ids[0] = base + 2; q.ids[1] = base + 4; q.ids[2] = base + 6;
+    q.cols = H; q.rows0 = H; q.rows1 = kv;
+    launch(const_cast<bf16 *>(lw.qkv_w), static_cast<int64_t>(m.Nqkv) * H, q);
+    SynthMap qb = q;
+    qb.ids[0] = base + 3; qb.ids[1] = base + 5; qb.ids[2] = base + 7; qb.cols = 1;
+    launch(const_cast<bf16 *>(lw.qkv_b), m.Nqkv, qb);
+    launch(const_cast<bf16 *>(lw.o_w), H * H, plain(base + 8));
+    SynthMap gu{};
+    gu.mode = kGateUp; gu.ids[0] = base + 9; gu.ids[1] = base + 10; gu.cols = H;
+    launch(const_cast<bf16 *>(lw.gu_w), 2LL * m.I * H, gu);
+    SynthMap dn{};
+    dn.mode = kDownPad; dn.ids[0] = base + 11; dn.cols = m.I; dn.dst_cols = m.I_pad;
+    launch(const_cast<bf16 *>(lw.down_w), H * m.I_pad, dn);
+  }
+  launch(e->final_norm, H, plain(1 + kLayerTensors * L));
+  SynthMap lm{};
+  lm.mode = kRowsPad; lm.ids[0] = 2 + kLayerTensors * L; lm.cols = H; lm.rows0 = m.V;
+  launch(e->lm_head, static_cast<int64_t>(m.V_pad) * H, lm);
+  cudaError_t err = cudaGetLastError();
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  return set_err(e, err, "synthetic weights");
+}
+
+int64_t import_payload_bytes(const Engine *e) {
+  return 2LL * e->m.L * kBatch * e->m.bs * e->m.nkv * e->m.d * 2;
+}
+
+// One epoch: H2D of the 8 inputs (+ optional import payload), one cooperative
+// launch, D2H of the 2 outputs.
+int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, const int32_t *seq_len,
+                  const int32_t *slot, const int32_t *active, const int32_t *block_table,
+                  const uint8_t *tiling, const int32_t *control, const void *payload,
+                  uint64_t payload_bytes, int64_t *history, int32_t *control_out, float *logits_out,
+                  const int64_t *forced = nullptr, bool payload_on_device = false) {
+  cudaSetDevice(e->device);
+  EpochIO *io = e->h_io;
+  std::memset(io, 0, sizeof(EpochIO));
+  std::memcpy(io->token, token, sizeof(io->token));
+  std::memcpy(io->position, position, sizeof(io->position));
+  std::memcpy(io->seq_len, seq_len, sizeof(io->seq_len));
+  std::memcpy(io->slot, slot, sizeof(io->slot));
+  std::memcpy(io->active, active, sizeof(io->active));
+  std::memcpy(io->block_table, block_table, sizeof(int32_t) * kBatch * e->m.bpr);
+  std::memcpy(io->control, control, sizeof(io->control));
+  if (tiling != nullptr) std::memcpy(io->tiling, tiling, kTilingBytes);
+  if (forced != nullptr) {
+    io->use_forced = 1;
+    std::memcpy(io->forced, forced, sizeof(io->forced));
+  }
+  const bool importing = (control[2 + kBatch] & kImportFlag) != 0;
+  cudaError_t err = cudaSuccess;
+  if (importing) {
+    if (payload == nullptr || payload_bytes != static_cast<uint64_t>(import_payload_bytes(e))) return -1;
+    if (!payload_on_device) {
+      if (e->d_payload == nullptr) {
+        err = cudaMalloc(&e->d_payload, payload_bytes);
+        if (err != cudaSuccess) return set_err(e, err, "import staging");
+        e->payload_bytes = payload_bytes;
+      }
+      err = cudaMemcpyAsync(e->d_payload, payload, payload_bytes, cudaMemcpyHostToDevice, e->stream);
+      if (err != cudaSuccess) return set_err(e, err, "import payload copy");
+    }
+  }
+  const size_t in_bytes = offsetof(EpochIO, history);
+  err = cudaMemcpyAsync(e->d_io, io, in_bytes, cudaMemcpyHostToDevice, e->stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sizeof(SyncState), e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "epoch inputs");
+
+  EpochParams p{};
+  p.m = e->m;
+  p.layers = e->d_layers;
+  p.embed = e->embed;
+  p.final_norm = e->final_norm;
+  p.lm_head = e->lm_head;
+  p.rope_cos = e->rope_cos;
+  p.rope_sin = e->rope_sin;
+  p.key_cache = e->key_cache;
+  p.value_cache = e->value_cache;
+  p.h = e->h;
+  p.qkv = e->qkv;
+  p.attn = e->attn;
+  p.act = e->act;
+  p.partials = e->partials;
+  p.arg_val = e->arg_val;
+  p.arg_idx = e->arg_idx;
+  p.arg_bad = e->arg_bad;
+  p.logits = logits_out != nullptr ? e->logits : nullptr;
+  p.import_payload = payload_on_device ? static_cast<const uint8_t *>(payload) : e->d_payload;
+  p.io = e->d_io;
+  p.res = e->d_res;
+  p.work = e->d_work;
+  p.sync = e->d_sync;
+  p.grid = e->sms;
+  p.stages = e->stages;
+  p.xs_stride = e->xs_stride;
+  p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
+  void *args[] = {&p};
+  cudaEventRecord(e->ev0, e->stream);
+  err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
+                                    dim3(kThreads), args, e->smem, e->stream);
+  cudaEventRecord(e->ev1, e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "epoch launch");
+  err = cudaMemcpyAsync(&io->history, &e->d_io->history,
+                        sizeof(EpochIO) - offsetof(EpochIO, history), cudaMemcpyDeviceToHost, e->stream);
+  if (err == cudaSuccess && logits_out != nullptr) {
+    err = cudaMemcpyAsync(logits_out, e->logits, sizeof(float) * kMaxSteps * kBatch * e->m.V,
+                          cudaMemcpyDeviceToHost, e->stream);
+  }
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "epoch completion");
+  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  e->last_launches = 1;
+  std::memcpy(history, io->history, sizeof(io->history));
+  std::memcpy(control_out, io->control_out, sizeof(io->control_out));
+  return 0;
+}
+
+// ---- reference bridge helpers (native/resident_epoch_bridge.cpp) -----------------------------
+#pragma pack(push, 1)
+struct TransferHeader {   // :73-89
+  uint64_t magic;
+  uint32_t version;
+  uint32_t header_bytes;
+  uint64_t transfer_id;
+  uint64_t payload_bytes;
+  uint32_t import_mask;
+  int32_t row_generations[kBatch];
+  uint32_t layers, batch_size, block_size, kv_heads, head_size, element_bytes;
+  uint32_t checksum;
+};
+#pragma pack(pop)
+static_assert(sizeof(TransferHeader) == CRUISE_RESIDENT_TRANSFER_HEADER_BYTES, "transfer header ABI");
+static_assert(sizeof(ResidentEpochIpcMetadata) == CRUISE_RESIDENT_IPC_METADATA_BYTES, "IPC metadata ABI");
+
+std::mutex g_lifecycle_mutex;
+bool g_bridge_active = false;
+
+struct BridgeEngine {
+  Engine *engine = nullptr;
+  std::map<std::string, void *> ipc_imports;
+};
+
+bool read_transfer(const Engine *e, const char *path, uint64_t transfer_id, const int32_t *gens,
+                   std::vector<uint8_t> &payload, int32_t &mask, uint32_t &checksum) {   // :108-154
+  if (path == nullptr || gens == nullptr || transfer_id == 0 || std::strncmp(path, "/dev/shm/", 9) != 0)
+    return false;
+  const uint64_t payload_bytes = static_cast<uint64_t>(import_payload_bytes(e));
+  std::ifstream stream(path, std::ios::binary | std::ios::ate);
+  if (!stream || static_cast<uint64_t>(stream.tellg()) != CRUISE_RESIDENT_TRANSFER_HEADER_BYTES + payload_bytes)
+    return false;
+  stream.seekg(0, std::ios::beg);
+  TransferHeader h{};
+  stream.read(reinterpret_cast<char *>(&h), sizeof(h));
+  if (!stream || h.magic != CRUISE_RESIDENT_TRANSFER_MAGIC || h.version != CRUISE_RESIDENT_TRANSFER_VERSION ||
+      h.header_bytes != CRUISE_RESIDENT_TRANSFER_HEADER_BYTES || h.transfer_id != transfer_id ||
+      h.payload_bytes != payload_bytes || h.import_mask == 0 || h.import_mask >= (1u << kBatch) ||
+      h.layers != static_cast<uint32_t>(e->m.L) || h.batch_size != kBatch ||
+      h.block_size != static_cast<uint32_t>(e->m.bs) || h.kv_heads != static_cast<uint32_t>(e->m.nkv) ||
+      h.head_size != static_cast<uint32_t>(e->m.d) || h.element_bytes != 2 || h.checksum == 0)
+    return false;
+  for (int r = 0; r < kBatch; ++r) {
+    const bool sel = (h.import_mask & (1u << r)) != 0;
+    if (sel) {
+      if (h.row_generations[r] <= 0 || h.row_generations[r] != gens[r]) return false;
+    } else if (h.row_generations[r] != 0) {
+      return false;
+    }
+  }
+  payload.resize(payload_bytes);
+  stream.read(reinterpret_cast<char *>(payload.data()), static_cast<std::streamsize>(payload.size()));
+  if (!stream) return false;
+  mask = static_cast<int32_t>(h.import_mask);
+  checksum = h.checksum;
+  return true;
+}
+
+bool validate_ipc(const Engine *e, const ResidentEpochIpcMetadata *md, const int32_t *gens) {   // :156-199
+  if (md == nullptr || gens == nullptr || md->magic != CRUISE_RESIDENT_IPC_METADATA_MAGIC ||
+      md->version != CRUISE_RESIDENT_IPC_METADATA_VERSION || md->source_bytes == 0 || md->import_mask == 0 ||
+      md->import_mask >= (1u << kBatch))
+    return false;
+  if (e->m.L * 2 > CRUISE_RESIDENT_IPC_KEY_COUNT) return false;
+  const uint64_t block_bytes = static_cast<uint64_t>(e->m.bs) * e->m.nkv * e->m.d * 2;
+  for (int r = 0; r < kBatch; ++r) {
+    const bool sel = (md->import_mask & (1u << r)) != 0;
+    if (sel) {
+      if (md->row_generations[r] <= 0 || md->row_generations[r] != gens[r] || md->block_ids[r] < 0) return false;
+    } else if (md->row_generations[r] != 0 || md->block_ids[r] != 0) {
+      return false;
+    }
+  }
+  for (int i = 0; i < 2 * e->m.L; ++i) {
+    for (int r = 0; r < kBatch; ++r) {
+      if ((md->import_mask & (1u << r)) == 0) continue;
+      const uint64_t end = (static_cast<uint64_t>(md->block_ids[r]) + 1u) * block_bytes;
+      if (md->source_offsets[i] > md->source_bytes || end > md->source_bytes - md->source_offsets[i]) return false;
+    }
+  }
+  return true;
+}
+
+// Opens the exporting process's K/V allocations (cudaIpcMemHandle_t in each
+// 64-byte key) and gathers the selected blocks into the import staging buffer
+// with device-to-device copies (:218-273).
+bool prepare_ipc_payload(BridgeEngine *be, const ResidentEpochIpcMetadata *md) {
+  Engine *e = be->engine;
+  const size_t bytes = static_cast<size_t>(import_payload_bytes(e));
+  if (e->d_payload == nullptr) {
+    if (cudaMalloc(&e->d_payload, bytes) != cudaSuccess) return false;
+    e->payload_bytes = bytes;
+  }
+  if (cudaMemsetAsync(e->d_payload, 0, bytes, e->stream) != cudaSuccess) return false;
+  const size_t block_bytes = static_cast<size_t>(e->m.bs) * e->m.nkv * e->m.d * 2;
+  const size_t cache_bytes = bytes / 2;
+  for (int layer = 0; layer < e->m.L; ++layer) {
+    void *src[2] = {nullptr, nullptr};
+    for (int kvi = 0; kvi < 2; ++kvi) {
+      const std::string key(md->keys[layer * 2 + kvi], CRUISE_RESIDENT_IPC_KEY_BYTES);
+      auto it = be->ipc_imports.find(key);
+      if (it == be->ipc_imports.end()) {
+        cudaIpcMemHandle_t handle;
+        std::memcpy(&handle, md->keys[layer * 2 + kvi], sizeof(handle));
+        void *ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return false;
+        it = be->ipc_imports.emplace(key, ptr).first;
+      }
+      src[kvi] = it->second;
+    }
+    for (int r = 0; r < kBatch; ++r) {
+      if ((md->import_mask & (1u << r)) == 0) continue;
+      const size_t off = static_cast<size_t>(md->block_ids[r]) * block_bytes;
+      const size_t row_off = (static_cast<size_t>(layer) * kBatch + r) * block_bytes;
+      for (int kvi = 0; kvi < 2; ++kvi) {
+        const uint8_t *s = static_cast<const uint8_t *>(src[kvi]) + md->source_offsets[layer * 2 + kvi] + off;
+        if (cudaMemcpyAsync(e->d_payload + kvi * cache_bytes + row_off, s, block_bytes, cudaMemcpyDeviceToDevice,
+                            e->stream) != cudaSuccess)
+          return false;
+      }
+    }
+  }
+  return true;
+}
+
+int64_t process_cpu_us() {
+  timespec v{};
+  if (clock_gettime(CLOCK_PROCESS_CPUTIME_ID, &v) != 0) return -1;
+  return static_cast<int64_t>(v.tv_sec) * 1000000LL + v.tv_nsec / 1000;
+}
+
+int32_t preset(const char *name, CruiseModelConfig *cfg) {
+  if (name == nullptr || cfg == nullptr) return -1;
+  std::memset(cfg, 0, sizeof(*cfg));
+  cfg->rms_eps = 1e-6f;
+  cfg->rope_theta = 1000000.0f;
+  cfg->blocks_per_row = 2;
+  cfg->num_blocks = 8;
+  if (std::strcmp(name, "qwen2.5-7b") == 0) {
+    cfg->num_layers = 28; cfg->hidden = 3584; cfg->num_heads = 28; cfg->num_kv_heads = 4;
+    cfg->head_dim = 128; cfg->intermediate = 18944; cfg->vocab = 152064; cfg->block_size = 128;
+    cfg->configured_eos = 151645;
+    return 0;
+  }
+  if (std::strcmp(name, "tiny") == 0) {
+    cfg->num_layers = 2; cfg->hidden = 256; cfg->num_heads = 4; cfg->num_kv_heads = 2;
+    cfg->head_dim = 64; cfg->intermediate = 688; cfg->vocab = 4096; cfg->block_size = 16;
+    cfg->configured_eos = 4095;
+    return 0;
+  }
+  return -1;
+}
+
+}  // namespace
+}  // namespace cruise
+
+using cruise::BridgeEngine;
+using cruise::Engine;
+using cruise::kBatch;
+using cruise::kMaxSteps;
+
+// ===================================== C ABI =========================================================
+extern "C" {
+
+int32_t cruise_epoch_preset(const char *name, CruiseModelConfig *cfg) { return cruise::preset(name, cfg); }
+
+void *cruise_epoch_create(const CruiseModelConfig *cfg, int32_t device, int32_t *status) {
+  int32_t dummy = 0;
+  if (status == nullptr) status = &dummy;
+  *status = 1;
+  if (cfg == nullptr) return nullptr;
+  return cruise::create_engine(*cfg, device, status);
+}
+
+void cruise_epoch_destroy(void *engine) { cruise::destroy_engine(static_cast<Engine *>(engine)); }
+
+int32_t cruise_epoch_init_synthetic(void *engine, uint64_t seed, double stddev) {
+  if (engine == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  return cruise::synth_all(e, seed, stddev);
+}
+
+int32_t cruise_epoch_set_weight(void *engine, const char *name, const void *host_bf16, uint64_t bytes) {
+  if (engine == nullptr || name == nullptr || host_bf16 == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  return cruise::copy_tensor(e, name, const_cast<void *>(host_bf16), bytes, true);
+}
+
+int32_t cruise_epoch_get_weight(void *engine, const char *name, void *host_bf16, uint64_t bytes) {
+  if (engine == nullptr || name == nullptr || host_bf16 == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  return cruise::copy_tensor(e, name, host_bf16, bytes, false);
+}
+
+int32_t cruise_epoch_set_rope_table(void *engine, const uint16_t *cos_bf16, const uint16_t *sin_bf16,
+                                    uint64_t bytes) {
+  if (engine == nullptr || cos_bf16 == nullptr || sin_bf16 == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  if (bytes != static_cast<uint64_t>(e->m.C) * e->m.d * 2) return -1;
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  cudaError_t err = cudaMemcpy(e->rope_cos, cos_bf16, bytes, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemcpy(e->rope_sin, sin_bf16, bytes, cudaMemcpyHostToDevice);
+  return cruise::set_err(e, err, "rope table");
+}
+
+int32_t cruise_epoch_read_kv(void *engine, void *key_host, void *value_host, uint64_t bytes_each) {
+  if (engine == nullptr || key_host == nullptr || value_host == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  const uint64_t expect = static_cast<uint64_t>(e->m.L) * e->m.NB * e->m.bs * e->m.nkv * e->m.d * 2;
+  if (bytes_each != expect) return -1;
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  cudaError_t err = cudaMemcpy(key_host, e->key_cache, bytes_each, cudaMemcpyDeviceToHost);
+  if (err == cudaSuccess) err = cudaMemcpy(value_host, e->value_cache, bytes_each, cudaMemcpyDeviceToHost);
+  return cruise::set_err(e, err, "read kv");
+}
+
+int32_t cruise_epoch_write_kv(void *engine, const void *key_host, const void *value_host, uint64_t bytes_each) {
+  if (engine == nullptr || key_host == nullptr || value_host == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  const uint64_t expect = static_cast<uint64_t>(e->m.L) * e->m.NB * e->m.bs * e->m.nkv * e->m.d * 2;
+  if (bytes_each != expect) return -1;
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  cudaError_t err = cudaMemcpy(e->key_cache, key_host, bytes_each, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemcpy(e->value_cache, value_host, bytes_each, cudaMemcpyHostToDevice);
+  return cruise::set_err(e, err, "write kv");
+}
+
+int32_t cruise_epoch_run(void *engine, const int64_t *token, const int64_t *position, const int32_t *seq_len,
+                         const int32_t *slot, const int32_t *active, const int32_t *block_table,
+                         const uint8_t *tiling, const int32_t *control, const void *import_payload,
+                         uint64_t import_bytes, const int64_t *forced_tokens, int64_t *history,
+                         int32_t *control_out, float *logits_out) {
+  if (engine == nullptr || token == nullptr || position == nullptr || seq_len == nullptr || slot == nullptr ||
+      active == nullptr || block_table == nullptr || control == nullptr || history == nullptr ||
+      control_out == nullptr)
+    return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  return cruise::run_epoch(e, token, position, seq_len, slot, active, block_table, tiling, control,
+                           import_payload, import_bytes, history, control_out, logits_out, forced_tokens);
+}
+
+int32_t cruise_epoch_last_timing(void *engine, double *device_us, int32_t *kernel_launches) {
+  if (engine == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  if (device_us) *device_us = static_cast<double>(e->last_ms) * 1000.0;
+  if (kernel_launches) *kernel_launches = e->last_launches;
+  return 0;
+}
+
+const char *cruise_epoch_last_error(void *engine) {
+  if (engine == nullptr) return "null engine";
+  return static_cast<Engine *>(engine)->last_error.c_str();
+}
+
+// ---- reference-compatible bridge ----------------------------------------------------------------------
+void *resident_epoch_create(const char *air_path, const char *graph_config, const char *func_config,
+                            const char *external_weight_dir, const char *tiling_path, int32_t *status) {
+  (void)graph_config;
+  (void)func_config;
+  if (status == nullptr) return nullptr;
+  *status = 1;
+  std::lock_guard<std::mutex> lifecycle(cruise::g_lifecycle_mutex);
+  if (cruise::g_bridge_active || air_path == nullptr || external_weight_dir == nullptr) return nullptr;
+  CruiseModelConfig cfg{};
+  if (cruise::preset(air_path, &cfg) != 0) { *status = 5; return nullptr; }
+  std::array<uint8_t, cruise::kTilingBytes> tiling{};
+  if (tiling_path != nullptr && tiling_path[0] != '\0') {
+    std::ifstream t(tiling_path, std::ios::binary | std::ios::ate);
+    if (!t || static_cast<size_t>(t.tellg()) != tiling.size()) { *status = 2; return nullptr; }
+    t.seekg(0, std::ios::beg);
+    t.read(reinterpret_cast<char *>(tiling.data()), tiling.size());
+    if (!t) { *status = 2; return nullptr; }
+  }
+  Engine *e = cruise::create_engine(cfg, 0, status);
+  if (e == nullptr) return nullptr;
+  e->tiling = tiling;
+  const std::string weights(external_weight_dir);
+  int32_t rc = 0;
+  if (weights.rfind("synthetic:", 0) == 0) {
+    rc = cruise::synth_all(e, std::strtoull(weights.c_str() + 10, nullptr, 10), 0.02);
+  } else {
+    // one raw bf16 file per checkpoint tensor
+    std::vector<std::string> names = {"model.embed_tokens.weight", "model.norm.weight", "lm_head.weight"};
+    for (int l = 0; l < e->m.L; ++l)
+      for (int k = 0; k < cruise::kLayerTensors; ++k)
+        names.push_back("model.layers." + std::to_string(l) + "." + cruise::kLayerKeys[k]);
+    for (const auto &n : names) {
+      std::ifstream f(weights + "/" + n + ".bin", std::ios::binary | std::ios::ate);
+      if (!f) { rc = -1; break; }
+      std::vector<char> buf(static_cast<size_t>(f.tellg()));
+      f.seekg(0, std::ios::beg);
+      f.read(buf.data(), static_cast<std::streamsize>(buf.size()));
+      if (!f || cruise::copy_tensor(e, n, buf.data(), buf.size(), true) != 0) { rc = -1; break; }
+    }
+  }
+  if (rc != 0) {
+    cruise::destroy_engine(e);
+    *status = 4;
+    return nullptr;
+  }
+  auto *be = new BridgeEngine();
+  be->engine = e;
+  cruise::g_bridge_active = true;
+  *status = 0;
+  return be;
+}
+
+int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_steps,
+                               const int64_t *input_token_ids, const int64_t *input_positions,
+                               const int32_t *input_sequence_lengths, const int32_t *input_eos_token_ids,
+                               const int32_t *input_row_generations, int64_t *output_token_ids,
+                               int32_t *output_executed, int32_t *output_row_generations,
+                               int32_t *output_model_calls, int32_t *output_device_status,
+                               int32_t *output_feed_calls, int32_t *output_fetch_calls,
+                               int32_t *output_commit_state, int32_t *output_kv_import_checksum,
+                               int64_t *output_wall_us, int64_t *output_native_cpu_us,
+                               int64_t *output_declared_input_bytes, int64_t *output_declared_output_bytes,
+                               const char *transfer_path, uint64_t transfer_id,
+                               const ResidentEpochIpcMetadata *ipc_metadata) {
+  if (output_commit_state == nullptr) return 10;
+  *output_commit_state = CRUISE_EPOCH_PREPARED;
+  const bool device_import = ipc_metadata != nullptr;
+  const bool importing = transfer_path != nullptr || device_import;
+  if (opaque == nullptr || request_count < 1 || request_count > kBatch || max_steps < 1 || max_steps > kMaxSteps ||
+      input_token_ids == nullptr || input_positions == nullptr || input_sequence_lengths == nullptr ||
+      input_eos_token_ids == nullptr || input_row_generations == nullptr || output_token_ids == nullptr ||
+      output_executed == nullptr || output_row_generations == nullptr || output_model_calls == nullptr ||
+      output_device_status == nullptr || output_feed_calls == nullptr || output_fetch_calls == nullptr ||
+      output_kv_import_checksum == nullptr || output_wall_us == nullptr || output_native_cpu_us == nullptr ||
+      output_declared_input_bytes == nullptr || output_declared_output_bytes == nullptr ||
+      (importing && transfer_id == 0) || (!importing && transfer_id != 0) ||
+      (transfer_path != nullptr && device_import))
+    return 10;
+  auto *be = static_cast<BridgeEngine *>(opaque);
+  Engine *e = be->engine;
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  const cruise::ModelDims &m = e->m;
+  std::vector<uint8_t> payload;
+  int32_t import_mask = 0;
+  uint32_t expected_checksum = 0;
+  if (importing && !device_import &&
+      !cruise::read_transfer(e, transfer_path, transfer_id, input_row_generations, payload, import_mask,
+                             expected_checksum))
+    return 13;
+  if (device_import) {
+    if (!cruise::validate_ipc(e, ipc_metadata, input_row_generations) || !cruise::prepare_ipc_payload(be, ipc_metadata))
+      return 35;
+    import_mask = static_cast<int32_t>(ipc_metadata->import_mask);
+  }
+  *output_model_calls = 0;
+  *output_device_status = -1;
+  *output_feed_calls = 0;
+  *output_fetch_calls = 0;
+  *output_kv_import_checksum = 0;
+  *output_wall_us = 0;
+  *output_native_cpu_us = 0;
+  const int64_t payload_bytes = cruise::import_payload_bytes(e);
+  *output_declared_input_bytes = device_import ? CRUISE_SIDECAR_REQUEST_BYTES + CRUISE_RESIDENT_IPC_METADATA_BYTES
+                                               : (importing ? payload_bytes + 244 : 260);
+  *output_declared_output_bytes = 368;
+  const int64_t cpu_start = cruise::process_cpu_us();
+  std::fill(output_token_ids, output_token_ids + kBatch * kMaxSteps, -1);
+  std::fill(output_executed, output_executed + kBatch, 0);
+  std::fill(output_row_generations, output_row_generations + kBatch, 0);
+
+  int64_t tokens[kBatch] = {0}, positions[kBatch] = {0};
+  int32_t lengths[kBatch] = {0}, slots[kBatch] = {0}, active[kBatch] = {0};
+  std::vector<int32_t> blocks(kBatch * m.bpr);
+  for (int r = 0; r < kBatch; ++r)
+    for (int j = 0; j < m.bpr; ++j) blocks[r * m.bpr + j] = r * m.bpr + j;   // :524-532
+  auto slot_of = [&](int r, int64_t pos) {
+    if (pos < 0 || pos >= m.C) return -1;
+    return static_cast<int32_t>((r * m.bpr + pos / m.bs) * m.bs + pos % m.bs);
+  };
+  for (int r = 0; r < kBatch; ++r) slots[r] = slot_of(r, 0);
+  int32_t count = 0;
+  for (int r = 0; r < kBatch; ++r) {
+    if (input_row_generations[r] == 0) continue;
+    ++count;
+    if (input_row_generations[r] < 0 || input_token_ids[r] < 0 || input_token_ids[r] >= m.V ||
+        input_positions[r] < 0 || input_positions[r] + max_steps > m.C ||
+        input_sequence_lengths[r] != input_positions[r] + 1 || input_eos_token_ids[r] < 0 ||
+        input_eos_token_ids[r] >= m.V)
+      return 11;
+    tokens[r] = input_token_ids[r];
+    positions[r] = input_positions[r];
+    lengths[r] = input_sequence_lengths[r];
+    slots[r] = slot_of(r, input_positions[r]);
+    active[r] = 1;
+  }
+  if (count != request_count) return 12;
+  int32_t control[cruise::kControlIn] = {0};
+  control[0] = max_steps;
+  for (int r = 0; r < kBatch; ++r)
+    control[1 + r] = input_row_generations[r] != 0 ? input_eos_token_ids[r] : e->cfg.configured_eos;
+  control[1 + kBatch] = 0;
+  control[2 + kBatch] = importing ? (cruise::kImportFlag | import_mask) : 0;
+  for (int r = 0; r < kBatch; ++r) control[3 + kBatch + r] = input_row_generations[r];
+
+  int64_t history[kMaxSteps * kBatch];
+  int32_t out[cruise::kControlOut];
+  const auto wall_start = std::chrono::steady_clock::now();
+  *output_commit_state = CRUISE_EPOCH_EXECUTING;
+  const int32_t rc = cruise::run_epoch(
+      e, tokens, positions, lengths, slots, active, blocks.data(), e->tiling.data(), control,
+      device_import ? static_cast<const void *>(e->d_payload) : (importing ? payload.data() : nullptr),
+      importing ? static_cast<uint64_t>(payload_bytes) : 0, history, out, nullptr, nullptr, device_import);
+  const auto wall_end = std::chrono::steady_clock::now();
+  *output_feed_calls = 1;
+  if (rc != 0) return 30;
+  *output_fetch_calls = 1;
+  *output_wall_us = std::chrono::duration_cast<std::chrono::microseconds>(wall_end - wall_start).count();
+  *output_device_status = out[3];
+  *output_model_calls = out[4];
+  *output_kv_import_checksum = out[5];
+  if (*output_device_status == 0) {
+    if (device_import && *output_kv_import_checksum == 0) return 34;
+    if (importing && !device_import && static_cast<uint32_t>(*output_kv_import_checksum) != expected_checksum)
+      return 34;
+  }
+  for (int r = 0; r < kBatch; ++r) {
+    const int32_t executed = out[6 + 2 * kBatch + r];
+    if (executed < 0 || executed > max_steps) return 33;
+    output_executed[r] = executed;
+    output_row_generations[r] = out[6 + 4 * kBatch + 2 + r];
+    for (int s = 0; s < executed; ++s) output_token_ids[r * kMaxSteps + s] = history[s * kBatch + r];
+  }
+  const int64_t cpu_end = cruise::process_cpu_us();
+  if (cpu_start >= 0 && cpu_end >= cpu_start) *output_native_cpu_us = cpu_end - cpu_start;
+  *output_commit_state = CRUISE_EPOCH_COMMITTED;
+  return 0;
+}
+
+void resident_epoch_destroy(void *opaque) {
+  if (opaque == nullptr) return;
+  std::lock_guard<std::mutex> lifecycle(cruise::g_lifecycle_mutex);
+  auto *be = static_cast<BridgeEngine *>(opaque);
+  {
+    std::lock_guard<std::mutex> lock(be->engine->execute_mutex);
+    cudaSetDevice(be->engine->device);
+    for (auto &entry : be->ipc_imports) cudaIpcCloseMemHandle(entry.second);
+    be->ipc_imports.clear();
+  }
+  cruise::destroy_engine(be->engine);
+  delete be;
+  cruise::g_bridge_active = false;
+}
+
+}  // extern "C"

@@ -1,0 +1,1096 @@
+// epoch_kernel.cuh -- the resident decode epoch as ONE persistent cooperative
+// kernel for sm_100a (one CTA per SM).
+//
+// The kernel runs the whole epoch of the reference's device controller
+// (controller/g4c_b4_resident_epoch.cpp:177-631) with no host involvement:
+// validation, the one-shot KV import with its Adler-32 proof, generation
+// continuity, then up to K full Qwen2 decoder steps
+// (batched_decoder_step.py:277-417) each ending in a greedy argmax and the
+// per-row EOS / max-step / slot / length bookkeeping.
+//
+// CTA layout: warps 0-7 are consumers (math, epilogues, control), warp 8 is
+// the weight producer.  The producer streams every weight tile this CTA will
+// consume, in consumption order, from HBM into a ring of shared-memory stages
+// with 1-D bulk (TMA) copies completed on mbarriers.  Weights do not depend on
+// activations, so it keeps prefetching across the grid barriers that separate
+// phases; the consumers only wait for activations.
+//
+// Projection (GEMV) phases: y[4,N] = x[4,K] . W[N,K]^T.  W is cut into tiles of
+// 16 rows x kc columns; the tiles of a phase are split into equal contiguous
+// ranges over the CTAs ("stream-K"), so a row group may be split between two
+// neighbouring CTAs: the upper part publishes fp32 partial sums, the lower
+// part adds them in fixed order and runs the epilogue.  Inside a tile the 8
+// consumer warps each take 64 columns and issue bf16 mma.sync m16n8k16 with W
+// as the A operand and the 4 activation rows padded to n = 8 as B (the padding
+// costs nothing: the phase is bandwidth bound).  A dot product may sum its k
+// terms in any order, so each thread loads 16 contiguous weights per row with
+// 128-bit shared loads and feeds them to four MMAs under one k permutation
+// that the A and B fragments share.
+//
+// Every cross-CTA wait (grid barrier, split partial flag) and every mbarrier
+// wait is bounded by a timeout; on expiry the kernel records status 207 and
+// all CTAs leave, so a fault can never leave the GPU spinning.
+#pragma once
+
+#include <cfloat>
+#include <climits>
+#include <cstdint>
+
+#include "epoch_types.h"
+#include "ptx.cuh"
+
+namespace cruise {
+
+enum GemvKind : int32_t { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
+enum XMode : int32_t { kXNorm = 0, kXCopy = 1 };
+
+struct Gemv {
+  const bf16 *W;
+  const bf16 *bias;      // kQKV only
+  const bf16 *norm_w;    // kXNorm only
+  const bf16 *xsrc;      // activation source, [4][xsrc_stride]
+  int32_t N, K, kc, kind;
+  int32_t xmode;
+  int32_t xsrc_stride;
+  int32_t embed_src;     // 1: the norm source is embed[token[b]] (layer 0)
+};
+
+__host__ __device__ inline int pick_kc(int K) {
+  // largest multiple of 64 that divides K and is <= kMaxKc
+  for (int kc = kMaxKc; kc >= 64; kc -= 64)
+    if (K % kc == 0) return kc;
+  return 64;
+}
+
+__device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int kind) {
+  const ModelDims &m = p.m;
+  Gemv g{};
+  g.kind = kind;
+  if (kind == kLM) {
+    g.W = p.lm_head; g.N = m.V_pad; g.K = m.H;
+    g.xmode = kXNorm; g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = p.final_norm;
+  } else {
+    const LayerWeights &lw = p.layers[layer];
+    switch (kind) {
+      case kQKV:
+        g.W = lw.qkv_w; g.bias = lw.qkv_b; g.N = m.Nqkv; g.K = m.H; g.xmode = kXNorm;
+        g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = lw.w_in; g.embed_src = layer == 0;
+        break;
+      case kO:
+        g.W = lw.o_w; g.N = m.H; g.K = m.H; g.xmode = kXCopy; g.xsrc = p.attn;
+        g.xsrc_stride = m.H;
+        break;
+      case kGU:
+        g.W = lw.gu_w; g.N = 2 * m.I; g.K = m.H; g.xmode = kXNorm; g.xsrc = p.h;
+        g.xsrc_stride = m.H; g.norm_w = lw.w_post;
+        break;
+      default:  // kDown
+        g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = kXCopy; g.xsrc = p.act;
+        g.xsrc_stride = m.I_pad;
+        break;
+    }
+  }
+  g.kc = pick_kc(g.K);
+  return g;
+}
+
+struct TileRange {
+  int64_t t0, t1;
+  int32_t KT;      // tiles per row group
+  int32_t ctas;    // CTAs that take part
+};
+
+// Equal contiguous tile ranges.  At most one CTA per row group of the phase
+// takes part, so every range holds at least one full row group's worth of
+// tiles and a row group is split between at most two neighbouring CTAs.
+__device__ __forceinline__ TileRange tile_range(const Gemv &g, int cta, int grid) {
+  TileRange r;
+  r.KT = g.K / g.kc;
+  const int64_t groups = g.N / kRows;
+  const int64_t T = groups * r.KT;
+  const int64_t ctas = groups < grid ? groups : grid;
+  r.ctas = static_cast<int32_t>(ctas);
+  if (cta >= ctas) {
+    r.t0 = r.t1 = 0;
+  } else {
+    r.t0 = T * cta / ctas;
+    r.t1 = T * (cta + 1) / ctas;
+  }
+  return r;
+}
+
+// The step program: per layer QKV, attention, O, gate/up, down; then lm_head
+// and control.  Phase index within a step: 5*layer + {0..4}, 5L, 5L+1.
+__device__ __forceinline__ int gemv_kind_of_phase(int ph, int L) {
+  if (ph == 5 * L) return kLM;
+  if (ph > 5 * L) return -1;  // control
+  switch (ph % 5) {
+    case 0: return kQKV;
+    case 2: return kO;
+    case 3: return kGU;
+    case 4: return kDown;
+    default: return -1;     // attention
+  }
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- shared memory map ------------------------------------------------------------
+struct Smem {
+  uint8_t *ring;           // stages x kStageBytes
+  bf16 *xs;                // [4][xs_stride]  (attention scratch aliases it)
+  float *red;              // [8 warps][64]
+  float *tot;              // [64]
+  uint64_t *full;          // [kMaxStages]
+  uint64_t *empty;         // [kMaxStages]
+  float *nrm;              // [8][4] norm partial sums, then [4] inverse rms at +32
+  float *best_val;         // [4]
+  int32_t *best_idx;       // [4]
+  int32_t *best_bad;       // [4]
+  int32_t *misc;           // [16] small broadcast values
+  volatile int *prod_ctl;  // producer control: >= s run step s, -1 stop
+};
+
+__host__ __device__ inline size_t smem_bytes(int stages, int xs_stride) {
+  return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(kBatch) * xs_stride * 2 +
+         kConsumerWarps * 64 * 4 + 64 * 4 + 2 * kMaxStages * 8 + 40 * 4 + 12 * 4 + 16 * 4 + 16;
+}
+
+__device__ __forceinline__ Smem carve_smem(uint8_t *base, const EpochParams &p) {
+  Smem s;
+  uint8_t *ptr = base;
+  s.ring = ptr;
+  ptr += static_cast<size_t>(p.stages) * kStageBytes;
+  s.xs = reinterpret_cast<bf16 *>(ptr);
+  ptr += static_cast<size_t>(kBatch) * p.xs_stride * 2;
+  s.red = reinterpret_cast<float *>(ptr);
+  ptr += kConsumerWarps * 64 * 4;
+  s.tot = reinterpret_cast<float *>(ptr);
+  ptr += 64 * 4;
+  s.full = reinterpret_cast<uint64_t *>(ptr);
+  ptr += kMaxStages * 8;
+  s.empty = reinterpret_cast<uint64_t *>(ptr);
+  ptr += kMaxStages * 8;
+  s.nrm = reinterpret_cast<float *>(ptr);
+  ptr += 40 * 4;
+  s.best_val = reinterpret_cast<float *>(ptr);
+  ptr += 4 * 4;
+  s.best_idx = reinterpret_cast<int32_t *>(ptr);
+  ptr += 4 * 4;
+  s.best_bad = reinterpret_cast<int32_t *>(ptr);
+  ptr += 4 * 4;
+  s.misc = reinterpret_cast<int32_t *>(ptr);
+  ptr += 16 * 4;
+  s.prod_ctl = reinterpret_cast<volatile int *>(ptr);
+  return s;
+}
+
+// ---- cross-CTA helpers ---------------------------------------------------------------
+__device__ __forceinline__ bool aborted(const EpochParams &p) {
+  return *reinterpret_cast<volatile uint32_t *>(&p.sync->error) != 0;
+}
+
+__device__ __forceinline__ void raise_error(const EpochParams &p, uint32_t where) {
+  if (atomicCAS(&p.sync->error, 0u, 1u) == 0u) p.sync->error_where = where;
+}
+
+// Grid barrier among the consumer warps of all CTAs.  `index` counts barriers
+// from 1 within the launch.  Returns false when the launch is aborting.
+__device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index, uint32_t where) {
+  named_sync(1, kConsumerThreads);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    __threadfence();
+    red_release_add_u32(&p.sync->barrier, 1u);
+    const uint32_t target = index * static_cast<uint32_t>(p.grid);
+    const uint64_t deadline = globaltimer() + p.timeout_ns;
+    uint32_t polls = 0;
+    while (static_cast<int32_t>(ld_acquire_u32(&p.sync->barrier) - target) < 0) {
+      if (aborted(p)) { ok = 0; break; }
+      if ((++polls & 15) == 0 && globaltimer() > deadline) {
+        raise_error(p, where);
+        ok = 0;
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (ok && aborted(p)) ok = 0;
+    s.misc[0] = ok;
+  }
+  named_sync(1, kConsumerThreads);
+  return s.misc[0] != 0;
+}
+
+__device__ __forceinline__ int compute_slot(const ModelDims &m, const int32_t *bt, int row,
+                                            int64_t position) {
+  if (row < 0 || row >= kBatch || position < 0 || position >= m.C) return -1;
+  const int logical = static_cast<int>(position / m.bs);
+  const int offset = static_cast<int>(position % m.bs);
+  if (logical >= m.bpr) return -1;
+  const int physical = bt[row * m.bpr + logical];
+  if (physical < 0 || physical >= m.NB) return -1;
+  return physical * m.bs + offset;
+}
+
+// ---- producer warp --------------------------------------------------------------------
+// Streams the weight tiles of every projection phase of a step, in the order the
+// consumers use them.  Waits for the consumers' go signal before each step.
+__device__ void producer_main(const EpochParams &p, const Smem &s) {
+  const int lane = threadIdx.x & 31;
+  const int L = p.m.L;
+  const int phases = 5 * L + 2;
+  uint32_t issued = 0;
+  bool stop = false;
+  for (int step = 0; step < kMaxSteps && !stop; ++step) {
+    if (lane == 0) {
+      const uint64_t deadline = globaltimer() + p.timeout_ns;
+      while (true) {
+        const int ctl = *s.prod_ctl;   // -2 not yet released, -1 stop, s: run step s
+        if (ctl == -1) { stop = true; break; }
+        if (ctl >= step) break;
+        if (aborted(p) || globaltimer() > deadline) { stop = true; break; }
+        __nanosleep(128);
+      }
+    }
+    stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
+    if (stop) break;
+    for (int ph = 0; ph < phases && !stop; ++ph) {
+      const int kind = gemv_kind_of_phase(ph, L);
+      if (kind < 0) continue;
+      const Gemv g = make_gemv(p, ph / 5, kind);
+      const TileRange tr = tile_range(g, blockIdx.x, p.grid);
+      const uint32_t row_bytes = static_cast<uint32_t>(g.kc) * 2u;
+      const uint32_t pitch = row_bytes + 16u;
+      for (int64_t t = tr.t0; t < tr.t1; ++t) {
+        const uint32_t slot = issued % p.stages;
+        const uint32_t parity = ((issued / p.stages) & 1u) ^ 1u;
+        if (lane == 0) {
+          const uint64_t deadline = globaltimer() + p.timeout_ns;
+          while (!mbar_test(&s.empty[slot], parity)) {
+            if (*s.prod_ctl == -1 || aborted(p) || globaltimer() > deadline) { stop = true; break; }
+            __nanosleep(20);
+          }
+        }
+        stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
+        if (stop) break;
+        const int64_t rg = t / tr.KT;
+        const int64_t kk = t % tr.KT;
+        const bf16 *src = g.W + (rg * kRows) * static_cast<int64_t>(g.K) + kk * g.kc;
+        uint8_t *dst = s.ring + static_cast<size_t>(slot) * kStageBytes;
+        if (lane == 0) mbar_arrive_expect_tx(&s.full[slot], row_bytes * kRows);
+        __syncwarp();
+        if (lane < kRows)
+          bulk_g2s(dst + lane * pitch, src + static_cast<int64_t>(lane) * g.K, row_bytes, &s.full[slot]);
+        ++issued;
+      }
+    }
+  }
+  // Drain: every copy this warp issued must land before the CTA may exit.
+  if (lane == 0) {
+    const uint32_t first = issued > static_cast<uint32_t>(p.stages) ? issued - p.stages : 0u;
+    for (uint32_t i = first; i < issued; ++i) {
+      const uint64_t deadline = globaltimer() + p.timeout_ns;
+      while (!mbar_test(&s.full[i % p.stages], (i / p.stages) & 1u)) {
+        if (globaltimer() > deadline) break;
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// ---- consumer: activation prologue ------------------------------------------------------
+// Fills s.xs[4][K] with the projection input: RMSNorm of the residual stream
+// (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU output).
+__device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
+  const int tid = threadIdx.x;
+  const int K = g.K;
+  const int K8 = K / 8;
+  if (g.xmode == kXCopy) {
+    for (int i = tid; i < kBatch * K8; i += kConsumerThreads) {
+      const int b = i / K8, k8 = i % K8;
+      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(g.xsrc + static_cast<size_t>(b) * g.xsrc_stride) + k8);
+      *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = v;
+    }
+    named_sync(1, kConsumerThreads);
+    return;
+  }
+  const bf16 *rows[kBatch];
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+    rows[b] = g.embed_src ? p.embed + __ldcg(&p.work->token[b]) * static_cast<int64_t>(K)
+                          : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
+  }
+  float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
+  for (int k8 = tid; k8 < K8; k8 += kConsumerThreads) {
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8);
+      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h2[j]);
+        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.x, f.x));
+        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.y, f.y));
+      }
+    }
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
+  }
+  named_sync(1, kConsumerThreads);
+  if (tid < kBatch) {
+    float total = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + tid];
+    // mean = sum / K; rsqrt = 1 / sqrt(mean + eps), each IEEE-rounded as on the CPU
+    const float var = __fdiv_rn(total, static_cast<float>(K));
+    s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
+  }
+  named_sync(1, kConsumerThreads);
+  for (int i = tid; i < kBatch * K8; i += kConsumerThreads) {
+    const int b = i / K8, k8 = i % K8;
+    const float r = s.nrm[32 + b];
+    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8);
+    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8);
+    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v);
+    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
+    uint4 o;
+    __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 hf = __bfloat1622float2(h2[j]);
+      const float2 wf = __bfloat1622float2(w2[j]);
+      const float nx = rbf(__fmul_rn(hf.x, r));   // (h * rsqrt).to(bf16)
+      const float ny = rbf(__fmul_rn(hf.y, r));
+      o2[j] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));  // * weight
+    }
+    *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = o;
+  }
+  named_sync(1, kConsumerThreads);
+}
+
+// ---- consumer: projection epilogues ----------------------------------------------------------
+// Runs on the finished fp32 sums s.tot[row*4 + b] of row group `rg`.
+__device__ void gemv_epilogue(const EpochParams &p, const Smem &s, const Gemv &g, int64_t rg,
+                              int step) {
+  const int tid = threadIdx.x;
+  const ModelDims &m = p.m;
+  if (g.kind == kQKV) {
+    // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
+    if (tid < 64) {
+      const int row = tid >> 2, b = tid & 3;
+      const int64_t n = rg * kRows + row;
+      const float v = __fadd_rn(s.tot[tid], bf(g.bias[n]));
+      p.qkv[static_cast<size_t>(b) * m.Nqkv + n] = tobf(v);
+    }
+  } else if (g.kind == kO || g.kind == kDown) {
+    // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
+    if (tid < 64) {
+      const int row = tid >> 2, b = tid & 3;
+      const int64_t n = rg * kRows + row;
+      bf16 *hp = p.h + static_cast<size_t>(b) * m.H + n;
+      const float hv = bf(__ldcg(hp));
+      *hp = tobf(__fadd_rn(hv, rbf(s.tot[tid])));
+    }
+  } else if (g.kind == kGU) {
+    // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398)
+    if (tid < 32) {
+      const int pair = tid >> 2, b = tid & 3;
+      const float gate = rbf(s.tot[pair * 4 + b]);
+      const float up = rbf(s.tot[(pair + 8) * 4 + b]);
+      const float silu = rbf(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
+      p.act[static_cast<size_t>(b) * m.I_pad + rg * 8 + pair] = tobf(__fmul_rn(silu, up));
+    }
+  } else {  // kLM: logits = f32(bf16(x W^T)) (:405-408), then first-max argmax partials
+    if (tid < 64) {
+      const int row = tid >> 2, b = tid & 3;
+      const int64_t n = rg * kRows + row;
+      const float v = rbf(s.tot[tid]);
+      s.tot[tid] = v;
+      if (p.logits != nullptr && n < m.V)
+        p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n] = v;
+    }
+    named_sync(1, kConsumerThreads);
+    if (tid < kBatch) {
+      const int b = tid;
+      float best = s.best_val[b];
+      int32_t idx = s.best_idx[b];
+      int32_t bad = s.best_bad[b];
+      for (int row = 0; row < kRows; ++row) {
+        const int64_t n = rg * kRows + row;
+        if (n >= m.V) break;
+        const float v = s.tot[row * 4 + b];
+        if (!isfinite(v)) bad = 1;
+        if (v > best) { best = v; idx = static_cast<int32_t>(n); }
+      }
+      s.best_val[b] = best;
+      s.best_idx[b] = idx;
+      s.best_bad[b] = bad;
+    }
+  }
+}
+
+// ---- consumer: one projection phase -------------------------------------------------------------
+// Returns false when the launch is aborting.
+__device__ bool gemv_phase(const EpochParams &p, const Smem &s, const Gemv &g, uint32_t &stage_ctr,
+                           uint32_t seq, int step) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int gi = lane >> 2, ci = lane & 3;
+  const TileRange tr = tile_range(g, blockIdx.x, p.grid);
+  if (g.kind == kLM && tid < kBatch) {
+    s.best_val[tid] = -INFINITY;
+    s.best_idx[tid] = INT_MAX;
+    s.best_bad[tid] = 0;
+  }
+  if (g.embed_src) {
+    // layer 0: every CTA materialises its slice of the residual stream h = E[token]
+    const int K8 = g.K / 8;
+    const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
+    const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
+    for (int i = tid; i < kBatch * (hi - lo); i += kConsumerThreads) {
+      const int b = i / (hi - lo), k8 = lo + i % (hi - lo);
+      const int64_t tok = __ldcg(&p.work->token[b]);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.embed + tok * g.K) + k8);
+      *reinterpret_cast<uint4 *>(p.h + static_cast<size_t>(b) * p.m.H + k8 * 8) = v;
+    }
+  }
+  if (tr.t0 < tr.t1) load_x(p, s, g);
+  const int kc = g.kc;
+  const int ksteps = kc / 64;
+  const uint32_t pitch = static_cast<uint32_t>(kc) * 2u + 16u;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int64_t seg_start = tr.t0;
+  for (int64_t t = tr.t0; t < tr.t1; ++t) {
+    const int64_t rg = t / tr.KT;
+    const int kk = static_cast<int>(t % tr.KT);
+    const uint32_t slot = stage_ctr % p.stages;
+    const uint32_t parity = (stage_ctr / p.stages) & 1u;
+    ++stage_ctr;
+    // Bounded wait.  On abort or timeout the phase still runs to its end (on
+    // garbage) so that every named barrier below is matched; the grid barrier
+    // that ends the phase then stops the launch uniformly.
+    bool landed = true;
+    {
+      const uint64_t deadline = globaltimer() + p.timeout_ns;
+      uint32_t polls = 0;
+      while (!mbar_test(&s.full[slot], parity)) {
+        if ((++polls & 63) == 0) {
+          if (aborted(p)) { landed = false; break; }
+          if (globaltimer() > deadline) { raise_error(p, 1000); landed = false; break; }
+        }
+      }
+    }
+    const uint8_t *st = s.ring + static_cast<size_t>(slot) * kStageBytes;
+    for (int ks = warp; ks < ksteps; ks += kConsumerWarps) {
+      const uint8_t *arow = st + gi * pitch + (ks * 64 + 16 * ci) * 2;
+      const uint4 a_lo0 = lds128(arow);
+      const uint4 a_lo1 = lds128(arow + 16);
+      const uint4 a_hi0 = lds128(arow + 8 * pitch);
+      const uint4 a_hi1 = lds128(arow + 8 * pitch + 16);
+      uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+      if (gi < kBatch) {
+        const bf16 *xrow = s.xs + static_cast<size_t>(gi) * p.xs_stride + kk * kc + ks * 64 + 16 * ci;
+        x0 = lds128(xrow);
+        x1 = lds128(xrow + 8);
+      }
+      // MMA j uses physical k = 16ci + 4j .. 4j+3 of this 64-wide slice, for both
+      // weight rows (gi, gi+8) and the activation column gi.
+      mma_bf16_16816(acc, a_lo0.x, a_hi0.x, a_lo0.y, a_hi0.y, x0.x, x0.y);
+      mma_bf16_16816(acc, a_lo0.z, a_hi0.z, a_lo0.w, a_hi0.w, x0.z, x0.w);
+      mma_bf16_16816(acc, a_lo1.x, a_hi1.x, a_lo1.y, a_hi1.y, x1.x, x1.y);
+      mma_bf16_16816(acc, a_lo1.z, a_hi1.z, a_lo1.w, a_hi1.w, x1.z, x1.w);
+    }
+    __syncwarp();
+    if (lane == 0 && landed) mbar_arrive(&s.empty[slot]);
+
+    const bool group_end = kk == tr.KT - 1;
+    if (!(group_end || t == tr.t1 - 1)) continue;
+    // ---- finish a row-group segment -------------------------------------------------
+    const bool head = (seg_start % tr.KT) == 0;   // this CTA holds the group's first tile
+    seg_start = t + 1;
+    if (ci < 2) {
+      float *r = s.red + warp * 64;
+      r[gi * 4 + 2 * ci] = acc[0];
+      r[gi * 4 + 2 * ci + 1] = acc[1];
+      r[(gi + 8) * 4 + 2 * ci] = acc[2];
+      r[(gi + 8) * 4 + 2 * ci + 1] = acc[3];
+    }
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    const bool finisher = head && !group_end;   // the rest of the group is on CTA + 1
+    if (finisher && tid == 0) {
+      const uint64_t deadline = globaltimer() + p.timeout_ns;
+      uint32_t polls = 0;
+      while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
+        if (aborted(p)) break;
+        if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
+        __nanosleep(32);
+      }
+    }
+    named_sync(1, kConsumerThreads);
+    if (tid < 64) {
+      float total = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) total += s.red[w * 64 + tid];
+      if (finisher) total += __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + tid);
+      if (!head) {
+        p.partials[static_cast<size_t>(blockIdx.x) * 64 + tid] = total;  // publish
+      } else {
+        s.tot[tid] = total;
+      }
+    }
+    named_sync(1, kConsumerThreads);
+    if (!head) {
+      if (tid == 0) {
+        __threadfence();
+        st_release_u32(&p.sync->flags[blockIdx.x], seq);
+      }
+    } else {
+      gemv_epilogue(p, s, g, rg, step);
+    }
+  }
+  if (g.kind == kLM) {
+    named_sync(1, kConsumerThreads);
+    if (tid < kBatch) {
+      p.arg_val[blockIdx.x * kBatch + tid] = s.best_val[tid];
+      p.arg_idx[blockIdx.x * kBatch + tid] = s.best_idx[tid];
+      p.arg_bad[blockIdx.x * kBatch + tid] = s.best_bad[tid];
+    }
+  }
+  return true;
+}
+
+// ---- consumer: paged GQA decode attention ---------------------------------------------------------
+// One unit per (row, query head), units spread over CTAs.  RoPE on q and k
+// (:231-240), the new k/v written at slot[row] for active rows (:242-264),
+// scores bf16(q.K) then bf16(s / sqrt(d)), softmax in fp32 rounded to bf16,
+// output bf16(P.V) (:334-379).  Positions >= seq_len contribute exactly zero in
+// the reference (masked to bf16.min), so they are skipped.
+__device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) {
+  const ModelDims &m = p.m;
+  const int tid = threadIdx.x;
+  const int d = m.d;
+  const int half = d / 2;
+  const int groups = m.nq / m.nkv;
+  float *qf = reinterpret_cast<float *>(s.xs);         // [d]  roped q (bf16 values)
+  bf16 *kn = reinterpret_cast<bf16 *>(qf + d);          // [d]  roped new k
+  bf16 *vn = kn + d;                                    // [d]  new v
+  float *sc = reinterpret_cast<float *>(vn + d);        // [C]  scores, then probabilities
+  float *rd = sc + m.C;                                 // [16] reductions, then [8][d] P.V partials
+  const size_t layer_off = static_cast<size_t>(layer) * m.NB * m.bs * m.nkv * d;
+  const int units = kBatch * m.nq;
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int u = blockIdx.x; u < units; u += p.grid) {
+    const int b = u / m.nq, qh = u % m.nq, kvh = qh / groups;
+    bf16 *out = p.attn + static_cast<size_t>(b) * m.H + qh * d;
+    if (__ldcg(&p.work->active[b]) == 0) {
+      for (int i = tid; i < d; i += kConsumerThreads) out[i] = tobf(0.f);
+      continue;
+    }
+    const int64_t pos = __ldcg(&p.work->position[b]);
+    const int len = __ldcg(&p.work->length[b]);
+    const int slot = __ldcg(&p.work->slot[b]);
+    const bf16 *qsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + qh * d;
+    const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + kvh * d;
+    const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + m.nkv * d + kvh * d;
+    const bf16 *cs = p.rope_cos + pos * d;
+    const bf16 *sn = p.rope_sin + pos * d;
+    for (int i = tid; i < d; i += kConsumerThreads) {
+      const float c = bf(cs[i]), sv = bf(sn[i]);
+      const float q = bf(__ldcg(qsrc + i));
+      const float qr = i < half ? -bf(__ldcg(qsrc + i + half)) : bf(__ldcg(qsrc + i - half));
+      qf[i] = rbf(__fadd_rn(rbf(__fmul_rn(q, c)), rbf(__fmul_rn(qr, sv))));
+      const float k = bf(__ldcg(ksrc + i));
+      const float kr = i < half ? -bf(__ldcg(ksrc + i + half)) : bf(__ldcg(ksrc + i - half));
+      kn[i] = tobf(__fadd_rn(rbf(__fmul_rn(k, c)), rbf(__fmul_rn(kr, sv))));
+      vn[i] = __ldcg(vsrc + i);
+    }
+    named_sync(1, kConsumerThreads);
+    if (qh % groups == 0 && slot >= 0 && slot < m.NB * m.bs) {
+      const size_t off = layer_off + (static_cast<size_t>(slot) * m.nkv + kvh) * d;
+      for (int i = tid; i < d; i += kConsumerThreads) {
+        p.key_cache[off + i] = kn[i];
+        p.value_cache[off + i] = vn[i];
+      }
+    }
+    // scores
+    float local_max = -INFINITY;
+    for (int t = tid; t < len; t += kConsumerThreads) {
+      const bf16 *krow;
+      if (t == pos) {
+        krow = kn;
+      } else {
+        const int st = compute_slot(m, p.work->bt, b, t);
+        krow = p.key_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * d;
+      }
+      float dot = 0.f;
+      for (int i = 0; i < d; i += 8) {
+        const uint4 kv = (t == pos) ? *reinterpret_cast<const uint4 *>(krow + i)
+                                    : __ldcg(reinterpret_cast<const uint4 *>(krow + i));
+        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 kf = __bfloat1622float2(k2[j]);
+          dot = fmaf(qf[i + 2 * j], kf.x, dot);
+          dot = fmaf(qf[i + 2 * j + 1], kf.y, dot);
+        }
+      }
+      const float s2 = rbf(__fdiv_rn(rbf(dot), m.sqrt_d));
+      sc[t] = s2;
+      local_max = fmaxf(local_max, s2);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, off));
+    if (lane == 0) rd[warp] = local_max;
+    named_sync(1, kConsumerThreads);
+    float mx = rd[0];
+    for (int w = 1; w < kConsumerWarps; ++w) mx = fmaxf(mx, rd[w]);
+    float local_sum = 0.f;
+    for (int t = tid; t < len; t += kConsumerThreads) {
+      const float e = expf(__fsub_rn(sc[t], mx));
+      sc[t] = e;
+      local_sum += e;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, off);
+    named_sync(1, kConsumerThreads);
+    if (lane == 0) rd[8 + warp] = local_sum;
+    named_sync(1, kConsumerThreads);
+    float sum = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) sum += rd[8 + w];
+    for (int t = tid; t < len; t += kConsumerThreads) sc[t] = rbf(__fdiv_rn(sc[t], sum));
+    named_sync(1, kConsumerThreads);
+    // output: warp w takes positions t = w (mod 8); each lane owns d/32 dims
+    {
+      const int dpl = d / 32;   // 4 (d=128) or 2 (d=64)
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int t = warp; t < len; t += kConsumerWarps) {
+        const bf16 *vrow;
+        if (t == pos) {
+          vrow = vn;
+        } else {
+          const int st = compute_slot(m, p.work->bt, b, t);
+          vrow = p.value_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * d;
+        }
+        const float pt = sc[t];
+        if (dpl == 4) {
+          const uint2 raw = (t == pos) ? *reinterpret_cast<const uint2 *>(vrow + lane * 4)
+                                       : __ldcg(reinterpret_cast<const uint2 *>(vrow + lane * 4));
+          const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+          const float2 f0 = __bfloat1622float2(v2[0]);
+          const float2 f1 = __bfloat1622float2(v2[1]);
+          o[0] = fmaf(pt, f0.x, o[0]);
+          o[1] = fmaf(pt, f0.y, o[1]);
+          o[2] = fmaf(pt, f1.x, o[2]);
+          o[3] = fmaf(pt, f1.y, o[3]);
+        } else {
+          for (int j = 0; j < dpl; ++j) {
+            const bf16 v = (t == pos) ? vrow[lane * dpl + j] : __ldcg(vrow + lane * dpl + j);
+            o[j] = fmaf(pt, bf(v), o[j]);
+          }
+        }
+      }
+      float *part = rd + 16;   // [8 warps][d]
+      for (int j = 0; j < dpl; ++j) part[warp * d + lane * dpl + j] = o[j];
+      named_sync(1, kConsumerThreads);
+      for (int i = tid; i < d; i += kConsumerThreads) {
+        float total = 0.f;
+        for (int w2 = 0; w2 < kConsumerWarps; ++w2) total += part[w2 * d + i];
+        out[i] = tobf(total);
+      }
+    }
+    named_sync(1, kConsumerThreads);
+  }
+}
+
+// ---- consumer: epoch prologue (CTA 0, thread 0) ---------------------------------------------------
+// Decodes the control vector and validates every input exactly like the
+// reference controller (:207-241, :335-385).  Returns the fallback status or 0.
+__device__ int32_t validate_inputs(const EpochParams &p) {
+  const ModelDims &m = p.m;
+  EpochIO *io = p.io;
+  EpochWork *w = p.work;
+  const int32_t encoded = io->control[2 + kBatch];
+  const bool importing = (encoded & kImportFlag) != 0;
+  w->importing = importing;
+  const int32_t mask = importing ? (encoded & (kImportFlag - 1)) : 0;
+  w->variant = importing ? (encoded & ~(kImportFlag | 0xF)) : encoded;
+  w->max_steps = io->control[0];
+  w->sampling = io->control[1 + kBatch];
+  w->import_rows = 0;
+  w->checksum = 0;
+  w->model_calls = 0;
+  for (int b = 0; b < kBatch; ++b) {
+    w->eos[b] = io->control[1 + b];
+    w->generation[b] = io->control[3 + kBatch + b];
+    w->token[b] = io->token[b];
+    w->position[b] = io->position[b];
+    w->length[b] = io->seq_len[b];
+    w->active[b] = io->active[b];
+    w->active0[b] = io->active[b];
+    w->executed[b] = 0;
+    w->reason[b] = kNone;
+    w->new_gen[b] = 0;
+  }
+  for (int i = 0; i < kBatch * m.bpr; ++i) w->bt[i] = io->block_table[i];
+  for (int b = 0; b < kBatch; ++b)
+    w->slot[b] = importing ? compute_slot(m, w->bt, b, w->position[b]) : io->slot[b];
+  for (int i = 0; i < kMaxSteps * kBatch; ++i) io->history[i] = -1;
+
+  if (w->max_steps < 1 || w->max_steps > kMaxSteps || w->sampling != 0 || w->variant != 0) {
+    if (w->sampling != 0) return kUnsupportedSampling;
+    if (w->variant != 0) return kUnsupportedGraph;
+    return kInvalidMetadata;
+  }
+  for (int b = 0; b < kBatch; ++b)
+    if (w->eos[b] < 0 || w->eos[b] >= m.V) return kInvalidMetadata;
+  unsigned long long seen[4] = {0ull, 0ull, 0ull, 0ull};
+  for (int i = 0; i < kBatch * m.bpr; ++i) {
+    const int blk = w->bt[i];
+    if (blk < 0 || blk >= m.NB || blk >= 256) return kInvalidBlockTable;
+    const unsigned long long bit = 1ull << (blk & 63);
+    if (seen[blk >> 6] & bit) return kInvalidBlockTable;
+    seen[blk >> 6] |= bit;
+  }
+  for (int b = 0; b < kBatch; ++b) {
+    const int32_t a = w->active0[b];
+    if ((a != 0 && a != 1) || w->token[b] < 0 || w->token[b] >= m.V || w->position[b] < 0 ||
+        w->position[b] >= m.C)
+      return kInvalidMetadata;
+    if (a == 1) {
+      if (w->generation[b] <= 0) return kInvalidMetadata;
+      if (w->length[b] != w->position[b] + 1) return kInvalidMetadata;
+      if (w->position[b] + w->max_steps > m.C) return kCapacityExceeded;
+    } else if (w->length[b] == 0) {
+      if (w->generation[b] != 0) return kInvalidMetadata;
+      w->reason[b] = kEmpty;
+    } else if (w->length[b] == w->position[b] + 1) {
+      w->reason[b] = kAlreadyFinished;
+    } else {
+      return kInvalidMetadata;
+    }
+    if (compute_slot(m, w->bt, b, w->position[b]) != w->slot[b]) return kSlotMismatch;
+  }
+  if (importing) {
+    if (mask <= 0 || mask >= (1 << kBatch)) return kInvalidMetadata;
+    // rows are imported in order; the first invalid row stops the import (:395-400)
+    for (int b = 0; b < kBatch; ++b) {
+      if ((mask & (1 << b)) == 0) continue;
+      if (w->active0[b] != 1 || w->generation[b] <= 0) return -kInvalidMetadata;  // partial import
+      w->import_rows |= 1 << b;
+    }
+  }
+  return kOk;
+}
+
+// Sum and position-weighted sum of one block for Adler-32 (mod 65521 on
+// combine): S1 = sum d_i, S2 = sum (n - i + 1) d_i, i = 1..n.
+__device__ void adler_block(const uint8_t *data, int n, uint64_t &S1, uint64_t &S2, float *scratch) {
+  const int tid = threadIdx.x;
+  const int per = n / kConsumerThreads;
+  const uint8_t *mine = data + static_cast<size_t>(tid) * per;
+  uint64_t s1 = 0, w = 0;
+  for (int i = 0; i < per; i += 16) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(mine + i));
+    const uint8_t *bytes = reinterpret_cast<const uint8_t *>(&v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      s1 += bytes[j];
+      w += static_cast<uint64_t>(per - (i + j)) * bytes[j];
+    }
+  }
+  const uint64_t tail = static_cast<uint64_t>(n) - static_cast<uint64_t>(tid + 1) * per;
+  uint64_t s2 = w + tail * s1;
+  // block reduction of (s1, s2) through shared memory (scratch holds 2*256 u64)
+  uint64_t *red = reinterpret_cast<uint64_t *>(scratch);
+  red[tid] = s1;
+  red[kConsumerThreads + tid] = s2;
+  named_sync(1, kConsumerThreads);
+  if (tid == 0) {
+    uint64_t a = 0, c = 0;
+    for (int i = 0; i < kConsumerThreads; ++i) {
+      a += red[i];
+      c += red[kConsumerThreads + i];
+    }
+    S1 = a;
+    S2 = c;
+  }
+  named_sync(1, kConsumerThreads);
+}
+
+// ---- the kernel ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const EpochParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const Smem s = carve_smem(smem_raw, p);
+  const int tid = threadIdx.x;
+  const ModelDims &m = p.m;
+  EpochWork *w = p.work;
+  EpochIO *io = p.io;
+
+  if (tid == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], kConsumerWarps);
+    }
+    *s.prod_ctl = -2;   // producer waits for "step 0 go"
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid >= kConsumerThreads) {
+    producer_main(p, s);
+    return;
+  }
+
+  uint32_t barrier_index = 0;
+  uint32_t stage_ctr = 0;
+  bool ok = true;
+  const size_t block_elems = static_cast<size_t>(m.bs) * m.nkv * m.d;
+  const size_t layer_elems = static_cast<size_t>(m.NB) * block_elems;
+
+  // 1. validation (CTA 0)
+  if (blockIdx.x == 0 && tid == 0) {
+    int32_t st = validate_inputs(p);
+    if (st < 0) {   // an imported row failed its check after earlier rows were imported
+      w->status = -st;
+    } else {
+      w->status = st;
+      if (st != kOk) w->import_rows = 0;
+    }
+    w->stop = w->status != kOk ? 1 : 0;
+  }
+  ok = grid_barrier(p, s, ++barrier_index, 1);
+
+  // 2. import: copy the payload block of each imported row into its first
+  //    block, zero its other blocks (:387-418); then the Adler-32 proof.
+  if (ok && __ldcg(&w->import_rows) != 0) {
+    const int rows = __ldcg(&w->import_rows);
+    const int units = 2 * m.L * kBatch * m.bpr;
+    for (int u = blockIdx.x; u < units; u += p.grid) {
+      const int j = u % m.bpr;
+      const int b = (u / m.bpr) % kBatch;
+      const int layer = (u / (m.bpr * kBatch)) % m.L;
+      const int cache = u / (m.bpr * kBatch * m.L);
+      if ((rows & (1 << b)) == 0) continue;
+      bf16 *dst = (cache == 0 ? p.key_cache : p.value_cache) + layer * layer_elems +
+                  static_cast<size_t>(w->bt[b * m.bpr + j]) * block_elems;
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+      const size_t n16 = block_elems * 2 / 16;
+      if (j == 0) {
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(
+            p.import_payload +
+            ((static_cast<size_t>(cache) * m.L + layer) * kBatch + b) * block_elems * 2);
+        for (size_t i = tid; i < n16; i += kConsumerThreads) d4[i] = __ldcg(s4 + i);
+      } else {
+        for (size_t i = tid; i < n16; i += kConsumerThreads) d4[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (blockIdx.x == 0 && tid == 0) {
+      for (int b = 0; b < kBatch; ++b) {
+        if ((rows & (1 << b)) == 0) continue;
+        p.res->generation[b] = w->generation[b];
+        p.res->token[b] = w->token[b];
+        p.res->position[b] = w->position[b];
+        p.res->length[b] = w->length[b];
+        p.res->valid[b] = 1;
+      }
+    }
+    ok = grid_barrier(p, s, ++barrier_index, 2);
+    if (ok && __ldcg(&w->status) == kOk) {
+      // blocks in checksum order: K then V, layer-major, row-minor (:419-432)
+      int nrows = 0;
+      int order[kBatch];
+      for (int b = 0; b < kBatch; ++b)
+        if (rows & (1 << b)) order[nrows++] = b;
+      const int units2 = 2 * m.L * nrows;
+      const int n = static_cast<int>(block_elems * 2);
+      for (int u = blockIdx.x; u < units2; u += p.grid) {
+        const int cache = u / (m.L * nrows);
+        const int layer = (u / nrows) % m.L;
+        const int b = order[u % nrows];
+        const bf16 *src = (cache == 0 ? p.key_cache : p.value_cache) + layer * layer_elems +
+                          static_cast<size_t>(w->bt[b * m.bpr]) * block_elems;
+        uint64_t S1 = 0, S2 = 0;
+        adler_block(reinterpret_cast<const uint8_t *>(src), n, S1, S2,
+                    reinterpret_cast<float *>(s.xs));
+        if (tid == 0) {
+          w->adler[2 * u] = S1;
+          w->adler[2 * u + 1] = S2;
+        }
+      }
+      ok = grid_barrier(p, s, ++barrier_index, 3);
+      if (ok && blockIdx.x == 0 && tid == 0) {
+        const uint64_t M = 65521;
+        uint64_t a = 1, c = 0;
+        for (int u = 0; u < units2; ++u) {
+          const uint64_t S1 = __ldcg(&w->adler[2 * u]) % M;
+          const uint64_t S2 = __ldcg(&w->adler[2 * u + 1]) % M;
+          c = (c + (static_cast<uint64_t>(n) % M) * a + S2) % M;
+          a = (a + S1) % M;
+        }
+        w->checksum = static_cast<uint32_t>((c << 16) | a);
+      }
+    }
+  }
+
+  // 3. generation continuity (:448-473), then clear the rows of new generations
+  if (ok && blockIdx.x == 0 && tid == 0 && w->status == kOk) {
+    for (int b = 0; b < kBatch && w->status == kOk; ++b) {
+      if (w->active0[b] == 0) continue;
+      if (p.res->generation[b] == w->generation[b]) {
+        if (p.res->valid[b] == 0 || p.res->token[b] != w->token[b] ||
+            p.res->position[b] != w->position[b] || p.res->length[b] != w->length[b])
+          w->status = kResidentContinuity;
+      } else {
+        if (w->position[b] != 0 || w->length[b] != 1) w->status = kResidentContinuity;
+        w->new_gen[b] = 1;
+      }
+    }
+    if (w->status != kOk) {
+      for (int b = 0; b < kBatch; ++b) w->new_gen[b] = 0;
+    }
+    w->stop = w->status != kOk ? 1 : 0;
+  }
+  if (ok) ok = grid_barrier(p, s, ++barrier_index, 4);
+  if (ok && __ldcg(&w->status) == kOk) {
+    bool any = false;
+    for (int b = 0; b < kBatch; ++b) any |= __ldcg(&w->new_gen[b]) != 0;
+    if (any) {
+      const int units = 2 * m.L * kBatch * m.bpr;
+      for (int u = blockIdx.x; u < units; u += p.grid) {
+        const int j = u % m.bpr;
+        const int b = (u / m.bpr) % kBatch;
+        const int layer = (u / (m.bpr * kBatch)) % m.L;
+        const int cache = u / (m.bpr * kBatch * m.L);
+        if (!__ldcg(&w->new_gen[b])) continue;
+        bf16 *dst = (cache == 0 ? p.key_cache : p.value_cache) + layer * layer_elems +
+                    static_cast<size_t>(w->bt[b * m.bpr + j]) * block_elems;
+        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+        for (size_t i = tid; i < block_elems * 2 / 16; i += kConsumerThreads) d4[i] = make_uint4(0, 0, 0, 0);
+      }
+      ok = grid_barrier(p, s, ++barrier_index, 5);
+    }
+  }
+
+  // 4. the K-loop (:485-591)
+  const int L = m.L;
+  const int phases = 5 * L + 2;
+  for (int step = 0; ok && step < kMaxSteps; ++step) {
+    if (__ldcg(&w->stop)) break;
+    if (tid == 0) *s.prod_ctl = step;   // release the producer for this step
+    for (int ph = 0; ok && ph < phases; ++ph) {
+      const uint32_t seq = static_cast<uint32_t>(step * phases + ph + 1);
+      const int kind = gemv_kind_of_phase(ph, L);
+      if (kind >= 0) {
+        const Gemv g = make_gemv(p, ph / 5, kind);
+        ok = gemv_phase(p, s, g, stage_ctr, seq, step);
+      } else if (ph < 5 * L) {
+        attention_phase(p, s, ph / 5);
+      } else if (blockIdx.x == 0) {
+        // control: two-pass argmax (pass 2 over the per-CTA partials), then the
+        // per-row bookkeeping of the reference K-loop body (:537-591)
+        if (tid < kBatch) {
+          const int lm_ctas = static_cast<int>(m.V_pad / kRows < p.grid ? m.V_pad / kRows : p.grid);
+          float best = -INFINITY;
+          int32_t idx = INT_MAX, bad = 0;
+          for (int c = 0; c < lm_ctas; ++c) {
+            const float v = __ldcg(&p.arg_val[c * kBatch + tid]);
+            const int32_t i = __ldcg(&p.arg_idx[c * kBatch + tid]);
+            bad |= __ldcg(&p.arg_bad[c * kBatch + tid]);
+            if (v > best || (v == best && i < idx)) { best = v; idx = i; }
+          }
+          s.best_idx[tid] = idx;
+          s.best_bad[tid] = bad;
+        }
+        named_sync(1, kConsumerThreads);
+        if (tid == 0) {
+          const int calls = ++w->model_calls;
+          const int st = calls - 1;
+          for (int b = 0; b < kBatch; ++b) {
+            if (w->active[b] == 0) continue;   // position stays (:547-552)
+            const int64_t forced = io->use_forced ? io->forced[st * kBatch + b] : -1;
+            if (forced < 0 && s.best_bad[b]) { w->status = kNonFiniteLogits; break; }
+            const int64_t tok = forced >= 0 ? forced : s.best_idx[b];
+            io->history[st * kBatch + b] = tok;
+            ++w->executed[b];
+            w->position[b] += 1;
+            w->token[b] = tok;
+            w->length[b] = static_cast<int32_t>(w->position[b] + 1);
+            if (w->position[b] == m.C) {
+              w->slot[b] = -1;
+            } else {
+              const int sl = compute_slot(m, w->bt, b, w->position[b]);
+              if (sl < 0) { w->status = kCapacityExceeded; break; }
+              w->slot[b] = sl;
+            }
+            if (tok == w->eos[b]) {
+              w->active[b] = 0;
+              w->reason[b] = kEos;
+            }
+          }
+          int any = 0;
+          for (int b = 0; b < kBatch; ++b) any |= w->active[b];
+          w->stop = (w->status != kOk || calls >= w->max_steps || any == 0) ? 1 : 0;
+        }
+      }
+      if (ok) ok = grid_barrier(p, s, ++barrier_index, 100 + ph);
+    }
+  }
+  if (tid == 0) *s.prod_ctl = -1;   // producer: no more steps
+
+  // 5. finish (:593-614) and emit (:296-324), CTA 0
+  if (blockIdx.x == 0 && tid == 0) {
+    int32_t status = w->status;
+    if (!ok || aborted(p)) status = kModelError;
+    const bool good = status == kOk;
+    for (int b = 0; b < kBatch; ++b) {
+      if (!good) {
+        w->reason[b] = kFallback;
+      } else if (w->active0[b] == 1 && w->reason[b] == kNone) {
+        w->reason[b] = kMaxStepsReason;
+      }
+    }
+    if (good) {
+      for (int b = 0; b < kBatch; ++b) {
+        if (w->active0[b] == 0) continue;
+        p.res->generation[b] = w->generation[b];
+        p.res->token[b] = w->token[b];
+        p.res->position[b] = w->position[b];
+        p.res->length[b] = w->length[b];
+        p.res->valid[b] = 1;
+      }
+    }
+    int32_t *c = io->control_out;
+    c[0] = w->max_steps;
+    c[1] = w->sampling;
+    c[2] = w->variant;
+    c[3] = status;
+    c[4] = w->model_calls;
+    c[5] = w->importing ? static_cast<int32_t>(w->checksum) : (good ? 0 : 1);
+    int init_count = 0, final_count = 0;
+    for (int b = 0; b < kBatch; ++b) {
+      c[6 + b] = w->eos[b];
+      c[6 + kBatch + b] = w->active0[b];
+      c[6 + 2 * kBatch + b] = w->executed[b];
+      c[6 + 3 * kBatch + b] = w->reason[b];
+      c[6 + 4 * kBatch + 2 + b] = w->active0[b] == 1 ? w->generation[b] : 0;
+      init_count += w->active0[b] != 0;
+      final_count += (good ? w->active[b] : w->active0[b]) != 0;
+    }
+    c[6 + 4 * kBatch] = init_count;
+    c[6 + 4 * kBatch + 1] = final_count;
+  }
+}
+
+}  // namespace cruise

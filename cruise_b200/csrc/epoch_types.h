@@ -1,0 +1,157 @@
+// epoch_types.h -- device data layout of the resident decode epoch, shared by
+// the host engine (engine.cu) and the persistent epoch kernel (epoch_kernel.cuh).
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+
+namespace cruise {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kBatch = 4;             // static rows per epoch (controller :16)
+constexpr int kMaxSteps = 8;          // max K (controller :17)
+constexpr int kMaxBlocksPerRow = 8;   // capacity of the block-table buffers
+constexpr int kControlIn = 11;        // [K, eos x4, sampling, variant, gen x4]
+constexpr int kControlOut = 28;       // emit layout (controller :296-324)
+constexpr int kTilingBytes = 72;
+constexpr int kImportFlag = 0x100;
+
+constexpr int kRows = 16;             // weight rows per tile (one m16 MMA slab)
+constexpr int kMaxKc = 512;           // k elements per tile
+constexpr int kStageBytes = kRows * (kMaxKc * 2 + 16);  // padded rows: 16 x 1040 B
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;         // + one producer warp
+constexpr int kMaxCtas = 1024;
+constexpr int kMaxStages = 12;
+
+// statuses and finish reasons of the reference controller (:51-74)
+enum Status : int32_t {
+  kOk = 0,
+  kInvalidMetadata = 201,
+  kCapacityExceeded = 202,
+  kInvalidBlockTable = 203,
+  kSlotMismatch = 204,
+  kUnsupportedSampling = 205,
+  kUnsupportedGraph = 206,
+  kModelError = 207,
+  kInvalidModelOutput = 208,
+  kNonFiniteLogits = 209,
+  kPositionProgress = 210,
+  kAllocationFailure = 211,
+  kResidentContinuity = 212,
+};
+enum Finish : int32_t { kNone = 0, kEos = 1, kMaxStepsReason = 2, kFallback = 3, kEmpty = 4, kAlreadyFinished = 5 };
+
+struct ModelDims {
+  int32_t L, H, nq, nkv, d, I, I_pad, V, V_pad, Nqkv;
+  float eps;
+  float sqrt_d;          // (float)sqrt(head_dim), the attention divisor
+  int32_t bs, bpr, NB, C;
+};
+
+struct LayerWeights {
+  const bf16 *w_in, *w_post;   // [H]
+  const bf16 *qkv_w;           // [Nqkv][H]   rows: q | k | v
+  const bf16 *qkv_b;           // [Nqkv]
+  const bf16 *o_w;             // [H][H]
+  const bf16 *gu_w;            // [I/8][16][H]  8 gate rows then 8 up rows
+  const bf16 *down_w;          // [H][I_pad]    columns >= I are zero
+};
+
+// One host->device and one device->host copy per epoch (the 8-in / 2-out ABI).
+struct EpochIO {
+  int64_t token[kBatch];
+  int64_t position[kBatch];
+  int32_t seq_len[kBatch];
+  int32_t slot[kBatch];
+  int32_t active[kBatch];
+  int32_t block_table[kBatch * kMaxBlocksPerRow];
+  int32_t control[kControlIn];
+  uint8_t tiling[kTilingBytes];
+  int32_t use_forced;                    // 1: forced[] overrides argmax (device prefill)
+  int64_t forced[kMaxSteps * kBatch];    // [step][row] teacher-forced next token, -1 = greedy
+  // outputs
+  int64_t history[kMaxSteps * kBatch];   // [step][row]
+  int32_t control_out[kControlOut];
+};
+
+// Per-row resident state kept across epochs (controller :624-631).
+struct ResidentState {
+  int32_t generation[kBatch];
+  int32_t valid[kBatch];
+  int32_t length[kBatch];
+  int32_t pad0[kBatch];
+  int64_t token[kBatch];
+  int64_t position[kBatch];
+};
+
+// Working state of the running epoch (written by CTA 0, read by all).
+struct EpochWork {
+  int64_t token[kBatch];
+  int64_t position[kBatch];
+  int32_t length[kBatch];
+  int32_t slot[kBatch];
+  int32_t active[kBatch];
+  int32_t active0[kBatch];
+  int32_t executed[kBatch];
+  int32_t reason[kBatch];
+  int32_t new_gen[kBatch];
+  int32_t eos[kBatch];
+  int32_t generation[kBatch];
+  int32_t bt[kBatch * kMaxBlocksPerRow];
+  int32_t status;
+  int32_t model_calls;
+  int32_t stop;          // 1: leave the step loop
+  int32_t importing;
+  int32_t import_rows;   // rows whose payload is copied
+  int32_t max_steps;
+  int32_t sampling;
+  int32_t variant;
+  uint32_t checksum;
+  int32_t pad0;
+  uint64_t adler[2 * 64 * kBatch * 2];  // per imported block: (S1, S2)
+};
+
+// Cross-CTA synchronisation words; zeroed by the host before every launch.
+struct SyncState {
+  uint32_t barrier;            // grid barrier arrivals (monotonic)
+  uint32_t error;              // non-zero: a wait timed out, every CTA leaves
+  uint32_t error_where;
+  uint32_t pad0;
+  uint32_t flags[kMaxCtas];    // split row-group partial published (phase seq)
+};
+
+struct EpochParams {
+  ModelDims m;
+  const LayerWeights *layers;  // [L] in device memory
+  const bf16 *embed;           // [V][H]
+  const bf16 *final_norm;      // [H]
+  const bf16 *lm_head;         // [V_pad][H]
+  const bf16 *rope_cos;        // [C][d]
+  const bf16 *rope_sin;        // [C][d]
+  bf16 *key_cache;             // [L][NB][bs][nkv][d]
+  bf16 *value_cache;
+  bf16 *h;                     // [4][H] residual stream
+  bf16 *qkv;                   // [4][Nqkv]
+  bf16 *attn;                  // [4][H]
+  bf16 *act;                   // [4][I_pad]
+  float *partials;             // [G][64] split row-group partial sums
+  float *arg_val;              // [G][4]
+  int32_t *arg_idx;            // [G][4]
+  int32_t *arg_bad;            // [G][4]
+  float *logits;               // optional [8][4][V]
+  const uint8_t *import_payload;  // device copy of the import payload
+  EpochIO *io;
+  ResidentState *res;
+  EpochWork *work;
+  SyncState *sync;
+  int32_t grid;                // CTAs (one per SM)
+  int32_t stages;              // weight ring depth
+  int32_t xs_stride;           // activation row stride in smem (elements)
+  int32_t pad0;
+  uint64_t timeout_ns;         // bound of every spin wait
+};
+
+}  // namespace cruise

@@ -1,0 +1,201 @@
+"""Python handle on the CUDA resident-epoch engine (over the C ABI).
+
+``EpochEngine.run`` is the 8-input / 2-output epoch ABI of the reference's
+device controller (``controller/g4c_b4_resident_epoch.cpp:40-49,296-324``):
+one call submits the whole epoch to the GPU and returns the token history and
+the 28-word control output.  PyTorch is used only for host tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .model_config import BATCH, MAX_STEPS, PRESETS, ModelConfig, layer_tensor_names
+
+CONTROL_IN = 11
+CONTROL_OUT = 28
+TILING_BYTES = 72
+
+
+def _ptr(array: np.ndarray, ctype):
+    return array.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+def rope_tables(config: ModelConfig) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 cos / sin tables [capacity, head_dim] computed exactly as the
+    reference's ``rope`` (``batched_decoder_step.py:212-216,235-240``)."""
+    d = config.head_dim
+    inv_freq = 1.0 / (config.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    positions = torch.arange(config.capacity, dtype=torch.int64)
+    frequencies = positions.float().reshape(-1, 1) * inv_freq.view(1, -1)
+    embedding = torch.cat((frequencies, frequencies), dim=-1)
+    return embedding.cos().to(torch.bfloat16), embedding.sin().to(torch.bfloat16)
+
+
+@dataclass
+class EpochOutput:
+    history: np.ndarray        # i64 [8, 4] step-major, -1 filled
+    control_out: np.ndarray    # i32 [28]
+    logits: np.ndarray | None  # f32 [8, 4, V] when requested
+    device_us: float           # CUDA-event time of the epoch kernel
+
+    @property
+    def status(self) -> int:
+        return int(self.control_out[3])
+
+    @property
+    def model_calls(self) -> int:
+        return int(self.control_out[4])
+
+
+class EngineError(RuntimeError):
+    pass
+
+
+class EpochEngine:
+    def __init__(self, config: ModelConfig | str, device: int = 0) -> None:
+        self.config = PRESETS[config] if isinstance(config, str) else config
+        self.lib = _lib.load()
+        status = ctypes.c_int32(-1)
+        c_config = self.config.to_c()
+        self.handle = self.lib.cruise_epoch_create(ctypes.byref(c_config), device, ctypes.byref(status))
+        if not self.handle or status.value != 0:
+            raise EngineError(f"cruise_epoch_create failed with status {status.value}")
+        self.device = device
+        cos, sin = rope_tables(self.config)
+        self._check(
+            self.lib.cruise_epoch_set_rope_table(
+                self.handle,
+                cos.view(torch.int16).numpy().ctypes.data,
+                sin.view(torch.int16).numpy().ctypes.data,
+                cos.numel() * 2,
+            ),
+            "set_rope_table",
+        )
+
+    # -- lifecycle -------------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.cruise_epoch_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int, what: str) -> None:
+        if rc != 0:
+            detail = self.lib.cruise_epoch_last_error(self.handle)
+            raise EngineError(f"{what} failed ({rc}): {detail.decode() if detail else ''}")
+
+    # -- weights -----------------------------------------------------------------
+    def init_synthetic(self, seed: int, std: float = 0.02) -> None:
+        self._check(self.lib.cruise_epoch_init_synthetic(self.handle, seed, std), "init_synthetic")
+
+    def set_weight(self, name: str, tensor: torch.Tensor) -> None:
+        value = tensor.detach().to(torch.bfloat16).contiguous().cpu()
+        raw = value.view(torch.int16).numpy()
+        self._check(
+            self.lib.cruise_epoch_set_weight(self.handle, name.encode(), raw.ctypes.data, raw.nbytes),
+            f"set_weight({name})",
+        )
+
+    def get_weight(self, name: str, shape: tuple[int, ...]) -> torch.Tensor:
+        out = np.empty(shape, dtype=np.int16)
+        self._check(
+            self.lib.cruise_epoch_get_weight(self.handle, name.encode(), out.ctypes.data, out.nbytes),
+            f"get_weight({name})",
+        )
+        return torch.from_numpy(out).view(torch.bfloat16)
+
+    def load_weights(self, weights: dict[str, torch.Tensor]) -> None:
+        for name in layer_tensor_names(self.config.num_layers):
+            self.set_weight(name, weights[name])
+
+    # -- KV cache ------------------------------------------------------------------
+    def read_kv(self) -> tuple[torch.Tensor, torch.Tensor]:
+        shape = self.config.kv_cache_shape
+        key = np.empty(shape, dtype=np.int16)
+        value = np.empty(shape, dtype=np.int16)
+        self._check(
+            self.lib.cruise_epoch_read_kv(self.handle, key.ctypes.data, value.ctypes.data, key.nbytes),
+            "read_kv",
+        )
+        return torch.from_numpy(key).view(torch.bfloat16), torch.from_numpy(value).view(torch.bfloat16)
+
+    def write_kv(self, key: torch.Tensor, value: torch.Tensor) -> None:
+        k = key.to(torch.bfloat16).contiguous().view(torch.int16).numpy()
+        v = value.to(torch.bfloat16).contiguous().view(torch.int16).numpy()
+        self._check(
+            self.lib.cruise_epoch_write_kv(self.handle, k.ctypes.data, v.ctypes.data, k.nbytes), "write_kv"
+        )
+
+    # -- one epoch (8-in / 2-out ABI) ------------------------------------------------
+    def run(
+        self,
+        token,
+        position,
+        seq_len,
+        slot,
+        active,
+        block_table,
+        control,
+        import_payload: torch.Tensor | bytes | None = None,
+        want_logits: bool = False,
+        tiling: np.ndarray | None = None,
+        forced: np.ndarray | None = None,
+    ) -> EpochOutput:
+        cfg = self.config
+        token = np.ascontiguousarray(np.asarray(token, dtype=np.int64).reshape(BATCH))
+        position = np.ascontiguousarray(np.asarray(position, dtype=np.int64).reshape(BATCH))
+        seq_len = np.ascontiguousarray(np.asarray(seq_len, dtype=np.int32).reshape(BATCH))
+        slot = np.ascontiguousarray(np.asarray(slot, dtype=np.int32).reshape(BATCH))
+        active = np.ascontiguousarray(np.asarray(active, dtype=np.int32).reshape(BATCH))
+        block_table = np.ascontiguousarray(
+            np.asarray(block_table, dtype=np.int32).reshape(BATCH * cfg.blocks_per_row)
+        )
+        control = np.ascontiguousarray(np.asarray(control, dtype=np.int32).reshape(CONTROL_IN))
+        tiling_arr = np.zeros(TILING_BYTES, dtype=np.uint8) if tiling is None else np.ascontiguousarray(
+            np.asarray(tiling, dtype=np.uint8).reshape(TILING_BYTES)
+        )
+        history = np.empty((MAX_STEPS, BATCH), dtype=np.int64)
+        control_out = np.empty(CONTROL_OUT, dtype=np.int32)
+        logits = np.empty((MAX_STEPS, BATCH, cfg.vocab), dtype=np.float32) if want_logits else None
+        forced_arr = None
+        if forced is not None:
+            forced_arr = np.ascontiguousarray(np.asarray(forced, dtype=np.int64).reshape(MAX_STEPS, BATCH))
+        payload_ptr, payload_bytes, keep = None, 0, None
+        if import_payload is not None:
+            if isinstance(import_payload, torch.Tensor):
+                keep = import_payload.detach().contiguous().cpu().view(torch.uint8).numpy()
+            else:
+                keep = np.frombuffer(import_payload, dtype=np.uint8)
+            payload_ptr, payload_bytes = keep.ctypes.data, keep.nbytes
+        rc = self.lib.cruise_epoch_run(
+            self.handle,
+            _ptr(token, ctypes.c_int64), _ptr(position, ctypes.c_int64), _ptr(seq_len, ctypes.c_int32),
+            _ptr(slot, ctypes.c_int32), _ptr(active, ctypes.c_int32), _ptr(block_table, ctypes.c_int32),
+            _ptr(tiling_arr, ctypes.c_uint8), _ptr(control, ctypes.c_int32),
+            payload_ptr, payload_bytes,
+            _ptr(forced_arr, ctypes.c_int64) if forced_arr is not None else None,
+            _ptr(history, ctypes.c_int64), _ptr(control_out, ctypes.c_int32),
+            _ptr(logits, ctypes.c_float) if logits is not None else None,
+        )
+        self._check(rc, "cruise_epoch_run")
+        device_us = ctypes.c_double(0.0)
+        launches = ctypes.c_int32(0)
+        self.lib.cruise_epoch_last_timing(self.handle, ctypes.byref(device_us), ctypes.byref(launches))
+        return EpochOutput(history, control_out, logits, float(device_us.value))
+
+    def last_timing(self) -> tuple[float, int]:
+        device_us = ctypes.c_double(0.0)
+        launches = ctypes.c_int32(0)
+        self.lib.cruise_epoch_last_timing(self.handle, ctypes.byref(device_us), ctypes.byref(launches))
+        return float(device_us.value), int(launches.value)

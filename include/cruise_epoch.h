@@ -1,0 +1,177 @@
+/*
+ * cruise_epoch.h -- C ABI of the B200 resident decode-epoch engine.
+ *
+ * Plain C types only: every buffer is caller-owned host memory unless a
+ * comment says otherwise, sizes are in bytes, and no entry point takes or
+ * returns a framework type.  One engine owns one CUDA device, the model
+ * weights, the resident paged K/V cache and the per-row resident state.
+ *
+ * Two layers of entry points:
+ *   1. resident_epoch_create / _execute / _destroy keep the exact signatures
+ *      of the reference host bridge (native/resident_epoch_bridge.h:24-45) so
+ *      an existing ctypes / C caller binds them unchanged.
+ *   2. cruise_epoch_* expose the engine directly: an explicit model geometry,
+ *      weight loading, and the 8-input / 2-output epoch ABI of the reference's
+ *      device controller (controller/g4c_b4_resident_epoch.cpp:40-49,296-324)
+ *      with an explicit block table.
+ */
+#ifndef CRUISE_EPOCH_H
+#define CRUISE_EPOCH_H
+
+#include <stdint.h>
+
+#include "cruise_protocol.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference-compatible bridge (native/resident_epoch_bridge.h) ------- */
+
+#pragma pack(push, 1)
+/* Device-IPC import metadata, byte-identical to the reference struct
+ * (native/resident_epoch_bridge.h:8-21).  On CUDA each 64-byte key holds a
+ * cudaIpcMemHandle_t of the exporting process's K or V cache allocation. */
+typedef struct ResidentEpochIpcMetadata {
+  uint64_t magic;
+  uint32_t version;
+  uint32_t import_mask;
+  uint64_t source_bytes;
+  int32_t row_generations[4];
+  int32_t block_ids[4];
+  uint64_t source_offsets[56];
+  char keys[56][64];
+} ResidentEpochIpcMetadata;
+#pragma pack(pop)
+
+/* Replaces resident_epoch_create (native/resident_epoch_bridge.cpp:360-422).
+ *   air_path            model preset: "qwen2.5-7b" or "tiny"
+ *   graph_config        ignored (may be NULL); kept for signature parity
+ *   func_config         ignored (may be NULL)
+ *   external_weight_dir "synthetic:<seed>" for seeded random-init weights, or a
+ *                       directory holding one raw bf16 file "<tensor name>.bin"
+ *                       per checkpoint tensor (HF names, row-major)
+ *   tiling_path         optional 72-byte tiling blob (accepted, unused)
+ * status: 0 ok, 1 bad arguments / engine already active, 2 tiling file,
+ *         3 CUDA init, 4 weight load, 5 model geometry, 6 device memory. */
+void *resident_epoch_create(const char *air_path, const char *graph_config,
+                            const char *func_config,
+                            const char *external_weight_dir,
+                            const char *tiling_path, int32_t *status);
+
+/* Replaces resident_epoch_execute (native/resident_epoch_bridge.cpp:424-649).
+ * Same arguments, same transport statuses (10 bad args, 11 bad row, 12 active
+ * count, 13 transfer file, 30 submit, 31 completion, 33 executed range,
+ * 34 import checksum, 35 device IPC import) and the same commit-state moves
+ * (0 -> 1 before submission -> 2 after a valid completion).  Row r owns the
+ * blocks r*blocks_per_row + j, as in the reference bridge (:524-532).
+ * output_token_ids is [4][8] row-major ([row][step]). */
+int32_t resident_epoch_execute(
+    void *opaque, int32_t request_count, int32_t max_steps,
+    const int64_t *input_token_ids, const int64_t *input_positions,
+    const int32_t *input_sequence_lengths, const int32_t *input_eos_token_ids,
+    const int32_t *input_row_generations, int64_t *output_token_ids,
+    int32_t *output_executed, int32_t *output_row_generations,
+    int32_t *output_model_calls, int32_t *output_device_status,
+    int32_t *output_feed_calls, int32_t *output_fetch_calls,
+    int32_t *output_commit_state, int32_t *output_kv_import_checksum,
+    int64_t *output_wall_us, int64_t *output_native_cpu_us,
+    int64_t *output_declared_input_bytes,
+    int64_t *output_declared_output_bytes, const char *transfer_path,
+    uint64_t transfer_id, const ResidentEpochIpcMetadata *ipc_metadata);
+
+/* Replaces resident_epoch_destroy (native/resident_epoch_bridge.cpp:651-670). */
+void resident_epoch_destroy(void *opaque);
+
+/* ---- engine API ---------------------------------------------------------- */
+
+/* Qwen2 geometry plus the paged-KV layout.  The static batch is 4 rows and an
+ * epoch runs at most 8 steps, as in the reference (controller :16-17).
+ * Replaces the hard-coded constants of controller/g4c_b4_resident_epoch.cpp:13-38. */
+typedef struct CruiseModelConfig {
+  int32_t num_layers;
+  int32_t hidden;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t intermediate;
+  int32_t vocab;
+  float rms_eps;
+  float rope_theta;
+  int32_t block_size;      /* tokens per KV block */
+  int32_t blocks_per_row;  /* logical capacity = block_size * blocks_per_row */
+  int32_t num_blocks;      /* physical blocks in the resident cache */
+  int32_t configured_eos;  /* EOS written for empty rows by the bridge */
+  int32_t reserved[7];
+} CruiseModelConfig;
+
+/* Fills *cfg with a preset ("qwen2.5-7b" or "tiny"); returns 0 or -1. */
+int32_t cruise_epoch_preset(const char *name, CruiseModelConfig *cfg);
+
+/* Creates an engine on `device` with all device memory allocated and zeroed.
+ * status as for resident_epoch_create.  Any number of engines may coexist
+ * (one per device for data-parallel cohorts). */
+void *cruise_epoch_create(const CruiseModelConfig *cfg, int32_t device,
+                          int32_t *status);
+void cruise_epoch_destroy(void *engine);
+
+/* Seeded random-init weights generated on the device: every tensor element is
+ * bf16(0.02-scaled Irwin-Hall(4) sum of a splitmix64 hash of (seed, tensor,
+ * index)).  Returns 0 or a CUDA error code. */
+int32_t cruise_epoch_init_synthetic(void *engine, uint64_t seed, double stddev);
+
+/* Copies one checkpoint tensor (HF name, row-major bf16) into the engine's
+ * layout / out of it.  bytes must equal the tensor size.  0 on success,
+ * -1 unknown name or size, else a CUDA error code. */
+int32_t cruise_epoch_set_weight(void *engine, const char *name,
+                                const void *host_bf16, uint64_t bytes);
+int32_t cruise_epoch_get_weight(void *engine, const char *name, void *host_bf16,
+                                uint64_t bytes);
+
+/* Overrides the RoPE tables: bf16 cos and sin, [capacity][head_dim]. */
+int32_t cruise_epoch_set_rope_table(void *engine, const uint16_t *cos_bf16,
+                                    const uint16_t *sin_bf16, uint64_t bytes);
+
+/* Whole resident K (or V) cache, bf16 [layers][num_blocks][block_size]
+ * [kv_heads][head_dim]: copy out / in.  0 or a CUDA error code. */
+int32_t cruise_epoch_read_kv(void *engine, void *key_host, void *value_host,
+                             uint64_t bytes_each);
+int32_t cruise_epoch_write_kv(void *engine, const void *key_host,
+                              const void *value_host, uint64_t bytes_each);
+
+/* One resident epoch through the 8-input / 2-output ABI of the reference's
+ * device controller, entirely on the GPU (one submission, no per-token host
+ * round trip).  Inputs (host): token i64[4], position i64[4], seq_len i32[4],
+ * slot i32[4], active i32[4], block_table i32[4*blocks_per_row], tiling
+ * u8[72] (may be NULL), control i32[11] = [K, eos x4, sampling, variant
+ * (|0x100|mask to import), generation x4].  import_payload: when importing,
+ * [K|V][layers][4 rows][block_size][kv_heads][head_dim] bf16 on the host.
+ * forced_tokens: NULL for greedy decoding, or i64[8][4] step-major where an
+ * entry >= 0 replaces the argmax of that row at that step (teacher forcing:
+ * the device prefill of a prompt runs as forced epochs).
+ * Outputs (host): history i64[8][4] step-major (-1 filled) and control_out
+ * i32[28] (layout of controller :296-324).  logits_out, if not NULL, receives
+ * f32 [8][4][vocab] (steps never run stay untouched).  Returns 0 when the
+ * epoch ran (the device status is control_out[3]) or a CUDA error code. */
+int32_t cruise_epoch_run(void *engine, const int64_t *token,
+                         const int64_t *position, const int32_t *seq_len,
+                         const int32_t *slot, const int32_t *active,
+                         const int32_t *block_table, const uint8_t *tiling,
+                         const int32_t *control, const void *import_payload,
+                         uint64_t import_bytes, const int64_t *forced_tokens,
+                         int64_t *history, int32_t *control_out,
+                         float *logits_out);
+
+/* Device time of the last epoch in microseconds (CUDA events around the
+ * epoch kernel) and the number of kernels it launched. */
+int32_t cruise_epoch_last_timing(void *engine, double *device_us,
+                                 int32_t *kernel_launches);
+
+/* Last CUDA error string of this engine (static storage). */
+const char *cruise_epoch_last_error(void *engine);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CRUISE_EPOCH_H */
