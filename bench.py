@@ -1,0 +1,512 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen2.5-7B-arch B=4 resident decode epochs (decode tok/s, us/step,
+% HBM roofline) on 1..N B200s of one node.
+
+Workload: the 7B architecture with seeded random-init
+bf16 weights (generated on the device), paged KV of 128-token blocks, 2 blocks
+per row, B=4 rows all active with prompts of 2-5 tokens (ids in [0, 151643)).
+Prompts are prefilled on the device with teacher-forced epochs, the prefilled
+first blocks are read back and re-imported once through the one-shot
+host-to-device KV import (the import epoch is the first K=2 epoch), and then
+K=2 greedy epochs keep decoding.  A "step" of this benchmark is one epoch.
+
+value    decode tokens/s over the timed epochs, device time (CUDA events around
+         the epoch kernel on its own stream), max over ranks, all ranks summed.
+e2e      the same through the C-ABI call with host buffers: H2D of the epoch
+         inputs and D2H of the token history + control output inside the timed
+         wall-clock region.
+--impl reference  times the CPU oracle (a port of the reference's torch decode
+         step and controller, the reference path itself needs Ascend hardware)
+         on the host cores on a bounded sample of the same workload.
+
+Multi-GPU (torchrun): each rank runs an independent B=4 cohort on its own GPU
+(data-parallel replicas, no collective on the data path); the process group is
+only used for the start/stop barrier and the max-over-ranks timing.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+METRIC = "Qwen2.5-7B-arch B=4 epoch: decode tok/s, µs/step, % HBM roofline"
+KV_BYTES_PER_TOKEN = 28 * 4 * 128 * 2 * 2   # K and V over all layers, one position
+FALLBACK_HBM_GBS = 6650.0
+EPOCH_H2D_BYTES = 616   # EpochIO inputs (8-in ABI + forced-token table), one copy per epoch
+EPOCH_D2H_BYTES = 368   # token history i64[8][4] + control output i32[28]
+
+
+def hbm_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def weight_bytes_per_step(cfg) -> int:
+    """Bytes of weights one decode step streams (every projection, the norms,
+    biases and lm_head; the embedding table contributes only 4 gathered rows)."""
+    h, kv, i, v, L = cfg.hidden, cfg.kv_width, cfg.intermediate, cfg.vocab, cfg.num_layers
+    per_layer = (h + 2 * kv) * h + (h + 2 * kv) + h * h + 2 * i * h + h * i + 2 * h
+    return 2 * (L * per_layer + v * h + h)
+
+
+def step_bytes(cfg, contexts: list[int]) -> int:
+    """Algorithmic HBM bytes of one decode step: weights + KV read over each
+    active row's context + KV write of the new position + embedding rows."""
+    kv_token = 2 * cfg.num_layers * cfg.kv_width * 2
+    return weight_bytes_per_step(cfg) + kv_token * (sum(contexts) + len(contexts)) + len(contexts) * cfg.hidden * 2
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def setup_cohort(engine, cfg, seed: int, k: int):
+    """Device prefill of a seeded B=4 cohort, then the one-shot import epoch."""
+    from scenario import decode_inputs, import_payload, make_scenario, prefill_epochs
+
+    sc = make_scenario(vocab=cfg.vocab, seed=seed, active_rows=(1, 1, 1, 1), prompt_len=(2, 5),
+                       budget=(2, 8), k=k, eos=cfg.configured_eos, token_high=min(151643, cfg.vocab - 1))
+    for inputs in prefill_epochs(sc, cfg.block_size, cfg.vocab):
+        out = engine.run(**inputs)
+        assert out.status == 0, f"prefill epoch status {out.status}"
+    key, value = engine.read_kv()
+    payload = import_payload(key, value, sc)
+    inputs = decode_inputs(sc, cfg.block_size, importing=True)
+    out = engine.run(**inputs, import_payload=payload)
+    assert out.status == 0, f"import epoch status {out.status}"
+    return sc, out
+
+
+class Cohort:
+    """Keeps a cohort decoding epoch after epoch (continuing resident state)."""
+
+    def __init__(self, engine, cfg, sc, last_out) -> None:
+        self.engine, self.cfg, self.sc = engine, cfg, sc
+        self.token = np.zeros(4, dtype=np.int64)
+        self.position = np.zeros(4, dtype=np.int64)
+        for r in range(4):
+            self.position[r] = len(sc.prompts[r]) - 1
+        self._advance(last_out)
+
+    def _advance(self, out):
+        for r in range(4):
+            executed = int(out.control_out[6 + 8 + r])
+            if executed:
+                self.token[r] = out.history[executed - 1, r]
+                self.position[r] += executed
+
+    def inputs(self):
+        from scenario import compute_slot
+
+        cfg, sc = self.cfg, self.sc
+        seq_len = (self.position + 1).astype(np.int32)
+        slot = np.array([compute_slot(sc.block_table, cfg.block_size, r, int(self.position[r])) for r in range(4)],
+                        dtype=np.int32)
+        control = np.array([sc.k, *sc.eos, 0, 0, *sc.generations], dtype=np.int32)
+        return dict(token=self.token.copy(), position=self.position.copy(), seq_len=seq_len, slot=slot,
+                    active=np.ones(4, dtype=np.int32), block_table=sc.block_table.reshape(-1), control=control)
+
+    def step(self):
+        inputs = self.inputs()
+        out = self.engine.run(**inputs)
+        if out.status != 0:
+            raise RuntimeError(f"epoch status {out.status}")
+        self._advance(out)
+        return out, inputs
+
+    def room(self) -> int:
+        return int(self.cfg.capacity - self.position.max() - 1)
+
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from cruise_b200.engine import EpochEngine
+    from cruise_b200.model_config import QWEN25_7B
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    device = local
+    cfg = QWEN25_7B
+    if args.layers or args.vocab:
+        # reduced geometry for profiler captures only (never a bench line)
+        cfg = cfg.with_(num_layers=args.layers or cfg.num_layers, vocab=args.vocab or cfg.vocab,
+                        configured_eos=(args.vocab or cfg.vocab) - 1)
+    engine = EpochEngine(cfg, device=device)
+    t0 = time.perf_counter()
+    engine.init_synthetic(seed=0)
+    synth_s = time.perf_counter() - t0
+    sc, first = setup_cohort(engine, cfg, seed=1000 + rank, k=args.k)
+    cohort = Cohort(engine, cfg, sc, first)
+    need = (args.warmup + args.steps + (1 if args.trace else 0)) * args.k
+    if cohort.room() < need:
+        raise RuntimeError(f"capacity {cfg.capacity} too small for {need} more positions")
+    for _ in range(args.warmup):
+        cohort.step()
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    # ---- timed region: device-resident epochs (value) ----
+    barrier()
+    tokens = 0
+    device_us = []
+    step_bytes_total = 0
+    with ClockSampler(device) as clocks:
+        wall0 = time.perf_counter()
+        for _ in range(args.steps):
+            out, inputs = cohort.step()
+            executed = out.control_out[6 + 8 : 6 + 12]
+            tokens += int(executed.sum())
+            device_us.append(out.device_us)
+            contexts0 = [int(p) for p in inputs["position"]]
+            for s in range(out.model_calls):
+                ctx = [c + s for c, e in zip(contexts0, executed) if e > s]
+                step_bytes_total += step_bytes(cfg, ctx)
+        wall = time.perf_counter() - wall0
+    barrier()
+    dev_s = sum(device_us) / 1e6
+    model_calls = args.steps * args.k
+    # max over ranks of the device time
+    t_max = dev_s
+    tok_total = tokens
+    if world > 1:
+        tt = torch.tensor([dev_s, float(tokens)], device=f"cuda:{device}", dtype=torch.float64)
+        tm = tt.clone()
+        dist.all_reduce(tm[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(tt[1:], op=dist.ReduceOp.SUM)
+        t_max, tok_total = float(tm[0]), float(tt[1])
+    value = tok_total / t_max
+    # e2e: wall clock per epoch through the C-ABI call (host buffers both ways)
+    e2e_tokens = tokens
+    e2e_wall = wall
+    if world > 1:
+        ew = torch.tensor([wall], device=f"cuda:{device}", dtype=torch.float64)
+        dist.all_reduce(ew, op=dist.ReduceOp.MAX)
+        e2e_wall = float(ew[0])
+        e2e_tokens = tok_total
+    if args.trace and rank == 0:
+        print_trace(engine, cohort, cfg, args.k)
+    peak, peak_kind = hbm_peak()
+    per_epoch_us = dev_s * 1e6 / args.steps
+    achieved_gbs = step_bytes_total / dev_s / 1e9
+    clock = clocks.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(per_epoch_us / 1e3, 4),
+            "us_per_decode_step": round(per_epoch_us / args.k, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights generated on the device; seeded prompts)",
+            "config": {
+                "workload": "BASELINE configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
+                            "one-shot H2D KV import of the device-prefilled prompts (2-5 tokens)" % args.k,
+                "model": "Qwen2.5-7B architecture (28 layers, hidden 3584, 28/4 heads x 128, I 18944, V 152064)",
+                "global_batch": 4 * world,
+                "epoch_k": args.k,
+                "kv": "paged, block 128, 2 blocks per row",
+                "parallelism": f"dp{world} (independent cohorts)" if world > 1 else "single GPU",
+                "l2": "no flush: every step streams 14.1 GB of weights, > 126 MB L2",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(achieved_gbs, 1),
+                "peak": peak,
+                "peak_kind": peak_kind,
+                "unit": "GB/s",
+                "frac": round(achieved_gbs / peak, 4),
+                "traffic": None,
+                "kernel": "resident_epoch_kernel",
+                "bytes_per_decode_step": step_bytes_total // model_calls,
+            },
+            "e2e": {
+                "value": round(e2e_tokens / e2e_wall, 2),
+                "unit": "tok/s",
+                "h2d_bytes_per_step": EPOCH_H2D_BYTES,
+                "d2h_bytes_per_step": EPOCH_D2H_BYTES,
+                "host_control_ms_per_epoch": round(wall * 1e3 / args.steps, 4),
+            },
+            "gpu_launches": args.steps,
+            "clocks": clock,
+            "setup": {"weight_synthesis_s": round(synth_s, 2)},
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(engine, cfg)
+        print(json.dumps(line), flush=True)
+    engine.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+PHASE_NAMES = ("qkv", "attention", "o_proj", "gate_up", "down")
+
+
+def print_trace(engine, cohort, cfg, k) -> None:
+    """One traced epoch: per-phase time between grid barriers (CTA 0 clock),
+    summed over layers and steps, and the weight bytes each kind streams."""
+    engine.set_trace(True)
+    out, _ = cohort.step()
+    engine.set_trace(False)
+    L = cfg.num_layers
+    phases = 5 * L + 2
+    count = 2 + out.model_calls * phases + 1
+    exit_ns, entry_ns = engine.read_trace(count)
+    first = 2   # validation and continuity barriers precede the loop
+    totals, work = {}, {}
+    for step in range(out.model_calls):
+        for ph in range(phases):
+            j = first + step * phases + ph + 1
+            name = "lm_head" if ph == 5 * L else "control" if ph > 5 * L else PHASE_NAMES[ph % 5]
+            totals[name] = totals.get(name, 0) + int(exit_ns[j]) - int(exit_ns[j - 1])
+            work[name] = work.get(name, 0) + int(entry_ns[j]) - int(exit_ns[j - 1])
+    h, kv, i = cfg.hidden, cfg.kv_width, cfg.intermediate
+    wbytes = {"qkv": (h + 2 * kv) * h * 2 * L, "o_proj": h * h * 2 * L, "gate_up": 2 * i * h * 2 * L,
+              "down": h * i * 2 * L, "lm_head": cfg.vocab * h * 2}
+    calls = out.model_calls
+    span = int(exit_ns[count - 1]) - int(exit_ns[first])
+    print(f"trace: epoch {out.device_us:.1f} us, {calls} steps, loop span {span / 1e3:.1f} us", file=sys.stderr)
+    for name in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "control"):
+        t = totals.get(name, 0) / calls
+        bw = wbytes.get(name, 0) / max(t, 1) if name in wbytes else 0.0   # bytes per ns = GB/s
+        per = t / (L if name in PHASE_NAMES else 1)
+        print(f"  {name:9s} {t / 1e3:8.1f} us/step  {per / 1e3:7.2f} us/phase  "
+              f"cta0-work {work.get(name, 0) / calls / 1e3:8.1f} us/step  {bw:6.0f} GB/s",
+              file=sys.stderr)
+
+
+def cpu_oracle_step_time(weights: dict, cfg, threads: int) -> tuple[float, str]:
+    """Seconds of one 7B decode step of the CPU oracle (bf16 torch ops, the
+    reference's own arithmetic), from a bounded sample: steps of the same
+    geometry truncated to 1 and 2 layers give the per-layer and fixed costs,
+    extrapolated to all layers."""
+    import torch
+
+    from oracle.decoder import OracleDecoder
+    from oracle.model import OracleConfig
+
+    torch.set_num_threads(threads)
+    times = {}
+    for layers in (1, 2):
+        ocfg = OracleConfig(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
+                            num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+                            intermediate=cfg.intermediate, vocab=cfg.vocab, block_size=cfg.block_size)
+        decoder = OracleDecoder(ocfg, weights)   # a truncation reads layers 0..layers-1 only
+        shape = (layers, ocfg.num_blocks, ocfg.block_size, ocfg.num_kv_heads, ocfg.head_dim)
+        key = torch.zeros(shape, dtype=torch.bfloat16)
+        value = torch.zeros(shape, dtype=torch.bfloat16)
+        token = torch.tensor([11, 12, 13, 14], dtype=torch.int64)
+        position = torch.tensor([4, 4, 4, 4], dtype=torch.int64)
+        seq_len = torch.tensor([5, 5, 5, 5], dtype=torch.int32)
+        bt = torch.arange(8, dtype=torch.int32).reshape(4, 2)
+        slot = torch.tensor([4, 260, 516, 772], dtype=torch.int32)
+        active = torch.ones(4, dtype=torch.int32)
+        decoder.step(token, position, seq_len, bt, slot, key, value, active)   # warm-up
+        samples = []
+        for _ in range(3):
+            t = time.perf_counter()
+            decoder.step(token, position, seq_len, bt, slot, key, value, active)
+            samples.append(time.perf_counter() - t)
+        times[layers] = min(samples)
+    per_layer = max(times[2] - times[1], 1e-9)
+    fixed = max(times[1] - per_layer, 0.0)
+    return fixed + cfg.num_layers * per_layer, (
+        f"1- and 2-layer truncations of the 7B decode step (B=4, ctx 5), best of 3, extrapolated to "
+        f"{cfg.num_layers} layers: {times[1]*1e3:.0f} / {times[2]*1e3:.0f} ms"
+    )
+
+
+def engine_weights_fn(engine):
+    import torch
+
+    from oracle.model import LAYER_KEYS
+
+    cfg = engine.config
+
+    def weights(layers: int):
+        shapes = {"model.embed_tokens.weight": (cfg.vocab, cfg.hidden), "model.norm.weight": (cfg.hidden,),
+                  "lm_head.weight": (cfg.vocab, cfg.hidden)}
+        h, kv, i = cfg.hidden, cfg.kv_width, cfg.intermediate
+        per = {"input_layernorm.weight": (h,), "post_attention_layernorm.weight": (h,),
+               "self_attn.q_proj.weight": (h, h), "self_attn.q_proj.bias": (h,),
+               "self_attn.k_proj.weight": (kv, h), "self_attn.k_proj.bias": (kv,),
+               "self_attn.v_proj.weight": (kv, h), "self_attn.v_proj.bias": (kv,),
+               "self_attn.o_proj.weight": (h, h), "mlp.gate_proj.weight": (i, h),
+               "mlp.up_proj.weight": (i, h), "mlp.down_proj.weight": (h, i)}
+        out = {name: engine.get_weight(name, shape) for name, shape in shapes.items()}
+        for layer in range(layers):
+            for key in LAYER_KEYS:
+                out[f"model.layers.{layer}.{key}"] = engine.get_weight(f"model.layers.{layer}.{key}", per[key])
+        return out
+
+    return weights
+
+
+def cpu_baseline(engine, cfg) -> dict:
+    threads = len(os.sched_getaffinity(0))
+    step_s, sample = cpu_oracle_step_time(engine_weights_fn(engine)(2), cfg, threads)
+    return {"value": round(4 / step_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": sample, "us_per_decode_step": round(step_s * 1e6, 1)}
+
+
+def run_reference(args) -> None:
+    """CPU arm: the oracle port of the reference path on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from cruise_b200.model_config import QWEN25_7B
+
+    cfg = QWEN25_7B
+    threads = len(os.sched_getaffinity(0))
+
+    weights = random_weights(cfg, layers=2, seed=0)
+    samples = []
+    sample_desc = ""
+    for _ in range(args.warmup + args.steps):
+        step_s, sample_desc = cpu_oracle_step_time(weights, cfg, threads)
+        samples.append(step_s)
+    timed = samples[args.warmup:]
+    step_s = sum(timed) / len(timed)
+    value = 4 / step_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * args.k * 1e3, 2),
+        "us_per_decode_step": round(step_s * 1e6, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE configs[1] decode steps (B=4, 7B arch) on the host cores",
+                   "epoch_k": args.k},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample_desc},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def random_weights(cfg, layers: int, seed: int) -> dict:
+    """N(0, 0.02) bf16 weights of the 7B geometry truncated to `layers` layers
+    (CPU timing does not depend on the values; torch's generator is fast)."""
+    import torch
+
+    from oracle.model import OracleConfig, tensor_shapes
+
+    ocfg = OracleConfig(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
+                        num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+                        intermediate=cfg.intermediate, vocab=cfg.vocab, block_size=cfg.block_size)
+    gen = torch.Generator().manual_seed(seed)
+    return {name: torch.empty(shape, dtype=torch.bfloat16).normal_(0.0, 0.02, generator=gen)
+            for name, shape in tensor_shapes(ocfg).items()}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--k", type=int, default=2, choices=(1, 2, 4, 8))
+    parser.add_argument("--impl", default="cruise", choices=("cruise", "reference"))
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--trace", action="store_true", help="per-phase timing of one extra epoch (stderr)")
+    parser.add_argument("--layers", type=int, default=0, help="profiling only: truncate the model to N layers")
+    parser.add_argument("--vocab", type=int, default=0, help="profiling only: vocabulary size")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -117,6 +117,9 @@ struct Engine {
   int sms = 0;
   int stages = 0;
   int xs_stride = 0;
+  int down_xglobal = 0;
+  uint64_t *trace = nullptr;     // per-launch phase timestamps (optional)
+  bool trace_on = false;
   size_t smem = 0;
   // device memory
   void *weights = nullptr;   // one allocation for every weight tensor
@@ -252,8 +255,11 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
     destroy_engine(e);
     return nullptr;
   }
-  // shared memory geometry: activation rows sized for the widest projection input
-  const int kmax = std::max(m.H, m.I_pad);
+  // shared memory geometry: the activation rows in smem hold the widest input of
+  // the projections that stage it there; the down projection reads its input
+  // from L2 instead when it runs one 64-wide k-step per consumer warp.
+  e->down_xglobal = pick_kc(m.I_pad) == 64 * kConsumerWarps;
+  const int kmax = e->down_xglobal ? m.H : std::max(m.H, m.I_pad);
   e->xs_stride = kmax + 8;
   const size_t limit = prop.sharedMemPerBlockOptin;
   int stages = kMaxStages;
@@ -328,6 +334,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   const size_t o_ai = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ab = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_lg = take2(static_cast<size_t>(kMaxSteps) * kBatch * m.V * 4);
+  const size_t o_trace = take2(2 * kTraceMax * sizeof(uint64_t));
   const size_t o_io = take2(sizeof(EpochIO)), o_res = take2(sizeof(ResidentState));
   const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sizeof(SyncState));
   if (cudaMalloc(&e->state, st) != cudaSuccess) { destroy_engine(e); return nullptr; }
@@ -346,6 +353,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   e->arg_idx = reinterpret_cast<int32_t *>(sb + o_ai);
   e->arg_bad = reinterpret_cast<int32_t *>(sb + o_ab);
   e->logits = reinterpret_cast<float *>(sb + o_lg);
+  e->trace = reinterpret_cast<uint64_t *>(sb + o_trace);
   e->d_io = reinterpret_cast<EpochIO *>(sb + o_io);
   e->d_res = reinterpret_cast<ResidentState *>(sb + o_res);
   e->d_work = reinterpret_cast<EpochWork *>(sb + o_work);
@@ -551,6 +559,8 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   p.grid = e->sms;
   p.stages = e->stages;
   p.xs_stride = e->xs_stride;
+  p.down_xglobal = e->down_xglobal;
+  p.trace = e->trace_on ? e->trace : nullptr;
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
   void *args[] = {&p};
   cudaEventRecord(e->ev0, e->stream);
@@ -588,6 +598,8 @@ struct TransferHeader {   // :73-89
 };
 #pragma pack(pop)
 static_assert(sizeof(TransferHeader) == CRUISE_RESIDENT_TRANSFER_HEADER_BYTES, "transfer header ABI");
+static_assert(offsetof(EpochIO, history) == 616, "epoch input block: 616 bytes host-to-device per epoch");
+static_assert(sizeof(EpochIO) - offsetof(EpochIO, history) == 368, "epoch output block: 368 bytes per epoch");
 static_assert(sizeof(ResidentEpochIpcMetadata) == CRUISE_RESIDENT_IPC_METADATA_BYTES, "IPC metadata ABI");
 
 std::mutex g_lifecycle_mutex;
@@ -831,6 +843,24 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us, int32_t *kerne
   if (device_us) *device_us = static_cast<double>(e->last_ms) * 1000.0;
   if (kernel_launches) *kernel_launches = e->last_launches;
   return 0;
+}
+
+int32_t cruise_epoch_set_trace(void *engine, int32_t enable) {
+  if (engine == nullptr) return -1;
+  static_cast<Engine *>(engine)->trace_on = enable != 0;
+  return 0;
+}
+
+int32_t cruise_epoch_read_trace(void *engine, uint64_t *exit_ns, uint64_t *entry_ns, int32_t count) {
+  if (engine == nullptr || exit_ns == nullptr || entry_ns == nullptr || count < 0 || count > cruise::kTraceMax)
+    return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  cudaError_t err = cudaMemcpy(exit_ns, e->trace, sizeof(uint64_t) * count, cudaMemcpyDeviceToHost);
+  if (err == cudaSuccess)
+    err = cudaMemcpy(entry_ns, e->trace + cruise::kTraceMax, sizeof(uint64_t) * count, cudaMemcpyDeviceToHost);
+  return cruise::set_err(e, err, "read trace");
 }
 
 const char *cruise_epoch_last_error(void *engine) {

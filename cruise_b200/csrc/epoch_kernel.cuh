@@ -42,7 +42,7 @@
 namespace cruise {
 
 enum GemvKind : int32_t { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
-enum XMode : int32_t { kXNorm = 0, kXCopy = 1 };
+enum XMode : int32_t { kXNorm = 0, kXCopy = 1, kXGlobal = 2 };
 
 struct Gemv {
   const bf16 *W;
@@ -85,8 +85,8 @@ __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int k
         g.xsrc_stride = m.H; g.norm_w = lw.w_post;
         break;
       default:  // kDown
-        g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = kXCopy; g.xsrc = p.act;
-        g.xsrc_stride = m.I_pad;
+        g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = p.down_xglobal ? kXGlobal : kXCopy;
+        g.xsrc = p.act; g.xsrc_stride = m.I_pad;
         break;
     }
   }
@@ -142,22 +142,26 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // ---- shared memory map ------------------------------------------------------------
 struct Smem {
   uint8_t *ring;           // stages x kStageBytes
-  bf16 *xs;                // [4][xs_stride]  (attention scratch aliases it)
-  float *red;              // [8 warps][64]
-  float *tot;              // [64]
-  uint64_t *full;          // [kMaxStages]
-  uint64_t *empty;         // [kMaxStages]
+  bf16 *xs;                // [4][xs_stride]  (attention and checksum scratch alias it)
+  float *red;              // [kRedSlots][8 warps][64] row-group partial sums
+  uint64_t *full;          // [kMaxStages]  weight stage landed
+  uint64_t *empty;         // [kMaxStages]  weight stage consumed
+  uint64_t *red_full;      // [kRedSlots]   partials written by the 8 consumer warps
+  uint64_t *red_empty;     // [kRedSlots]   partials read by the epilogue warp
+  uint64_t *phase_done;    // epilogue warp finished the current projection phase
   float *nrm;              // [8][4] norm partial sums, then [4] inverse rms at +32
-  float *best_val;         // [4]
-  int32_t *best_idx;       // [4]
-  int32_t *best_bad;       // [4]
+  float *best_val;         // [8]
+  int32_t *best_idx;       // [8]
+  int32_t *best_bad;       // [8]
   int32_t *misc;           // [16] small broadcast values
-  volatile int *prod_ctl;  // producer control: >= s run step s, -1 stop
+  volatile int *prod_ctl;  // producer / epilogue control: -2 wait, >= s run step s, -1 stop
+  volatile int *phase_started;  // sequence number of the projection phase the consumers began
 };
 
 __host__ __device__ inline size_t smem_bytes(int stages, int xs_stride) {
   return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(kBatch) * xs_stride * 2 +
-         kConsumerWarps * 64 * 4 + 64 * 4 + 2 * kMaxStages * 8 + 40 * 4 + 12 * 4 + 16 * 4 + 16;
+         static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4 + 2 * kMaxStages * 8 +
+         2 * kRedSlots * 8 + 8 + 40 * 4 + 24 * 4 + 16 * 4 + 16;
 }
 
 __device__ __forceinline__ Smem carve_smem(uint8_t *base, const EpochParams &p) {
@@ -168,26 +172,40 @@ __device__ __forceinline__ Smem carve_smem(uint8_t *base, const EpochParams &p) 
   s.xs = reinterpret_cast<bf16 *>(ptr);
   ptr += static_cast<size_t>(kBatch) * p.xs_stride * 2;
   s.red = reinterpret_cast<float *>(ptr);
-  ptr += kConsumerWarps * 64 * 4;
-  s.tot = reinterpret_cast<float *>(ptr);
-  ptr += 64 * 4;
+  ptr += static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4;
   s.full = reinterpret_cast<uint64_t *>(ptr);
   ptr += kMaxStages * 8;
   s.empty = reinterpret_cast<uint64_t *>(ptr);
   ptr += kMaxStages * 8;
+  s.red_full = reinterpret_cast<uint64_t *>(ptr);
+  ptr += kRedSlots * 8;
+  s.red_empty = reinterpret_cast<uint64_t *>(ptr);
+  ptr += kRedSlots * 8;
+  s.phase_done = reinterpret_cast<uint64_t *>(ptr);
+  ptr += 8;
   s.nrm = reinterpret_cast<float *>(ptr);
   ptr += 40 * 4;
   s.best_val = reinterpret_cast<float *>(ptr);
-  ptr += 4 * 4;
+  ptr += 8 * 4;
   s.best_idx = reinterpret_cast<int32_t *>(ptr);
-  ptr += 4 * 4;
+  ptr += 8 * 4;
   s.best_bad = reinterpret_cast<int32_t *>(ptr);
-  ptr += 4 * 4;
+  ptr += 8 * 4;
   s.misc = reinterpret_cast<int32_t *>(ptr);
   ptr += 16 * 4;
   s.prod_ctl = reinterpret_cast<volatile int *>(ptr);
+  s.phase_started = reinterpret_cast<volatile int *>(ptr + 4);
   return s;
 }
+
+// Position in a ring of mbarrier-guarded slots.
+struct RingCursor {
+  uint32_t slot = 0;
+  uint32_t parity = 0;
+  __device__ __forceinline__ void advance(uint32_t n) {
+    if (++slot == n) { slot = 0; parity ^= 1u; }
+  }
+};
 
 // ---- cross-CTA helpers ---------------------------------------------------------------
 __device__ __forceinline__ bool aborted(const EpochParams &p) {
@@ -204,6 +222,8 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
   named_sync(1, kConsumerThreads);
   if (threadIdx.x == 0) {
     int ok = 1;
+    const bool trace = p.trace != nullptr && blockIdx.x == 0 && index < kTraceMax;
+    if (trace) p.trace[kTraceMax + index] = globaltimer();   // CTA 0 finished its share
     __threadfence();
     red_release_add_u32(&p.sync->barrier, 1u);
     const uint32_t target = index * static_cast<uint32_t>(p.grid);
@@ -219,6 +239,7 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
       __nanosleep(32);
     }
     if (ok && aborted(p)) ok = 0;
+    if (trace) p.trace[index] = globaltimer();                // every CTA arrived
     s.misc[0] = ok;
   }
   named_sync(1, kConsumerThreads);
@@ -236,6 +257,36 @@ __device__ __forceinline__ int compute_slot(const ModelDims &m, const int32_t *b
   return physical * m.bs + offset;
 }
 
+// Waits for phase `parity` of `bar` with try_wait.  Gives up (false) when the
+// launch aborts, when `*stop` reads -1, or after the launch's timeout.
+__device__ __forceinline__ bool wait_bar(const EpochParams &p, uint64_t *bar, uint32_t parity,
+                                         const volatile int *stop, uint32_t where) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t deadline = globaltimer() + p.timeout_ns;
+  for (uint32_t polls = 1;; ++polls) {
+    if (mbar_try(bar, parity)) return true;
+    if ((polls & 15) == 0) {
+      if (aborted(p) || (stop != nullptr && *stop == -1)) return false;
+      if (globaltimer() > deadline) {
+        raise_error(p, where);
+        return false;
+      }
+    }
+  }
+}
+
+// Waits until the consumers release step `step` (true) or stop (false).
+__device__ __forceinline__ bool wait_step(const EpochParams &p, const Smem &s, int step) {
+  const uint64_t deadline = globaltimer() + p.timeout_ns;
+  while (true) {
+    const int ctl = *s.prod_ctl;   // -2 not yet released, -1 stop, s: run step s
+    if (ctl == -1) return false;
+    if (ctl >= step) return true;
+    if (aborted(p) || globaltimer() > deadline) return false;
+    __nanosleep(64);
+  }
+}
+
 // ---- producer warp --------------------------------------------------------------------
 // Streams the weight tiles of every projection phase of a step, in the order the
 // consumers use them.  Waits for the consumers' go signal before each step.
@@ -243,19 +294,11 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
   const int lane = threadIdx.x & 31;
   const int L = p.m.L;
   const int phases = 5 * L + 2;
+  RingCursor ring;
   uint32_t issued = 0;
   bool stop = false;
   for (int step = 0; step < kMaxSteps && !stop; ++step) {
-    if (lane == 0) {
-      const uint64_t deadline = globaltimer() + p.timeout_ns;
-      while (true) {
-        const int ctl = *s.prod_ctl;   // -2 not yet released, -1 stop, s: run step s
-        if (ctl == -1) { stop = true; break; }
-        if (ctl >= step) break;
-        if (aborted(p) || globaltimer() > deadline) { stop = true; break; }
-        __nanosleep(128);
-      }
-    }
+    if (lane == 0) stop = !wait_step(p, s, step);
     stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
     if (stop) break;
     for (int ph = 0; ph < phases && !stop; ++ph) {
@@ -265,27 +308,21 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
       const TileRange tr = tile_range(g, blockIdx.x, p.grid);
       const uint32_t row_bytes = static_cast<uint32_t>(g.kc) * 2u;
       const uint32_t pitch = row_bytes + 16u;
+      int64_t rg = tr.t0 / tr.KT;
+      int kk = static_cast<int>(tr.t0 % tr.KT);
       for (int64_t t = tr.t0; t < tr.t1; ++t) {
-        const uint32_t slot = issued % p.stages;
-        const uint32_t parity = ((issued / p.stages) & 1u) ^ 1u;
-        if (lane == 0) {
-          const uint64_t deadline = globaltimer() + p.timeout_ns;
-          while (!mbar_test(&s.empty[slot], parity)) {
-            if (*s.prod_ctl == -1 || aborted(p) || globaltimer() > deadline) { stop = true; break; }
-            __nanosleep(20);
-          }
-        }
+        if (lane == 0) stop = !wait_bar(p, &s.empty[ring.slot], ring.parity ^ 1u, s.prod_ctl, 900);
         stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
         if (stop) break;
-        const int64_t rg = t / tr.KT;
-        const int64_t kk = t % tr.KT;
-        const bf16 *src = g.W + (rg * kRows) * static_cast<int64_t>(g.K) + kk * g.kc;
-        uint8_t *dst = s.ring + static_cast<size_t>(slot) * kStageBytes;
-        if (lane == 0) mbar_arrive_expect_tx(&s.full[slot], row_bytes * kRows);
+        const bf16 *src = g.W + (rg * kRows) * static_cast<int64_t>(g.K) + static_cast<int64_t>(kk) * g.kc;
+        uint8_t *dst = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
+        if (lane == 0) mbar_arrive_expect_tx(&s.full[ring.slot], row_bytes * kRows);
         __syncwarp();
         if (lane < kRows)
-          bulk_g2s(dst + lane * pitch, src + static_cast<int64_t>(lane) * g.K, row_bytes, &s.full[slot]);
+          bulk_g2s(dst + lane * pitch, src + static_cast<int64_t>(lane) * g.K, row_bytes, &s.full[ring.slot]);
+        ring.advance(p.stages);
         ++issued;
+        if (++kk == tr.KT) { kk = 0; ++rg; }
       }
     }
   }
@@ -294,9 +331,8 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
     const uint32_t first = issued > static_cast<uint32_t>(p.stages) ? issued - p.stages : 0u;
     for (uint32_t i = first; i < issued; ++i) {
       const uint64_t deadline = globaltimer() + p.timeout_ns;
-      while (!mbar_test(&s.full[i % p.stages], (i / p.stages) & 1u)) {
+      while (!mbar_try(&s.full[i % p.stages], (i / p.stages) & 1u)) {
         if (globaltimer() > deadline) break;
-        __nanosleep(64);
       }
     }
   }
@@ -319,21 +355,27 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
     named_sync(1, kConsumerThreads);
     return;
   }
+  // One pass over L2: each thread keeps its (at most 2 x 8) elements of every
+  // row in registers (K <= 4096), reduces the fp32 sums of squares, then
+  // normalises from registers.
   const bf16 *rows[kBatch];
 #pragma unroll
   for (int b = 0; b < kBatch; ++b) {
     rows[b] = g.embed_src ? p.embed + __ldcg(&p.work->token[b]) * static_cast<int64_t>(K)
                           : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
   }
+  uint4 v[2][kBatch];
   float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
-  for (int k8 = tid; k8 < K8; k8 += kConsumerThreads) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
-      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8);
-      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v);
+      v[j][b] = k8 < K8 ? __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8) : make_uint4(0, 0, 0, 0);
+      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h2[j]);
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
         ss[b] = __fadd_rn(ss[b], __fmul_rn(f.x, f.x));
         ss[b] = __fadd_rn(ss[b], __fmul_rn(f.y, f.y));
       }
@@ -358,102 +400,42 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
     s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
   }
   named_sync(1, kConsumerThreads);
-  for (int i = tid; i < kBatch * K8; i += kConsumerThreads) {
-    const int b = i / K8, k8 = i % K8;
-    const float r = s.nrm[32 + b];
-    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8);
-    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8);
-    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v);
-    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
-    uint4 o;
-    __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 hf = __bfloat1622float2(h2[j]);
-      const float2 wf = __bfloat1622float2(w2[j]);
-      const float nx = rbf(__fmul_rn(hf.x, r));   // (h * rsqrt).to(bf16)
-      const float ny = rbf(__fmul_rn(hf.y, r));
-      o2[j] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));  // * weight
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+    if (k8 >= K8) continue;
+    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8);
+    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const float r = s.nrm[32 + b];
+      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
+      uint4 o;
+      __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 hf = __bfloat1622float2(h2[q]);
+        const float2 wf = __bfloat1622float2(w2[q]);
+        const float nx = rbf(__fmul_rn(hf.x, r));   // (h * rsqrt).to(bf16)
+        const float ny = rbf(__fmul_rn(hf.y, r));
+        o2[q] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));  // * weight
+      }
+      *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = o;
     }
-    *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = o;
   }
   named_sync(1, kConsumerThreads);
 }
 
-// ---- consumer: projection epilogues ----------------------------------------------------------
-// Runs on the finished fp32 sums s.tot[row*4 + b] of row group `rg`.
-__device__ void gemv_epilogue(const EpochParams &p, const Smem &s, const Gemv &g, int64_t rg,
-                              int step) {
-  const int tid = threadIdx.x;
-  const ModelDims &m = p.m;
-  if (g.kind == kQKV) {
-    // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
-    if (tid < 64) {
-      const int row = tid >> 2, b = tid & 3;
-      const int64_t n = rg * kRows + row;
-      const float v = __fadd_rn(s.tot[tid], bf(g.bias[n]));
-      p.qkv[static_cast<size_t>(b) * m.Nqkv + n] = tobf(v);
-    }
-  } else if (g.kind == kO || g.kind == kDown) {
-    // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
-    if (tid < 64) {
-      const int row = tid >> 2, b = tid & 3;
-      const int64_t n = rg * kRows + row;
-      bf16 *hp = p.h + static_cast<size_t>(b) * m.H + n;
-      const float hv = bf(__ldcg(hp));
-      *hp = tobf(__fadd_rn(hv, rbf(s.tot[tid])));
-    }
-  } else if (g.kind == kGU) {
-    // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398)
-    if (tid < 32) {
-      const int pair = tid >> 2, b = tid & 3;
-      const float gate = rbf(s.tot[pair * 4 + b]);
-      const float up = rbf(s.tot[(pair + 8) * 4 + b]);
-      const float silu = rbf(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
-      p.act[static_cast<size_t>(b) * m.I_pad + rg * 8 + pair] = tobf(__fmul_rn(silu, up));
-    }
-  } else {  // kLM: logits = f32(bf16(x W^T)) (:405-408), then first-max argmax partials
-    if (tid < 64) {
-      const int row = tid >> 2, b = tid & 3;
-      const int64_t n = rg * kRows + row;
-      const float v = rbf(s.tot[tid]);
-      s.tot[tid] = v;
-      if (p.logits != nullptr && n < m.V)
-        p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n] = v;
-    }
-    named_sync(1, kConsumerThreads);
-    if (tid < kBatch) {
-      const int b = tid;
-      float best = s.best_val[b];
-      int32_t idx = s.best_idx[b];
-      int32_t bad = s.best_bad[b];
-      for (int row = 0; row < kRows; ++row) {
-        const int64_t n = rg * kRows + row;
-        if (n >= m.V) break;
-        const float v = s.tot[row * 4 + b];
-        if (!isfinite(v)) bad = 1;
-        if (v > best) { best = v; idx = static_cast<int32_t>(n); }
-      }
-      s.best_val[b] = best;
-      s.best_idx[b] = idx;
-      s.best_bad[b] = bad;
-    }
-  }
-}
-
-// ---- consumer: one projection phase -------------------------------------------------------------
-// Returns false when the launch is aborting.
-__device__ bool gemv_phase(const EpochParams &p, const Smem &s, const Gemv &g, uint32_t &stage_ctr,
-                           uint32_t seq, int step) {
+// ---- consumer warps: one projection phase ---------------------------------------------------
+// Streams this CTA's tiles through the MMA and hands every finished row-group
+// segment (fp32 partials of 16 rows x 4 batch rows per warp) to the epilogue
+// warp through the reduction ring; no CTA-wide synchronisation in the stream.
+__device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &ring,
+                             RingCursor &red) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int gi = lane >> 2, ci = lane & 3;
   const TileRange tr = tile_range(g, blockIdx.x, p.grid);
-  if (g.kind == kLM && tid < kBatch) {
-    s.best_val[tid] = -INFINITY;
-    s.best_idx[tid] = INT_MAX;
-    s.best_bad[tid] = 0;
-  }
   if (g.embed_src) {
     // layer 0: every CTA materialises its slice of the residual stream h = E[token]
     const int K8 = g.K / 8;
@@ -466,41 +448,48 @@ __device__ bool gemv_phase(const EpochParams &p, const Smem &s, const Gemv &g, u
       *reinterpret_cast<uint4 *>(p.h + static_cast<size_t>(b) * p.m.H + k8 * 8) = v;
     }
   }
-  if (tr.t0 < tr.t1) load_x(p, s, g);
+  if (tr.t0 >= tr.t1) return;
+  const bool xg = g.xmode == kXGlobal;
+  if (!xg) load_x(p, s, g);
   const int kc = g.kc;
   const int ksteps = kc / 64;
   const uint32_t pitch = static_cast<uint32_t>(kc) * 2u + 16u;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int64_t seg_start = tr.t0;
-  for (int64_t t = tr.t0; t < tr.t1; ++t) {
-    const int64_t rg = t / tr.KT;
-    const int kk = static_cast<int>(t % tr.KT);
-    const uint32_t slot = stage_ctr % p.stages;
-    const uint32_t parity = (stage_ctr / p.stages) & 1u;
-    ++stage_ctr;
-    // Bounded wait.  On abort or timeout the phase still runs to its end (on
-    // garbage) so that every named barrier below is matched; the grid barrier
-    // that ends the phase then stops the launch uniformly.
-    bool landed = true;
-    {
-      const uint64_t deadline = globaltimer() + p.timeout_ns;
-      uint32_t polls = 0;
-      while (!mbar_test(&s.full[slot], parity)) {
-        if ((++polls & 63) == 0) {
-          if (aborted(p)) { landed = false; break; }
-          if (globaltimer() > deadline) { raise_error(p, 1000); landed = false; break; }
-        }
-      }
+  // kXGlobal (one 64-wide k-step per warp and tile): each thread with gi < 4
+  // keeps the activation fragments of the next two tiles in flight from L2.
+  const bf16 *xg_base = g.xsrc + static_cast<size_t>(gi) * g.xsrc_stride + warp * 64 + 16 * ci;
+  const bool xg_lane = xg && gi < kBatch;
+  auto xg_load = [&](int64_t tt, int tkk, uint4 &lo, uint4 &hi) {
+    if (xg_lane && tt < tr.t1) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(xg_base + static_cast<int64_t>(tkk) * kc);
+      lo = __ldcg(src);
+      hi = __ldcg(src + 1);
+    } else {
+      lo = make_uint4(0, 0, 0, 0);
+      hi = make_uint4(0, 0, 0, 0);
     }
-    const uint8_t *st = s.ring + static_cast<size_t>(slot) * kStageBytes;
+  };
+  int kk = static_cast<int>(tr.t0 % tr.KT);
+  int kk1 = kk + 1 == tr.KT ? 0 : kk + 1;
+  int kk2 = kk1 + 1 == tr.KT ? 0 : kk1 + 1;
+  uint4 xa0, xa1, xb0, xb1, xc0, xc1;
+  xg_load(tr.t0, kk, xa0, xa1);
+  xg_load(tr.t0 + 1, kk1, xb0, xb1);
+  for (int64_t t = tr.t0; t < tr.t1; ++t) {
+    xg_load(t + 2, kk2, xc0, xc1);
+    // Bounded wait.  On abort or timeout the phase still runs to its end (on
+    // garbage) so that every barrier below is matched; the grid barrier that
+    // ends the phase then stops the launch uniformly.
+    const bool landed = wait_bar(p, &s.full[ring.slot], ring.parity, nullptr, 1000);
+    const uint8_t *st = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
     for (int ks = warp; ks < ksteps; ks += kConsumerWarps) {
       const uint8_t *arow = st + gi * pitch + (ks * 64 + 16 * ci) * 2;
       const uint4 a_lo0 = lds128(arow);
       const uint4 a_lo1 = lds128(arow + 16);
       const uint4 a_hi0 = lds128(arow + 8 * pitch);
       const uint4 a_hi1 = lds128(arow + 8 * pitch + 16);
-      uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
-      if (gi < kBatch) {
+      uint4 x0 = xa0, x1 = xa1;
+      if (!xg && gi < kBatch) {
         const bf16 *xrow = s.xs + static_cast<size_t>(gi) * p.xs_stride + kk * kc + ks * 64 + 16 * ci;
         x0 = lds128(xrow);
         x1 = lds128(xrow + 8);
@@ -513,62 +502,173 @@ __device__ bool gemv_phase(const EpochParams &p, const Smem &s, const Gemv &g, u
       mma_bf16_16816(acc, a_lo1.z, a_hi1.z, a_lo1.w, a_hi1.w, x1.z, x1.w);
     }
     __syncwarp();
-    if (lane == 0 && landed) mbar_arrive(&s.empty[slot]);
+    if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
+    ring.advance(p.stages);
+    xa0 = xb0; xa1 = xb1; xb0 = xc0; xb1 = xc1;
+    if (kk == tr.KT - 1 || t == tr.t1 - 1) {
+      // segment end: this warp's 16 x 4 partial sums go to the epilogue warp
+      wait_bar(p, &s.red_empty[red.slot], red.parity ^ 1u, nullptr, 1002);
+      if (ci < 2) {
+        float *r = s.red + (static_cast<size_t>(red.slot) * kConsumerWarps + warp) * 64;
+        r[gi * 4 + 2 * ci] = acc[0];
+        r[gi * 4 + 2 * ci + 1] = acc[1];
+        r[(gi + 8) * 4 + 2 * ci] = acc[2];
+        r[(gi + 8) * 4 + 2 * ci + 1] = acc[3];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.red_full[red.slot]);
+      red.advance(kRedSlots);
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+    kk = kk1;
+    kk1 = kk2;
+    kk2 = kk2 + 1 == tr.KT ? 0 : kk2 + 1;
+  }
+}
 
+// ---- epilogue warp: one projection phase --------------------------------------------------------
+// Lane l owns rows (l/4, l/4 + 8) of the row group and batch row l%4.  For each
+// segment it sums the 8 warps' partials in fixed order, then either publishes
+// them (the segment's row group started on the previous CTA), or adds the next
+// CTA's published part (the row group continues there) and runs the epilogue.
+__device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &red,
+                            uint32_t seq, int step) {
+  const int lane = threadIdx.x & 31;
+  const ModelDims &m = p.m;
+  const TileRange tr = tile_range(g, blockIdx.x, p.grid);
+  float best = -INFINITY;
+  int32_t best_i = INT_MAX, bad = 0;
+  int64_t seg_start = tr.t0;
+  int64_t rg = tr.t0 / tr.KT;
+  int kk = static_cast<int>(tr.t0 % tr.KT);
+  for (int64_t t = tr.t0; t < tr.t1; ++t) {
     const bool group_end = kk == tr.KT - 1;
-    if (!(group_end || t == tr.t1 - 1)) continue;
-    // ---- finish a row-group segment -------------------------------------------------
-    const bool head = (seg_start % tr.KT) == 0;   // this CTA holds the group's first tile
-    seg_start = t + 1;
-    if (ci < 2) {
-      float *r = s.red + warp * 64;
-      r[gi * 4 + 2 * ci] = acc[0];
-      r[gi * 4 + 2 * ci + 1] = acc[1];
-      r[(gi + 8) * 4 + 2 * ci] = acc[2];
-      r[(gi + 8) * 4 + 2 * ci + 1] = acc[3];
-    }
-    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-    const bool finisher = head && !group_end;   // the rest of the group is on CTA + 1
-    if (finisher && tid == 0) {
-      const uint64_t deadline = globaltimer() + p.timeout_ns;
-      uint32_t polls = 0;
-      while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
-        if (aborted(p)) break;
-        if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
-        __nanosleep(32);
-      }
-    }
-    named_sync(1, kConsumerThreads);
-    if (tid < 64) {
-      float total = 0.f;
+    if (group_end || t == tr.t1 - 1) {
+      wait_bar(p, &s.red_full[red.slot], red.parity, s.prod_ctl, 1003);
+      const float *r = s.red + static_cast<size_t>(red.slot) * kConsumerWarps * 64;
+      float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) total += s.red[w * 64 + tid];
-      if (finisher) total += __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + tid);
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        v0 += r[w * 64 + lane];
+        v1 += r[w * 64 + lane + 32];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.red_empty[red.slot]);
+      red.advance(kRedSlots);
+      const bool head = (seg_start % tr.KT) == 0;   // this CTA holds the group's first tile
+      seg_start = t + 1;
       if (!head) {
-        p.partials[static_cast<size_t>(blockIdx.x) * 64 + tid] = total;  // publish
+        p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane] = v0;
+        p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane + 32] = v1;
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          st_release_u32(&p.sync->flags[blockIdx.x], seq);
+        }
       } else {
-        s.tot[tid] = total;
+        if (!group_end) {   // the rest of the row group is on CTA + 1
+          if (lane == 0) {
+            const uint64_t deadline = globaltimer() + p.timeout_ns;
+            uint32_t polls = 0;
+            while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
+              if (aborted(p)) break;
+              if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
+              __nanosleep(32);
+            }
+          }
+          __syncwarp();
+          v0 += __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane);
+          v1 += __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane + 32);
+        }
+        const int b = lane & 3;
+        const int64_t n0 = rg * kRows + (lane >> 2), n1 = n0 + 8;
+        if (g.kind == kQKV) {
+          // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
+          p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, bf(g.bias[n0])));
+          p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, bf(g.bias[n1])));
+        } else if (g.kind == kO || g.kind == kDown) {
+          // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
+          bf16 *h0 = p.h + static_cast<size_t>(b) * m.H + n0;
+          bf16 *h1 = p.h + static_cast<size_t>(b) * m.H + n1;
+          const float r0 = bf(__ldcg(h0)), r1 = bf(__ldcg(h1));
+          *h0 = tobf(__fadd_rn(r0, rbf(v0)));
+          *h1 = tobf(__fadd_rn(r1, rbf(v1)));
+        } else if (g.kind == kGU) {
+          // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398);
+          // rows 0-7 of the group are gate rows, 8-15 the matching up rows
+          const float gate = rbf(v0);
+          const float up = rbf(v1);
+          const float silu = rbf(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
+          p.act[static_cast<size_t>(b) * m.I_pad + rg * 8 + (lane >> 2)] = tobf(__fmul_rn(silu, up));
+        } else {
+          // logits = f32(bf16(x W^T)) (:405-408); first-max argmax partials
+          const float l0 = rbf(v0), l1 = rbf(v1);
+          float cb = -INFINITY;
+          int32_t ci = INT_MAX, cbad = 0;
+          if (n0 < m.V) {
+            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n0] = l0;
+            cbad |= !isfinite(l0);
+            if (l0 > cb) { cb = l0; ci = static_cast<int32_t>(n0); }
+          }
+          if (n1 < m.V) {
+            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n1] = l1;
+            cbad |= !isfinite(l1);
+            if (l1 > cb) { cb = l1; ci = static_cast<int32_t>(n1); }
+          }
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) {   // lanes sharing b: l ^ 4, 8, 16
+            const float ob = __shfl_xor_sync(0xffffffffu, cb, off);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, ci, off);
+            cbad |= __shfl_xor_sync(0xffffffffu, cbad, off);
+            if (ob > cb || (ob == cb && oi < ci)) { cb = ob; ci = oi; }
+          }
+          if (cb > best || (cb == best && ci < best_i)) { best = cb; best_i = ci; }
+          bad |= cbad;
+        }
       }
     }
-    named_sync(1, kConsumerThreads);
-    if (!head) {
-      if (tid == 0) {
-        __threadfence();
-        st_release_u32(&p.sync->flags[blockIdx.x], seq);
+    if (++kk == tr.KT) { kk = 0; ++rg; }
+  }
+  if (g.kind == kLM && lane < kBatch) {
+    p.arg_val[blockIdx.x * kBatch + lane] = best;
+    p.arg_idx[blockIdx.x * kBatch + lane] = best_i;
+    p.arg_bad[blockIdx.x * kBatch + lane] = bad;
+  }
+  __syncwarp();
+  __threadfence();   // the phase's outputs are visible GPU-wide before the grid barrier
+  if (lane == 0) mbar_arrive(s.phase_done);
+}
+
+// Epilogue warp main loop: follows the projection phases of every step.
+__device__ void epilogue_main(const EpochParams &p, const Smem &s) {
+  const int lane = threadIdx.x & 31;
+  const int L = p.m.L;
+  const int phases = 5 * L + 2;
+  RingCursor red;
+  for (int step = 0; step < kMaxSteps; ++step) {
+    bool go = true;
+    if (lane == 0) go = wait_step(p, s, step);
+    go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
+    if (!go) return;
+    for (int ph = 0; ph < phases; ++ph) {
+      const int kind = gemv_kind_of_phase(ph, L);
+      if (kind < 0) continue;
+      const int seq = step * phases + ph + 1;
+      // never finish a phase before the consumers started it
+      bool started = true;
+      if (lane == 0) {
+        const uint64_t deadline = globaltimer() + p.timeout_ns;
+        while (*s.phase_started < seq) {
+          if (*s.prod_ctl == -1 || aborted(p) || globaltimer() > deadline) { started = false; break; }
+          __nanosleep(32);
+        }
       }
-    } else {
-      gemv_epilogue(p, s, g, rg, step);
+      started = __shfl_sync(0xffffffffu, started ? 1 : 0, 0) != 0;
+      if (!started) return;
+      const Gemv g = make_gemv(p, ph / 5, kind);
+      gemv_finish(p, s, g, red, static_cast<uint32_t>(seq), step);
     }
   }
-  if (g.kind == kLM) {
-    named_sync(1, kConsumerThreads);
-    if (tid < kBatch) {
-      p.arg_val[blockIdx.x * kBatch + tid] = s.best_val[tid];
-      p.arg_idx[blockIdx.x * kBatch + tid] = s.best_idx[tid];
-      p.arg_bad[blockIdx.x * kBatch + tid] = s.best_bad[tid];
-    }
-  }
-  return true;
 }
 
 // ---- consumer: paged GQA decode attention ---------------------------------------------------------
@@ -844,17 +944,29 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], kConsumerWarps);
     }
-    *s.prod_ctl = -2;   // producer waits for "step 0 go"
+    for (int i = 0; i < kRedSlots; ++i) {
+      mbar_init(&s.red_full[i], kConsumerWarps);
+      mbar_init(&s.red_empty[i], 1);
+    }
+    mbar_init(s.phase_done, 1);
+    *s.prod_ctl = -2;        // producer and epilogue warps wait for "step 0 go"
+    *s.phase_started = 0;
     mbar_fence_init();
   }
   __syncthreads();
-  if (tid >= kConsumerThreads) {
+  const int warp_id = tid >> 5;
+  if (warp_id == kProducerWarp) {
     producer_main(p, s);
+    return;
+  }
+  if (warp_id == kEpilogueWarp) {
+    epilogue_main(p, s);
     return;
   }
 
   uint32_t barrier_index = 0;
-  uint32_t stage_ctr = 0;
+  RingCursor ring, red;
+  uint32_t done_parity = 0;
   bool ok = true;
   const size_t block_elems = static_cast<size_t>(m.bs) * m.nkv * m.d;
   const size_t layer_elems = static_cast<size_t>(m.NB) * block_elems;
@@ -994,34 +1106,59 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       const int kind = gemv_kind_of_phase(ph, L);
       if (kind >= 0) {
         const Gemv g = make_gemv(p, ph / 5, kind);
-        ok = gemv_phase(p, s, g, stage_ctr, seq, step);
+        if (tid == 0) *s.phase_started = static_cast<int>(seq);
+        gemv_consume(p, s, g, ring, red);
+        // the epilogue warp has written every output of the phase
+        if (tid == 0) wait_bar(p, s.phase_done, done_parity, nullptr, 1004);
+        done_parity ^= 1u;
       } else if (ph < 5 * L) {
         attention_phase(p, s, ph / 5);
       } else if (blockIdx.x == 0) {
         // control: two-pass argmax (pass 2 over the per-CTA partials), then the
         // per-row bookkeeping of the reference K-loop body (:537-591)
-        if (tid < kBatch) {
+        {
+          // two warps per row: lane-strided over the CTA partials, then shuffles
           const int lm_ctas = static_cast<int>(m.V_pad / kRows < p.grid ? m.V_pad / kRows : p.grid);
+          const int b = tid >> 6, sub = tid & 63;
           float best = -INFINITY;
           int32_t idx = INT_MAX, bad = 0;
-          for (int c = 0; c < lm_ctas; ++c) {
-            const float v = __ldcg(&p.arg_val[c * kBatch + tid]);
-            const int32_t i = __ldcg(&p.arg_idx[c * kBatch + tid]);
-            bad |= __ldcg(&p.arg_bad[c * kBatch + tid]);
+          for (int c = sub; c < lm_ctas; c += 64) {
+            const float v = __ldcg(&p.arg_val[c * kBatch + b]);
+            const int32_t i = __ldcg(&p.arg_idx[c * kBatch + b]);
+            bad |= __ldcg(&p.arg_bad[c * kBatch + b]);
             if (v > best || (v == best && i < idx)) { best = v; idx = i; }
           }
-          s.best_idx[tid] = idx;
-          s.best_bad[tid] = bad;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, idx, off);
+            bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+            if (ob > best || (ob == best && oi < idx)) { best = ob; idx = oi; }
+          }
+          if ((tid & 31) == 0) {
+            s.best_val[tid >> 5] = best;
+            s.best_idx[tid >> 5] = idx;
+            s.best_bad[tid >> 5] = bad;
+          }
+          named_sync(1, kConsumerThreads);
+          if (tid < kBatch) {
+            const int w0 = 2 * tid, w1 = 2 * tid + 1;
+            const bool second = s.best_val[w1] > s.best_val[w0] ||
+                                (s.best_val[w1] == s.best_val[w0] && s.best_idx[w1] < s.best_idx[w0]);
+            s.misc[4 + tid] = second ? s.best_idx[w1] : s.best_idx[w0];
+            s.misc[8 + tid] = s.best_bad[w0] | s.best_bad[w1];
+          }
+          named_sync(1, kConsumerThreads);
         }
-        named_sync(1, kConsumerThreads);
         if (tid == 0) {
           const int calls = ++w->model_calls;
           const int st = calls - 1;
           for (int b = 0; b < kBatch; ++b) {
             if (w->active[b] == 0) continue;   // position stays (:547-552)
             const int64_t forced = io->use_forced ? io->forced[st * kBatch + b] : -1;
-            if (forced < 0 && s.best_bad[b]) { w->status = kNonFiniteLogits; break; }
-            const int64_t tok = forced >= 0 ? forced : s.best_idx[b];
+            if (forced >= m.V) { w->status = kInvalidMetadata; break; }   // next embedding row must exist
+            if (forced < 0 && s.misc[8 + b]) { w->status = kNonFiniteLogits; break; }
+            const int64_t tok = forced >= 0 ? forced : s.misc[4 + b];
             io->history[st * kBatch + b] = tok;
             ++w->executed[b];
             w->position[b] += 1;

@@ -22,9 +22,13 @@ constexpr int kMaxKc = 512;           // k elements per tile
 constexpr int kStageBytes = kRows * (kMaxKc * 2 + 16);  // padded rows: 16 x 1040 B
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;         // + one producer warp
+constexpr int kProducerWarp = kConsumerWarps;          // warp 8: weight producer (TMA)
+constexpr int kEpilogueWarp = kConsumerWarps + 1;      // warp 9: reductions and epilogues
+constexpr int kThreads = kConsumerThreads + 64;
+constexpr int kRedSlots = 4;                           // row-group partial-sum ring
 constexpr int kMaxCtas = 1024;
 constexpr int kMaxStages = 12;
+constexpr int kTraceMax = 2048;       // grid barriers recorded per launch
 
 // statuses and finish reasons of the reference controller (:51-74)
 enum Status : int32_t {
@@ -150,7 +154,8 @@ struct EpochParams {
   int32_t grid;                // CTAs (one per SM)
   int32_t stages;              // weight ring depth
   int32_t xs_stride;           // activation row stride in smem (elements)
-  int32_t pad0;
+  int32_t down_xglobal;        // 1: the down projection reads its input from L2, not smem
+  uint64_t *trace;             // optional: CTA 0 globaltimer at each grid barrier (exit, entry)
   uint64_t timeout_ns;         // bound of every spin wait
 };
 

@@ -50,6 +50,20 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
+// One potentially blocking probe (the hardware may suspend the thread for a
+// short, system-defined time); true once phase `parity` completed.
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait: spins until the phase completes, `*abort` becomes non-zero,
 // or `limit` polls elapse.  Returns true only when the phase completed.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,

@@ -194,6 +194,21 @@ class EpochEngine:
         self.lib.cruise_epoch_last_timing(self.handle, ctypes.byref(device_us), ctypes.byref(launches))
         return EpochOutput(history, control_out, logits, float(device_us.value))
 
+    def set_trace(self, enable: bool) -> None:
+        self.lib.cruise_epoch_set_trace(self.handle, 1 if enable else 0)
+
+    def read_trace(self, count: int) -> tuple[np.ndarray, np.ndarray]:
+        """(exit_ns, entry_ns) of grid barriers 0..count-1 of the last epoch."""
+        exit_ns = np.zeros(count, dtype=np.uint64)
+        entry_ns = np.zeros(count, dtype=np.uint64)
+        self._check(
+            self.lib.cruise_epoch_read_trace(
+                self.handle, _ptr(exit_ns, ctypes.c_uint64), _ptr(entry_ns, ctypes.c_uint64), count
+            ),
+            "read_trace",
+        )
+        return exit_ns, entry_ns
+
     def last_timing(self) -> tuple[float, int]:
         device_us = ctypes.c_double(0.0)
         launches = ctypes.c_int32(0)

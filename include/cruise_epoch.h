@@ -167,6 +167,14 @@ int32_t cruise_epoch_run(void *engine, const int64_t *token,
 int32_t cruise_epoch_last_timing(void *engine, double *device_us,
                                  int32_t *kernel_launches);
 
+/* Phase trace (tracing / profiling aid): when enabled, each epoch records, per
+ * grid barrier j (1-based, in launch order), the globaltimer ns at which CTA 0
+ * finished its share of the preceding phase (entry_ns[j]) and at which every
+ * CTA had arrived (exit_ns[j]).  At most 2048 barriers per epoch. */
+int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
+int32_t cruise_epoch_read_trace(void *engine, uint64_t *exit_ns,
+                                uint64_t *entry_ns, int32_t count);
+
 /* Last CUDA error string of this engine (static storage). */
 const char *cruise_epoch_last_error(void *engine);
 
