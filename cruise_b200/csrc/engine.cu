@@ -53,6 +53,8 @@ struct SynthMap {
   int64_t cols;         // row length of the canonical tensor(s)
   int64_t rows0, rows1; // q rows / k rows (kQkvRows); valid rows (kRowsPad)
   int64_t dst_cols;     // packed row length (kDownPad)
+  int32_t tiled;        // destination is a tiled matrix with dst_cols columns
+  int32_t kc;           // its tile width
 };
 
 __device__ __forceinline__ uint16_t synth_value(uint64_t key, int64_t index, float scale) {
@@ -65,8 +67,18 @@ __device__ __forceinline__ uint16_t synth_value(uint64_t key, int64_t index, flo
 }
 
 __global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_t seed, float scale) {
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < count;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  for (int64_t d = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; d < count;
+       d += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t e = d;   // logical row-major index of the packed matrix
+    if (map.tiled) {
+      const int64_t kc = map.kc;
+      const int64_t tile = d / (kRows * kc), rem = d % (kRows * kc);
+      const int64_t r = rem / kc, pu = (rem % kc) >> 3, el = rem & 7;
+      const int64_t KT = map.dst_cols / kc;
+      const int64_t n = (tile / KT) * kRows + r;
+      const int64_t k = (tile % KT) * kc + ((pu ^ (r & 7)) << 3) + el;
+      e = n * map.dst_cols + k;
+    }
     int32_t id = map.ids[0];
     int64_t idx = e;
     bool zero = false;
@@ -99,7 +111,33 @@ __global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_
         break;
     }
     const uint64_t key = mix64(seed * kGamma + static_cast<uint64_t>(id + 1) * kKeyMul);
-    dst[e] = zero ? 0 : synth_value(key, idx, scale);
+    dst[d] = zero ? 0 : synth_value(key, idx, scale);
+  }
+}
+
+// Canonical row i of a checkpoint tensor -> logical row of the packed matrix.
+enum RowMap : int32_t { kRowOffset = 0, kRowGate = 1, kRowUp = 2 };
+
+__device__ __forceinline__ int64_t packed_row(int32_t map, int64_t i, int64_t offset) {
+  if (map == kRowGate) return (i / 8) * 16 + (i % 8);
+  if (map == kRowUp) return (i / 8) * 16 + 8 + (i % 8);
+  return offset + i;
+}
+
+// Moves one canonical [rows][cols] tensor into (to_tiled) or out of a tiled
+// matrix with K columns and tile width kc.
+__global__ void tile_copy_kernel(uint16_t *tiled, uint16_t *canonical, int64_t rows, int64_t cols, int32_t map,
+                                 int64_t offset, int64_t K, int32_t kc, int32_t to_tiled) {
+  const int64_t count = rows * cols;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < count;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = e / cols, c = e % cols;
+    const int64_t dst = tiled_offset(packed_row(map, i, offset), c, K, kc);
+    if (to_tiled) {
+      tiled[dst] = canonical[e];
+    } else {
+      canonical[e] = tiled[dst];
+    }
   }
 }
 
@@ -373,19 +411,28 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
 
 // ---- weight tensors by checkpoint name ---------------------------------------------------
 struct TensorPlace {
-  enum Kind { kFlat, kRowsAt, kGate, kUp, kDownCols } kind = kFlat;
   bf16 *base = nullptr;
   int64_t rows = 0, cols = 0;  // canonical shape
-  int64_t row_offset = 0;      // kRowsAt: destination row offset
-  int64_t dst_cols = 0;        // packed row pitch (elements)
+  bool tiled = false;          // false: a plain vector / row-major table at base + offset
+  int32_t row_map = kRowOffset;
+  int64_t offset = 0;          // destination row offset (plain: element offset)
+  int64_t K = 0;               // packed columns of the tiled matrix
 };
 
 bool locate(Engine *e, const std::string &name, TensorPlace &tp) {
   const ModelDims &m = e->m;
   const int64_t H = m.H, kv = static_cast<int64_t>(m.nkv) * m.d;
-  if (name == "model.embed_tokens.weight") { tp = {TensorPlace::kFlat, e->embed, m.V, H, 0, H}; return true; }
-  if (name == "model.norm.weight") { tp = {TensorPlace::kFlat, e->final_norm, 1, H, 0, H}; return true; }
-  if (name == "lm_head.weight") { tp = {TensorPlace::kFlat, e->lm_head, m.V, H, 0, H}; return true; }
+  auto plain = [&](const bf16 *base, int64_t rows, int64_t cols, int64_t offset) {
+    tp = TensorPlace{const_cast<bf16 *>(base), rows, cols, false, kRowOffset, offset, cols};
+    return true;
+  };
+  auto tiled = [&](const bf16 *base, int64_t rows, int64_t cols, int32_t map, int64_t offset, int64_t K) {
+    tp = TensorPlace{const_cast<bf16 *>(base), rows, cols, true, map, offset, K};
+    return true;
+  };
+  if (name == "model.embed_tokens.weight") return plain(e->embed, m.V, H, 0);
+  if (name == "model.norm.weight") return plain(e->final_norm, 1, H, 0);
+  if (name == "lm_head.weight") return tiled(e->lm_head, m.V, H, kRowOffset, 0, H);
   const std::string prefix = "model.layers.";
   if (name.compare(0, prefix.size(), prefix) != 0) return false;
   const size_t dot = name.find('.', prefix.size());
@@ -394,19 +441,18 @@ bool locate(Engine *e, const std::string &name, TensorPlace &tp) {
   if (layer < 0 || layer >= m.L) return false;
   const std::string key = name.substr(dot + 1);
   const LayerWeights &lw = e->layers[layer];
-  auto mut = [](const bf16 *p) { return const_cast<bf16 *>(p); };
-  if (key == "input_layernorm.weight") { tp = {TensorPlace::kFlat, mut(lw.w_in), 1, H, 0, H}; return true; }
-  if (key == "post_attention_layernorm.weight") { tp = {TensorPlace::kFlat, mut(lw.w_post), 1, H, 0, H}; return true; }
-  if (key == "self_attn.q_proj.weight") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_w), H, H, 0, H}; return true; }
-  if (key == "self_attn.k_proj.weight") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_w), kv, H, H, H}; return true; }
-  if (key == "self_attn.v_proj.weight") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_w), kv, H, H + kv, H}; return true; }
-  if (key == "self_attn.q_proj.bias") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_b), H, 1, 0, 1}; return true; }
-  if (key == "self_attn.k_proj.bias") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_b), kv, 1, H, 1}; return true; }
-  if (key == "self_attn.v_proj.bias") { tp = {TensorPlace::kRowsAt, mut(lw.qkv_b), kv, 1, H + kv, 1}; return true; }
-  if (key == "self_attn.o_proj.weight") { tp = {TensorPlace::kFlat, mut(lw.o_w), H, H, 0, H}; return true; }
-  if (key == "mlp.gate_proj.weight") { tp = {TensorPlace::kGate, mut(lw.gu_w), m.I, H, 0, H}; return true; }
-  if (key == "mlp.up_proj.weight") { tp = {TensorPlace::kUp, mut(lw.gu_w), m.I, H, 0, H}; return true; }
-  if (key == "mlp.down_proj.weight") { tp = {TensorPlace::kDownCols, mut(lw.down_w), H, m.I, 0, m.I_pad}; return true; }
+  if (key == "input_layernorm.weight") return plain(lw.w_in, 1, H, 0);
+  if (key == "post_attention_layernorm.weight") return plain(lw.w_post, 1, H, 0);
+  if (key == "self_attn.q_proj.weight") return tiled(lw.qkv_w, H, H, kRowOffset, 0, H);
+  if (key == "self_attn.k_proj.weight") return tiled(lw.qkv_w, kv, H, kRowOffset, H, H);
+  if (key == "self_attn.v_proj.weight") return tiled(lw.qkv_w, kv, H, kRowOffset, H + kv, H);
+  if (key == "self_attn.q_proj.bias") return plain(lw.qkv_b, 1, H, 0);
+  if (key == "self_attn.k_proj.bias") return plain(lw.qkv_b, 1, kv, H);
+  if (key == "self_attn.v_proj.bias") return plain(lw.qkv_b, 1, kv, H + kv);
+  if (key == "self_attn.o_proj.weight") return tiled(lw.o_w, H, H, kRowOffset, 0, H);
+  if (key == "mlp.gate_proj.weight") return tiled(lw.gu_w, m.I, H, kRowGate, 0, H);
+  if (key == "mlp.up_proj.weight") return tiled(lw.gu_w, m.I, H, kRowUp, 0, H);
+  if (key == "mlp.down_proj.weight") return tiled(lw.down_w, H, m.I, kRowOffset, 0, m.I_pad);
   return false;
 }
 
@@ -414,33 +460,37 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
   TensorPlace tp;
   if (!locate(e, name, tp)) return -1;
   if (bytes != static_cast<uint64_t>(tp.rows * tp.cols * 2)) return -1;
-  const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
   cudaError_t err = cudaSuccess;
-  const size_t row_bytes = static_cast<size_t>(tp.cols) * 2;
-  switch (tp.kind) {
-    case TensorPlace::kFlat:
-    case TensorPlace::kRowsAt: {
-      bf16 *dev = tp.base + tp.row_offset * tp.cols;
-      err = to_device ? cudaMemcpy(dev, host, bytes, kind) : cudaMemcpy(host, dev, bytes, kind);
-      break;
-    }
-    case TensorPlace::kGate:
-    case TensorPlace::kUp: {
-      // packed [I/8][16][H]: gate rows at 0..7, up rows at 8..15 of each group
-      bf16 *dev = tp.base + (tp.kind == TensorPlace::kUp ? 8 : 0) * tp.cols;
-      const size_t dpitch = 16 * row_bytes, spitch = 8 * row_bytes;
-      const size_t height = static_cast<size_t>(tp.rows / 8);
-      err = to_device ? cudaMemcpy2D(dev, dpitch, host, spitch, spitch, height, kind)
-                      : cudaMemcpy2D(host, spitch, dev, dpitch, spitch, height, kind);
-      break;
-    }
-    case TensorPlace::kDownCols: {
-      const size_t dpitch = static_cast<size_t>(tp.dst_cols) * 2;
-      err = to_device ? cudaMemcpy2D(tp.base, dpitch, host, row_bytes, row_bytes, tp.rows, kind)
-                      : cudaMemcpy2D(host, row_bytes, tp.base, dpitch, row_bytes, tp.rows, kind);
-      break;
-    }
+  if (!tp.tiled) {
+    bf16 *dev = tp.base + tp.offset;
+    err = to_device ? cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice)
+                    : cudaMemcpy(host, dev, bytes, cudaMemcpyDeviceToHost);
+    return set_err(e, err, name.c_str());
   }
+  void *staging = nullptr;
+  err = cudaMalloc(&staging, bytes);
+  if (err != cudaSuccess) return set_err(e, err, "weight staging");
+  const int kc = pick_kc(static_cast<int>(tp.K));
+  const int64_t count = tp.rows * tp.cols;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148LL * 64));
+  if (to_device) {
+    err = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess) {
+      tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
+                                                      static_cast<uint16_t *>(staging), tp.rows, tp.cols,
+                                                      tp.row_map, tp.offset, tp.K, kc, 1);
+      err = cudaGetLastError();
+      if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    }
+  } else {
+    tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
+                                                    static_cast<uint16_t *>(staging), tp.rows, tp.cols,
+                                                    tp.row_map, tp.offset, tp.K, kc, 0);
+    err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    if (err == cudaSuccess) err = cudaMemcpy(host, staging, bytes, cudaMemcpyDeviceToHost);
+  }
+  cudaFree(staging);
   return set_err(e, err, name.c_str());
 }
 
@@ -456,6 +506,7 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
         reinterpret_cast<uint16_t *>(dst), count, map, seed, scale);
   };
   auto plain = [&](int id) { SynthMap s{}; s.mode = kPlain; s.ids[0] = id; return s; };
+  auto tile = [&](SynthMap s, int64_t K) { s.tiled = 1; s.dst_cols = K; s.kc = pick_kc(static_cast<int>(K)); return s; };
   const int L = m.L;
   launch(e->embed, static_cast<int64_t>(m.V) * H, plain(0));
   for (int l = 0; l < L; ++l) {
@@ -466,22 +517,24 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
     SynthMap q{};
     q.mode = kQkvRows; q.ids[0] = base + 2; q.ids[1] = base + 4; q.ids[2] = base + 6;
     q.cols = H; q.rows0 = H; q.rows1 = kv;
-    launch(const_cast<bf16 *>(lw.qkv_w), static_cast<int64_t>(m.Nqkv) * H, q);
     SynthMap qb = q;
     qb.ids[0] = base + 3; qb.ids[1] = base + 5; qb.ids[2] = base + 7; qb.cols = 1;
+    launch(const_cast<bf16 *>(lw.qkv_w), static_cast<int64_t>(m.Nqkv) * H, tile(q, H));
     launch(const_cast<bf16 *>(lw.qkv_b), m.Nqkv, qb);
-    launch(const_cast<bf16 *>(lw.o_w), H * H, plain(base + 8));
+    SynthMap o = plain(base + 8);
+    launch(const_cast<bf16 *>(lw.o_w), H * H, tile(o, H));
     SynthMap gu{};
     gu.mode = kGateUp; gu.ids[0] = base + 9; gu.ids[1] = base + 10; gu.cols = H;
-    launch(const_cast<bf16 *>(lw.gu_w), 2LL * m.I * H, gu);
+    launch(const_cast<bf16 *>(lw.gu_w), 2LL * m.I * H, tile(gu, H));
     SynthMap dn{};
-    dn.mode = kDownPad; dn.ids[0] = base + 11; dn.cols = m.I; dn.dst_cols = m.I_pad;
+    dn.mode = kDownPad; dn.ids[0] = base + 11; dn.cols = m.I;
+    dn = tile(dn, m.I_pad);
     launch(const_cast<bf16 *>(lw.down_w), H * m.I_pad, dn);
   }
   launch(e->final_norm, H, plain(1 + kLayerTensors * L));
   SynthMap lm{};
   lm.mode = kRowsPad; lm.ids[0] = 2 + kLayerTensors * L; lm.cols = H; lm.rows0 = m.V;
-  launch(e->lm_head, static_cast<int64_t>(m.V_pad) * H, lm);
+  launch(e->lm_head, static_cast<int64_t>(m.V_pad) * H, tile(lm, H));
   cudaError_t err = cudaGetLastError();
   if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
   return set_err(e, err, "synthetic weights");

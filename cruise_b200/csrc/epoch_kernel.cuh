@@ -56,10 +56,18 @@ struct Gemv {
 };
 
 __host__ __device__ inline int pick_kc(int K) {
-  // largest multiple of 64 that divides K and is <= kMaxKc
-  for (int kc = kMaxKc; kc >= 64; kc -= 64)
+  // largest power of two in 64..kMaxKc that divides K (K is a multiple of 64)
+  for (int kc = kMaxKc; kc >= 64; kc >>= 1)
     if (K % kc == 0) return kc;
   return 64;
+}
+
+// Element offset of logical (n, k) inside a tiled matrix with K columns.
+__host__ __device__ inline int64_t tiled_offset(int64_t n, int64_t k, int64_t K, int kc) {
+  const int64_t rg = n / kRows, r = n % kRows;
+  const int64_t kk = k / kc, kin = k % kc;
+  const int64_t unit = (kin >> 3) ^ (r & 7);
+  return ((rg * (K / kc) + kk) * kRows + r) * kc + unit * 8 + (kin & 7);
 }
 
 __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int kind) {
@@ -306,23 +314,23 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
       if (kind < 0) continue;
       const Gemv g = make_gemv(p, ph / 5, kind);
       const TileRange tr = tile_range(g, blockIdx.x, p.grid);
-      const uint32_t row_bytes = static_cast<uint32_t>(g.kc) * 2u;
-      const uint32_t pitch = row_bytes + 16u;
-      int64_t rg = tr.t0 / tr.KT;
-      int kk = static_cast<int>(tr.t0 % tr.KT);
-      for (int64_t t = tr.t0; t < tr.t1; ++t) {
-        if (lane == 0) stop = !wait_bar(p, &s.empty[ring.slot], ring.parity ^ 1u, s.prod_ctl, 900);
+      const int64_t tile_elems = static_cast<int64_t>(kRows) * g.kc;
+      const int per_stage = kStageBytes / (kRows * g.kc * 2);
+      for (int64_t t = tr.t0; t < tr.t1; t += per_stage) {
+        const int n = static_cast<int>(tr.t1 - t < per_stage ? tr.t1 - t : per_stage);
+        if (lane == 0) {
+          stop = !wait_bar(p, &s.empty[ring.slot], ring.parity ^ 1u, s.prod_ctl, 900);
+          if (!stop) {
+            const uint32_t bytes = static_cast<uint32_t>(n * tile_elems * 2);
+            mbar_arrive_expect_tx(&s.full[ring.slot], bytes);
+            bulk_g2s(s.ring + static_cast<size_t>(ring.slot) * kStageBytes, g.W + t * tile_elems, bytes,
+                     &s.full[ring.slot]);
+          }
+        }
         stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
         if (stop) break;
-        const bf16 *src = g.W + (rg * kRows) * static_cast<int64_t>(g.K) + static_cast<int64_t>(kk) * g.kc;
-        uint8_t *dst = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
-        if (lane == 0) mbar_arrive_expect_tx(&s.full[ring.slot], row_bytes * kRows);
-        __syncwarp();
-        if (lane < kRows)
-          bulk_g2s(dst + lane * pitch, src + static_cast<int64_t>(lane) * g.K, row_bytes, &s.full[ring.slot]);
         ring.advance(p.stages);
         ++issued;
-        if (++kk == tr.KT) { kk = 0; ++rg; }
       }
     }
   }
@@ -453,10 +461,13 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
   if (!xg) load_x(p, s, g);
   const int kc = g.kc;
   const int ksteps = kc / 64;
-  const uint32_t pitch = static_cast<uint32_t>(kc) * 2u + 16u;
+  const uint32_t row_bytes = static_cast<uint32_t>(kc) * 2u;
+  const uint32_t tile_bytes = row_bytes * kRows;
+  const int per_stage = kStageBytes / static_cast<int>(tile_bytes);
+  const uint32_t sw = static_cast<uint32_t>(gi & 7);   // row swizzle of rows gi and gi + 8
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   // kXGlobal (one 64-wide k-step per warp and tile): each thread with gi < 4
-  // keeps the activation fragments of the next two tiles in flight from L2.
+  // keeps the activation fragments of the next four tiles in flight from L2.
   const bf16 *xg_base = g.xsrc + static_cast<size_t>(gi) * g.xsrc_stride + warp * 64 + 16 * ci;
   const bool xg_lane = xg && gi < kBatch;
   auto xg_load = [&](int64_t tt, int tkk, uint4 &lo, uint4 &hi) {
@@ -469,60 +480,67 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
       hi = make_uint4(0, 0, 0, 0);
     }
   };
+  auto next_kk = [&](int v) { return v + 1 == tr.KT ? 0 : v + 1; };
   int kk = static_cast<int>(tr.t0 % tr.KT);
-  int kk1 = kk + 1 == tr.KT ? 0 : kk + 1;
-  int kk2 = kk1 + 1 == tr.KT ? 0 : kk1 + 1;
-  uint4 xa0, xa1, xb0, xb1, xc0, xc1;
-  xg_load(tr.t0, kk, xa0, xa1);
-  xg_load(tr.t0 + 1, kk1, xb0, xb1);
-  for (int64_t t = tr.t0; t < tr.t1; ++t) {
-    xg_load(t + 2, kk2, xc0, xc1);
+  int kq = kk;   // k-tile of the next prefetch
+  uint4 x00, x01, x10, x11, x20, x21, x30, x31;
+  xg_load(tr.t0, kq, x00, x01); kq = next_kk(kq);
+  xg_load(tr.t0 + 1, kq, x10, x11); kq = next_kk(kq);
+  xg_load(tr.t0 + 2, kq, x20, x21); kq = next_kk(kq);
+  for (int64_t t = tr.t0; t < tr.t1;) {
+    const int n = static_cast<int>(tr.t1 - t < per_stage ? tr.t1 - t : per_stage);
     // Bounded wait.  On abort or timeout the phase still runs to its end (on
     // garbage) so that every barrier below is matched; the grid barrier that
     // ends the phase then stops the launch uniformly.
     const bool landed = wait_bar(p, &s.full[ring.slot], ring.parity, nullptr, 1000);
-    const uint8_t *st = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
-    for (int ks = warp; ks < ksteps; ks += kConsumerWarps) {
-      const uint8_t *arow = st + gi * pitch + (ks * 64 + 16 * ci) * 2;
-      const uint4 a_lo0 = lds128(arow);
-      const uint4 a_lo1 = lds128(arow + 16);
-      const uint4 a_hi0 = lds128(arow + 8 * pitch);
-      const uint4 a_hi1 = lds128(arow + 8 * pitch + 16);
-      uint4 x0 = xa0, x1 = xa1;
-      if (!xg && gi < kBatch) {
-        const bf16 *xrow = s.xs + static_cast<size_t>(gi) * p.xs_stride + kk * kc + ks * 64 + 16 * ci;
-        x0 = lds128(xrow);
-        x1 = lds128(xrow + 8);
+    const uint8_t *stage = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
+    for (int j = 0; j < n; ++j, ++t) {
+      xg_load(t + 3, kq, x30, x31);
+      kq = next_kk(kq);
+      const uint8_t *tile = stage + j * tile_bytes;
+      for (int ks = warp; ks < ksteps; ks += kConsumerWarps) {
+        const uint32_t u0 = (static_cast<uint32_t>(ks * 8 + 2 * ci) ^ sw) * 16u;
+        const uint32_t u1 = (static_cast<uint32_t>(ks * 8 + 2 * ci + 1) ^ sw) * 16u;
+        const uint8_t *rlo = tile + gi * row_bytes;
+        const uint8_t *rhi = rlo + 8 * row_bytes;
+        const uint4 a_lo0 = lds128(rlo + u0);
+        const uint4 a_lo1 = lds128(rlo + u1);
+        const uint4 a_hi0 = lds128(rhi + u0);
+        const uint4 a_hi1 = lds128(rhi + u1);
+        uint4 x0 = x00, x1 = x01;
+        if (!xg && gi < kBatch) {
+          const bf16 *xrow = s.xs + static_cast<size_t>(gi) * p.xs_stride + kk * kc + ks * 64 + 16 * ci;
+          x0 = lds128(xrow);
+          x1 = lds128(xrow + 8);
+        }
+        // MMA j uses physical k = 16ci + 4j .. 4j+3 of this 64-wide slice, for both
+        // weight rows (gi, gi+8) and the activation column gi.
+        mma_bf16_16816(acc, a_lo0.x, a_hi0.x, a_lo0.y, a_hi0.y, x0.x, x0.y);
+        mma_bf16_16816(acc, a_lo0.z, a_hi0.z, a_lo0.w, a_hi0.w, x0.z, x0.w);
+        mma_bf16_16816(acc, a_lo1.x, a_hi1.x, a_lo1.y, a_hi1.y, x1.x, x1.y);
+        mma_bf16_16816(acc, a_lo1.z, a_hi1.z, a_lo1.w, a_hi1.w, x1.z, x1.w);
       }
-      // MMA j uses physical k = 16ci + 4j .. 4j+3 of this 64-wide slice, for both
-      // weight rows (gi, gi+8) and the activation column gi.
-      mma_bf16_16816(acc, a_lo0.x, a_hi0.x, a_lo0.y, a_hi0.y, x0.x, x0.y);
-      mma_bf16_16816(acc, a_lo0.z, a_hi0.z, a_lo0.w, a_hi0.w, x0.z, x0.w);
-      mma_bf16_16816(acc, a_lo1.x, a_hi1.x, a_lo1.y, a_hi1.y, x1.x, x1.y);
-      mma_bf16_16816(acc, a_lo1.z, a_hi1.z, a_lo1.w, a_hi1.w, x1.z, x1.w);
+      x00 = x10; x01 = x11; x10 = x20; x11 = x21; x20 = x30; x21 = x31;
+      if (kk == tr.KT - 1 || t == tr.t1 - 1) {
+        // segment end: this warp's 16 x 4 partial sums go to the epilogue warp
+        wait_bar(p, &s.red_empty[red.slot], red.parity ^ 1u, nullptr, 1002);
+        if (ci < 2) {
+          float *r = s.red + (static_cast<size_t>(red.slot) * kConsumerWarps + warp) * 64;
+          r[gi * 4 + 2 * ci] = acc[0];
+          r[gi * 4 + 2 * ci + 1] = acc[1];
+          r[(gi + 8) * 4 + 2 * ci] = acc[2];
+          r[(gi + 8) * 4 + 2 * ci + 1] = acc[3];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.red_full[red.slot]);
+        red.advance(kRedSlots);
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      }
+      kk = next_kk(kk);
     }
     __syncwarp();
     if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
     ring.advance(p.stages);
-    xa0 = xb0; xa1 = xb1; xb0 = xc0; xb1 = xc1;
-    if (kk == tr.KT - 1 || t == tr.t1 - 1) {
-      // segment end: this warp's 16 x 4 partial sums go to the epilogue warp
-      wait_bar(p, &s.red_empty[red.slot], red.parity ^ 1u, nullptr, 1002);
-      if (ci < 2) {
-        float *r = s.red + (static_cast<size_t>(red.slot) * kConsumerWarps + warp) * 64;
-        r[gi * 4 + 2 * ci] = acc[0];
-        r[gi * 4 + 2 * ci + 1] = acc[1];
-        r[(gi + 8) * 4 + 2 * ci] = acc[2];
-        r[(gi + 8) * 4 + 2 * ci + 1] = acc[3];
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.red_full[red.slot]);
-      red.advance(kRedSlots);
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-    }
-    kk = kk1;
-    kk1 = kk2;
-    kk2 = kk2 + 1 == tr.KT ? 0 : kk2 + 1;
   }
 }
 

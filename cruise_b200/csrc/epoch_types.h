@@ -18,8 +18,8 @@ constexpr int kTilingBytes = 72;
 constexpr int kImportFlag = 0x100;
 
 constexpr int kRows = 16;             // weight rows per tile (one m16 MMA slab)
-constexpr int kMaxKc = 512;           // k elements per tile
-constexpr int kStageBytes = kRows * (kMaxKc * 2 + 16);  // padded rows: 16 x 1040 B
+constexpr int kMaxKc = 512;           // k elements per tile (power of two, 64..512)
+constexpr int kStageBytes = 32768;    // one bulk copy: consecutive tiles of the stream
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;          // warp 8: weight producer (TMA)
@@ -27,7 +27,7 @@ constexpr int kEpilogueWarp = kConsumerWarps + 1;      // warp 9: reductions and
 constexpr int kThreads = kConsumerThreads + 64;
 constexpr int kRedSlots = 4;                           // row-group partial-sum ring
 constexpr int kMaxCtas = 1024;
-constexpr int kMaxStages = 12;
+constexpr int kMaxStages = 8;
 constexpr int kTraceMax = 2048;       // grid barriers recorded per launch
 
 // statuses and finish reasons of the reference controller (:51-74)
@@ -55,13 +55,18 @@ struct ModelDims {
   int32_t bs, bpr, NB, C;
 };
 
+// Projection matrices are stored TILED: tile (rg, kk) holds rows rg*16..+15,
+// columns kk*kc..+kc-1 as 16 contiguous rows of kc bf16 with the 16-byte units
+// of row r permuted by unit ^ (r & 7) (conflict-free 128-bit shared loads);
+// tiles are laid out in stream order [rg][kk], so any run of consecutive tiles
+// is one contiguous block of HBM.  Logical shapes:
 struct LayerWeights {
   const bf16 *w_in, *w_post;   // [H]
-  const bf16 *qkv_w;           // [Nqkv][H]   rows: q | k | v
+  const bf16 *qkv_w;           // tiled [Nqkv][H]   rows: q | k | v
   const bf16 *qkv_b;           // [Nqkv]
-  const bf16 *o_w;             // [H][H]
-  const bf16 *gu_w;            // [I/8][16][H]  8 gate rows then 8 up rows
-  const bf16 *down_w;          // [H][I_pad]    columns >= I are zero
+  const bf16 *o_w;             // tiled [H][H]
+  const bf16 *gu_w;            // tiled [2I][H]: per 16 rows, 8 gate rows then the 8 matching up rows
+  const bf16 *down_w;          // tiled [H][I_pad]  columns >= I are zero
 };
 
 // One host->device and one device->host copy per epoch (the 8-in / 2-out ABI).
