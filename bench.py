@@ -332,36 +332,45 @@ PHASE_NAMES = ("qkv", "attention", "o_proj", "gate_up", "down")
 
 
 def print_trace(engine, cohort, cfg, k) -> None:
-    """One traced epoch: per-phase time between grid barriers (CTA 0 clock),
-    summed over layers and steps, and the weight bytes each kind streams."""
+    """One traced epoch: per phase kind, the time between grid barriers and its
+    parts on CTA 0 (activation staging, tile stream, epilogue drain, wait for the
+    last CTA, barrier release), summed over layers and steps."""
     engine.set_trace(True)
     out, _ = cohort.step()
     engine.set_trace(False)
     L = cfg.num_layers
     phases = 5 * L + 2
     count = 2 + out.model_calls * phases + 1
-    exit_ns, entry_ns = engine.read_trace(count)
+    tr = engine.read_trace(count).astype(np.int64)
+    exit_ns, entry_ns, xready, tiles, last = tr
     first = 2   # validation and continuity barriers precede the loop
-    totals, work = {}, {}
+    acc = {}
     for step in range(out.model_calls):
         for ph in range(phases):
             j = first + step * phases + ph + 1
             name = "lm_head" if ph == 5 * L else "control" if ph > 5 * L else PHASE_NAMES[ph % 5]
-            totals[name] = totals.get(name, 0) + int(exit_ns[j]) - int(exit_ns[j - 1])
-            work[name] = work.get(name, 0) + int(entry_ns[j]) - int(exit_ns[j - 1])
+            a = acc.setdefault(name, np.zeros(6))
+            start = exit_ns[j - 1]
+            a[0] += exit_ns[j] - start
+            if xready[j]:
+                a[1] += xready[j] - start
+                a[2] += tiles[j] - xready[j]
+                a[3] += entry_ns[j] - tiles[j]
+            else:
+                a[3] += entry_ns[j] - start
+            a[4] += max(last[j] - entry_ns[j], 0)
+            a[5] += exit_ns[j] - max(last[j], entry_ns[j])
     h, kv, i = cfg.hidden, cfg.kv_width, cfg.intermediate
     wbytes = {"qkv": (h + 2 * kv) * h * 2 * L, "o_proj": h * h * 2 * L, "gate_up": 2 * i * h * 2 * L,
               "down": h * i * 2 * L, "lm_head": cfg.vocab * h * 2}
     calls = out.model_calls
-    span = int(exit_ns[count - 1]) - int(exit_ns[first])
-    print(f"trace: epoch {out.device_us:.1f} us, {calls} steps, loop span {span / 1e3:.1f} us", file=sys.stderr)
+    print(f"trace: epoch {out.device_us:.1f} us, {calls} steps; per step, us "
+          f"[total | x-staging  tiles  epilogue | wait-last-CTA  release] and weight GB/s", file=sys.stderr)
     for name in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "control"):
-        t = totals.get(name, 0) / calls
-        bw = wbytes.get(name, 0) / max(t, 1) if name in wbytes else 0.0   # bytes per ns = GB/s
-        per = t / (L if name in PHASE_NAMES else 1)
-        print(f"  {name:9s} {t / 1e3:8.1f} us/step  {per / 1e3:7.2f} us/phase  "
-              f"cta0-work {work.get(name, 0) / calls / 1e3:8.1f} us/step  {bw:6.0f} GB/s",
-              file=sys.stderr)
+        a = acc.get(name, np.zeros(6)) / calls / 1e3
+        bw = wbytes.get(name, 0) / (a[0] * 1e3) if name in wbytes and a[0] else 0.0
+        print(f"  {name:9s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} {a[5]:7.1f}   "
+              f"{bw:6.0f}", file=sys.stderr)
 
 
 def cpu_oracle_step_time(weights: dict, cfg, threads: int) -> tuple[float, str]:

@@ -70,8 +70,7 @@ SIGNATURES = {
     ),
     "cruise_epoch_set_trace": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32]),
     "cruise_epoch_read_trace": (
-        ctypes.c_int32,
-        [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32],
+        ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
     ),
     "cruise_epoch_last_error": (ctypes.c_char_p, [ctypes.c_void_p]),
 }

@@ -185,6 +185,15 @@ struct Engine {
   std::array<uint8_t, kTilingBytes> tiling{};
 };
 
+// Every host<->device copy runs on the engine's own (non-blocking) stream and is
+// waited for: a pageable-memory cudaMemcpy on the legacy stream may return before
+// its DMA lands, and the engine's stream does not order after the legacy stream.
+cudaError_t copy_sync(Engine *e, void *dst, const void *src, size_t bytes, cudaMemcpyKind kind) {
+  cudaError_t err = cudaMemcpyAsync(dst, src, bytes, kind, e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  return err;
+}
+
 int32_t set_err(Engine *e, cudaError_t err, const char *what) {
   if (err != cudaSuccess && e != nullptr) {
     e->last_error = std::string(what) + ": " + cudaGetErrorString(err);
@@ -372,7 +381,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   const size_t o_ai = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ab = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_lg = take2(static_cast<size_t>(kMaxSteps) * kBatch * m.V * 4);
-  const size_t o_trace = take2(2 * kTraceMax * sizeof(uint64_t));
+  const size_t o_trace = take2(5 * kTraceMax * sizeof(uint64_t));
   const size_t o_io = take2(sizeof(EpochIO)), o_res = take2(sizeof(ResidentState));
   const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sizeof(SyncState));
   if (cudaMalloc(&e->state, st) != cudaSuccess) { destroy_engine(e); return nullptr; }
@@ -463,8 +472,8 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
   cudaError_t err = cudaSuccess;
   if (!tp.tiled) {
     bf16 *dev = tp.base + tp.offset;
-    err = to_device ? cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice)
-                    : cudaMemcpy(host, dev, bytes, cudaMemcpyDeviceToHost);
+    err = to_device ? copy_sync(e, dev, host, bytes, cudaMemcpyHostToDevice)
+                    : copy_sync(e, host, dev, bytes, cudaMemcpyDeviceToHost);
     return set_err(e, err, name.c_str());
   }
   void *staging = nullptr;
@@ -474,7 +483,7 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
   const int64_t count = tp.rows * tp.cols;
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148LL * 64));
   if (to_device) {
-    err = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
+    err = copy_sync(e, staging, host, bytes, cudaMemcpyHostToDevice);
     if (err == cudaSuccess) {
       tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
                                                       static_cast<uint16_t *>(staging), tp.rows, tp.cols,
@@ -488,7 +497,7 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
                                                     tp.row_map, tp.offset, tp.K, kc, 0);
     err = cudaGetLastError();
     if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
-    if (err == cudaSuccess) err = cudaMemcpy(host, staging, bytes, cudaMemcpyDeviceToHost);
+    if (err == cudaSuccess) err = copy_sync(e, host, staging, bytes, cudaMemcpyDeviceToHost);
   }
   cudaFree(staging);
   return set_err(e, err, name.c_str());
@@ -614,6 +623,7 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   p.xs_stride = e->xs_stride;
   p.down_xglobal = e->down_xglobal;
   p.trace = e->trace_on ? e->trace : nullptr;
+  if (e->trace_on) cudaMemsetAsync(e->trace, 0, 5 * kTraceMax * sizeof(uint64_t), e->stream);
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
   void *args[] = {&p};
   cudaEventRecord(e->ev0, e->stream);
@@ -846,8 +856,8 @@ int32_t cruise_epoch_set_rope_table(void *engine, const uint16_t *cos_bf16, cons
   if (bytes != static_cast<uint64_t>(e->m.C) * e->m.d * 2) return -1;
   std::lock_guard<std::mutex> lock(e->execute_mutex);
   cudaSetDevice(e->device);
-  cudaError_t err = cudaMemcpy(e->rope_cos, cos_bf16, bytes, cudaMemcpyHostToDevice);
-  if (err == cudaSuccess) err = cudaMemcpy(e->rope_sin, sin_bf16, bytes, cudaMemcpyHostToDevice);
+  cudaError_t err = cruise::copy_sync(e, e->rope_cos, cos_bf16, bytes, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cruise::copy_sync(e, e->rope_sin, sin_bf16, bytes, cudaMemcpyHostToDevice);
   return cruise::set_err(e, err, "rope table");
 }
 
@@ -858,8 +868,8 @@ int32_t cruise_epoch_read_kv(void *engine, void *key_host, void *value_host, uin
   if (bytes_each != expect) return -1;
   std::lock_guard<std::mutex> lock(e->execute_mutex);
   cudaSetDevice(e->device);
-  cudaError_t err = cudaMemcpy(key_host, e->key_cache, bytes_each, cudaMemcpyDeviceToHost);
-  if (err == cudaSuccess) err = cudaMemcpy(value_host, e->value_cache, bytes_each, cudaMemcpyDeviceToHost);
+  cudaError_t err = cruise::copy_sync(e, key_host, e->key_cache, bytes_each, cudaMemcpyDeviceToHost);
+  if (err == cudaSuccess) err = cruise::copy_sync(e, value_host, e->value_cache, bytes_each, cudaMemcpyDeviceToHost);
   return cruise::set_err(e, err, "read kv");
 }
 
@@ -870,8 +880,8 @@ int32_t cruise_epoch_write_kv(void *engine, const void *key_host, const void *va
   if (bytes_each != expect) return -1;
   std::lock_guard<std::mutex> lock(e->execute_mutex);
   cudaSetDevice(e->device);
-  cudaError_t err = cudaMemcpy(e->key_cache, key_host, bytes_each, cudaMemcpyHostToDevice);
-  if (err == cudaSuccess) err = cudaMemcpy(e->value_cache, value_host, bytes_each, cudaMemcpyHostToDevice);
+  cudaError_t err = cruise::copy_sync(e, e->key_cache, key_host, bytes_each, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cruise::copy_sync(e, e->value_cache, value_host, bytes_each, cudaMemcpyHostToDevice);
   return cruise::set_err(e, err, "write kv");
 }
 
@@ -904,15 +914,14 @@ int32_t cruise_epoch_set_trace(void *engine, int32_t enable) {
   return 0;
 }
 
-int32_t cruise_epoch_read_trace(void *engine, uint64_t *exit_ns, uint64_t *entry_ns, int32_t count) {
-  if (engine == nullptr || exit_ns == nullptr || entry_ns == nullptr || count < 0 || count > cruise::kTraceMax)
+int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns, int32_t count) {
+  if (engine == nullptr || ns == nullptr || series < 0 || series > 4 || count < 0 || count > cruise::kTraceMax)
     return -1;
   Engine *e = static_cast<Engine *>(engine);
   std::lock_guard<std::mutex> lock(e->execute_mutex);
   cudaSetDevice(e->device);
-  cudaError_t err = cudaMemcpy(exit_ns, e->trace, sizeof(uint64_t) * count, cudaMemcpyDeviceToHost);
-  if (err == cudaSuccess)
-    err = cudaMemcpy(entry_ns, e->trace + cruise::kTraceMax, sizeof(uint64_t) * count, cudaMemcpyDeviceToHost);
+  cudaError_t err = cruise::copy_sync(e, ns, e->trace + static_cast<size_t>(series) * cruise::kTraceMax,
+                                      sizeof(uint64_t) * count, cudaMemcpyDeviceToHost);
   return cruise::set_err(e, err, "read trace");
 }
 

@@ -232,19 +232,25 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
     int ok = 1;
     const bool trace = p.trace != nullptr && blockIdx.x == 0 && index < kTraceMax;
     if (trace) p.trace[kTraceMax + index] = globaltimer();   // CTA 0 finished its share
+    if (p.trace != nullptr && index < kTraceMax)
+      atomicMax(reinterpret_cast<unsigned long long *>(&p.trace[4 * kTraceMax + index]),
+                static_cast<unsigned long long>(globaltimer()));   // the last CTA to arrive
+    // every thread of the CTA wrote before the bar.sync above; the fence makes
+    // those writes visible GPU-wide before the arrival is
     __threadfence();
     red_release_add_u32(&p.sync->barrier, 1u);
     const uint32_t target = index * static_cast<uint32_t>(p.grid);
     const uint64_t deadline = globaltimer() + p.timeout_ns;
     uint32_t polls = 0;
     while (static_cast<int32_t>(ld_acquire_u32(&p.sync->barrier) - target) < 0) {
-      if (aborted(p)) { ok = 0; break; }
-      if ((++polls & 15) == 0 && globaltimer() > deadline) {
-        raise_error(p, where);
-        ok = 0;
-        break;
+      if ((++polls & 15) == 0) {
+        if (aborted(p)) { ok = 0; break; }
+        if (globaltimer() > deadline) {
+          raise_error(p, where);
+          ok = 0;
+          break;
+        }
       }
-      __nanosleep(32);
     }
     if (ok && aborted(p)) ok = 0;
     if (trace) p.trace[index] = globaltimer();                // every CTA arrived
@@ -439,7 +445,7 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
 // segment (fp32 partials of 16 rows x 4 batch rows per warp) to the epilogue
 // warp through the reduction ring; no CTA-wide synchronisation in the stream.
 __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &ring,
-                             RingCursor &red) {
+                             RingCursor &red, uint32_t trace_slot) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int gi = lane >> 2, ci = lane & 3;
@@ -459,6 +465,8 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
   if (tr.t0 >= tr.t1) return;
   const bool xg = g.xmode == kXGlobal;
   if (!xg) load_x(p, s, g);
+  if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
+    p.trace[2 * kTraceMax + trace_slot] = globaltimer();   // activations staged
   const int kc = g.kc;
   const int ksteps = kc / 64;
   const uint32_t row_bytes = static_cast<uint32_t>(kc) * 2u;
@@ -542,6 +550,8 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
     if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
     ring.advance(p.stages);
   }
+  if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
+    p.trace[3 * kTraceMax + trace_slot] = globaltimer();   // last tile consumed by warp 0
 }
 
 // ---- epilogue warp: one projection phase --------------------------------------------------------
@@ -559,9 +569,47 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
   int64_t seg_start = tr.t0;
   int64_t rg = tr.t0 / tr.KT;
   int kk = static_cast<int>(tr.t0 % tr.KT);
+  // Operands of the epilogue that do not depend on this phase's sums (residual
+  // rows, biases) are loaded up front for the first two row groups this CTA
+  // finishes; the small projections have at most two.
+  const int b_lane = lane & 3;
+  float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+  int64_t pa_rg = -1, pb_rg = -1;
+  if (g.kind == kQKV || g.kind == kO || g.kind == kDown) {
+    const int64_t first_head = tr.t0 % tr.KT == 0 ? tr.t0 / tr.KT : tr.t0 / tr.KT + 1;
+    auto fetch = [&](int64_t r, float &v0, float &v1) {
+      const int64_t n0 = r * kRows + (lane >> 2), n1 = n0 + 8;
+      if (g.kind == kQKV) {
+        v0 = bf(g.bias[n0]);
+        v1 = bf(g.bias[n1]);
+      } else {
+        v0 = bf(__ldcg(p.h + static_cast<size_t>(b_lane) * m.H + n0));
+        v1 = bf(__ldcg(p.h + static_cast<size_t>(b_lane) * m.H + n1));
+      }
+    };
+    if (first_head * tr.KT < tr.t1) { pa_rg = first_head; fetch(pa_rg, pa0, pa1); }
+    if ((first_head + 1) * tr.KT < tr.t1) { pb_rg = first_head + 1; fetch(pb_rg, pb0, pb1); }
+  }
   for (int64_t t = tr.t0; t < tr.t1; ++t) {
     const bool group_end = kk == tr.KT - 1;
     if (group_end || t == tr.t1 - 1) {
+      const bool head_seg = (seg_start % tr.KT) == 0;
+      float part0 = 0.f, part1 = 0.f;
+      if (head_seg && !group_end) {
+        // finisher: the next CTA publishes the rest of this row group early in
+        // its range; fetch it while the consumers are still streaming
+        if (lane == 0) {
+          const uint64_t deadline = globaltimer() + p.timeout_ns;
+          uint32_t polls = 0;
+          while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
+            if (aborted(p)) break;
+            if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
+          }
+        }
+        __syncwarp();
+        part0 = __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane);
+        part1 = __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane + 32);
+      }
       wait_bar(p, &s.red_full[red.slot], red.parity, s.prod_ctl, 1003);
       const float *r = s.red + static_cast<size_t>(red.slot) * kConsumerWarps * 64;
       float v0 = 0.f, v1 = 0.f;
@@ -573,7 +621,7 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.red_empty[red.slot]);
       red.advance(kRedSlots);
-      const bool head = (seg_start % tr.KT) == 0;   // this CTA holds the group's first tile
+      const bool head = head_seg;   // this CTA holds the group's first tile
       seg_start = t + 1;
       if (!head) {
         p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane] = v0;
@@ -584,33 +632,36 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
           st_release_u32(&p.sync->flags[blockIdx.x], seq);
         }
       } else {
-        if (!group_end) {   // the rest of the row group is on CTA + 1
-          if (lane == 0) {
-            const uint64_t deadline = globaltimer() + p.timeout_ns;
-            uint32_t polls = 0;
-            while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
-              if (aborted(p)) break;
-              if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
-              __nanosleep(32);
-            }
-          }
-          __syncwarp();
-          v0 += __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane);
-          v1 += __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane + 32);
+        if (!group_end) {   // the rest of the row group came from CTA + 1
+          v0 += part0;
+          v1 += part1;
         }
-        const int b = lane & 3;
+        const int b = b_lane;
         const int64_t n0 = rg * kRows + (lane >> 2), n1 = n0 + 8;
+        float e0, e1;   // bias (QKV) or residual (O, down) of rows n0, n1
+        if (rg == pa_rg) {
+          e0 = pa0;
+          e1 = pa1;
+        } else if (rg == pb_rg) {
+          e0 = pb0;
+          e1 = pb1;
+        } else if (g.kind == kQKV) {
+          e0 = bf(g.bias[n0]);
+          e1 = bf(g.bias[n1]);
+        } else if (g.kind == kO || g.kind == kDown) {
+          e0 = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n0));
+          e1 = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n1));
+        } else {
+          e0 = e1 = 0.f;
+        }
         if (g.kind == kQKV) {
           // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
-          p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, bf(g.bias[n0])));
-          p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, bf(g.bias[n1])));
+          p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, e0));
+          p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, e1));
         } else if (g.kind == kO || g.kind == kDown) {
           // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
-          bf16 *h0 = p.h + static_cast<size_t>(b) * m.H + n0;
-          bf16 *h1 = p.h + static_cast<size_t>(b) * m.H + n1;
-          const float r0 = bf(__ldcg(h0)), r1 = bf(__ldcg(h1));
-          *h0 = tobf(__fadd_rn(r0, rbf(v0)));
-          *h1 = tobf(__fadd_rn(r1, rbf(v1)));
+          p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(v0)));
+          p.h[static_cast<size_t>(b) * m.H + n1] = tobf(__fadd_rn(e1, rbf(v1)));
         } else if (g.kind == kGU) {
           // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398);
           // rows 0-7 of the group are gate rows, 8-15 the matching up rows
@@ -652,8 +703,10 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
     p.arg_idx[blockIdx.x * kBatch + lane] = best_i;
     p.arg_bad[blockIdx.x * kBatch + lane] = bad;
   }
+  // the phase's outputs written by this warp are visible GPU-wide before the
+  // consumers may arrive at the grid barrier
+  __threadfence();
   __syncwarp();
-  __threadfence();   // the phase's outputs are visible GPU-wide before the grid barrier
   if (lane == 0) mbar_arrive(s.phase_done);
 }
 
@@ -695,36 +748,38 @@ __device__ void epilogue_main(const EpochParams &p, const Smem &s) {
 // scores bf16(q.K) then bf16(s / sqrt(d)), softmax in fp32 rounded to bf16,
 // output bf16(P.V) (:334-379).  Positions >= seq_len contribute exactly zero in
 // the reference (masked to bf16.min), so they are skipped.
-__device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) {
+template <int D>
+__device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer) {
   const ModelDims &m = p.m;
   const int tid = threadIdx.x;
-  const int d = m.d;
-  const int half = d / 2;
+  constexpr int half = D / 2;
+  constexpr int dpl = D / 32;            // dims per lane in P.V (4 or 2)
   const int groups = m.nq / m.nkv;
-  float *qf = reinterpret_cast<float *>(s.xs);         // [d]  roped q (bf16 values)
-  bf16 *kn = reinterpret_cast<bf16 *>(qf + d);          // [d]  roped new k
-  bf16 *vn = kn + d;                                    // [d]  new v
-  float *sc = reinterpret_cast<float *>(vn + d);        // [C]  scores, then probabilities
-  float *rd = sc + m.C;                                 // [16] reductions, then [8][d] P.V partials
-  const size_t layer_off = static_cast<size_t>(layer) * m.NB * m.bs * m.nkv * d;
+  float *qf = reinterpret_cast<float *>(s.xs);         // [D]  roped q (bf16 values)
+  bf16 *kn = reinterpret_cast<bf16 *>(qf + D);          // [D]  roped new k
+  bf16 *vn = kn + D;                                    // [D]  new v
+  float *sc = reinterpret_cast<float *>(vn + D);        // [C]  scores, then probabilities
+  float *rd = sc + m.C;                                 // [16] reductions, then [8][D] P.V partials
+  const size_t layer_off = static_cast<size_t>(layer) * m.NB * m.bs * m.nkv * D;
   const int units = kBatch * m.nq;
   const int warp = tid >> 5, lane = tid & 31;
   for (int u = blockIdx.x; u < units; u += p.grid) {
     const int b = u / m.nq, qh = u % m.nq, kvh = qh / groups;
-    bf16 *out = p.attn + static_cast<size_t>(b) * m.H + qh * d;
+    bf16 *out = p.attn + static_cast<size_t>(b) * m.H + qh * D;
     if (__ldcg(&p.work->active[b]) == 0) {
-      for (int i = tid; i < d; i += kConsumerThreads) out[i] = tobf(0.f);
+      for (int i = tid; i < D; i += kConsumerThreads) out[i] = tobf(0.f);
       continue;
     }
     const int64_t pos = __ldcg(&p.work->position[b]);
     const int len = __ldcg(&p.work->length[b]);
     const int slot = __ldcg(&p.work->slot[b]);
-    const bf16 *qsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + qh * d;
-    const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + kvh * d;
-    const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + m.nkv * d + kvh * d;
-    const bf16 *cs = p.rope_cos + pos * d;
-    const bf16 *sn = p.rope_sin + pos * d;
-    for (int i = tid; i < d; i += kConsumerThreads) {
+    const bf16 *qsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + qh * D;
+    const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + kvh * D;
+    const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + m.nkv * D + kvh * D;
+    const bf16 *cs = p.rope_cos + pos * D;
+    const bf16 *sn = p.rope_sin + pos * D;
+    if (tid < D) {
+      const int i = tid;
       const float c = bf(cs[i]), sv = bf(sn[i]);
       const float q = bf(__ldcg(qsrc + i));
       const float qr = i < half ? -bf(__ldcg(qsrc + i + half)) : bf(__ldcg(qsrc + i - half));
@@ -735,33 +790,35 @@ __device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) 
       vn[i] = __ldcg(vsrc + i);
     }
     named_sync(1, kConsumerThreads);
-    if (qh % groups == 0 && slot >= 0 && slot < m.NB * m.bs) {
-      const size_t off = layer_off + (static_cast<size_t>(slot) * m.nkv + kvh) * d;
-      for (int i = tid; i < d; i += kConsumerThreads) {
-        p.key_cache[off + i] = kn[i];
-        p.value_cache[off + i] = vn[i];
-      }
+    if (qh % groups == 0 && slot >= 0 && slot < m.NB * m.bs && tid < D) {
+      const size_t off = layer_off + (static_cast<size_t>(slot) * m.nkv + kvh) * D;
+      p.key_cache[off + tid] = kn[tid];
+      p.value_cache[off + tid] = vn[tid];
     }
-    // scores
+    // scores: thread t owns position t; its whole K row is requested at once
+    // (the new key comes from shared memory)
     float local_max = -INFINITY;
     for (int t = tid; t < len; t += kConsumerThreads) {
-      const bf16 *krow;
-      if (t == pos) {
-        krow = kn;
-      } else {
+      uint4 krow[D / 8];
+      const uint4 *src = reinterpret_cast<const uint4 *>(kn);
+      if (t != pos) {
         const int st = compute_slot(m, p.work->bt, b, t);
-        krow = p.key_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * d;
+        src = reinterpret_cast<const uint4 *>(p.key_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * D);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) krow[i] = __ldcg(src + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) krow[i] = src[i];
       }
       float dot = 0.f;
-      for (int i = 0; i < d; i += 8) {
-        const uint4 kv = (t == pos) ? *reinterpret_cast<const uint4 *>(krow + i)
-                                    : __ldcg(reinterpret_cast<const uint4 *>(krow + i));
-        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kv);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&krow[i]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float2 kf = __bfloat1622float2(k2[j]);
-          dot = fmaf(qf[i + 2 * j], kf.x, dot);
-          dot = fmaf(qf[i + 2 * j + 1], kf.y, dot);
+          dot = fmaf(qf[8 * i + 2 * j], kf.x, dot);
+          dot = fmaf(qf[8 * i + 2 * j + 1], kf.y, dot);
         }
       }
       const float s2 = rbf(__fdiv_rn(rbf(dot), m.sqrt_d));
@@ -774,6 +831,7 @@ __device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) 
     if (lane == 0) rd[warp] = local_max;
     named_sync(1, kConsumerThreads);
     float mx = rd[0];
+#pragma unroll
     for (int w = 1; w < kConsumerWarps; ++w) mx = fmaxf(mx, rd[w]);
     float local_sum = 0.f;
     for (int t = tid; t < len; t += kConsumerThreads) {
@@ -783,53 +841,59 @@ __device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) 
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, off);
-    named_sync(1, kConsumerThreads);
     if (lane == 0) rd[8 + warp] = local_sum;
     named_sync(1, kConsumerThreads);
     float sum = 0.f;
+#pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) sum += rd[8 + w];
     for (int t = tid; t < len; t += kConsumerThreads) sc[t] = rbf(__fdiv_rn(sc[t], sum));
     named_sync(1, kConsumerThreads);
-    // output: warp w takes positions t = w (mod 8); each lane owns d/32 dims
-    {
-      const int dpl = d / 32;   // 4 (d=128) or 2 (d=64)
-      float o[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int t = warp; t < len; t += kConsumerWarps) {
-        const bf16 *vrow;
-        if (t == pos) {
-          vrow = vn;
-        } else {
+    // output: warp w takes positions t = w (mod 8), four at a time; lane owns D/32 dims
+    float o[dpl];
+#pragma unroll
+    for (int j = 0; j < dpl; ++j) o[j] = 0.f;
+    for (int t0 = warp; t0 < len; t0 += 4 * kConsumerWarps) {
+      float vv[4][dpl];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = t0 + q * kConsumerWarps;
+        const bf16 *vrow = vn;
+        if (t < len && t != pos) {
           const int st = compute_slot(m, p.work->bt, b, t);
-          vrow = p.value_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * d;
+          vrow = p.value_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * D;
         }
-        const float pt = sc[t];
-        if (dpl == 4) {
-          const uint2 raw = (t == pos) ? *reinterpret_cast<const uint2 *>(vrow + lane * 4)
-                                       : __ldcg(reinterpret_cast<const uint2 *>(vrow + lane * 4));
-          const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-          const float2 f0 = __bfloat1622float2(v2[0]);
-          const float2 f1 = __bfloat1622float2(v2[1]);
-          o[0] = fmaf(pt, f0.x, o[0]);
-          o[1] = fmaf(pt, f0.y, o[1]);
-          o[2] = fmaf(pt, f1.x, o[2]);
-          o[3] = fmaf(pt, f1.y, o[3]);
-        } else {
-          for (int j = 0; j < dpl; ++j) {
-            const bf16 v = (t == pos) ? vrow[lane * dpl + j] : __ldcg(vrow + lane * dpl + j);
-            o[j] = fmaf(pt, bf(v), o[j]);
-          }
-        }
+#pragma unroll
+        for (int j = 0; j < dpl; ++j)
+          vv[q][j] = t < len ? bf(t == pos ? vrow[lane * dpl + j] : __ldcg(vrow + lane * dpl + j)) : 0.f;
       }
-      float *part = rd + 16;   // [8 warps][d]
-      for (int j = 0; j < dpl; ++j) part[warp * d + lane * dpl + j] = o[j];
-      named_sync(1, kConsumerThreads);
-      for (int i = tid; i < d; i += kConsumerThreads) {
-        float total = 0.f;
-        for (int w2 = 0; w2 < kConsumerWarps; ++w2) total += part[w2 * d + i];
-        out[i] = tobf(total);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int t = t0 + q * kConsumerWarps;
+        if (t < len) {
+#pragma unroll
+          for (int j = 0; j < dpl; ++j) o[j] = fmaf(sc[t], vv[q][j], o[j]);
+        }
       }
     }
+    float *part = rd + 16;   // [8 warps][D]
+#pragma unroll
+    for (int j = 0; j < dpl; ++j) part[warp * D + lane * dpl + j] = o[j];
     named_sync(1, kConsumerThreads);
+    if (tid < D) {
+      float total = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kConsumerWarps; ++w2) total += part[w2 * D + tid];
+      out[tid] = tobf(total);
+    }
+    named_sync(1, kConsumerThreads);
+  }
+}
+
+__device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) {
+  if (p.m.d == 128) {
+    attention_phase_d<128>(p, s, layer);
+  } else {
+    attention_phase_d<64>(p, s, layer);
   }
 }
 
@@ -1125,7 +1189,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       if (kind >= 0) {
         const Gemv g = make_gemv(p, ph / 5, kind);
         if (tid == 0) *s.phase_started = static_cast<int>(seq);
-        gemv_consume(p, s, g, ring, red);
+        gemv_consume(p, s, g, ring, red, barrier_index + 1);
         // the epilogue warp has written every output of the phase
         if (tid == 0) wait_bar(p, s.phase_done, done_parity, nullptr, 1004);
         done_parity ^= 1u;

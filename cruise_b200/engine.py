@@ -197,17 +197,16 @@ class EpochEngine:
     def set_trace(self, enable: bool) -> None:
         self.lib.cruise_epoch_set_trace(self.handle, 1 if enable else 0)
 
-    def read_trace(self, count: int) -> tuple[np.ndarray, np.ndarray]:
-        """(exit_ns, entry_ns) of grid barriers 0..count-1 of the last epoch."""
-        exit_ns = np.zeros(count, dtype=np.uint64)
-        entry_ns = np.zeros(count, dtype=np.uint64)
-        self._check(
-            self.lib.cruise_epoch_read_trace(
-                self.handle, _ptr(exit_ns, ctypes.c_uint64), _ptr(entry_ns, ctypes.c_uint64), count
-            ),
-            "read_trace",
-        )
-        return exit_ns, entry_ns
+    def read_trace(self, count: int) -> np.ndarray:
+        """[5, count] globaltimer ns per grid barrier of the last epoch: CTA 0
+        exit, CTA 0 entry, activations staged, last tile consumed, last arrival."""
+        out = np.zeros((5, count), dtype=np.uint64)
+        for series in range(5):
+            self._check(
+                self.lib.cruise_epoch_read_trace(self.handle, series, _ptr(out[series], ctypes.c_uint64), count),
+                "read_trace",
+            )
+        return out
 
     def last_timing(self) -> tuple[float, int]:
         device_us = ctypes.c_double(0.0)

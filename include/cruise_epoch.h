@@ -168,12 +168,17 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us,
                                  int32_t *kernel_launches);
 
 /* Phase trace (tracing / profiling aid): when enabled, each epoch records, per
- * grid barrier j (1-based, in launch order), the globaltimer ns at which CTA 0
- * finished its share of the preceding phase (entry_ns[j]) and at which every
- * CTA had arrived (exit_ns[j]).  At most 2048 barriers per epoch. */
+ * grid barrier j (1-based, in launch order; at most 2048 per epoch), globaltimer
+ * nanoseconds in five series:
+ *   0  CTA 0 left barrier j (every CTA had arrived)
+ *   1  CTA 0 arrived at barrier j (finished its share of the phase)
+ *   2  CTA 0 had staged the phase's activations (projection phases)
+ *   3  CTA 0's warp 0 consumed its last weight tile (projection phases)
+ *   4  the last CTA arrived at barrier j
+ * cruise_epoch_read_trace copies `count` entries of one series. */
 int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
-int32_t cruise_epoch_read_trace(void *engine, uint64_t *exit_ns,
-                                uint64_t *entry_ns, int32_t count);
+int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,
+                                int32_t count);
 
 /* Last CUDA error string of this engine (static storage). */
 const char *cruise_epoch_last_error(void *engine);
