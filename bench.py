@@ -2,7 +2,7 @@
 """Benchmark: Qwen2.5-7B-arch B=4 resident decode epochs (decode tok/s, us/step,
 % HBM roofline) on 1..N B200s of one node.
 
-Workload: the 7B architecture with seeded random-init
+Workload (benchmark configuration 2 of the task): the 7B architecture with seeded random-init
 bf16 weights (generated on the device), paged KV of 128-token blocks, 2 blocks
 per row, B=4 rows all active with prompts of 2-5 tokens (ids in [0, 151643)).
 Prompts are prefilled on the device with teacher-forced epochs, the prefilled
@@ -193,6 +193,22 @@ class Cohort:
         return int(self.cfg.capacity - self.position.max() - 1)
 
 
+def reduce_over_ranks(dev_s: float, tokens: int, wall_s: float, device) -> tuple[float, float, float]:
+    """(max device seconds, total tokens, max wall seconds) over the ranks of
+    the default process group (identity without one)."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return dev_s, float(tokens), wall_s
+    where = f"cuda:{device}" if device is not None else "cpu"
+    times = torch.tensor([dev_s, wall_s], dtype=torch.float64, device=where)
+    total = torch.tensor([float(tokens)], dtype=torch.float64, device=where)
+    dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    dist.all_reduce(total, op=dist.ReduceOp.SUM)
+    return float(times[0]), float(total[0]), float(times[1])
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -249,24 +265,9 @@ def run_gpu(args) -> None:
     barrier()
     dev_s = sum(device_us) / 1e6
     model_calls = args.steps * args.k
-    # max over ranks of the device time
-    t_max = dev_s
-    tok_total = tokens
-    if world > 1:
-        tt = torch.tensor([dev_s, float(tokens)], device=f"cuda:{device}", dtype=torch.float64)
-        tm = tt.clone()
-        dist.all_reduce(tm[:1], op=dist.ReduceOp.MAX)
-        dist.all_reduce(tt[1:], op=dist.ReduceOp.SUM)
-        t_max, tok_total = float(tm[0]), float(tt[1])
+    t_max, tok_total, e2e_wall = reduce_over_ranks(dev_s, tokens, wall, device=device if world > 1 else None)
     value = tok_total / t_max
-    # e2e: wall clock per epoch through the C-ABI call (host buffers both ways)
-    e2e_tokens = tokens
-    e2e_wall = wall
-    if world > 1:
-        ew = torch.tensor([wall], device=f"cuda:{device}", dtype=torch.float64)
-        dist.all_reduce(ew, op=dist.ReduceOp.MAX)
-        e2e_wall = float(ew[0])
-        e2e_tokens = tok_total
+    e2e_tokens = tok_total
     if args.trace and rank == 0:
         print_trace(engine, cohort, cfg, args.k)
     peak, peak_kind = hbm_peak()
@@ -289,7 +290,7 @@ def run_gpu(args) -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded random-init weights generated on the device; seeded prompts)",
             "config": {
-                "workload": "BASELINE configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
+                "workload": "configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
                             "one-shot H2D KV import of the device-prefilled prompts (2-5 tokens)" % args.k,
                 "model": "Qwen2.5-7B architecture (28 layers, hidden 3584, 28/4 heads x 128, I 18944, V 152064)",
                 "global_batch": 4 * world,
@@ -373,11 +374,14 @@ def print_trace(engine, cohort, cfg, k) -> None:
               f"{bw:6.0f}", file=sys.stderr)
 
 
+SAMPLE_LAYERS = (1, 5)
+
+
 def cpu_oracle_step_time(weights: dict, cfg, threads: int) -> tuple[float, str]:
     """Seconds of one 7B decode step of the CPU oracle (bf16 torch ops, the
     reference's own arithmetic), from a bounded sample: steps of the same
-    geometry truncated to 1 and 2 layers give the per-layer and fixed costs,
-    extrapolated to all layers."""
+    geometry truncated to 1 and 5 layers give the per-layer and the fixed
+    (embedding, final norm, lm_head) costs, extrapolated to all layers."""
     import torch
 
     from oracle.decoder import OracleDecoder
@@ -385,7 +389,7 @@ def cpu_oracle_step_time(weights: dict, cfg, threads: int) -> tuple[float, str]:
 
     torch.set_num_threads(threads)
     times = {}
-    for layers in (1, 2):
+    for layers in SAMPLE_LAYERS:
         ocfg = OracleConfig(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
                             num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
                             intermediate=cfg.intermediate, vocab=cfg.vocab, block_size=cfg.block_size)
@@ -406,11 +410,12 @@ def cpu_oracle_step_time(weights: dict, cfg, threads: int) -> tuple[float, str]:
             decoder.step(token, position, seq_len, bt, slot, key, value, active)
             samples.append(time.perf_counter() - t)
         times[layers] = min(samples)
-    per_layer = max(times[2] - times[1], 1e-9)
-    fixed = max(times[1] - per_layer, 0.0)
+    lo, hi = SAMPLE_LAYERS
+    per_layer = max((times[hi] - times[lo]) / (hi - lo), 1e-9)
+    fixed = max(times[lo] - lo * per_layer, 0.0)
     return fixed + cfg.num_layers * per_layer, (
-        f"1- and 2-layer truncations of the 7B decode step (B=4, ctx 5), best of 3, extrapolated to "
-        f"{cfg.num_layers} layers: {times[1]*1e3:.0f} / {times[2]*1e3:.0f} ms"
+        f"{lo}- and {hi}-layer truncations of the 7B decode step (B=4, ctx 5, {threads} threads), best of 3, "
+        f"extrapolated to {cfg.num_layers} layers: {times[lo]*1e3:.0f} / {times[hi]*1e3:.0f} ms"
     )
 
 
@@ -442,7 +447,7 @@ def engine_weights_fn(engine):
 
 def cpu_baseline(engine, cfg) -> dict:
     threads = len(os.sched_getaffinity(0))
-    step_s, sample = cpu_oracle_step_time(engine_weights_fn(engine)(2), cfg, threads)
+    step_s, sample = cpu_oracle_step_time(engine_weights_fn(engine)(SAMPLE_LAYERS[-1]), cfg, threads)
     return {"value": round(4 / step_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": sample, "us_per_decode_step": round(step_s * 1e6, 1)}
 
@@ -459,7 +464,7 @@ def run_reference(args) -> None:
     cfg = QWEN25_7B
     threads = len(os.sched_getaffinity(0))
 
-    weights = random_weights(cfg, layers=2, seed=0)
+    weights = random_weights(cfg, layers=SAMPLE_LAYERS[-1], seed=0)
     samples = []
     sample_desc = ""
     for _ in range(args.warmup + args.steps):
@@ -473,7 +478,7 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * args.k * 1e3, 2),
         "us_per_decode_step": round(step_s * 1e6, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "BASELINE configs[1] decode steps (B=4, 7B arch) on the host cores",
+        "config": {"workload": "configs[1] decode steps (B=4, 7B arch) on the host cores",
                    "epoch_k": args.k},
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": sample_desc},

@@ -1,6 +1,6 @@
 """Seeded epoch scenarios shared by the GPU parity tests, ``smoke()`` and ``bench.py``.
 
-A scenario is the BASELINE configuration-1 workload generalised over the
+A scenario is the tiny-configuration epoch workload generalised over the
 model geometry: 4 rows, some inactive through the active mask, a seeded block
 table, prompts of seeded length and ids, and a K-step greedy epoch.  Prompts
 are prefilled row by row with teacher-forced epochs (the engine's device

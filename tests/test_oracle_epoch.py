@@ -1,0 +1,152 @@
+"""The oracle controller on the CPU: statuses, termination, continuity, import
+proof, and the host bridge statuses (controller/g4c_b4_resident_epoch.cpp:335-631,
+native/resident_epoch_bridge.cpp:424-649; recovery cases of
+g4c-attempt70a-r1-*/protocol.md:33-38)."""
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.decoder import OracleDecoder
+from oracle.epoch import EpochTrace, OracleEpochController, bridge_execute, compute_slot
+from oracle.model import TINY, seeded_weights
+from scenario import decode_inputs, import_payload, make_scenario, prefill_epochs
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return seeded_weights(TINY, 0)
+
+
+def controller(weights, dtype=torch.bfloat16):
+    return OracleEpochController(OracleDecoder(TINY, weights, dtype))
+
+
+def prefilled(weights, seed=0, **kw):
+    sc = make_scenario(vocab=TINY.vocab, seed=seed, **kw)
+    ctl = controller(weights)
+    for inputs in prefill_epochs(sc, TINY.block_size, TINY.vocab):
+        _, out = ctl.run(**inputs)
+        assert out[3] == 0
+    return sc, ctl
+
+
+def test_prefill_writes_prompt_positions_and_resident_state(weights):
+    sc, ctl = prefilled(weights)
+    for row, prompt in enumerate(sc.prompts):
+        if not prompt:
+            continue
+        assert ctl.res_generation[row] == sc.generations[row]
+        assert ctl.res_token[row] == prompt[-1] and ctl.res_position[row] == len(prompt) - 1
+        block = int(sc.block_table[row, 0])
+        written = ctl.key[:, block, : len(prompt) - 1].float().abs().sum()
+        untouched = ctl.key[:, block, len(prompt) - 1:].float().abs().sum()
+        assert written > 0 and untouched == 0
+
+
+@pytest.mark.parametrize("mutate, status", [
+    (lambda i: i["control"].__setitem__(0, 9), 201),
+    (lambda i: i["control"].__setitem__(0, 0), 201),
+    (lambda i: i["control"].__setitem__(5, 1), 205),
+    (lambda i: i["control"].__setitem__(6, 1), 206),
+    (lambda i: i["control"].__setitem__(1, TINY.vocab), 201),
+    (lambda i: i["block_table"].__setitem__(1, i["block_table"][0]), 203),
+    (lambda i: i["block_table"].__setitem__(1, 8), 203),
+    (lambda i: i["slot"].__setitem__(0, i["slot"][0] + 1), 204),
+    (lambda i: i["position"].__setitem__(0, 31) or i["seq_len"].__setitem__(0, 32), 202),
+    (lambda i: i["seq_len"].__setitem__(3, 2), 201),
+    (lambda i: i["token"].__setitem__(1, -1), 201),
+])
+def test_recovery_statuses_run_no_step(weights, mutate, status):
+    sc, ctl = prefilled(weights, seed=3)
+    key0 = ctl.key.clone()
+    inputs = decode_inputs(sc, TINY.block_size)
+    mutate(inputs)
+    history, out = ctl.run(**inputs)
+    assert out[3] == status and out[4] == 0
+    assert (history == -1).all()
+    assert list(out[18:22]) == [3, 3, 3, 3]          # every row finishes with FALLBACK
+    assert out[5] == 1                                # fallback flag
+    assert torch.equal(key0, ctl.key)
+
+
+def test_eos_stops_a_row_mid_epoch_and_shrinks_the_batch(weights):
+    sc, ctl = prefilled(weights, seed=4)
+    probe = controller(weights)
+    for inputs in prefill_epochs(sc, TINY.block_size, TINY.vocab):
+        probe.run(**inputs)
+    inputs = decode_inputs(sc, TINY.block_size)
+    inputs["control"][0] = 4
+    history, _ = probe.run(**inputs)
+    eos = int(history[1, 1])                          # what row 1 emits at step 2
+    inputs["control"][1:5] = eos
+    history, out = ctl.run(**inputs)
+    assert history[1, 1] == eos and (history[2:, 1] == -1).all()
+    assert out[6 + 2 * 4 + 1] == 2 and out[6 + 3 * 4 + 1] == 1       # executed 2, reason EOS
+    assert out[6 + 4 * 4 + 1] < out[6 + 4 * 4]                         # final active < initial
+
+
+def test_generation_continuity_is_enforced(weights):
+    sc, ctl = prefilled(weights, seed=1)
+    inputs = decode_inputs(sc, TINY.block_size)
+    _, out = ctl.run(**inputs)
+    assert out[3] == 0
+    history, out = ctl.run(**inputs)                  # same inputs again: resident state moved on
+    assert out[3] == 212
+
+
+def test_new_generation_clears_the_row_blocks(weights):
+    sc, ctl = prefilled(weights, seed=2)
+    row = 0
+    inputs = decode_inputs(sc, TINY.block_size)
+    inputs["token"][row], inputs["position"][row], inputs["seq_len"][row] = 5, 0, 1
+    inputs["slot"][row] = compute_slot(TINY, inputs["block_table"], row, 0)
+    inputs["control"][3 + 4 + row] = 99               # a new request reuses the row
+    _, out = ctl.run(**inputs)
+    assert out[3] == 0
+    block1 = int(sc.block_table[row, 1])
+    assert ctl.key[:, block1].float().abs().sum() == 0
+
+
+def test_import_checksum_is_the_zlib_adler_of_the_imported_blocks(weights):
+    sc, pre = prefilled(weights)
+    payload = import_payload(pre.key, pre.value, sc)
+    ctl = controller(weights)
+    inputs = decode_inputs(sc, TINY.block_size, importing=True)
+    _, out = ctl.run(**inputs, import_payload=payload)
+    raw = payload.contiguous().view(torch.int16).numpy().tobytes()
+    block = TINY.block_size * TINY.kv_width * 2
+    expected = 1
+    mask = [r for r in range(4) if sc.prompts[r]]
+    for cache in range(2):
+        for layer in range(TINY.num_layers):
+            for row in mask:
+                start = ((cache * TINY.num_layers + layer) * 4 + row) * block
+                expected = zlib.adler32(raw[start:start + block], expected)
+    assert out[3] == 0 and (int(out[5]) & 0xFFFFFFFF) == expected
+
+
+def test_fp32_mode_runs_the_tiny_configuration(weights):
+    sc = make_scenario(vocab=TINY.vocab, seed=0)
+    ctl = controller(weights, torch.float32)
+    for inputs in prefill_epochs(sc, TINY.block_size, TINY.vocab):
+        ctl.run(**inputs)
+    trace = EpochTrace()
+    history, out = ctl.run(**decode_inputs(sc, TINY.block_size), trace=trace)
+    assert out[3] == 0 and out[4] == 2 and trace.logits[0].dtype == torch.float32
+
+
+def test_bridge_statuses(weights):
+    ctl = controller(weights)
+    base = dict(token_ids=[1, 0, 0, 0], positions=[0, 0, 0, 0], seq_lens=[1, 0, 0, 0], eos_ids=[4095] * 4,
+                row_generations=[1, 0, 0, 0])
+    assert bridge_execute(ctl, 0, 1, configured_eos=4095, **base).ret == 10
+    assert bridge_execute(ctl, 1, 9, configured_eos=4095, **base).ret == 10
+    assert bridge_execute(ctl, 2, 1, configured_eos=4095, **base).ret == 12
+    bad = dict(base, seq_lens=[2, 0, 0, 0])
+    assert bridge_execute(ctl, 1, 1, configured_eos=4095, **bad).ret == 11
+    ok = bridge_execute(ctl, 1, 2, configured_eos=4095, **base)
+    assert ok.ret == 0 and ok.commit_state == 2 and ok.device_status == 0 and ok.executed[0] == 2
+    assert ok.declared_input_bytes == 260 and ok.declared_output_bytes == 368
