@@ -308,6 +308,12 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   e->down_xglobal = pick_kc(m.I_pad) == 64 * kConsumerWarps;
   const int kmax = e->down_xglobal ? m.H : std::max(m.H, m.I_pad);
   e->xs_stride = kmax + 8;
+  // the attention unit's scratch aliases the activation rows and the reduction ring
+  if (attn_scratch_bytes(m.d, m.C) >
+      static_cast<size_t>(kBatch) * e->xs_stride * 2 + static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4) {
+    destroy_engine(e);
+    return nullptr;
+  }
   const size_t limit = prop.sharedMemPerBlockOptin;
   int stages = kMaxStages;
   while (stages > 2 && smem_bytes(stages, e->xs_stride) > limit) --stages;

@@ -164,12 +164,18 @@ struct Smem {
   int32_t *misc;           // [16] small broadcast values
   volatile int *prod_ctl;  // producer / epilogue control: -2 wait, >= s run step s, -1 stop
   volatile int *phase_started;  // sequence number of the projection phase the consumers began
+  int64_t *row_pos;        // [4] row state of the current step (attention)
+  int32_t *row_len;        // [4]
+  int32_t *row_slot;       // [4]
+  int32_t *row_act;        // [4]
+  int32_t *bt;             // [4][kMaxBlocksPerRow] block table of the epoch
 };
 
 __host__ __device__ inline size_t smem_bytes(int stages, int xs_stride) {
   return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(kBatch) * xs_stride * 2 +
          static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4 + 2 * kMaxStages * 8 +
-         2 * kRedSlots * 8 + 8 + 40 * 4 + 24 * 4 + 16 * 4 + 16;
+         2 * kRedSlots * 8 + 8 + 40 * 4 + 24 * 4 + 16 * 4 + 16 + kBatch * 8 + 3 * kBatch * 4 +
+         kBatch * kMaxBlocksPerRow * 4;
 }
 
 __device__ __forceinline__ Smem carve_smem(uint8_t *base, const EpochParams &p) {
@@ -203,6 +209,13 @@ __device__ __forceinline__ Smem carve_smem(uint8_t *base, const EpochParams &p) 
   ptr += 16 * 4;
   s.prod_ctl = reinterpret_cast<volatile int *>(ptr);
   s.phase_started = reinterpret_cast<volatile int *>(ptr + 4);
+  ptr += 16;
+  s.row_pos = reinterpret_cast<int64_t *>(ptr);
+  ptr += kBatch * 8;
+  s.row_len = reinterpret_cast<int32_t *>(ptr);
+  s.row_slot = s.row_len + kBatch;
+  s.row_act = s.row_slot + kBatch;
+  s.bt = s.row_act + kBatch;
   return s;
 }
 
@@ -225,36 +238,56 @@ __device__ __forceinline__ void raise_error(const EpochParams &p, uint32_t where
 }
 
 // Grid barrier among the consumer warps of all CTAs.  `index` counts barriers
-// from 1 within the launch.  Returns false when the launch is aborting.
+// from 1 within the launch.  Arrivals are spread over eight counters (CTA c
+// adds to counter c % 8) so that they do not serialise on one L2 line; lanes
+// 0-7 of warp 0 poll the eight counters in parallel with relaxed loads and the
+// CTA proceeds after a fence once every counter reached its target.
+// Returns false when the launch is aborting.
 __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index, uint32_t where) {
   named_sync(1, kConsumerThreads);
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     int ok = 1;
-    const bool trace = p.trace != nullptr && blockIdx.x == 0 && index < kTraceMax;
-    if (trace) p.trace[kTraceMax + index] = globaltimer();   // CTA 0 finished its share
-    if (p.trace != nullptr && index < kTraceMax)
-      atomicMax(reinterpret_cast<unsigned long long *>(&p.trace[4 * kTraceMax + index]),
-                static_cast<unsigned long long>(globaltimer()));   // the last CTA to arrive
-    // every thread of the CTA wrote before the bar.sync above; the fence makes
-    // those writes visible GPU-wide before the arrival is
-    __threadfence();
-    red_release_add_u32(&p.sync->barrier, 1u);
-    const uint32_t target = index * static_cast<uint32_t>(p.grid);
+    if (lane == 0) {
+      if (p.trace != nullptr && index < kTraceMax) {
+        if (blockIdx.x == 0) p.trace[kTraceMax + index] = globaltimer();   // CTA 0 finished its share
+        atomicMax(reinterpret_cast<unsigned long long *>(&p.trace[4 * kTraceMax + index]),
+                  static_cast<unsigned long long>(globaltimer()));         // the last CTA to arrive
+      }
+      // every thread of the CTA wrote before the bar.sync above; the fence makes
+      // those writes visible GPU-wide before the arrival is
+      __threadfence();
+      atomicAdd(&p.sync->barrier[blockIdx.x % kBarrierLanes][0], 1u);
+    }
+    const int grid = p.grid;
+    const uint32_t members = lane < kBarrierLanes ? static_cast<uint32_t>((grid - lane + kBarrierLanes - 1) / kBarrierLanes) : 0u;
+    const uint32_t target = index * members;
     const uint64_t deadline = globaltimer() + p.timeout_ns;
-    uint32_t polls = 0;
-    while (static_cast<int32_t>(ld_acquire_u32(&p.sync->barrier) - target) < 0) {
-      if ((++polls & 15) == 0) {
-        if (aborted(p)) { ok = 0; break; }
-        if (globaltimer() > deadline) {
-          raise_error(p, where);
-          ok = 0;
-          break;
+    for (uint32_t polls = 1;; ++polls) {
+      const bool mine = lane >= kBarrierLanes ||
+                        static_cast<int32_t>(ld_relaxed_u32(&p.sync->barrier[lane][0]) - target) >= 0;
+      if (__all_sync(0xffffffffu, mine)) break;
+      if ((polls & 15) == 0) {
+        int stop = 0;
+        if (lane == 0) {
+          if (aborted(p)) {
+            stop = 1;
+          } else if (globaltimer() > deadline) {
+            raise_error(p, where);
+            stop = 1;
+          }
         }
+        if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
       }
     }
-    if (ok && aborted(p)) ok = 0;
-    if (trace) p.trace[index] = globaltimer();                // every CTA arrived
-    s.misc[0] = ok;
+    // acquire, in every lane that observed a counter: the other CTAs' writes
+    // before their arrivals are visible
+    __threadfence();
+    if (lane == 0) {
+      if (ok && aborted(p)) ok = 0;
+      if (p.trace != nullptr && blockIdx.x == 0 && index < kTraceMax) p.trace[index] = globaltimer();
+      s.misc[0] = ok;
+    }
   }
   named_sync(1, kConsumerThreads);
   return s.misc[0] != 0;
@@ -748,31 +781,98 @@ __device__ void epilogue_main(const EpochParams &p, const Smem &s) {
 // scores bf16(q.K) then bf16(s / sqrt(d)), softmax in fp32 rounded to bf16,
 // output bf16(P.V) (:334-379).  Positions >= seq_len contribute exactly zero in
 // the reference (masked to bf16.min), so they are skipped.
+//
+// Latency layout: a unit is one dependent trip to memory.  Together with the
+// q/k/v loads every thread issues its cached K row (scores pass: thread t owns
+// position t of a 256-position chunk) and, with cp.async into the free part of
+// the scratch, the V slices it consumes in the P.V pass (thread = position
+// group x 8-dim slice) for the first positions that fit; the row state and the
+// block table come from shared memory.  Longer contexts load the remaining K
+// chunks and V rows in their loops.
+constexpr int kAttnChunk = kConsumerThreads;   // positions per scores chunk
+
+template <int D>
+__host__ __device__ constexpr int attn_groups() { return kConsumerThreads / (D / 8); }
+
+// Shared scratch of one attention unit: qf[D] f32, kn[D] + vn[D] bf16, sc[C]
+// f32, rd[16] f32, part[groups][D] f32; the staged V rows follow.
+__host__ __device__ inline size_t attn_scratch_bytes(int D, int C) {
+  const int groups = kConsumerThreads / (D / 8);
+  return static_cast<size_t>(D) * 4 + static_cast<size_t>(D) * 4 + static_cast<size_t>((C + 3) & ~3) * 4 +
+         16 * 4 + static_cast<size_t>(groups) * D * 4;
+}
+
 template <int D>
 __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer) {
   const ModelDims &m = p.m;
   const int tid = threadIdx.x;
   constexpr int half = D / 2;
-  constexpr int dpl = D / 32;            // dims per lane in P.V (4 or 2)
+  constexpr int kSlices = D / 8;                 // 16-byte slices of a K/V row
+  constexpr int kGroups = attn_groups<D>();      // position groups of the P.V pass
   const int groups = m.nq / m.nkv;
   float *qf = reinterpret_cast<float *>(s.xs);         // [D]  roped q (bf16 values)
   bf16 *kn = reinterpret_cast<bf16 *>(qf + D);          // [D]  roped new k
   bf16 *vn = kn + D;                                    // [D]  new v
   float *sc = reinterpret_cast<float *>(vn + D);        // [C]  scores, then probabilities
-  float *rd = sc + m.C;                                 // [16] reductions, then [8][D] P.V partials
+  float *rd = sc + ((m.C + 3) & ~3);                    // [16] reductions
+  float *part = rd + 16;                                // [groups][D] P.V partials
+  bf16 *vs = reinterpret_cast<bf16 *>(reinterpret_cast<uint8_t *>(s.xs) + attn_scratch_bytes(D, m.C));
+  // positions whose V rows are staged in shared memory
+  const size_t scratch = static_cast<size_t>(kBatch) * p.xs_stride * 2 +
+                         static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4;
+  const int vcap = static_cast<int>(min(static_cast<size_t>(m.C), (scratch - attn_scratch_bytes(D, m.C)) / (D * 2)));
+  if (layer == 0) {   // the row state is constant over the layers of a step
+    if (tid < kBatch) {
+      s.row_pos[tid] = __ldcg(&p.work->position[tid]);
+      s.row_len[tid] = __ldcg(&p.work->length[tid]);
+      s.row_slot[tid] = __ldcg(&p.work->slot[tid]);
+      s.row_act[tid] = __ldcg(&p.work->active[tid]);
+    }
+    named_sync(1, kConsumerThreads);
+  }
   const size_t layer_off = static_cast<size_t>(layer) * m.NB * m.bs * m.nkv * D;
+  const size_t row_stride = static_cast<size_t>(m.nkv) * D;   // elements between cache slots
   const int units = kBatch * m.nq;
   const int warp = tid >> 5, lane = tid & 31;
+  const int vslice = tid % kSlices, vgroup = tid / kSlices;
   for (int u = blockIdx.x; u < units; u += p.grid) {
     const int b = u / m.nq, qh = u % m.nq, kvh = qh / groups;
     bf16 *out = p.attn + static_cast<size_t>(b) * m.H + qh * D;
-    if (__ldcg(&p.work->active[b]) == 0) {
+    if (s.row_act[b] == 0) {
       for (int i = tid; i < D; i += kConsumerThreads) out[i] = tobf(0.f);
       continue;
     }
-    const int64_t pos = __ldcg(&p.work->position[b]);
-    const int len = __ldcg(&p.work->length[b]);
-    const int slot = __ldcg(&p.work->slot[b]);
+    const int64_t pos = s.row_pos[b];
+    const int len = s.row_len[b];
+    const int slot = s.row_slot[b];
+    const bf16 *kcache = p.key_cache + layer_off + kvh * D;
+    const bf16 *vcache = p.value_cache + layer_off + kvh * D;
+    // a cached row of position t (never the new position: its k/v come from
+    // shared memory); nullptr outside the row's valid blocks
+    auto cached = [&](const bf16 *base, int t) -> const uint4 * {
+      const int st = compute_slot(m, s.bt, b, t);
+      return st < 0 ? nullptr : reinterpret_cast<const uint4 *>(base + static_cast<size_t>(st) * row_stride);
+    };
+    auto load_k = [&](uint4 (&krow)[kSlices], int c0) {
+      const int t = c0 + tid;
+      const uint4 *src = (t < len && t != pos) ? cached(kcache, t) : nullptr;
+#pragma unroll
+      for (int i = 0; i < kSlices; ++i) krow[i] = src != nullptr ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
+    };
+    uint4 krow[kSlices];
+    load_k(krow, 0);
+    const int vstaged = min(len, vcap);
+    for (int t = vgroup; t < vstaged; t += kGroups) {
+      if (t == pos) continue;
+      const uint4 *src = cached(vcache, t);
+      bf16 *dst = vs + static_cast<size_t>(t) * D + vslice * 8;
+      if (src != nullptr) {
+        cp_async16(dst, src + vslice);
+      } else {
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
     const bf16 *qsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + qh * D;
     const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + kvh * D;
     const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + m.nkv * D + kvh * D;
@@ -795,35 +895,31 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
       p.key_cache[off + tid] = kn[tid];
       p.value_cache[off + tid] = vn[tid];
     }
-    // scores: thread t owns position t; its whole K row is requested at once
-    // (the new key comes from shared memory)
+    // scores: thread t owns position t of each chunk
     float local_max = -INFINITY;
-    for (int t = tid; t < len; t += kConsumerThreads) {
-      uint4 krow[D / 8];
-      const uint4 *src = reinterpret_cast<const uint4 *>(kn);
-      if (t != pos) {
-        const int st = compute_slot(m, p.work->bt, b, t);
-        src = reinterpret_cast<const uint4 *>(p.key_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * D);
+    for (int c0 = 0; c0 < len; c0 += kAttnChunk) {
+      if (c0 > 0) load_k(krow, c0);
+      const int t = c0 + tid;
+      if (t < len) {
+        if (t == pos) {
 #pragma unroll
-        for (int i = 0; i < D / 8; ++i) krow[i] = __ldcg(src + i);
-      } else {
-#pragma unroll
-        for (int i = 0; i < D / 8; ++i) krow[i] = src[i];
-      }
-      float dot = 0.f;
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) {
-        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&krow[i]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 kf = __bfloat1622float2(k2[j]);
-          dot = fmaf(qf[8 * i + 2 * j], kf.x, dot);
-          dot = fmaf(qf[8 * i + 2 * j + 1], kf.y, dot);
+          for (int i = 0; i < kSlices; ++i) krow[i] = reinterpret_cast<const uint4 *>(kn)[i];
         }
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < kSlices; ++i) {
+          const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&krow[i]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 kf = __bfloat1622float2(k2[j]);
+            dot = fmaf(qf[8 * i + 2 * j], kf.x, dot);
+            dot = fmaf(qf[8 * i + 2 * j + 1], kf.y, dot);
+          }
+        }
+        const float s2 = rbf(__fdiv_rn(rbf(dot), m.sqrt_d));
+        sc[t] = s2;
+        local_max = fmaxf(local_max, s2);
       }
-      const float s2 = rbf(__fdiv_rn(rbf(dot), m.sqrt_d));
-      sc[t] = s2;
-      local_max = fmaxf(local_max, s2);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
@@ -848,41 +944,46 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
     for (int w = 0; w < kConsumerWarps; ++w) sum += rd[8 + w];
     for (int t = tid; t < len; t += kConsumerThreads) sc[t] = rbf(__fdiv_rn(sc[t], sum));
     named_sync(1, kConsumerThreads);
-    // output: warp w takes positions t = w (mod 8), four at a time; lane owns D/32 dims
-    float o[dpl];
+    // output: this thread accumulates dims [8*vslice, 8*vslice+8) over the
+    // positions vgroup + kGroups*i in ascending order (its own staged V slices,
+    // then four rows at a time from memory beyond the staged ones)
+    float o[8];
 #pragma unroll
-    for (int j = 0; j < dpl; ++j) o[j] = 0.f;
-    for (int t0 = warp; t0 < len; t0 += 4 * kConsumerWarps) {
-      float vv[4][dpl];
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    auto accumulate = [&](const uint4 &v4, float pr) {
+      const __nv_bfloat162 *v2 = reinterpret_cast<const __nv_bfloat162 *>(&v4);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 vf = __bfloat1622float2(v2[j]);
+        o[2 * j] = fmaf(pr, vf.x, o[2 * j]);
+        o[2 * j + 1] = fmaf(pr, vf.y, o[2 * j + 1]);
+      }
+    };
+    const uint4 vnew = reinterpret_cast<const uint4 *>(vn)[vslice];
+    cp_async_wait_all();
+    int t = vgroup;
+    for (; t < vstaged; t += kGroups)
+      accumulate(t == pos ? vnew : lds128(vs + static_cast<size_t>(t) * D + vslice * 8), sc[t]);
+    for (; t < len; t += 4 * kGroups) {
+      uint4 vv[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int t = t0 + q * kConsumerWarps;
-        const bf16 *vrow = vn;
-        if (t < len && t != pos) {
-          const int st = compute_slot(m, p.work->bt, b, t);
-          vrow = p.value_cache + layer_off + (static_cast<size_t>(st) * m.nkv + kvh) * D;
-        }
-#pragma unroll
-        for (int j = 0; j < dpl; ++j)
-          vv[q][j] = t < len ? bf(t == pos ? vrow[lane * dpl + j] : __ldcg(vrow + lane * dpl + j)) : 0.f;
+        const int tq = t + q * kGroups;
+        const uint4 *src = (tq < len && tq != pos) ? cached(vcache, tq) : nullptr;
+        vv[q] = tq == pos ? vnew : (src != nullptr ? __ldcg(src + vslice) : make_uint4(0, 0, 0, 0));
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int t = t0 + q * kConsumerWarps;
-        if (t < len) {
-#pragma unroll
-          for (int j = 0; j < dpl; ++j) o[j] = fmaf(sc[t], vv[q][j], o[j]);
-        }
-      }
+      for (int q = 0; q < 4; ++q)
+        if (t + q * kGroups < len) accumulate(vv[q], sc[t + q * kGroups]);
     }
-    float *part = rd + 16;   // [8 warps][D]
-#pragma unroll
-    for (int j = 0; j < dpl; ++j) part[warp * D + lane * dpl + j] = o[j];
+    float4 *dst = reinterpret_cast<float4 *>(part + vgroup * D + vslice * 8);
+    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_float4(o[4], o[5], o[6], o[7]);
     named_sync(1, kConsumerThreads);
     if (tid < D) {
       float total = 0.f;
 #pragma unroll
-      for (int w2 = 0; w2 < kConsumerWarps; ++w2) total += part[w2 * D + tid];
+      for (int g2 = 0; g2 < kGroups; ++g2) total += part[g2 * D + tid];
       out[tid] = tobf(total);
     }
     named_sync(1, kConsumerThreads);
@@ -1157,6 +1258,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
     w->stop = w->status != kOk ? 1 : 0;
   }
   if (ok) ok = grid_barrier(p, s, ++barrier_index, 4);
+  // the validated block table, read by the attention units of every step
+  for (int i = tid; i < kBatch * m.bpr; i += kConsumerThreads) s.bt[i] = __ldcg(&w->bt[i]);
   if (ok && __ldcg(&w->status) == kOk) {
     bool any = false;
     for (int b = 0; b < kBatch; ++b) any |= __ldcg(&w->new_gen[b]) != 0;

@@ -124,11 +124,12 @@ struct EpochWork {
 };
 
 // Cross-CTA synchronisation words; zeroed by the host before every launch.
+constexpr int kBarrierLanes = 8;     // arrival counters of the grid barrier
 struct SyncState {
-  uint32_t barrier;            // grid barrier arrivals (monotonic)
+  uint32_t barrier[kBarrierLanes][32];   // CTA c arrives on counter c % 8 (one 128-B line each)
   uint32_t error;              // non-zero: a wait timed out, every CTA leaves
   uint32_t error_where;
-  uint32_t pad0;
+  uint32_t pad0[30];
   uint32_t flags[kMaxCtas];    // split row-group partial published (phase seq)
 };
 

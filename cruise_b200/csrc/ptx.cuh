@@ -110,10 +110,26 @@ __device__ __forceinline__ uint4 lds128(const void *ptr) {
   return v;
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), completed by the
+// issuing thread's cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // ---- global memory ordering ------------------------------------------------------
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *ptr) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *ptr) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
   return v;
 }
 
