@@ -65,6 +65,9 @@ SIGNATURES = {
             ctypes.c_void_p, ctypes.c_uint64, i64p, i64p, i32p, f32p,
         ],
     ),
+    "cruise_epoch_run_noalloc": (
+        ctypes.c_int32, [ctypes.c_void_p, i64p, i64p, i32p, i32p, i32p, i32p, i32p, i64p, i32p],
+    ),
     "cruise_epoch_last_timing": (
         ctypes.c_int32, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), i32p]
     ),

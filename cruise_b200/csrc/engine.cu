@@ -811,6 +811,149 @@ int32_t preset(const char *name, CruiseModelConfig *cfg) {
 }  // namespace
 }  // namespace cruise
 
+// ===================================== allocation-free epoch ======================================
+// Scratch of cruise_epoch_run_noalloc, sized once at build time.  Each GPU on
+// which this library's device code is loaded holds these bytes until the
+// process exits.  Host code names the array only to look up its device address.
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace cruise {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void *g_noalloc_base[kNoAllocMaxDevices] = {};
+
+// Device address of the static scratch on `device`, which must be current.  The
+// lookup runs once per device, on that device's first allocation-free call.
+cudaError_t noalloc_base(int device, void **base) {
+  if (device < 0 || device >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_base[device] == nullptr) {
+    void *ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess) return err;
+    g_noalloc_base[device] = ptr;
+  }
+  *base = g_noalloc_base[device];
+  return cudaSuccess;
+}
+
+// Offsets in the static scratch of everything one epoch uses besides the
+// engine's model state (weights, KV cache, RoPE tables, resident row state).
+struct NoAllocLayout {
+  size_t io, work, sync, h, qkv, attn, act, part, av, ai, ab, total;
+};
+
+NoAllocLayout noalloc_layout(const Engine *e) {
+  const ModelDims &m = e->m;
+  NoAllocLayout l{};
+  size_t st = 0;
+  auto take = [&](size_t bytes) {
+    const size_t off = st;
+    st = align_up(st + bytes, 256);
+    return off;
+  };
+  l.io = take(sizeof(EpochIO));
+  l.work = take(sizeof(EpochWork));
+  l.sync = take(sizeof(SyncState));
+  l.h = take(static_cast<size_t>(kBatch) * m.H * 2);
+  l.qkv = take(static_cast<size_t>(kBatch) * m.Nqkv * 2);
+  l.attn = take(static_cast<size_t>(kBatch) * m.H * 2);
+  l.act = take(static_cast<size_t>(kBatch) * m.I_pad * 2);
+  l.part = take(static_cast<size_t>(e->sms) * 64 * 4);
+  l.av = take(static_cast<size_t>(e->sms) * kBatch * 4);
+  l.ai = take(static_cast<size_t>(e->sms) * kBatch * 4);
+  l.ab = take(static_cast<size_t>(e->sms) * kBatch * 4);
+  l.total = st;
+  return l;
+}
+
+}  // namespace
+
+// One greedy epoch whose scratch is the static array instead of the engine's
+// allocation; inputs and outputs are host arrays as in run_epoch.
+int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *position, const int32_t *seq_len,
+                          const int32_t *slot, const int32_t *active, const int32_t *block_table,
+                          const int32_t *control, int64_t *history, int32_t *control_out) {
+  cudaError_t err = cudaSetDevice(e->device);
+  if (err != cudaSuccess) return set_err(e, err, "noalloc set device");
+  const NoAllocLayout l = noalloc_layout(e);
+  if (l.total > kNoAllocScratchBytes) {
+    e->last_error = "cruise_epoch_run_noalloc: this model needs " + std::to_string(l.total) +
+                    " bytes of scratch, the static scratch holds " + std::to_string(kNoAllocScratchBytes);
+    return -2;
+  }
+  if ((control[2 + kBatch] & kImportFlag) != 0) {
+    e->last_error = "cruise_epoch_run_noalloc: a KV import needs the payload staging of cruise_epoch_run";
+    return -3;
+  }
+  void *base = nullptr;
+  err = noalloc_base(e->device, &base);
+  if (err != cudaSuccess) return set_err(e, err, "noalloc scratch address");
+  uint8_t *sb = static_cast<uint8_t *>(base);
+  EpochIO io;
+  std::memset(&io, 0, sizeof(io));
+  std::memcpy(io.token, token, sizeof(io.token));
+  std::memcpy(io.position, position, sizeof(io.position));
+  std::memcpy(io.seq_len, seq_len, sizeof(io.seq_len));
+  std::memcpy(io.slot, slot, sizeof(io.slot));
+  std::memcpy(io.active, active, sizeof(io.active));
+  std::memcpy(io.block_table, block_table, sizeof(int32_t) * kBatch * e->m.bpr);
+  std::memcpy(io.control, control, sizeof(io.control));
+  // every call starts from zeroed scratch: grid-barrier counters, split-partial
+  // flags, error word and the padded activation columns must read zero
+  err = cudaMemsetAsync(sb, 0, l.total, e->stream);
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(sb + l.io, &io, offsetof(EpochIO, history), cudaMemcpyHostToDevice, e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "noalloc epoch inputs");
+
+  EpochParams p{};
+  p.m = e->m;
+  p.layers = e->d_layers;
+  p.embed = e->embed;
+  p.final_norm = e->final_norm;
+  p.lm_head = e->lm_head;
+  p.rope_cos = e->rope_cos;
+  p.rope_sin = e->rope_sin;
+  p.key_cache = e->key_cache;
+  p.value_cache = e->value_cache;
+  p.h = reinterpret_cast<bf16 *>(sb + l.h);
+  p.qkv = reinterpret_cast<bf16 *>(sb + l.qkv);
+  p.attn = reinterpret_cast<bf16 *>(sb + l.attn);
+  p.act = reinterpret_cast<bf16 *>(sb + l.act);
+  p.partials = reinterpret_cast<float *>(sb + l.part);
+  p.arg_val = reinterpret_cast<float *>(sb + l.av);
+  p.arg_idx = reinterpret_cast<int32_t *>(sb + l.ai);
+  p.arg_bad = reinterpret_cast<int32_t *>(sb + l.ab);
+  p.logits = nullptr;
+  p.import_payload = nullptr;
+  p.io = reinterpret_cast<EpochIO *>(sb + l.io);
+  p.res = e->d_res;
+  p.work = reinterpret_cast<EpochWork *>(sb + l.work);
+  p.sync = reinterpret_cast<SyncState *>(sb + l.sync);
+  p.grid = e->sms;
+  p.stages = e->stages;
+  p.xs_stride = e->xs_stride;
+  p.down_xglobal = e->down_xglobal;
+  p.trace = nullptr;
+  p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
+  void *args[] = {&p};
+  err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
+                                    dim3(kThreads), args, e->smem, e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "noalloc epoch launch");
+  err = cudaMemcpyAsync(&io.history, sb + l.io + offsetof(EpochIO, history),
+                        sizeof(EpochIO) - offsetof(EpochIO, history), cudaMemcpyDeviceToHost, e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "noalloc epoch completion");
+  std::memcpy(history, io.history, sizeof(io.history));
+  std::memcpy(control_out, io.control_out, sizeof(io.control_out));
+  return 0;
+}
+
+}  // namespace cruise
+
 using cruise::BridgeEngine;
 using cruise::Engine;
 using cruise::kBatch;
@@ -904,6 +1047,20 @@ int32_t cruise_epoch_run(void *engine, const int64_t *token, const int64_t *posi
   std::lock_guard<std::mutex> lock(e->execute_mutex);
   return cruise::run_epoch(e, token, position, seq_len, slot, active, block_table, tiling, control,
                            import_payload, import_bytes, history, control_out, logits_out, forced_tokens);
+}
+
+int32_t cruise_epoch_run_noalloc(void *engine, const int64_t *token, const int64_t *position,
+                                 const int32_t *seq_len, const int32_t *slot, const int32_t *active,
+                                 const int32_t *block_table, const int32_t *control, int64_t *history,
+                                 int32_t *control_out) {
+  if (engine == nullptr || token == nullptr || position == nullptr || seq_len == nullptr || slot == nullptr ||
+      active == nullptr || block_table == nullptr || control == nullptr || history == nullptr ||
+      control_out == nullptr)
+    return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  return cruise::run_epoch_noalloc(e, token, position, seq_len, slot, active, block_table, control, history,
+                                   control_out);
 }
 
 int32_t cruise_epoch_last_timing(void *engine, double *device_us, int32_t *kernel_launches) {

@@ -162,6 +162,37 @@ int32_t cruise_epoch_run(void *engine, const int64_t *token,
                          int64_t *history, int32_t *control_out,
                          float *logits_out);
 
+/* No counterpart in the reference.  The same greedy epoch as cruise_epoch_run
+ * for callers that must not allocate device memory once they are serving:
+ * a host whose device memory is all handed to its own pool up front (a
+ * serving worker that reserves most of HBM for its KV pool at start-up, where
+ * a cudaMalloc behind its back fails or fragments the pool), or a runtime
+ * whose policy forbids allocation after warm-up.  This call allocates
+ * nothing: the epoch's scratch (inputs/outputs block, grid-barrier counters,
+ * activations, split-tile partials, argmax partials) lives in one static
+ * 1 MiB device array compiled into this library, which every GPU that loads
+ * the library holds until the process exits.  The engine's weights, KV cache
+ * and resident row state are used as by cruise_epoch_run, so both calls may
+ * be mixed on one engine.
+ * Arguments mean what they mean for cruise_epoch_run (host arrays; no tiling,
+ * forced tokens or logits).  KV imports are not accepted here.
+ * The first call on a device looks up the array's device address (once per
+ * device); make that first call before any stream capture.  Every call, on
+ * every engine of the process, shares the one array and clears it first:
+ * calls that overlap in time (two threads, two engines on one GPU) race and
+ * must be serialised by the caller.
+ * Returns 0 when the epoch ran (device status in control_out[3]), -1 for a
+ * NULL argument, -2 when the model's scratch exceeds the 1 MiB array, -3 for
+ * an import request, or a CUDA error code; cruise_epoch_last_error explains
+ * -2 and -3. */
+int32_t cruise_epoch_run_noalloc(void *engine, const int64_t *token,
+                                 const int64_t *position,
+                                 const int32_t *seq_len, const int32_t *slot,
+                                 const int32_t *active,
+                                 const int32_t *block_table,
+                                 const int32_t *control, int64_t *history,
+                                 int32_t *control_out);
+
 /* Device time of the last epoch in microseconds (CUDA events around the
  * epoch kernel) and the number of kernels it launched. */
 int32_t cruise_epoch_last_timing(void *engine, double *device_us,
