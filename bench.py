@@ -43,6 +43,12 @@ sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "tests"))
 
 METRIC = "Qwen2.5-7B-arch B=4 epoch: decode tok/s, µs/step, % HBM roofline"
+
+# DRAM traffic of one resident_epoch_kernel launch of the default workload (K=2,
+# 7B geometry), dram__bytes_read.sum + dram__bytes_write.sum from a one-pass ncu
+# capture of this bench command; reported per decode step beside the
+# algorithmic bytes.  It applies to the default K only.
+PROFILED_TRAFFIC = {"k": 2, "bytes_per_launch": 28298194688 + 21556480, "steps_per_launch": 2}
 KV_BYTES_PER_TOKEN = 28 * 4 * 128 * 2 * 2   # K and V over all layers, one position
 FALLBACK_HBM_GBS = 6650.0
 EPOCH_H2D_BYTES = 616   # EpochIO inputs (8-in ABI + forced-token table), one copy per epoch
@@ -75,18 +81,39 @@ def step_bytes(cfg, contexts: list[int]) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed
+    region: NVML queries every 10 ms from a thread (read-only), else
+    nvidia-smi at its 100 ms floor."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, device: int) -> None:
         self.device = device
         self.proc = None
+        self.nvml = None
         self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self.stop = threading.Event()
 
     def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.device)
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            deadline = time.time() + 2.0
+            while not self.samples and time.time() < deadline:   # the first sample precedes the timed region
+                time.sleep(0.002)
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
@@ -99,11 +126,32 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                reasons = get_reasons(self.handle)
+                self.samples.append((float(sm), float(mx), int(reasons)))
+            except Exception:
+                break
+            time.sleep(0.01)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml is not None:
+            self.thread.join(timeout=1)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -113,6 +161,11 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
+        if self.samples:
+            reasons = {name for name, bit in self.REASONS.items() if any(r & bit for _, _, r in self.samples)}
+            return {"sm_mhz": statistics.median(sm for sm, _, _ in self.samples),
+                    "sm_max_mhz": self.samples[-1][1], "reasons": sorted(reasons),
+                    "samples": len(self.samples), "source": "nvml, 10 ms"}
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in self.lines:
@@ -306,7 +359,9 @@ def run_gpu(args) -> None:
                 "peak_kind": peak_kind,
                 "unit": "GB/s",
                 "frac": round(achieved_gbs / peak, 4),
-                "traffic": None,
+                "traffic": (PROFILED_TRAFFIC["bytes_per_launch"] // PROFILED_TRAFFIC["steps_per_launch"]
+                            if args.k == PROFILED_TRAFFIC["k"] and not args.layers and not args.vocab else None),
+                "traffic_unit": "bytes per decode step (ncu dram read + write)",
                 "kernel": "resident_epoch_kernel",
                 "bytes_per_decode_step": step_bytes_total // model_calls,
             },

@@ -56,7 +56,7 @@ struct SynthMap {
   int64_t rows0, rows1; // q rows / k rows (kQkvRows); valid rows (kRowsPad)
   int64_t dst_cols;     // packed row length (kDownPad)
   int32_t tiled;        // destination is a tiled matrix with dst_cols columns
-  int32_t pad;
+  int32_t kc;           // its tile width
 };
 
 __device__ __forceinline__ uint16_t synth_value(uint64_t key, int64_t index, float scale) {
@@ -73,8 +73,12 @@ __global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_
        d += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int64_t e = d;   // logical row-major index of the packed matrix
     if (map.tiled) {
-      int64_t n, k;
-      tiled_coords(d, map.dst_cols, n, k);
+      const int64_t kc = map.kc;
+      const int64_t tile = d / (kRows * kc), rem = d % (kRows * kc);
+      const int64_t r = rem / kc, pu = (rem % kc) >> 3, el = rem & 7;
+      const int64_t KT = map.dst_cols / kc;
+      const int64_t n = (tile / KT) * kRows + r;
+      const int64_t k = (tile % KT) * kc + ((pu ^ (r & 7)) << 3) + el;
       e = n * map.dst_cols + k;
     }
     int32_t id = map.ids[0];
@@ -93,7 +97,6 @@ __global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_
         const int64_t blk = R / 16, rr = R % 16;
         id = rr < 8 ? map.ids[0] : map.ids[1];
         idx = (blk * 8 + (rr & 7)) * map.cols + c;
-        zero = blk * 8 + (rr & 7) >= map.rows0;   // padding rows past the intermediate size
         break;
       }
       case kDownPad: {
@@ -126,12 +129,12 @@ __device__ __forceinline__ int64_t packed_row(int32_t map, int64_t i, int64_t of
 // Moves one canonical [rows][cols] tensor into (to_tiled) or out of a tiled
 // matrix with K columns and tile width kc.
 __global__ void tile_copy_kernel(uint16_t *tiled, uint16_t *canonical, int64_t rows, int64_t cols, int32_t map,
-                                 int64_t offset, int64_t K, int32_t to_tiled) {
+                                 int64_t offset, int64_t K, int32_t kc, int32_t to_tiled) {
   const int64_t count = rows * cols;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < count;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t i = e / cols, c = e % cols;
-    const int64_t dst = tiled_offset(packed_row(map, i, offset), c, K);
+    const int64_t dst = tiled_offset(packed_row(map, i, offset), c, K, kc);
     if (to_tiled) {
       tiled[dst] = canonical[e];
     } else {
@@ -153,8 +156,9 @@ struct Engine {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int sms = 0;
   int stages = 0;
-  int xslots = 0;
+  int xs_stride = 0;
   uint32_t l2_ahead = 0;   // bytes of L2 run-ahead per CTA (CRUISE_L2_AHEAD_KB)
+  int down_xglobal = 0;
   uint64_t *trace = nullptr;     // per-launch phase timestamps (optional)
   bool trace_on = false;
   size_t smem = 0;
@@ -209,9 +213,7 @@ bool valid_config(const CruiseModelConfig &c) {
   if (c.vocab < 2) return false;
   if (c.block_size < 1 || c.blocks_per_row < 1 || c.blocks_per_row > kMaxBlocksPerRow) return false;
   if (c.num_blocks < kBatch * c.blocks_per_row || c.num_blocks > 256) return false;
-  // projection rows come in 128-row tiles; RMSNorm staging holds K <= 4096
-  if (c.hidden % kTileRows != 0 || c.hidden > 4096) return false;
-  if (((2 * c.num_kv_heads * c.head_dim) % kTileRows) != 0) return false;
+  if (((2 * c.num_kv_heads * c.head_dim) % kRows) != 0) return false;
   // Adler-32 splits a block over 256 threads in 16-byte pieces
   if ((static_cast<int64_t>(c.block_size) * c.num_kv_heads * c.head_dim * 2) % (256 * 16) != 0) return false;
   if (c.configured_eos < 0 || c.configured_eos >= c.vocab) return false;
@@ -229,7 +231,7 @@ void fill_dims(Engine *e) {
   m.I = c.intermediate;
   m.I_pad = static_cast<int32_t>(align_up(c.intermediate, 64));
   m.V = c.vocab;
-  m.V_pad = static_cast<int32_t>(align_up(c.vocab, kTileRows));
+  m.V_pad = static_cast<int32_t>(align_up(c.vocab, kRows));
   m.Nqkv = c.hidden + 2 * c.num_kv_heads * c.head_dim;
   m.eps = c.rms_eps;
   m.sqrt_d = static_cast<float>(std::sqrt(static_cast<double>(c.head_dim)));
@@ -303,28 +305,28 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
     destroy_engine(e);
     return nullptr;
   }
+  // shared memory geometry: the activation rows in smem hold the widest input of
+  // the projections that stage it there; the down projection reads its input
+  // from L2 instead when it runs one 64-wide k-step per consumer warp.
+  e->down_xglobal = pick_kc(m.I_pad) == 64 * kConsumerWarps;
+  const int kmax = e->down_xglobal ? m.H : std::max(m.H, m.I_pad);
+  e->xs_stride = kmax + 8;
   {
     const char *env = std::getenv("CRUISE_L2_AHEAD_KB");
     const long kb = env != nullptr ? std::strtol(env, nullptr, 10) : kDefaultL2AheadKb;
     e->l2_ahead = static_cast<uint32_t>(std::min(std::max(kb, 0L), 4096L)) * 1024u;
   }
-  // shared memory geometry: the activation chunks hold the most any CTA's range
-  // of any projection uses; the attention unit's and the checksum's scratch
-  // alias them
-  {
-    const int shapes[5][2] = {{m.Nqkv, m.H}, {m.H, m.H}, {2 * m.I_pad, m.H}, {m.H, m.I_pad}, {m.V_pad, m.H}};
-    int need = 4;   // the Adler-32 block reduction: 2 x 256 u64
-    for (const auto &nk : shapes)
-      for (int c = 0; c < e->sms; ++c) need = std::max(need, xslots_needed(tile_range(nk[0], nk[1], c, e->sms)));
-    const size_t attn = attn_scratch_bytes(m.d, m.C);
-    need = std::max(need, static_cast<int>((attn + kXSlotBytes - 1) / kXSlotBytes));
-    e->xslots = need;
+  // the attention unit's scratch aliases the activation rows and the reduction ring
+  if (attn_scratch_bytes(m.d, m.C) >
+      static_cast<size_t>(kBatch) * e->xs_stride * 2 + static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4) {
+    destroy_engine(e);
+    return nullptr;
   }
   const size_t limit = prop.sharedMemPerBlockOptin;
   int stages = kMaxStages;
-  while (stages > 2 && smem_bytes(stages, e->xslots) > limit) --stages;
+  while (stages > 2 && smem_bytes(stages, e->xs_stride) > limit) --stages;
   e->stages = stages;
-  e->smem = smem_bytes(stages, e->xslots);
+  e->smem = smem_bytes(stages, e->xs_stride);
   if (e->smem > limit) { *status = 5; destroy_engine(e); return nullptr; }
   if (cudaFuncSetAttribute(resident_epoch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(e->smem)) != cudaSuccess) {
@@ -354,7 +356,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
     lo[l].qkv_w = take(static_cast<int64_t>(m.Nqkv) * H);
     lo[l].qkv_b = take(m.Nqkv);
     lo[l].o_w = take(H * H);
-    lo[l].gu_w = take(2LL * m.I_pad * H);
+    lo[l].gu_w = take(2LL * m.I * H);
     lo[l].down_w = take(H * m.I_pad);
   }
   const size_t off_norm = take(H);
@@ -388,7 +390,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   const size_t o_cos = take2(static_cast<size_t>(m.C) * m.d * 2), o_sin = take2(static_cast<size_t>(m.C) * m.d * 2);
   const size_t o_h = take2(kBatch * H * 2), o_qkv = take2(static_cast<size_t>(kBatch) * m.Nqkv * 2);
   const size_t o_attn = take2(kBatch * H * 2), o_act = take2(static_cast<size_t>(kBatch) * m.I_pad * 2);
-  const size_t o_part = take2(static_cast<size_t>(e->sms) * kPartialFloats * 4);
+  const size_t o_part = take2(static_cast<size_t>(e->sms) * 64 * 4);
   const size_t o_av = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ai = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ab = take2(static_cast<size_t>(e->sms) * kBatch * 4);
@@ -491,6 +493,7 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
   void *staging = nullptr;
   err = cudaMalloc(&staging, bytes);
   if (err != cudaSuccess) return set_err(e, err, "weight staging");
+  const int kc = pick_kc(static_cast<int>(tp.K));
   const int64_t count = tp.rows * tp.cols;
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148LL * 64));
   if (to_device) {
@@ -498,14 +501,14 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
     if (err == cudaSuccess) {
       tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
                                                       static_cast<uint16_t *>(staging), tp.rows, tp.cols,
-                                                      tp.row_map, tp.offset, tp.K, 1);
+                                                      tp.row_map, tp.offset, tp.K, kc, 1);
       err = cudaGetLastError();
       if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
     }
   } else {
     tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
                                                     static_cast<uint16_t *>(staging), tp.rows, tp.cols,
-                                                    tp.row_map, tp.offset, tp.K, 0);
+                                                    tp.row_map, tp.offset, tp.K, kc, 0);
     err = cudaGetLastError();
     if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
     if (err == cudaSuccess) err = copy_sync(e, host, staging, bytes, cudaMemcpyDeviceToHost);
@@ -526,7 +529,7 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
         reinterpret_cast<uint16_t *>(dst), count, map, seed, scale);
   };
   auto plain = [&](int id) { SynthMap s{}; s.mode = kPlain; s.ids[0] = id; return s; };
-  auto tile = [&](SynthMap s, int64_t K) { s.tiled = 1; s.dst_cols = K; return s; };
+  auto tile = [&](SynthMap s, int64_t K) { s.tiled = 1; s.dst_cols = K; s.kc = pick_kc(static_cast<int>(K)); return s; };
   const int L = m.L;
   launch(e->embed, static_cast<int64_t>(m.V) * H, plain(0));
   for (int l = 0; l < L; ++l) {
@@ -544,8 +547,8 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
     SynthMap o = plain(base + 8);
     launch(const_cast<bf16 *>(lw.o_w), H * H, tile(o, H));
     SynthMap gu{};
-    gu.mode = kGateUp; gu.ids[0] = base + 9; gu.ids[1] = base + 10; gu.cols = H; gu.rows0 = m.I;
-    launch(const_cast<bf16 *>(lw.gu_w), 2LL * m.I_pad * H, tile(gu, H));
+    gu.mode = kGateUp; gu.ids[0] = base + 9; gu.ids[1] = base + 10; gu.cols = H;
+    launch(const_cast<bf16 *>(lw.gu_w), 2LL * m.I * H, tile(gu, H));
     SynthMap dn{};
     dn.mode = kDownPad; dn.ids[0] = base + 11; dn.cols = m.I;
     dn = tile(dn, m.I_pad);
@@ -631,7 +634,8 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   p.sync = e->d_sync;
   p.grid = e->sms;
   p.stages = e->stages;
-  p.xslots = e->xslots;
+  p.xs_stride = e->xs_stride;
+  p.down_xglobal = e->down_xglobal;
   p.trace = e->trace_on ? e->trace : nullptr;
   if (e->trace_on) cudaMemsetAsync(e->trace, 0, 5 * kTraceMax * sizeof(uint64_t), e->stream);
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
@@ -867,7 +871,7 @@ NoAllocLayout noalloc_layout(const Engine *e) {
   l.qkv = take(static_cast<size_t>(kBatch) * m.Nqkv * 2);
   l.attn = take(static_cast<size_t>(kBatch) * m.H * 2);
   l.act = take(static_cast<size_t>(kBatch) * m.I_pad * 2);
-  l.part = take(static_cast<size_t>(e->sms) * kPartialFloats * 4);
+  l.part = take(static_cast<size_t>(e->sms) * 64 * 4);
   l.av = take(static_cast<size_t>(e->sms) * kBatch * 4);
   l.ai = take(static_cast<size_t>(e->sms) * kBatch * 4);
   l.ab = take(static_cast<size_t>(e->sms) * kBatch * 4);
@@ -940,7 +944,8 @@ int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *positi
   p.sync = reinterpret_cast<SyncState *>(sb + l.sync);
   p.grid = e->sms;
   p.stages = e->stages;
-  p.xslots = e->xslots;
+  p.xs_stride = e->xs_stride;
+  p.down_xglobal = e->down_xglobal;
   p.trace = nullptr;
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
   p.l2_ahead = e->l2_ahead;

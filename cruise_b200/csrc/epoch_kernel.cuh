@@ -11,25 +11,21 @@
 // CTA layout: warps 0-7 are consumers (math, epilogues, control), warp 8 is
 // the weight producer.  The producer streams every weight tile this CTA will
 // consume, in consumption order, from HBM into a ring of shared-memory stages
-// with 1-D bulk (TMA) copies completed on mbarriers, and keeps a window of
-// L2 prefetches ahead of them.  Weights do not depend on activations, so it
-// keeps streaming across the grid barriers that separate phases; the
-// consumers only wait for activations.
+// with 1-D bulk (TMA) copies completed on mbarriers.  Weights do not depend on
+// activations, so it keeps prefetching across the grid barriers that separate
+// phases; the consumers only wait for activations.
 //
-// Projection (GEMV) phases: y[4,N] = x[4,K] . W[N,K]^T on the 5th-generation
-// tensor cores.  W is stored as 16 KB tiles of 128 rows x 64 k in the
-// canonical K-major 128-byte-swizzled layout, in stream order; the 4
-// activation rows, padded to 8, are staged per phase as 1 KB swizzled chunks
-// of 64 k.  One thread (warp 4, lane 0) issues tcgen05.mma (M = 128, N = 8,
-// K = 16) straight from the shared-memory descriptors into one of four
-// accumulator sets in tensor memory and commits each finished stage back to
-// the producer's ring and each finished row-group segment to the epilogue.
-// Warps 0-3 (the 128 TMEM lanes, one weight row per thread) read the
-// accumulators with tcgen05.ld and run the epilogue.  The tiles of a phase
-// are split into equal contiguous ranges over all CTAs ("stream-K"): a row
-// group may span several neighbouring CTAs; every CTA whose range starts
-// inside a group publishes that first segment as an fp32 partial, and the CTA
-// holding the group's first tile adds them in CTA order and finishes the group.
+// Projection (GEMV) phases: y[4,N] = x[4,K] . W[N,K]^T.  W is cut into tiles of
+// 16 rows x kc columns; the tiles of a phase are split into equal contiguous
+// ranges over the CTAs ("stream-K"), so a row group may be split between two
+// neighbouring CTAs: the upper part publishes fp32 partial sums, the lower
+// part adds them in fixed order and runs the epilogue.  Inside a tile the 8
+// consumer warps each take 64 columns and issue bf16 mma.sync m16n8k16 with W
+// as the A operand and the 4 activation rows padded to n = 8 as B (the padding
+// costs nothing: the phase is bandwidth bound).  A dot product may sum its k
+// terms in any order, so each thread loads 16 contiguous weights per row with
+// 128-bit shared loads and feeds them to four MMAs under one k permutation
+// that the A and B fragments share.
 //
 // Every cross-CTA wait (grid barrier, split partial flag) and every mbarrier
 // wait is bounded by a timeout; on expiry the kernel records status 207 and
@@ -46,37 +42,32 @@
 namespace cruise {
 
 enum GemvKind : int32_t { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
-enum XMode : int32_t { kXNorm = 0, kXCopy = 1 };
+enum XMode : int32_t { kXNorm = 0, kXCopy = 1, kXGlobal = 2 };
 
 struct Gemv {
   const bf16 *W;
   const bf16 *bias;      // kQKV only
   const bf16 *norm_w;    // kXNorm only
   const bf16 *xsrc;      // activation source, [4][xsrc_stride]
-  int32_t N, K, kind;
+  int32_t N, K, kc, kind;
   int32_t xmode;
   int32_t xsrc_stride;
   int32_t embed_src;     // 1: the norm source is embed[token[b]] (layer 0)
 };
 
-// Element offset of logical (n, k) inside a tiled matrix with K columns
-// (K a multiple of 64, rows padded to a multiple of 128): tiles in
-// [row group][k tile] order; inside a tile row r holds its 64 k as eight
-// 16-byte units, unit u stored at position u ^ (r & 7).
-__host__ __device__ inline int64_t tiled_offset(int64_t n, int64_t k, int64_t K) {
-  const int64_t rg = n / kTileRows, r = n % kTileRows;
-  const int64_t kt = k / kTileK, kin = k % kTileK;
-  const int64_t unit = (kin >> 3) ^ (r & 7);
-  return ((rg * (K / kTileK) + kt) * kTileRows + r) * kTileK + unit * 8 + (kin & 7);
+__host__ __device__ inline int pick_kc(int K) {
+  // largest power of two in 64..kMaxKc that divides K (K is a multiple of 64)
+  for (int kc = kMaxKc; kc >= 64; kc >>= 1)
+    if (K % kc == 0) return kc;
+  return 64;
 }
 
-// Inverse of tiled_offset: the logical (n, k) stored at element d.
-__host__ __device__ inline void tiled_coords(int64_t d, int64_t K, int64_t &n, int64_t &k) {
-  const int64_t tile = d / (kTileRows * kTileK), rem = d % (kTileRows * kTileK);
-  const int64_t r = rem / kTileK, pu = (rem % kTileK) >> 3, el = rem & 7;
-  const int64_t KT = K / kTileK;
-  n = (tile / KT) * kTileRows + r;
-  k = (tile % KT) * kTileK + ((pu ^ (r & 7)) << 3) + el;
+// Element offset of logical (n, k) inside a tiled matrix with K columns.
+__host__ __device__ inline int64_t tiled_offset(int64_t n, int64_t k, int64_t K, int kc) {
+  const int64_t rg = n / kRows, r = n % kRows;
+  const int64_t kk = k / kc, kin = k % kc;
+  const int64_t unit = (kin >> 3) ^ (r & 7);
+  return ((rg * (K / kc) + kk) * kRows + r) * kc + unit * 8 + (kin & 7);
 }
 
 __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int kind) {
@@ -98,15 +89,16 @@ __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int k
         g.xsrc_stride = m.H;
         break;
       case kGU:
-        g.W = lw.gu_w; g.N = 2 * m.I_pad; g.K = m.H; g.xmode = kXNorm; g.xsrc = p.h;
+        g.W = lw.gu_w; g.N = 2 * m.I; g.K = m.H; g.xmode = kXNorm; g.xsrc = p.h;
         g.xsrc_stride = m.H; g.norm_w = lw.w_post;
         break;
       default:  // kDown
-        g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = kXCopy;
+        g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = p.down_xglobal ? kXGlobal : kXCopy;
         g.xsrc = p.act; g.xsrc_stride = m.I_pad;
         break;
     }
   }
+  g.kc = pick_kc(g.K);
   return g;
 }
 
@@ -116,13 +108,15 @@ struct TileRange {
   int32_t ctas;    // CTAs that take part
 };
 
-// Equal contiguous tile ranges over min(tiles, grid) CTAs; a row group may
-// span several neighbouring CTAs.
-__host__ __device__ __forceinline__ TileRange tile_range(int N, int K, int cta, int grid) {
+// Equal contiguous tile ranges.  At most one CTA per row group of the phase
+// takes part, so every range holds at least one full row group's worth of
+// tiles and a row group is split between at most two neighbouring CTAs.
+__device__ __forceinline__ TileRange tile_range(const Gemv &g, int cta, int grid) {
   TileRange r;
-  r.KT = K / kTileK;
-  const int64_t T = static_cast<int64_t>(N / kTileRows) * r.KT;
-  const int64_t ctas = T < grid ? T : grid;
+  r.KT = g.K / g.kc;
+  const int64_t groups = g.N / kRows;
+  const int64_t T = groups * r.KT;
+  const int64_t ctas = groups < grid ? groups : grid;
   r.ctas = static_cast<int32_t>(ctas);
   if (cta >= ctas) {
     r.t0 = r.t1 = 0;
@@ -131,21 +125,6 @@ __host__ __device__ __forceinline__ TileRange tile_range(int N, int K, int cta, 
     r.t1 = T * (cta + 1) / ctas;
   }
   return r;
-}
-
-__device__ __forceinline__ TileRange tile_range(const Gemv &g, int cta, int grid) {
-  return tile_range(g.N, g.K, cta, grid);
-}
-
-// Activation chunks a CTA stages for its range: every chunk of K when the range
-// covers a whole row group's worth of tiles, else one per tile of the range.
-__host__ __device__ __forceinline__ int xslots_needed(const TileRange &tr) {
-  const int64_t n = tr.t1 - tr.t0;
-  return static_cast<int>(n >= tr.KT ? tr.KT : n);
-}
-
-__device__ __forceinline__ int xslot_of_tile(const TileRange &tr, int64_t t) {
-  return static_cast<int>(tr.t1 - tr.t0 >= tr.KT ? t % tr.KT : t - tr.t0);
 }
 
 // The step program: per layer QKV, attention, O, gate/up, down; then lm_head
@@ -170,59 +149,53 @@ __device__ __forceinline__ uint64_t globaltimer() {
 
 // ---- shared memory map ------------------------------------------------------------
 struct Smem {
-  uint8_t *ring;           // stages x kStageBytes (1024-byte aligned)
-  uint8_t *xs;             // xslots x 1 KB swizzled activation chunks (attention and checksum scratch alias it)
+  uint8_t *ring;           // stages x kStageBytes
+  bf16 *xs;                // [4][xs_stride]  (attention and checksum scratch alias it)
+  float *red;              // [kRedSlots][8 warps][64] row-group partial sums
   uint64_t *full;          // [kMaxStages]  weight stage landed
-  uint64_t *empty;         // [kMaxStages]  weight stage consumed by the tensor core
-  uint64_t *acc_full;      // [kAccSets]    accumulator set complete (tcgen05.commit)
-  uint64_t *acc_empty;     // [kAccSets]    accumulator set read by the 4 epilogue warps
-  uint64_t *drain;         // every MMA of the launch completed
-  uint32_t *tmem;          // TMEM base address written by tcgen05.alloc
+  uint64_t *empty;         // [kMaxStages]  weight stage consumed
+  uint64_t *red_full;      // [kRedSlots]   partials written by the 8 consumer warps
+  uint64_t *red_empty;     // [kRedSlots]   partials read by the epilogue warp
+  uint64_t *phase_done;    // epilogue warp finished the current projection phase
   float *nrm;              // [8][4] norm partial sums, then [4] inverse rms at +32
   float *best_val;         // [8]
   int32_t *best_idx;       // [8]
   int32_t *best_bad;       // [8]
   int32_t *misc;           // [16] small broadcast values
-  volatile int *prod_ctl;  // producer control: -2 wait, >= s run step s, -1 stop
+  volatile int *prod_ctl;  // producer / epilogue control: -2 wait, >= s run step s, -1 stop
+  volatile int *phase_started;  // sequence number of the projection phase the consumers began
   int64_t *row_pos;        // [4] row state of the current step (attention)
   int32_t *row_len;        // [4]
   int32_t *row_slot;       // [4]
   int32_t *row_act;        // [4]
   int32_t *bt;             // [4][kMaxBlocksPerRow] block table of the epoch
-  float *lm_val;           // [4 warps][4] lm_head argmax partials of the epilogue warps
-  int32_t *lm_idx;         // [4][4]
-  int32_t *lm_bad;         // [4][4]
 };
 
-constexpr size_t kSmemAlign = 1024;   // swizzle atoms of the UMMA operands
-constexpr size_t kSmemTail = 2 * kMaxStages * 8 + 2 * kAccSets * 8 + 8 + 8 + 40 * 4 + 24 * 4 + 16 * 4 + 16 +
-                             kBatch * 8 + 3 * kBatch * 4 + kBatch * kMaxBlocksPerRow * 4 + 3 * 16 * 4;
-
-__host__ __device__ inline size_t smem_bytes(int stages, int xslots) {
-  return kSmemAlign + static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(xslots) * kXSlotBytes +
-         kSmemTail;
+__host__ __device__ inline size_t smem_bytes(int stages, int xs_stride) {
+  return static_cast<size_t>(stages) * kStageBytes + static_cast<size_t>(kBatch) * xs_stride * 2 +
+         static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4 + 2 * kMaxStages * 8 +
+         2 * kRedSlots * 8 + 8 + 40 * 4 + 24 * 4 + 16 * 4 + 16 + kBatch * 8 + 3 * kBatch * 4 +
+         kBatch * kMaxBlocksPerRow * 4;
 }
 
-__device__ __forceinline__ Smem carve_smem(uint8_t *raw, const EpochParams &p) {
+__device__ __forceinline__ Smem carve_smem(uint8_t *base, const EpochParams &p) {
   Smem s;
-  // the dynamic window's shared address rounded up to the swizzle alignment
-  const uint32_t a = smem_u32(raw);
-  uint8_t *ptr = raw + ((kSmemAlign - (a & (kSmemAlign - 1))) & (kSmemAlign - 1));
+  uint8_t *ptr = base;
   s.ring = ptr;
   ptr += static_cast<size_t>(p.stages) * kStageBytes;
-  s.xs = ptr;
-  ptr += static_cast<size_t>(p.xslots) * kXSlotBytes;
+  s.xs = reinterpret_cast<bf16 *>(ptr);
+  ptr += static_cast<size_t>(kBatch) * p.xs_stride * 2;
+  s.red = reinterpret_cast<float *>(ptr);
+  ptr += static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4;
   s.full = reinterpret_cast<uint64_t *>(ptr);
   ptr += kMaxStages * 8;
   s.empty = reinterpret_cast<uint64_t *>(ptr);
   ptr += kMaxStages * 8;
-  s.acc_full = reinterpret_cast<uint64_t *>(ptr);
-  ptr += kAccSets * 8;
-  s.acc_empty = reinterpret_cast<uint64_t *>(ptr);
-  ptr += kAccSets * 8;
-  s.drain = reinterpret_cast<uint64_t *>(ptr);
-  ptr += 8;
-  s.tmem = reinterpret_cast<uint32_t *>(ptr);
+  s.red_full = reinterpret_cast<uint64_t *>(ptr);
+  ptr += kRedSlots * 8;
+  s.red_empty = reinterpret_cast<uint64_t *>(ptr);
+  ptr += kRedSlots * 8;
+  s.phase_done = reinterpret_cast<uint64_t *>(ptr);
   ptr += 8;
   s.nrm = reinterpret_cast<float *>(ptr);
   ptr += 40 * 4;
@@ -235,6 +208,7 @@ __device__ __forceinline__ Smem carve_smem(uint8_t *raw, const EpochParams &p) {
   s.misc = reinterpret_cast<int32_t *>(ptr);
   ptr += 16 * 4;
   s.prod_ctl = reinterpret_cast<volatile int *>(ptr);
+  s.phase_started = reinterpret_cast<volatile int *>(ptr + 4);
   ptr += 16;
   s.row_pos = reinterpret_cast<int64_t *>(ptr);
   ptr += kBatch * 8;
@@ -242,9 +216,6 @@ __device__ __forceinline__ Smem carve_smem(uint8_t *raw, const EpochParams &p) {
   s.row_slot = s.row_len + kBatch;
   s.row_act = s.row_slot + kBatch;
   s.bt = s.row_act + kBatch;
-  s.lm_val = reinterpret_cast<float *>(s.bt + kBatch * kMaxBlocksPerRow);
-  s.lm_idx = reinterpret_cast<int32_t *>(s.lm_val + 16);
-  s.lm_bad = s.lm_idx + 16;
   return s;
 }
 
@@ -390,7 +361,7 @@ struct L2RunAhead {
         const TileRange tr = tile_range(g, blockIdx.x, p.grid);
         t = tr.t0;
         t1 = tr.t1;
-        tile_bytes = kTileBytes;
+        tile_bytes = static_cast<int64_t>(kRows) * g.kc * 2;
         W = reinterpret_cast<const uint8_t *>(g.W);
         continue;
       }
@@ -422,8 +393,8 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
       if (kind < 0) continue;
       const Gemv g = make_gemv(p, ph / 5, kind);
       const TileRange tr = tile_range(g, blockIdx.x, p.grid);
-      const int64_t tile_elems = static_cast<int64_t>(kTileRows) * kTileK;
-      const int per_stage = kStageBytes / kTileBytes;
+      const int64_t tile_elems = static_cast<int64_t>(kRows) * g.kc;
+      const int per_stage = kStageBytes / (kRows * g.kc * 2);
       for (int64_t t = tr.t0; t < tr.t1; t += per_stage) {
         const int n = static_cast<int>(tr.t1 - t < per_stage ? tr.t1 - t : per_stage);
         if (lane == 0) {
@@ -458,410 +429,101 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
 }
 
 // ---- consumer: activation prologue ------------------------------------------------------
-// Stages the projection input of this CTA's tile range as swizzled 1 KB chunks
-// (the B operand: 8 rows x 64 k, row b at b*128 bytes with its 16-byte units
-// permuted u ^ b; rows 4-7 zero): the RMSNorm of the residual stream
-// (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU
-// output).  Only the chunks the range uses are written.
-__device__ void stage_x(const EpochParams &p, const Smem &s, const Gemv &g, const TileRange &tr) {
+// Fills s.xs[4][K] with the projection input: RMSNorm of the residual stream
+// (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU output).
+__device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
   const int tid = threadIdx.x;
   const int K = g.K;
   const int K8 = K / 8;
-  const int KT = tr.KT;
-  const int nslots = xslots_needed(tr);
-  const bool all = tr.t1 - tr.t0 >= KT;
-  const int first = static_cast<int>(tr.t0 % KT);
-  auto put = [&](int sl, int b, int c, const uint4 &v) {
-    *reinterpret_cast<uint4 *>(s.xs + sl * kXSlotBytes + b * 128 + ((c ^ b) << 4)) = v;
-  };
-  // padding rows 4-7 of every chunk in use
-  for (int i = tid; i < nslots * 32; i += kConsumerThreads)
-    put(i >> 5, 4 + ((i >> 3) & 3), i & 7, make_uint4(0, 0, 0, 0));
   if (g.xmode == kXCopy) {
-    for (int i = tid; i < nslots * 32; i += kConsumerThreads) {
-      const int sl = i >> 5, b = (i >> 3) & 3, c = i & 7;
-      const int j = all ? sl : (first + sl) % KT;
-      const uint4 v = __ldcg(
-          reinterpret_cast<const uint4 *>(g.xsrc + static_cast<size_t>(b) * g.xsrc_stride + j * kTileK) + c);
-      put(sl, b, c, v);
-    }
-  } else {
-    // One pass over L2: each thread keeps its (at most 2 x 8) elements of every
-    // row and its norm weights in registers (K <= 4096), reduces the fp32 sums
-    // of squares, then normalises from registers.
-    const bf16 *rows[kBatch];
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      rows[b] = g.embed_src ? p.embed + __ldcg(&p.work->token[b]) * static_cast<int64_t>(K)
-                            : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
-    }
-    uint4 v[2][kBatch];
-    uint4 wv[2];
-    float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int k8 = tid + j * kConsumerThreads;
-      wv[j] = k8 < K8 ? __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b)
-        v[j][b] = k8 < K8 ? __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __bfloat1622float2(h2[q]);
-          ss[b] = __fadd_rn(ss[b], __fmul_rn(f.x, f.x));
-          ss[b] = __fadd_rn(ss[b], __fmul_rn(f.y, f.y));
-        }
-      }
-    }
-    const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], off);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
+    for (int i = tid; i < kBatch * K8; i += kConsumerThreads) {
+      const int b = i / K8, k8 = i % K8;
+      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(g.xsrc + static_cast<size_t>(b) * g.xsrc_stride) + k8);
+      *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = v;
     }
     named_sync(1, kConsumerThreads);
-    if (tid < kBatch) {
-      float total = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + tid];
-      // mean = sum / K; rsqrt = 1 / sqrt(mean + eps), each IEEE-rounded as on the CPU
-      const float var = __fdiv_rn(total, static_cast<float>(K));
-      s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
-    }
-    named_sync(1, kConsumerThreads);
+    return;
+  }
+  // One pass over L2: each thread keeps its (at most 2 x 8) elements of every
+  // row in registers (K <= 4096), reduces the fp32 sums of squares, then
+  // normalises from registers.
+  const bf16 *rows[kBatch];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int k8 = tid + j * kConsumerThreads;
-      if (k8 >= K8) continue;
-      const int chunk = k8 >> 3, c = k8 & 7;
-      int sl = chunk;
-      if (!all) {
-        sl = chunk - first < 0 ? chunk - first + KT : chunk - first;
-        if (sl >= nslots) continue;   // not used by this range
-      }
-      const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv[j]);
+  for (int b = 0; b < kBatch; ++b) {
+    rows[b] = g.embed_src ? p.embed + __ldcg(&p.work->token[b]) * static_cast<int64_t>(K)
+                          : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
+  }
+  uint4 v[2][kBatch];
+  float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const float r = s.nrm[32 + b];
-        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
-        uint4 o;
-        __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 hf = __bfloat1622float2(h2[q]);
-          const float2 wf = __bfloat1622float2(w2[q]);
-          const float nx = rbf(__fmul_rn(hf.x, r));   // (h * rsqrt).to(bf16)
-          const float ny = rbf(__fmul_rn(hf.y, r));
-          o2[q] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));  // * weight
-        }
-        put(sl, b, c, o);
+    for (int b = 0; b < kBatch; ++b) {
+      v[j][b] = k8 < K8 ? __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8) : make_uint4(0, 0, 0, 0);
+      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
+        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.x, f.x));
+        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.y, f.y));
       }
     }
   }
-  // the chunks are read by the tensor core (async proxy)
-  fence_proxy_async_smem();
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
+  }
+  named_sync(1, kConsumerThreads);
+  if (tid < kBatch) {
+    float total = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + tid];
+    // mean = sum / K; rsqrt = 1 / sqrt(mean + eps), each IEEE-rounded as on the CPU
+    const float var = __fdiv_rn(total, static_cast<float>(K));
+    s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
+  }
+  named_sync(1, kConsumerThreads);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+    if (k8 >= K8) continue;
+    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8);
+    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const float r = s.nrm[32 + b];
+      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
+      uint4 o;
+      __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 hf = __bfloat1622float2(h2[q]);
+        const float2 wf = __bfloat1622float2(w2[q]);
+        const float nx = rbf(__fmul_rn(hf.x, r));   // (h * rsqrt).to(bf16)
+        const float ny = rbf(__fmul_rn(hf.y, r));
+        o2[q] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));  // * weight
+      }
+      *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = o;
+    }
+  }
   named_sync(1, kConsumerThreads);
 }
 
-// ---- MMA issuer (warp 4, lane 0): one projection phase -----------------------------------------
-// For each tile: 4 x tcgen05.mma (K = 16 each) of the 128-row weight tile
-// against the staged activation chunk into the 4 sub-accumulators of the
-// current set; the first tile of a row-group segment overwrites them.  A
-// finished stage is committed to the producer's `empty` barrier, a finished
-// segment to the epilogue's `acc_full` barrier.
-//
-// This one thread is on the critical path of every tile and each branch or
-// barrier operation after an MMA costs it tens of cycles, so a stage whose two
-// tiles lie inside one row-group segment (and do not end it) runs as straight
-// code: wait, 8 MMAs, commit.  Segment ends, segment starts and the range's
-// last stage take the general path.  After a failed wait the issuer stops
-// (the launch is aborting).
-__device__ __forceinline__ bool wait_shared(const EpochParams &p, uint32_t bar, uint32_t parity, uint32_t where) {
-  if (mbar_try_u32(bar, parity)) return true;
-  const uint64_t deadline = globaltimer() + p.timeout_ns;
-  for (uint32_t polls = 1;; ++polls) {
-    if (mbar_try_u32(bar, parity)) return true;
-    if ((polls & 15) == 0) {
-      if (aborted(p)) return false;
-      if (globaltimer() > deadline) {
-        raise_error(p, where);
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void advance_by(RingCursor &c, int n, int size) {
-  const int total = static_cast<int>(c.slot) + n;
-  c.slot = static_cast<uint32_t>(total % size);
-  c.parity ^= static_cast<uint32_t>((total / size) & 1);
-}
-
-__device__ void mma_issue(const EpochParams &p, const Smem &s, const TileRange &tr, RingCursor &ring_io,
-                          RingCursor &acc_io) {
-  static_assert(kStageBytes == 2 * kTileBytes, "the straight path issues two tiles per stage");
-  constexpr uint32_t kTileDesc = kTileBytes >> 4, kSlotDesc = kXSlotBytes >> 4;
-  const uint32_t full0 = smem_u32(s.full), empty0 = smem_u32(s.empty);
-  const uint32_t accf0 = smem_u32(s.acc_full), acce0 = smem_u32(s.acc_empty);
-  // descriptors of stage 0 and of x chunk 0; the start address field (bits
-  // 0-13, in 16-byte units) is advanced by plain adds
-  const uint64_t ring_desc = umma_desc_k128(smem_u32(s.ring));
-  const uint64_t xs_desc = umma_desc_k128(smem_u32(s.xs));
-  const uint32_t tmem = *s.tmem;
-  const int stages = p.stages, KT = tr.KT;
-  const int count = static_cast<int>(tr.t1 - tr.t0);
-  const int kk0 = static_cast<int>(tr.t0 % KT);
-  const bool all = count >= KT;
-  const int nst = (count + 1) / 2;
-  const int first_len = KT - kk0 < count ? KT - kk0 : count;
-  const int nseg = 1 + (count - first_len + KT - 1) / KT;
-  uint32_t rslot = ring_io.slot, rpar = ring_io.parity, aslot = acc_io.slot, apar = acc_io.parity;
-  int i = 0, seg_end = first_len;
-  uint64_t b = xs_desc + static_cast<uint64_t>(all ? kk0 : 0) * kSlotDesc;
-  uint32_t accf = 0u;   // 0 until the current segment's first tile is issued
-  bool ok = wait_shared(p, acce0 + 8 * aslot, apar ^ 1u, 1005);
-  tc_fence_after_sync();
-  uint32_t d = tmem + aslot * kAccCols;
-  while (ok && i < count) {
-    if (!wait_shared(p, full0 + 8 * rslot, rpar, 1000)) { ok = false; break; }
-    const uint64_t a = ring_desc + rslot * (kStageBytes >> 4);
-    if (i + 2 < seg_end) {
-      umma_bf16(d, a, b, kIdescBf16M128N8, accf);
-      umma_bf16(d + 8, a + 2, b + 2, kIdescBf16M128N8, accf);
-      umma_bf16(d + 16, a + 4, b + 4, kIdescBf16M128N8, accf);
-      umma_bf16(d + 24, a + 6, b + 6, kIdescBf16M128N8, accf);
-      umma_bf16(d, a + kTileDesc, b + kSlotDesc, kIdescBf16M128N8, 1u);
-      umma_bf16(d + 8, a + kTileDesc + 2, b + kSlotDesc + 2, kIdescBf16M128N8, 1u);
-      umma_bf16(d + 16, a + kTileDesc + 4, b + kSlotDesc + 4, kIdescBf16M128N8, 1u);
-      umma_bf16(d + 24, a + kTileDesc + 6, b + kSlotDesc + 6, kIdescBf16M128N8, 1u);
-      accf = 1u;
-      b += 2 * kSlotDesc;
-      i += 2;
-    } else {
-      const int n = count - i < 2 ? count - i : 2;
-      for (int j = 0; j < n && ok; ++j, ++i) {
-        const uint64_t aj = a + static_cast<uint64_t>(j) * kTileDesc;
-        umma_bf16(d, aj, b, kIdescBf16M128N8, accf);
-        umma_bf16(d + 8, aj + 2, b + 2, kIdescBf16M128N8, accf);
-        umma_bf16(d + 16, aj + 4, b + 4, kIdescBf16M128N8, accf);
-        umma_bf16(d + 24, aj + 6, b + 6, kIdescBf16M128N8, accf);
-        accf = 1u;
-        b += kSlotDesc;
-        if (i + 1 == seg_end) {   // segment end: hand the set to the epilogue
-          umma_commit_u32(accf0 + 8 * aslot);
-          aslot = aslot + 1 == kAccSets ? 0u : aslot + 1;
-          apar ^= aslot == 0 ? 1u : 0u;
-          if (i + 1 < count) {    // the next row group starts: a free set, k chunk 0
-            seg_end = seg_end + KT < count ? seg_end + KT : count;
-            if (all) b = xs_desc;
-            ok = wait_shared(p, acce0 + 8 * aslot, apar ^ 1u, 1005);
-            tc_fence_after_sync();
-            d = tmem + aslot * kAccCols;
-            accf = 0u;
-          }
-        }
-      }
-    }
-    if (!ok) break;
-    umma_commit_u32(empty0 + 8 * rslot);   // the stage returns to the producer once read
-    rslot = rslot + 1 == static_cast<uint32_t>(stages) ? 0u : rslot + 1;
-    rpar ^= rslot == 0 ? 1u : 0u;
-  }
-  // the cursors after the whole phase (also after an abort, when they no longer matter)
-  advance_by(ring_io, nst, stages);
-  advance_by(acc_io, nseg, kAccSets);
-}
-
-// ---- epilogue warps 0-3: one projection phase ------------------------------------------------------
-// Thread r owns row r of each 128-row group (TMEM lane r) for the 4 batch rows.
-// For each segment of the range it reads the accumulator set, then either
-// publishes it (the range starts inside the group) or adds the published first
-// segments of the following CTAs that continue the group, in CTA order, and
-// runs the epilogue.
-__device__ void gemv_epilogue(const EpochParams &p, const Smem &s, const Gemv &g, const TileRange &tr,
-                              RingCursor &acc, uint32_t seq, int step) {
-  const int r = threadIdx.x;
-  const int warp = r >> 5, lane = r & 31;
-  const ModelDims &m = p.m;
-  const uint32_t tmem = *s.tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  float best[kBatch];
-  int32_t best_i[kBatch];
-  int32_t bad = 0;
-#pragma unroll
-  for (int b = 0; b < kBatch; ++b) {
-    best[b] = -INFINITY;
-    best_i[b] = INT_MAX;
-  }
-  bool ok = true;
-  for (int64_t t = tr.t0; t < tr.t1;) {
-    const int64_t grp = t / tr.KT;
-    const int64_t grp_end = (grp + 1) * tr.KT;
-    const int64_t seg_end = grp_end < tr.t1 ? grp_end : tr.t1;
-    const bool head = t % tr.KT == 0;   // this CTA holds the group's first tile
-    const int64_t n = grp * kTileRows + r;
-    // operands that do not depend on the sums, fetched before the wait
-    float e[kBatch] = {0.f, 0.f, 0.f, 0.f};
-    if (head) {
-      if (g.kind == kQKV) {
-        const float bv = bf(g.bias[n]);
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) e[b] = bv;
-      } else if (g.kind == kO || g.kind == kDown) {
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) e[b] = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n));
-      }
-    }
-    // one poller per warp: spinning lanes would compete for issue slots and the
-    // mbarrier unit with the MMA issuer on the same sub-partition
-    int landed = 1;
-    if (lane == 0 && ok) landed = wait_bar(p, &s.acc_full[acc.slot], acc.parity, nullptr, 1003) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, landed, 0) != 0 && ok;
-    tc_fence_after_sync();   // tcgen05.ld (warp-collective) after the completion lane 0 observed
-    float v[8];
-    {
-      float raw[kAccCols];
-      tmem_ld32(tmem + acc.slot * kAccCols, raw);
-#pragma unroll
-      for (int b = 0; b < 8; ++b) v[b] = (raw[b] + raw[8 + b]) + (raw[16 + b] + raw[24 + b]);
-    }
-    tc_fence_before_sync();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&s.acc_empty[acc.slot]);
-    acc.advance(kAccSets);
-    if (!head) {
-      *reinterpret_cast<float4 *>(p.partials + static_cast<size_t>(blockIdx.x) * kPartialFloats + r * 4) =
-          make_float4(v[0], v[1], v[2], v[3]);
-      __threadfence();
-      named_sync(2, kEpilogueThreads);
-      if (r == 0) st_release_u32(&p.sync->flags[blockIdx.x], seq);
-    } else {
-      if (seg_end < grp_end) {
-        // the CTAs after this one whose ranges start inside the group: lane i of
-        // every warp waits for partner i, then all partials are added in CTA order
-        int partners = 0;
-        while (blockIdx.x + 1 + partners < tr.ctas && tile_range(g, blockIdx.x + 1 + partners, p.grid).t0 < grp_end)
-          ++partners;
-        for (int base = 0; base < partners && ok; base += 32) {
-          int ready = 1;
-          if (base + lane < partners) {
-            const uint32_t *flag = &p.sync->flags[blockIdx.x + 1 + base + lane];
-            const uint64_t deadline = globaltimer() + p.timeout_ns;
-            uint32_t polls = 0;
-            while (ld_acquire_u32(flag) != seq) {
-              if ((++polls & 15) == 0) {
-                if (aborted(p)) { ready = 0; break; }
-                if (globaltimer() > deadline) { raise_error(p, 1001); ready = 0; break; }
-              }
-            }
-          }
-          ok = __all_sync(0xffffffffu, ready) != 0;
-        }
-        if (ok) {
-          for (int i = 0; i < partners; ++i) {
-            const float4 q = __ldcg(reinterpret_cast<const float4 *>(
-                p.partials + static_cast<size_t>(blockIdx.x + 1 + i) * kPartialFloats + r * 4));
-            v[0] += q.x;
-            v[1] += q.y;
-            v[2] += q.z;
-            v[3] += q.w;
-          }
-        }
-      }
-      if (g.kind == kQKV) {
-        // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) p.qkv[static_cast<size_t>(b) * m.Nqkv + n] = tobf(__fadd_rn(v[b], e[b]));
-      } else if (g.kind == kO || g.kind == kDown) {
-        // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) p.h[static_cast<size_t>(b) * m.H + n] = tobf(__fadd_rn(e[b], rbf(v[b])));
-      } else if (g.kind == kGU) {
-        // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398);
-        // of every 16 rows the first 8 are gate rows, the next 8 the matching up rows
-        float up[kBatch];
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) up[b] = __shfl_xor_sync(0xffffffffu, v[b], 8);
-        if ((r & 8) == 0) {
-          const int64_t i = (n >> 4) * 8 + (n & 7);
-#pragma unroll
-          for (int b = 0; b < kBatch; ++b) {
-            const float gate = rbf(v[b]);
-            const float u = rbf(up[b]);
-            const float silu = rbf(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
-            p.act[static_cast<size_t>(b) * m.I_pad + i] = tobf(__fmul_rn(silu, u));
-          }
-        }
-      } else if (n < m.V) {
-        // logits = f32(bf16(x W^T)) (:405-408); rows in increasing order per thread,
-        // so a strict > keeps the first maximum
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-          const float l = rbf(v[b]);
-          if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n] = l;
-          bad |= !isfinite(l);
-          if (l > best[b]) {
-            best[b] = l;
-            best_i[b] = static_cast<int32_t>(n);
-          }
-        }
-      }
-    }
-    t = seg_end;
-  }
-  if (g.kind == kLM) {
-    // first-max argmax over the CTA's rows: warps, then the 4 warps in order
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      float cb = best[b];
-      int32_t ci = best_i[b];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, cb, off);
-        const int32_t oi = __shfl_xor_sync(0xffffffffu, ci, off);
-        if (ob > cb || (ob == cb && oi < ci)) { cb = ob; ci = oi; }
-      }
-      if (lane == 0) {
-        s.lm_val[warp * 4 + b] = cb;
-        s.lm_idx[warp * 4 + b] = ci;
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) bad |= __shfl_xor_sync(0xffffffffu, bad, off);
-    if (lane == 0) s.lm_bad[warp] = bad;
-    named_sync(2, kEpilogueThreads);
-    if (r < kBatch) {
-      float cb = s.lm_val[r];
-      int32_t ci = s.lm_idx[r];
-      int32_t cbad = s.lm_bad[0];
-      for (int w = 1; w < kEpilogueThreads / 32; ++w) {
-        const float ob = s.lm_val[w * 4 + r];
-        const int32_t oi = s.lm_idx[w * 4 + r];
-        cbad |= s.lm_bad[w];
-        if (ob > cb || (ob == cb && oi < ci)) { cb = ob; ci = oi; }
-      }
-      p.arg_val[blockIdx.x * kBatch + r] = cb;
-      p.arg_idx[blockIdx.x * kBatch + r] = ci;
-      p.arg_bad[blockIdx.x * kBatch + r] = cbad;
-    }
-  }
-  // the phase's outputs are visible GPU-wide before the grid barrier
-  __threadfence();
-}
-
 // ---- consumer warps: one projection phase ---------------------------------------------------
-__device__ void gemv_phase(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &ring, RingCursor &acc,
-                           uint32_t seq, int step, uint32_t trace_slot) {
+// Streams this CTA's tiles through the MMA and hands every finished row-group
+// segment (fp32 partials of 16 rows x 4 batch rows per warp) to the epilogue
+// warp through the reduction ring; no CTA-wide synchronisation in the stream.
+__device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &ring,
+                             RingCursor &red, uint32_t trace_slot) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  const int gi = lane >> 2, ci = lane & 3;
   const TileRange tr = tile_range(g, blockIdx.x, p.grid);
   if (g.embed_src) {
     // layer 0: every CTA materialises its slice of the residual stream h = E[token]
@@ -876,18 +538,285 @@ __device__ void gemv_phase(const EpochParams &p, const Smem &s, const Gemv &g, R
     }
   }
   if (tr.t0 >= tr.t1) return;
-  stage_x(p, s, g, tr);
+  const bool xg = g.xmode == kXGlobal;
+  if (!xg) load_x(p, s, g);
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
     p.trace[2 * kTraceMax + trace_slot] = globaltimer();   // activations staged
-  if (warp < kEpilogueThreads / 32) {
-    gemv_epilogue(p, s, g, tr, acc, seq, step);
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      mma_issue(p, s, tr, ring, acc);
-      if (p.trace != nullptr && blockIdx.x == 0 && trace_slot < kTraceMax)
-        p.trace[3 * kTraceMax + trace_slot] = globaltimer();   // last tile issued
+  const int kc = g.kc;
+  const int ksteps = kc / 64;
+  const uint32_t row_bytes = static_cast<uint32_t>(kc) * 2u;
+  const uint32_t tile_bytes = row_bytes * kRows;
+  const int per_stage = kStageBytes / static_cast<int>(tile_bytes);
+  const uint32_t sw = static_cast<uint32_t>(gi & 7);   // row swizzle of rows gi and gi + 8
+  // two accumulator sets halve the dependent MMA chain of a tile
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  // kXGlobal (one 64-wide k-step per warp and tile): each thread with gi < 4
+  // keeps the activation fragments of the next four tiles in flight from L2.
+  const bf16 *xg_base = g.xsrc + static_cast<size_t>(gi) * g.xsrc_stride + warp * 64 + 16 * ci;
+  const bool xg_lane = xg && gi < kBatch;
+  auto xg_load = [&](int64_t tt, int tkk, uint4 &lo, uint4 &hi) {
+    if (xg_lane && tt < tr.t1) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(xg_base + static_cast<int64_t>(tkk) * kc);
+      lo = __ldcg(src);
+      hi = __ldcg(src + 1);
+    } else {
+      lo = make_uint4(0, 0, 0, 0);
+      hi = make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto next_kk = [&](int v) { return v + 1 == tr.KT ? 0 : v + 1; };
+  int kk = static_cast<int>(tr.t0 % tr.KT);
+  int kq = kk;   // k-tile of the next prefetch
+  uint4 x00, x01, x10, x11, x20, x21, x30, x31;
+  xg_load(tr.t0, kq, x00, x01); kq = next_kk(kq);
+  xg_load(tr.t0 + 1, kq, x10, x11); kq = next_kk(kq);
+  xg_load(tr.t0 + 2, kq, x20, x21); kq = next_kk(kq);
+  for (int64_t t = tr.t0; t < tr.t1;) {
+    const int n = static_cast<int>(tr.t1 - t < per_stage ? tr.t1 - t : per_stage);
+    // Bounded wait.  On abort or timeout the phase still runs to its end (on
+    // garbage) so that every barrier below is matched; the grid barrier that
+    // ends the phase then stops the launch uniformly.
+    const bool landed = wait_bar(p, &s.full[ring.slot], ring.parity, nullptr, 1000);
+    const uint8_t *stage = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
+    for (int j = 0; j < n; ++j, ++t) {
+      xg_load(t + 3, kq, x30, x31);
+      kq = next_kk(kq);
+      const uint8_t *tile = stage + j * tile_bytes;
+      for (int ks = warp; ks < ksteps; ks += kConsumerWarps) {
+        const uint32_t u0 = (static_cast<uint32_t>(ks * 8 + 2 * ci) ^ sw) * 16u;
+        const uint32_t u1 = (static_cast<uint32_t>(ks * 8 + 2 * ci + 1) ^ sw) * 16u;
+        const uint8_t *rlo = tile + gi * row_bytes;
+        const uint8_t *rhi = rlo + 8 * row_bytes;
+        const uint4 a_lo0 = lds128(rlo + u0);
+        const uint4 a_lo1 = lds128(rlo + u1);
+        const uint4 a_hi0 = lds128(rhi + u0);
+        const uint4 a_hi1 = lds128(rhi + u1);
+        uint4 x0 = x00, x1 = x01;
+        if (!xg && gi < kBatch) {
+          const bf16 *xrow = s.xs + static_cast<size_t>(gi) * p.xs_stride + kk * kc + ks * 64 + 16 * ci;
+          x0 = lds128(xrow);
+          x1 = lds128(xrow + 8);
+        }
+        // MMA j uses physical k = 16ci + 4j .. 4j+3 of this 64-wide slice, for both
+        // weight rows (gi, gi+8) and the activation column gi.
+        mma_bf16_16816(acc, a_lo0.x, a_hi0.x, a_lo0.y, a_hi0.y, x0.x, x0.y);
+        mma_bf16_16816(acc2, a_lo0.z, a_hi0.z, a_lo0.w, a_hi0.w, x0.z, x0.w);
+        mma_bf16_16816(acc, a_lo1.x, a_hi1.x, a_lo1.y, a_hi1.y, x1.x, x1.y);
+        mma_bf16_16816(acc2, a_lo1.z, a_hi1.z, a_lo1.w, a_hi1.w, x1.z, x1.w);
+      }
+      x00 = x10; x01 = x11; x10 = x20; x11 = x21; x20 = x30; x21 = x31;
+      if (kk == tr.KT - 1 || t == tr.t1 - 1) {
+        // segment end: this warp's 16 x 4 partial sums go to the epilogue warp
+        wait_bar(p, &s.red_empty[red.slot], red.parity ^ 1u, nullptr, 1002);
+        if (ci < 2) {
+          float *r = s.red + (static_cast<size_t>(red.slot) * kConsumerWarps + warp) * 64;
+          r[gi * 4 + 2 * ci] = acc[0] + acc2[0];
+          r[gi * 4 + 2 * ci + 1] = acc[1] + acc2[1];
+          r[(gi + 8) * 4 + 2 * ci] = acc[2] + acc2[2];
+          r[(gi + 8) * 4 + 2 * ci + 1] = acc[3] + acc2[3];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.red_full[red.slot]);
+        red.advance(kRedSlots);
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        acc2[0] = acc2[1] = acc2[2] = acc2[3] = 0.f;
+      }
+      kk = next_kk(kk);
     }
     __syncwarp();
+    if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
+    ring.advance(p.stages);
+  }
+  if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
+    p.trace[3 * kTraceMax + trace_slot] = globaltimer();   // last tile consumed by warp 0
+}
+
+// ---- epilogue warp: one projection phase --------------------------------------------------------
+// Lane l owns rows (l/4, l/4 + 8) of the row group and batch row l%4.  For each
+// segment it sums the 8 warps' partials in fixed order, then either publishes
+// them (the segment's row group started on the previous CTA), or adds the next
+// CTA's published part (the row group continues there) and runs the epilogue.
+__device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &red,
+                            uint32_t seq, int step) {
+  const int lane = threadIdx.x & 31;
+  const ModelDims &m = p.m;
+  const TileRange tr = tile_range(g, blockIdx.x, p.grid);
+  float best = -INFINITY;
+  int32_t best_i = INT_MAX, bad = 0;
+  int64_t seg_start = tr.t0;
+  int64_t rg = tr.t0 / tr.KT;
+  int kk = static_cast<int>(tr.t0 % tr.KT);
+  // Operands of the epilogue that do not depend on this phase's sums (residual
+  // rows, biases) are loaded up front for the first two row groups this CTA
+  // finishes; the small projections have at most two.
+  const int b_lane = lane & 3;
+  float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+  int64_t pa_rg = -1, pb_rg = -1;
+  if (g.kind == kQKV || g.kind == kO || g.kind == kDown) {
+    const int64_t first_head = tr.t0 % tr.KT == 0 ? tr.t0 / tr.KT : tr.t0 / tr.KT + 1;
+    auto fetch = [&](int64_t r, float &v0, float &v1) {
+      const int64_t n0 = r * kRows + (lane >> 2), n1 = n0 + 8;
+      if (g.kind == kQKV) {
+        v0 = bf(g.bias[n0]);
+        v1 = bf(g.bias[n1]);
+      } else {
+        v0 = bf(__ldcg(p.h + static_cast<size_t>(b_lane) * m.H + n0));
+        v1 = bf(__ldcg(p.h + static_cast<size_t>(b_lane) * m.H + n1));
+      }
+    };
+    if (first_head * tr.KT < tr.t1) { pa_rg = first_head; fetch(pa_rg, pa0, pa1); }
+    if ((first_head + 1) * tr.KT < tr.t1) { pb_rg = first_head + 1; fetch(pb_rg, pb0, pb1); }
+  }
+  for (int64_t t = tr.t0; t < tr.t1; ++t) {
+    const bool group_end = kk == tr.KT - 1;
+    if (group_end || t == tr.t1 - 1) {
+      const bool head_seg = (seg_start % tr.KT) == 0;
+      float part0 = 0.f, part1 = 0.f;
+      if (head_seg && !group_end) {
+        // finisher: the next CTA publishes the rest of this row group early in
+        // its range; fetch it while the consumers are still streaming
+        if (lane == 0) {
+          const uint64_t deadline = globaltimer() + p.timeout_ns;
+          uint32_t polls = 0;
+          while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
+            if (aborted(p)) break;
+            if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
+          }
+        }
+        __syncwarp();
+        part0 = __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane);
+        part1 = __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane + 32);
+      }
+      wait_bar(p, &s.red_full[red.slot], red.parity, s.prod_ctl, 1003);
+      const float *r = s.red + static_cast<size_t>(red.slot) * kConsumerWarps * 64;
+      float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        v0 += r[w * 64 + lane];
+        v1 += r[w * 64 + lane + 32];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.red_empty[red.slot]);
+      red.advance(kRedSlots);
+      const bool head = head_seg;   // this CTA holds the group's first tile
+      seg_start = t + 1;
+      if (!head) {
+        p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane] = v0;
+        p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane + 32] = v1;
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          st_release_u32(&p.sync->flags[blockIdx.x], seq);
+        }
+      } else {
+        if (!group_end) {   // the rest of the row group came from CTA + 1
+          v0 += part0;
+          v1 += part1;
+        }
+        const int b = b_lane;
+        const int64_t n0 = rg * kRows + (lane >> 2), n1 = n0 + 8;
+        float e0, e1;   // bias (QKV) or residual (O, down) of rows n0, n1
+        if (rg == pa_rg) {
+          e0 = pa0;
+          e1 = pa1;
+        } else if (rg == pb_rg) {
+          e0 = pb0;
+          e1 = pb1;
+        } else if (g.kind == kQKV) {
+          e0 = bf(g.bias[n0]);
+          e1 = bf(g.bias[n1]);
+        } else if (g.kind == kO || g.kind == kDown) {
+          e0 = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n0));
+          e1 = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n1));
+        } else {
+          e0 = e1 = 0.f;
+        }
+        if (g.kind == kQKV) {
+          // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
+          p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, e0));
+          p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, e1));
+        } else if (g.kind == kO || g.kind == kDown) {
+          // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
+          p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(v0)));
+          p.h[static_cast<size_t>(b) * m.H + n1] = tobf(__fadd_rn(e1, rbf(v1)));
+        } else if (g.kind == kGU) {
+          // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398);
+          // rows 0-7 of the group are gate rows, 8-15 the matching up rows
+          const float gate = rbf(v0);
+          const float up = rbf(v1);
+          const float silu = rbf(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
+          p.act[static_cast<size_t>(b) * m.I_pad + rg * 8 + (lane >> 2)] = tobf(__fmul_rn(silu, up));
+        } else {
+          // logits = f32(bf16(x W^T)) (:405-408); first-max argmax partials
+          const float l0 = rbf(v0), l1 = rbf(v1);
+          float cb = -INFINITY;
+          int32_t ci = INT_MAX, cbad = 0;
+          if (n0 < m.V) {
+            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n0] = l0;
+            cbad |= !isfinite(l0);
+            if (l0 > cb) { cb = l0; ci = static_cast<int32_t>(n0); }
+          }
+          if (n1 < m.V) {
+            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n1] = l1;
+            cbad |= !isfinite(l1);
+            if (l1 > cb) { cb = l1; ci = static_cast<int32_t>(n1); }
+          }
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) {   // lanes sharing b: l ^ 4, 8, 16
+            const float ob = __shfl_xor_sync(0xffffffffu, cb, off);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, ci, off);
+            cbad |= __shfl_xor_sync(0xffffffffu, cbad, off);
+            if (ob > cb || (ob == cb && oi < ci)) { cb = ob; ci = oi; }
+          }
+          if (cb > best || (cb == best && ci < best_i)) { best = cb; best_i = ci; }
+          bad |= cbad;
+        }
+      }
+    }
+    if (++kk == tr.KT) { kk = 0; ++rg; }
+  }
+  if (g.kind == kLM && lane < kBatch) {
+    p.arg_val[blockIdx.x * kBatch + lane] = best;
+    p.arg_idx[blockIdx.x * kBatch + lane] = best_i;
+    p.arg_bad[blockIdx.x * kBatch + lane] = bad;
+  }
+  // the phase's outputs written by this warp are visible GPU-wide before the
+  // consumers may arrive at the grid barrier
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(s.phase_done);
+}
+
+// Epilogue warp main loop: follows the projection phases of every step.
+__device__ void epilogue_main(const EpochParams &p, const Smem &s) {
+  const int lane = threadIdx.x & 31;
+  const int L = p.m.L;
+  const int phases = 5 * L + 2;
+  RingCursor red;
+  for (int step = 0; step < kMaxSteps; ++step) {
+    bool go = true;
+    if (lane == 0) go = wait_step(p, s, step);
+    go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
+    if (!go) return;
+    for (int ph = 0; ph < phases; ++ph) {
+      const int kind = gemv_kind_of_phase(ph, L);
+      if (kind < 0) continue;
+      const int seq = step * phases + ph + 1;
+      // never finish a phase before the consumers started it
+      bool started = true;
+      if (lane == 0) {
+        const uint64_t deadline = globaltimer() + p.timeout_ns;
+        while (*s.phase_started < seq) {
+          if (*s.prod_ctl == -1 || aborted(p) || globaltimer() > deadline) { started = false; break; }
+          __nanosleep(32);
+        }
+      }
+      started = __shfl_sync(0xffffffffu, started ? 1 : 0, 0) != 0;
+      if (!started) return;
+      const Gemv g = make_gemv(p, ph / 5, kind);
+      gemv_finish(p, s, g, red, static_cast<uint32_t>(seq), step);
+    }
   }
 }
 
@@ -934,7 +863,8 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
   float *part = rd + 16;                                // [groups][D] P.V partials
   bf16 *vs = reinterpret_cast<bf16 *>(reinterpret_cast<uint8_t *>(s.xs) + attn_scratch_bytes(D, m.C));
   // positions whose V rows are staged in shared memory
-  const size_t scratch = static_cast<size_t>(p.xslots) * kXSlotBytes;
+  const size_t scratch = static_cast<size_t>(kBatch) * p.xs_stride * 2 +
+                         static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4;
   const int vcap = static_cast<int>(min(static_cast<size_t>(m.C), (scratch - attn_scratch_bytes(D, m.C)) / (D * 2)));
   if (layer == 0) {   // the row state is constant over the layers of a step
     if (tid < kBatch) {
@@ -1240,32 +1170,31 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
   if (tid == 0) {
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);     // tcgen05.commit of the stage's MMAs
+      mbar_init(&s.empty[i], kConsumerWarps);
     }
-    for (int i = 0; i < kAccSets; ++i) {
-      mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], kEpilogueThreads / 32);
+    for (int i = 0; i < kRedSlots; ++i) {
+      mbar_init(&s.red_full[i], kConsumerWarps);
+      mbar_init(&s.red_empty[i], 1);
     }
-    mbar_init(s.drain, 1);
-    *s.prod_ctl = -2;        // the producer waits for "step 0 go"
+    mbar_init(s.phase_done, 1);
+    *s.prod_ctl = -2;        // producer and epilogue warps wait for "step 0 go"
+    *s.phase_started = 0;
     mbar_fence_init();
   }
-  const int warp_id = tid >> 5;
-  if (warp_id == 0) {
-    __syncwarp();   // tcgen05.alloc is warp-collective
-    tmem_alloc(s.tmem, kTmemCols);   // accumulator sets: kAccSets x kAccSub x 8 fp32 columns x 128 lanes
-    tmem_relinquish();
-    tc_fence_before_sync();
-  }
   __syncthreads();
-  tc_fence_after_sync();
+  const int warp_id = tid >> 5;
   if (warp_id == kProducerWarp) {
     producer_main(p, s);
     return;
   }
+  if (warp_id == kEpilogueWarp) {
+    epilogue_main(p, s);
+    return;
+  }
 
   uint32_t barrier_index = 0;
-  RingCursor ring, acc;
+  RingCursor ring, red;
+  uint32_t done_parity = 0;
   bool ok = true;
   const size_t block_elems = static_cast<size_t>(m.bs) * m.nkv * m.d;
   const size_t layer_elems = static_cast<size_t>(m.NB) * block_elems;
@@ -1407,7 +1336,11 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       const int kind = gemv_kind_of_phase(ph, L);
       if (kind >= 0) {
         const Gemv g = make_gemv(p, ph / 5, kind);
-        gemv_phase(p, s, g, ring, acc, seq, step, barrier_index + 1);
+        if (tid == 0) *s.phase_started = static_cast<int>(seq);
+        gemv_consume(p, s, g, ring, red, barrier_index + 1);
+        // the epilogue warp has written every output of the phase
+        if (tid == 0) wait_bar(p, s.phase_done, done_parity, nullptr, 1004);
+        done_parity ^= 1u;
       } else if (ph < 5 * L) {
         attention_phase(p, s, ph / 5);
       } else if (blockIdx.x == 0) {
@@ -1415,7 +1348,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
         // per-row bookkeeping of the reference K-loop body (:537-591)
         {
           // two warps per row: lane-strided over the CTA partials, then shuffles
-          const int lm_ctas = tile_range(m.V_pad, m.H, 0, p.grid).ctas;
+          const int lm_ctas = static_cast<int>(m.V_pad / kRows < p.grid ? m.V_pad / kRows : p.grid);
           const int b = tid >> 6, sub = tid & 63;
           float best = -INFINITY;
           int32_t idx = INT_MAX, bad = 0;
@@ -1482,25 +1415,6 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
     }
   }
   if (tid == 0) *s.prod_ctl = -1;   // producer: no more steps
-
-  // every MMA of the launch has completed before tensor memory is released
-  // (also after an abort: only the timeout ends this wait)
-  if (warp_id == kMmaWarp && (tid & 31) == 0) {
-    umma_commit(s.drain);
-    const uint64_t deadline = globaltimer() + p.timeout_ns;
-    while (!mbar_try(s.drain, 0)) {
-      if (globaltimer() > deadline) {
-        raise_error(p, 1006);
-        break;
-      }
-    }
-  }
-  named_sync(1, kConsumerThreads);
-  if (warp_id == 0) {
-    __syncwarp();
-    tc_fence_after_sync();
-    tmem_dealloc(*s.tmem, kTmemCols);
-  }
 
   // 5. finish (:593-614) and emit (:296-324), CTA 0
   if (blockIdx.x == 0 && tid == 0) {

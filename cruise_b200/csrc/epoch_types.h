@@ -17,25 +17,15 @@ constexpr int kControlOut = 28;       // emit layout (controller :296-324)
 constexpr int kTilingBytes = 72;
 constexpr int kImportFlag = 0x100;
 
-// Weight tiles: 128 rows (the UMMA M) x 64 k elements (one 128-byte swizzle
-// row), 16 KB, in the canonical K-major 128-byte-swizzled layout that
-// tcgen05.mma reads from shared memory.
-constexpr int kTileRows = 128;
-constexpr int kTileK = 64;
-constexpr int kTileBytes = kTileRows * kTileK * 2;
-constexpr int kStageBytes = 32768;    // one bulk copy: two consecutive tiles of the stream
-constexpr int kXSlotBytes = 1024;     // one 64-k chunk of the 8 (4 real) activation rows
-constexpr int kAccSets = 4;           // TMEM accumulator sets in flight
-constexpr int kAccSub = 4;            // independent accumulators per set (one per k step of a tile)
-constexpr int kAccCols = 8 * kAccSub; // fp32 columns of one set (8 = N)
-constexpr int kTmemCols = kAccSets * kAccCols;
+constexpr int kRows = 16;             // weight rows per tile (one m16 MMA slab)
+constexpr int kMaxKc = 512;           // k elements per tile (power of two, 64..512)
+constexpr int kStageBytes = 32768;    // one bulk copy: consecutive tiles of the stream
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kEpilogueThreads = 128;                  // warps 0-3: TMEM lanes 0-127
-constexpr int kMmaWarp = 4;                            // lane 0 issues tcgen05.mma
 constexpr int kProducerWarp = kConsumerWarps;          // warp 8: weight producer (TMA)
-constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kPartialFloats = kTileRows * kBatch;     // one split row-group partial
+constexpr int kEpilogueWarp = kConsumerWarps + 1;      // warp 9: reductions and epilogues
+constexpr int kThreads = kConsumerThreads + 64;
+constexpr int kRedSlots = 4;                           // row-group partial-sum ring
 constexpr int kMaxCtas = 1024;
 constexpr int kMaxStages = 8;
 constexpr int kTraceMax = 2048;       // grid barriers recorded per launch
@@ -75,7 +65,7 @@ struct LayerWeights {
   const bf16 *qkv_w;           // tiled [Nqkv][H]   rows: q | k | v
   const bf16 *qkv_b;           // [Nqkv]
   const bf16 *o_w;             // tiled [H][H]
-  const bf16 *gu_w;            // tiled [2 I_pad][H]: per 16 rows, 8 gate rows then the 8 matching up rows
+  const bf16 *gu_w;            // tiled [2I][H]: per 16 rows, 8 gate rows then the 8 matching up rows
   const bf16 *down_w;          // tiled [H][I_pad]  columns >= I are zero
 };
 
@@ -157,7 +147,7 @@ struct EpochParams {
   bf16 *qkv;                   // [4][Nqkv]
   bf16 *attn;                  // [4][H]
   bf16 *act;                   // [4][I_pad]
-  float *partials;             // [G][128 rows][4] split row-group partial sums
+  float *partials;             // [G][64] split row-group partial sums
   float *arg_val;              // [G][4]
   int32_t *arg_idx;            // [G][4]
   int32_t *arg_bad;            // [G][4]
@@ -169,8 +159,8 @@ struct EpochParams {
   SyncState *sync;
   int32_t grid;                // CTAs (one per SM)
   int32_t stages;              // weight ring depth
-  int32_t xslots;              // 64-k activation chunks the shared-memory staging holds
-  int32_t pad2;
+  int32_t xs_stride;           // activation row stride in smem (elements)
+  int32_t down_xglobal;        // 1: the down projection reads its input from L2, not smem
   uint64_t *trace;             // optional: CTA 0 globaltimer at each grid barrier (exit, entry)
   uint64_t timeout_ns;         // bound of every spin wait
   uint32_t l2_ahead;           // bytes of weights prefetched into L2 beyond the ring (0: off)
