@@ -515,33 +515,128 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
   named_sync(1, kConsumerThreads);
 }
 
-// ---- consumer warps: one projection phase ---------------------------------------------------
-// Streams this CTA's tiles through the MMA and hands every finished row-group
-// segment (fp32 partials of 16 rows x 4 batch rows per warp) to the epilogue
-// warp through the reduction ring; no CTA-wide synchronisation in the stream.
-__device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &ring,
-                             RingCursor &red, uint32_t trace_slot) {
+// Flushes one warp's 16 x 4 partial sums of a finished row-group segment to
+// the epilogue warp through the reduction ring.
+__device__ __forceinline__ void flush_segment(const EpochParams &p, const Smem &s, RingCursor &red, int warp,
+                                              int lane, float (&acc)[4], float (&acc2)[4]) {
+  const int gi = lane >> 2, ci = lane & 3;
+  wait_bar(p, &s.red_empty[red.slot], red.parity ^ 1u, nullptr, 1002);
+  if (ci < 2) {
+    float *r = s.red + (static_cast<size_t>(red.slot) * kConsumerWarps + warp) * 64;
+    r[gi * 4 + 2 * ci] = acc[0] + acc2[0];
+    r[gi * 4 + 2 * ci + 1] = acc[1] + acc2[1];
+    r[(gi + 8) * 4 + 2 * ci] = acc[2] + acc2[2];
+    r[(gi + 8) * 4 + 2 * ci + 1] = acc[3] + acc2[3];
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&s.red_full[red.slot]);
+  red.advance(kRedSlots);
+  acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  acc2[0] = acc2[1] = acc2[2] = acc2[3] = 0.f;
+}
+
+// Tile loop for kc = 512 (every 7B-shaped projection): warp w owns the 64-k
+// slice w of every tile and a stage holds two tiles.  Per stage all shared
+// loads of both tiles (8 A fragments, 4 activation fragments) are issued
+// before the 8 MMAs, so a stage costs one shared-memory latency; addresses are
+// precomputed per warp.  kXGlobal keeps the activation fragments of the next
+// four tiles in flight from L2, as in the general loop.
+__device__ void gemv_tiles_k512(const EpochParams &p, const Smem &s, const Gemv &g, const TileRange &tr,
+                                RingCursor &ring, RingCursor &red) {
+  constexpr int kc = 64 * kConsumerWarps;
+  constexpr uint32_t row_bytes = kc * 2, tile_bytes = row_bytes * kRows;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int gi = lane >> 2, ci = lane & 3;
-  const TileRange tr = tile_range(g, blockIdx.x, p.grid);
-  if (g.embed_src) {
-    // layer 0: every CTA materialises its slice of the residual stream h = E[token]
-    const int K8 = g.K / 8;
-    const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
-    const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
-    for (int i = tid; i < kBatch * (hi - lo); i += kConsumerThreads) {
-      const int b = i / (hi - lo), k8 = lo + i % (hi - lo);
-      const int64_t tok = __ldcg(&p.work->token[b]);
-      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.embed + tok * g.K) + k8);
-      *reinterpret_cast<uint4 *>(p.h + static_cast<size_t>(b) * p.m.H + k8 * 8) = v;
-    }
-  }
-  if (tr.t0 >= tr.t1) return;
+  const uint32_t sw = static_cast<uint32_t>(gi & 7);
+  const uint32_t off_lo0 = gi * row_bytes + ((static_cast<uint32_t>(warp * 8 + 2 * ci) ^ sw) << 4);
+  const uint32_t off_lo1 = gi * row_bytes + ((static_cast<uint32_t>(warp * 8 + 2 * ci + 1) ^ sw) << 4);
+  const uint32_t off_hi0 = off_lo0 + 8 * row_bytes, off_hi1 = off_lo1 + 8 * row_bytes;
   const bool xg = g.xmode == kXGlobal;
-  if (!xg) load_x(p, s, g);
-  if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
-    p.trace[2 * kTraceMax + trace_slot] = globaltimer();   // activations staged
+  const bool xlane = gi < kBatch;
+  // staged activations: row gi, k = kk * kc + warp * 64 + 16 ci (+8)
+  const bf16 *xs_row = s.xs + static_cast<size_t>(xlane ? gi : 0) * p.xs_stride + warp * 64 + 16 * ci;
+  const bf16 *xg_base = g.xsrc + static_cast<size_t>(xlane ? gi : 0) * g.xsrc_stride + warp * 64 + 16 * ci;
+  const int KT = tr.KT;
+  const int count = static_cast<int>(tr.t1 - tr.t0);
+  int kk = static_cast<int>(tr.t0 % KT);   // k tile of the next tile
+  int kq = kk;                              // k tile of the next L2 prefetch (kXGlobal)
+  auto xg_load = [&](int i, uint4 &lo, uint4 &hi) {
+    if (xg && xlane && i < count) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(xg_base + static_cast<int64_t>(kq) * kc);
+      lo = __ldcg(src);
+      hi = __ldcg(src + 1);
+    } else {
+      lo = make_uint4(0, 0, 0, 0);
+      hi = make_uint4(0, 0, 0, 0);
+    }
+    kq = kq + 1 == KT ? 0 : kq + 1;
+  };
+  uint4 x00, x01, x10, x11, x20, x21, x30, x31;
+  xg_load(0, x00, x01);
+  xg_load(1, x10, x11);
+  xg_load(2, x20, x21);
+  xg_load(3, x30, x31);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < count; i += 2) {
+    const bool two = i + 1 < count;
+    const bool landed = wait_bar(p, &s.full[ring.slot], ring.parity, nullptr, 1000);
+    const uint8_t *t0 = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
+    const uint8_t *t1 = t0 + tile_bytes;
+    const int kk1 = kk + 1 == KT ? 0 : kk + 1;
+    // all shared loads of the stage first
+    const uint4 a0lo0 = lds128(t0 + off_lo0), a0lo1 = lds128(t0 + off_lo1);
+    const uint4 a0hi0 = lds128(t0 + off_hi0), a0hi1 = lds128(t0 + off_hi1);
+    uint4 a1lo0 = make_uint4(0, 0, 0, 0), a1lo1 = a1lo0, a1hi0 = a1lo0, a1hi1 = a1lo0;
+    if (two) {
+      a1lo0 = lds128(t1 + off_lo0);
+      a1lo1 = lds128(t1 + off_lo1);
+      a1hi0 = lds128(t1 + off_hi0);
+      a1hi1 = lds128(t1 + off_hi1);
+    }
+    uint4 xa0 = x00, xa1 = x01, xb0 = x10, xb1 = x11;
+    if (!xg && xlane) {
+      xa0 = lds128(xs_row + kk * kc);
+      xa1 = lds128(xs_row + kk * kc + 8);
+      if (two) {
+        xb0 = lds128(xs_row + kk1 * kc);
+        xb1 = lds128(xs_row + kk1 * kc + 8);
+      }
+    }
+    // L2 prefetch of the activation fragments four tiles ahead (kXGlobal)
+    x00 = x20; x01 = x21; x10 = x30; x11 = x31;
+    xg_load(i + 4, x20, x21);
+    xg_load(i + 5, x30, x31);
+    // tile 0
+    mma_bf16_16816(acc, a0lo0.x, a0hi0.x, a0lo0.y, a0hi0.y, xa0.x, xa0.y);
+    mma_bf16_16816(acc2, a0lo0.z, a0hi0.z, a0lo0.w, a0hi0.w, xa0.z, xa0.w);
+    mma_bf16_16816(acc, a0lo1.x, a0hi1.x, a0lo1.y, a0hi1.y, xa1.x, xa1.y);
+    mma_bf16_16816(acc2, a0lo1.z, a0hi1.z, a0lo1.w, a0hi1.w, xa1.z, xa1.w);
+    if (kk == KT - 1 || i == count - 1) flush_segment(p, s, red, warp, lane, acc, acc2);
+    if (two) {
+      mma_bf16_16816(acc, a1lo0.x, a1hi0.x, a1lo0.y, a1hi0.y, xb0.x, xb0.y);
+      mma_bf16_16816(acc2, a1lo0.z, a1hi0.z, a1lo0.w, a1hi0.w, xb0.z, xb0.w);
+      mma_bf16_16816(acc, a1lo1.x, a1hi1.x, a1lo1.y, a1hi1.y, xb1.x, xb1.y);
+      mma_bf16_16816(acc2, a1lo1.z, a1hi1.z, a1lo1.w, a1hi1.w, xb1.z, xb1.w);
+      if (kk1 == KT - 1 || i + 1 == count - 1) flush_segment(p, s, red, warp, lane, acc, acc2);
+    }
+    kk = kk1 + 1 == KT ? 0 : kk1 + 1;
+    if (!two) kk = kk1;
+    __syncwarp();
+    if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
+    ring.advance(p.stages);
+  }
+}
+
+// General tile loop (any kc): each warp takes the 64-k slices warp, warp + 8,
+// ... of every tile.
+__device__ void gemv_tiles_general(const EpochParams &p, const Smem &s, const Gemv &g, const TileRange &tr,
+                                   RingCursor &ring, RingCursor &red) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int gi = lane >> 2, ci = lane & 3;
+  const bool xg = g.xmode == kXGlobal;
   const int kc = g.kc;
   const int ksteps = kc / 64;
   const uint32_t row_bytes = static_cast<uint32_t>(kc) * 2u;
@@ -627,6 +722,38 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
     __syncwarp();
     if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
     ring.advance(p.stages);
+  }
+}
+
+// ---- consumer warps: one projection phase ---------------------------------------------------
+// Streams this CTA's tiles through the MMA and hands every finished row-group
+// segment (fp32 partials of 16 rows x 4 batch rows per warp) to the epilogue
+// warp through the reduction ring; no CTA-wide synchronisation in the stream.
+__device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &ring,
+                             RingCursor &red, uint32_t trace_slot) {
+  const int tid = threadIdx.x;
+  const TileRange tr = tile_range(g, blockIdx.x, p.grid);
+  if (g.embed_src) {
+    // layer 0: every CTA materialises its slice of the residual stream h = E[token]
+    const int K8 = g.K / 8;
+    const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
+    const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
+    for (int i = tid; i < kBatch * (hi - lo); i += kConsumerThreads) {
+      const int b = i / (hi - lo), k8 = lo + i % (hi - lo);
+      const int64_t tok = __ldcg(&p.work->token[b]);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.embed + tok * g.K) + k8);
+      *reinterpret_cast<uint4 *>(p.h + static_cast<size_t>(b) * p.m.H + k8 * 8) = v;
+    }
+  }
+  if (tr.t0 >= tr.t1) return;
+  const bool xg = g.xmode == kXGlobal;
+  if (!xg) load_x(p, s, g);
+  if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
+    p.trace[2 * kTraceMax + trace_slot] = globaltimer();   // activations staged
+  if (g.kc == 64 * kConsumerWarps && kStageBytes / (kRows * g.kc * 2) == 2) {
+    gemv_tiles_k512(p, s, g, tr, ring, red);
+  } else {
+    gemv_tiles_general(p, s, g, tr, ring, red);
   }
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
     p.trace[3 * kTraceMax + trace_slot] = globaltimer();   // last tile consumed by warp 0
