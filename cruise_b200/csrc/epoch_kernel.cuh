@@ -240,8 +240,8 @@ __device__ __forceinline__ void raise_error(const EpochParams &p, uint32_t where
 // Grid barrier among the consumer warps of all CTAs.  `index` counts barriers
 // from 1 within the launch.  Arrivals are spread over eight counters (CTA c
 // adds to counter c % 8) so that they do not serialise on one L2 line; lanes
-// 0-7 of warp 0 poll the eight counters in parallel with relaxed loads and the
-// CTA proceeds after a fence once every counter reached its target.
+// 0-7 of warp 0 poll the eight counters in parallel with acquire loads and the
+// CTA proceeds once every counter reached its target.
 // Returns false when the launch is aborting.
 __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index, uint32_t where) {
   named_sync(1, kConsumerThreads);
@@ -254,18 +254,19 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
         atomicMax(reinterpret_cast<unsigned long long *>(&p.trace[4 * kTraceMax + index]),
                   static_cast<unsigned long long>(globaltimer()));         // the last CTA to arrive
       }
-      // every thread of the CTA wrote before the bar.sync above; the fence makes
-      // those writes visible GPU-wide before the arrival is
-      __threadfence();
-      atomicAdd(&p.sync->barrier[blockIdx.x % kBarrierLanes][0], 1u);
+      // every thread of the CTA wrote before the bar.sync above; the release
+      // add makes those writes visible GPU-wide before the arrival is
+      red_release_add_u32(&p.sync->barrier[blockIdx.x % kBarrierLanes][0], 1u);
     }
     const int grid = p.grid;
     const uint32_t members = lane < kBarrierLanes ? static_cast<uint32_t>((grid - lane + kBarrierLanes - 1) / kBarrierLanes) : 0u;
     const uint32_t target = index * members;
     const uint64_t deadline = globaltimer() + p.timeout_ns;
     for (uint32_t polls = 1;; ++polls) {
+      // acquire: once a counter reached its target, the writes released
+      // before those arrivals are visible to this lane
       const bool mine = lane >= kBarrierLanes ||
-                        static_cast<int32_t>(ld_relaxed_u32(&p.sync->barrier[lane][0]) - target) >= 0;
+                        static_cast<int32_t>(ld_acquire_u32(&p.sync->barrier[lane][0]) - target) >= 0;
       if (__all_sync(0xffffffffu, mine)) break;
       if ((polls & 15) == 0) {
         int stop = 0;
@@ -280,9 +281,7 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
         if (__shfl_sync(0xffffffffu, stop, 0)) { ok = 0; break; }
       }
     }
-    // acquire, in every lane that observed a counter: the other CTAs' writes
-    // before their arrivals are visible
-    __threadfence();
+    __syncwarp();   // lanes 0-7's acquires order the CTA's reads after the bar.sync below
     if (lane == 0) {
       if (ok && aborted(p)) ok = 0;
       if (p.trace != nullptr && blockIdx.x == 0 && index < kTraceMax) p.trace[index] = globaltimer();
@@ -291,6 +290,16 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
   }
   named_sync(1, kConsumerThreads);
   return s.misc[0] != 0;
+}
+
+// Slot of a position inside a row's valid range (32-bit: 0 <= t < C); -1 for
+// an invalid block-table entry.  The attention's per-position lookup.
+__device__ __forceinline__ int slot_in_row(const ModelDims &m, const int32_t *bt, int row, int t) {
+  const int logical = t / m.bs;
+  if (logical >= m.bpr) return -1;
+  const int physical = bt[row * m.bpr + logical];
+  if (physical < 0 || physical >= m.NB) return -1;
+  return physical * m.bs + (t - logical * m.bs);
 }
 
 __device__ __forceinline__ int compute_slot(const ModelDims &m, const int32_t *bt, int row,
@@ -454,7 +463,13 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
                           : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
   }
   uint4 v[2][kBatch];
+  uint4 wv[2];   // norm weights, requested together with the activations
   float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+    wv[j] = k8 < K8 ? __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8) : make_uint4(0, 0, 0, 0);
+  }
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int k8 = tid + j * kConsumerThreads;
@@ -493,8 +508,7 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
   for (int j = 0; j < 2; ++j) {
     const int k8 = tid + j * kConsumerThreads;
     if (k8 >= K8) continue;
-    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8);
-    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
+    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv[j]);
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const float r = s.nrm[32 + b];
@@ -579,10 +593,15 @@ __device__ void gemv_tiles_k512(const EpochParams &p, const Smem &s, const Gemv 
   xg_load(3, x30, x31);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  // loop-invariant state in registers
+  const uint8_t *const ring_base = s.ring;
+  uint64_t *const full = s.full;
+  uint64_t *const empty = s.empty;
+  const int stages = p.stages;
   for (int i = 0; i < count; i += 2) {
     const bool two = i + 1 < count;
-    const bool landed = wait_bar(p, &s.full[ring.slot], ring.parity, nullptr, 1000);
-    const uint8_t *t0 = s.ring + static_cast<size_t>(ring.slot) * kStageBytes;
+    const bool landed = wait_bar(p, full + ring.slot, ring.parity, nullptr, 1000);
+    const uint8_t *t0 = ring_base + static_cast<size_t>(ring.slot) * kStageBytes;
     const uint8_t *t1 = t0 + tile_bytes;
     const int kk1 = kk + 1 == KT ? 0 : kk + 1;
     // all shared loads of the stage first
@@ -624,8 +643,8 @@ __device__ void gemv_tiles_k512(const EpochParams &p, const Smem &s, const Gemv 
     kk = kk1 + 1 == KT ? 0 : kk1 + 1;
     if (!two) kk = kk1;
     __syncwarp();
-    if (lane == 0 && landed) mbar_arrive(&s.empty[ring.slot]);
-    ring.advance(p.stages);
+    if (lane == 0 && landed) mbar_arrive(empty + ring.slot);
+    ring.advance(stages);
   }
 }
 
@@ -1022,7 +1041,7 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
     // a cached row of position t (never the new position: its k/v come from
     // shared memory); nullptr outside the row's valid blocks
     auto cached = [&](const bf16 *base, int t) -> const uint4 * {
-      const int st = compute_slot(m, s.bt, b, t);
+      const int st = slot_in_row(m, s.bt, b, t);
       return st < 0 ? nullptr : reinterpret_cast<const uint4 *>(base + static_cast<size_t>(st) * row_stride);
     };
     auto load_k = [&](uint4 (&krow)[kSlices], int c0) {

@@ -102,14 +102,14 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Not volatile, so that the scheduler may hoist it past register-only work;
-// the memory clobber keeps it after the mbarrier wait that guards the data.
+// Volatile (kept after the volatile mbarrier wait that guards the data) but
+// without a memory clobber, which would make every shared load a compiler
+// barrier and force pointers kept in memory to be reloaded around it.
 __device__ __forceinline__ uint4 lds128(const void *ptr) {
   uint4 v;
-  asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "r"(smem_u32(ptr))
-      : "memory");
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(ptr)));
   return v;
 }
 
