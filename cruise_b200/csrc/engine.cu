@@ -47,14 +47,17 @@ __host__ __device__ inline uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
-enum SynthMode : int32_t { kPlain = 0, kQkvRows = 1, kGateUp = 2, kDownPad = 3, kRowsPad = 4 };
+enum SynthMode : int32_t { kPlain = 0, kQkvRows = 1, kGateUp = 2, kDownPad = 3, kRowsPad = 4, kColsOff = 5 };
 
 struct SynthMap {
   int32_t mode;
   int32_t ids[3];       // tensor ids (q,k,v for kQkvRows; gate,up for kGateUp)
   int64_t cols;         // row length of the canonical tensor(s)
   int64_t rows0, rows1; // q rows / k rows (kQkvRows); valid rows (kRowsPad)
-  int64_t dst_cols;     // packed row length (kDownPad)
+  int64_t dst_cols;     // packed row length (kDownPad, kColsOff)
+  int64_t off0, off1;   // shard offsets into the canonical tensor (tensor parallelism):
+                        // q row / k,v row (kQkvRows), intermediate row (kGateUp),
+                        // column (kDownPad, kColsOff), vocabulary row (kRowsPad)
   int32_t tiled;        // destination is a tiled matrix with dst_cols columns
   int32_t kc;           // its tile width
 };
@@ -87,26 +90,33 @@ __global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_
     switch (map.mode) {
       case kQkvRows: {
         const int64_t r = e / map.cols, c = e % map.cols;
-        if (r < map.rows0) { id = map.ids[0]; idx = r * map.cols + c; }
-        else if (r < map.rows0 + map.rows1) { id = map.ids[1]; idx = (r - map.rows0) * map.cols + c; }
-        else { id = map.ids[2]; idx = (r - map.rows0 - map.rows1) * map.cols + c; }
+        if (r < map.rows0) { id = map.ids[0]; idx = (map.off0 + r) * map.cols + c; }
+        else if (r < map.rows0 + map.rows1) { id = map.ids[1]; idx = (map.off1 + r - map.rows0) * map.cols + c; }
+        else { id = map.ids[2]; idx = (map.off1 + r - map.rows0 - map.rows1) * map.cols + c; }
         break;
       }
       case kGateUp: {
         const int64_t R = e / map.cols, c = e % map.cols;
         const int64_t blk = R / 16, rr = R % 16;
         id = rr < 8 ? map.ids[0] : map.ids[1];
-        idx = (blk * 8 + (rr & 7)) * map.cols + c;
+        idx = (map.off0 + blk * 8 + (rr & 7)) * map.cols + c;
         break;
       }
       case kDownPad: {
         const int64_t r = e / map.dst_cols, c = e % map.dst_cols;
-        zero = c >= map.cols;
-        idx = r * map.cols + c;
+        zero = c >= map.rows0;
+        idx = r * map.cols + map.off0 + c;
         break;
       }
       case kRowsPad: {
-        zero = e / map.cols >= map.rows0;
+        const int64_t r = e / map.cols, c = e % map.cols;
+        zero = r >= map.rows0;
+        idx = (map.off0 + r) * map.cols + c;
+        break;
+      }
+      case kColsOff: {
+        const int64_t r = e / map.dst_cols, c = e % map.dst_cols;
+        idx = r * map.cols + map.off0 + c;
         break;
       }
       default:
@@ -186,6 +196,14 @@ struct Engine {
   std::string last_error;
   std::mutex execute_mutex;
   std::array<uint8_t, kTilingBytes> tiling{};
+  // tensor parallelism
+  int tp_rank = 0, tp_size = 1;
+  TpExchange *xchg = nullptr;              // this rank's exchange block (IPC-exported)
+  TpExchange **d_peers = nullptr;          // device array of every rank's block
+  std::vector<void *> opened;              // peer blocks opened through IPC
+  bool tp_connected = false;
+  uint32_t launches = 0;                   // epochs launched (exchange sequence base)
+  bf16 *h_alt = nullptr;
 };
 
 // Every host<->device copy runs on the engine's own (non-blocking) stream and is
@@ -206,6 +224,7 @@ int32_t set_err(Engine *e, cudaError_t err, const char *what) {
 
 bool valid_config(const CruiseModelConfig &c) {
   if (c.num_layers < 1 || c.num_layers > 64 || c.hidden < 64 || c.hidden % 64 != 0) return false;
+  if (c.hidden > 4096) return false;   // RMSNorm staging: 2 x 8 elements per thread and row
   if (c.num_heads < 1 || c.num_kv_heads < 1 || c.num_heads % c.num_kv_heads != 0) return false;
   if (c.head_dim != 64 && c.head_dim != 128) return false;
   if (c.num_heads * c.head_dim != c.hidden) return false;
@@ -220,19 +239,64 @@ bool valid_config(const CruiseModelConfig &c) {
   return true;
 }
 
+// Shard of tensor-parallel rank `rank` of `size`: query heads [q0, q0+nq) and
+// KV heads [kv0, kv0+nkv) (a rank holds whole KV groups when size <= KV heads,
+// else size / KV-heads ranks share one KV head and split its query heads,
+// the first ranks of a group taking one more), intermediate rows [i0, i0+ni)
+// and vocabulary rows [v0, v0+nv).
+struct TpGeom {
+  int q0, nq, kv0, nkv, i0, ni, v0, nv;
+};
+
+bool tp_geometry(const CruiseModelConfig &c, int rank, int size, TpGeom &g) {
+  if (size < 1 || size > kMaxTp || rank < 0 || rank >= size) return false;
+  const int nq = c.num_heads, nkv = c.num_kv_heads, grp = nq / nkv;
+  if (size <= nkv) {
+    if (nkv % size != 0) return false;
+    g.nkv = nkv / size;
+    g.kv0 = rank * g.nkv;
+    g.q0 = g.kv0 * grp;
+    g.nq = g.nkv * grp;
+  } else {
+    if (size % nkv != 0) return false;
+    const int per = size / nkv;   // ranks sharing one KV head
+    if (grp < per) return false;
+    const int part = rank % per, base = grp / per, extra = grp % per;
+    g.kv0 = rank / per;
+    g.nkv = 1;
+    g.q0 = g.kv0 * grp + part * base + std::min(part, extra);
+    g.nq = base + (part < extra ? 1 : 0);
+  }
+  if (c.intermediate % size != 0 || (c.intermediate / size) % 8 != 0) return false;
+  g.ni = c.intermediate / size;
+  g.i0 = rank * g.ni;
+  const int vs = (c.vocab + size - 1) / size;
+  g.v0 = rank * vs;
+  g.nv = std::min(vs, c.vocab - g.v0);
+  return g.nv > 0;
+}
+
 void fill_dims(Engine *e) {
   const CruiseModelConfig &c = e->cfg;
   ModelDims &m = e->m;
+  TpGeom g{};
+  tp_geometry(c, e->tp_rank, e->tp_size, g);   // validated by the caller
   m.L = c.num_layers;
   m.H = c.hidden;
-  m.nq = c.num_heads;
-  m.nkv = c.num_kv_heads;
+  m.nq = g.nq;
+  m.nkv = g.nkv;
   m.d = c.head_dim;
-  m.I = c.intermediate;
-  m.I_pad = static_cast<int32_t>(align_up(c.intermediate, 64));
+  m.q0 = g.q0;
+  m.kv0 = g.kv0;
+  m.nkv_all = c.num_kv_heads;
+  m.Hq = g.nq * c.head_dim;
+  m.I = g.ni;
+  m.I_pad = static_cast<int32_t>(align_up(g.ni, 64));
   m.V = c.vocab;
-  m.V_pad = static_cast<int32_t>(align_up(c.vocab, kRows));
-  m.Nqkv = c.hidden + 2 * c.num_kv_heads * c.head_dim;
+  m.v0 = g.v0;
+  m.Vl = g.nv;
+  m.V_pad = static_cast<int32_t>(align_up(g.nv, kRows));
+  m.Nqkv = (g.nq + 2 * g.nkv) * c.head_dim;
   m.eps = c.rms_eps;
   m.sqrt_d = static_cast<float>(std::sqrt(static_cast<double>(c.head_dim)));
   m.bs = c.block_size;
@@ -274,6 +338,10 @@ void destroy_engine(Engine *e) {
   cudaFree(e->state);
   cudaFree(e->d_layers);
   cudaFree(e->d_payload);
+  for (void *ptr : e->opened) cudaIpcCloseMemHandle(ptr);
+  cudaFree(e->d_peers);
+  cudaFree(e->xchg);
+  cudaFree(e->h_alt);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
@@ -281,29 +349,52 @@ void destroy_engine(Engine *e) {
   delete e;
 }
 
-Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status) {
+// why the calling thread's last create_engine returned null ("" after a success)
+thread_local std::string g_create_error;
+
+Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status, int tp_rank = 0,
+                      int tp_size = 1) {
+  g_create_error.clear();
   *status = 5;
-  if (!valid_config(cfg)) return nullptr;
+  if (!valid_config(cfg)) {
+    g_create_error = "unsupported model configuration";
+    return nullptr;
+  }
+  TpGeom geom{};
+  if (!tp_geometry(cfg, tp_rank, tp_size, geom)) {
+    g_create_error = "no tensor-parallel sharding of this model over " + std::to_string(tp_size) + " ranks";
+    return nullptr;
+  }
   Engine *e = new Engine();
   e->cfg = cfg;
   e->device = device;
+  e->tp_rank = tp_rank;
+  e->tp_size = tp_size;
   fill_dims(e);
   const ModelDims &m = e->m;
   *status = 3;
-  if (cudaSetDevice(device) != cudaSuccess) { delete e; return nullptr; }
-  cudaDeviceProp prop{};
-  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) {
-    delete e;
+  // records why creation stopped (read back through cruise_epoch_last_error(NULL))
+  auto fail = [&](const char *what, bool destroy = true) -> Engine * {
+    const cudaError_t err = cudaGetLastError();
+    g_create_error = std::string(what) + (err != cudaSuccess ? std::string(": ") + cudaGetErrorString(err) : "");
+    if (destroy) {
+      destroy_engine(e);
+    } else {
+      delete e;
+    }
     return nullptr;
-  }
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return fail("cudaSetDevice", false);
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return fail("cudaGetDeviceProperties", false);
+  if (prop.major < 10) return fail("the engine is built for sm_100a (compute capability 10.x)", false);
   int coop = 0;
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
-  if (!coop) { delete e; return nullptr; }
+  if (!coop) return fail("the device does not support cooperative launches", false);
   e->sms = std::min(prop.multiProcessorCount, kMaxCtas);
   if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreate(&e->ev0) != cudaSuccess || cudaEventCreate(&e->ev1) != cudaSuccess) {
-    destroy_engine(e);
-    return nullptr;
+    return fail("stream or event creation");
   }
   // shared memory geometry: the activation rows in smem hold the widest input of
   // the projections that stage it there; the down projection reads its input
@@ -319,23 +410,24 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   // the attention unit's scratch aliases the activation rows and the reduction ring
   if (attn_scratch_bytes(m.d, m.C) >
       static_cast<size_t>(kBatch) * e->xs_stride * 2 + static_cast<size_t>(kRedSlots) * kConsumerWarps * 64 * 4) {
-    destroy_engine(e);
-    return nullptr;
+    return fail("the attention scratch does not fit the activation rows");
   }
   const size_t limit = prop.sharedMemPerBlockOptin;
   int stages = kMaxStages;
   while (stages > 2 && smem_bytes(stages, e->xs_stride) > limit) --stages;
   e->stages = stages;
   e->smem = smem_bytes(stages, e->xs_stride);
-  if (e->smem > limit) { *status = 5; destroy_engine(e); return nullptr; }
+  if (e->smem > limit) {
+    *status = 5;
+    return fail("shared memory of the smallest stage ring exceeds the per-block limit");
+  }
   if (cudaFuncSetAttribute(resident_epoch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(e->smem)) != cudaSuccess) {
-    destroy_engine(e);
-    return nullptr;
+    return fail("cudaFuncSetAttribute(max dynamic shared memory)");
   }
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, resident_epoch_kernel, kThreads, e->smem);
-  if (per_sm < 1) { destroy_engine(e); return nullptr; }
+  if (per_sm < 1) return fail("the epoch kernel has no resident CTA per SM (registers or shared memory)");
 
   // ---- weights: one allocation ----
   *status = 6;
@@ -355,7 +447,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
     lo[l].w_post = take(H);
     lo[l].qkv_w = take(static_cast<int64_t>(m.Nqkv) * H);
     lo[l].qkv_b = take(m.Nqkv);
-    lo[l].o_w = take(H * H);
+    lo[l].o_w = take(H * static_cast<int64_t>(m.Hq));
     lo[l].gu_w = take(2LL * m.I * H);
     lo[l].down_w = take(H * m.I_pad);
   }
@@ -363,7 +455,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   const size_t off_lm = take(static_cast<int64_t>(m.V_pad) * H);
   (void)kv;
   e->weight_bytes = total;
-  if (cudaMalloc(&e->weights, total) != cudaSuccess) { destroy_engine(e); return nullptr; }
+  if (cudaMalloc(&e->weights, total) != cudaSuccess) return fail("weight allocation");
   cudaMemsetAsync(e->weights, 0, total, e->stream);
   uint8_t *wb = static_cast<uint8_t *>(e->weights);
   auto wp = [&](size_t off) { return reinterpret_cast<bf16 *>(wb + off); };
@@ -375,7 +467,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
     e->layers[l] = LayerWeights{wp(lo[l].w_in), wp(lo[l].w_post), wp(lo[l].qkv_w), wp(lo[l].qkv_b),
                                 wp(lo[l].o_w),  wp(lo[l].gu_w),   wp(lo[l].down_w)};
   }
-  if (cudaMalloc(&e->d_layers, sizeof(LayerWeights) * m.L) != cudaSuccess) { destroy_engine(e); return nullptr; }
+  if (cudaMalloc(&e->d_layers, sizeof(LayerWeights) * m.L) != cudaSuccess) return fail("layer table allocation");
   cudaMemcpyAsync(e->d_layers, e->layers.data(), sizeof(LayerWeights) * m.L, cudaMemcpyHostToDevice, e->stream);
 
   // ---- caches, activations, control blocks: one allocation ----
@@ -398,7 +490,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   const size_t o_trace = take2(5 * kTraceMax * sizeof(uint64_t));
   const size_t o_io = take2(sizeof(EpochIO)), o_res = take2(sizeof(ResidentState));
   const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sizeof(SyncState));
-  if (cudaMalloc(&e->state, st) != cudaSuccess) { destroy_engine(e); return nullptr; }
+  if (cudaMalloc(&e->state, st) != cudaSuccess) return fail("state allocation");
   cudaMemsetAsync(e->state, 0, st, e->stream);
   uint8_t *sb = static_cast<uint8_t *>(e->state);
   e->key_cache = reinterpret_cast<bf16 *>(sb + o_k);
@@ -420,14 +512,27 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status)
   e->d_work = reinterpret_cast<EpochWork *>(sb + o_work);
   e->d_sync = reinterpret_cast<SyncState *>(sb + o_sync);
   if (cudaHostAlloc(reinterpret_cast<void **>(&e->h_io), sizeof(EpochIO), cudaHostAllocDefault) != cudaSuccess) {
-    destroy_engine(e);
-    return nullptr;
+    return fail("pinned host allocation");
+  }
+  if (e->tp_size > 1) {
+    // the exchange block is its own allocation so that it can be exported by IPC
+    if (cudaMalloc(reinterpret_cast<void **>(&e->xchg), sizeof(TpExchange)) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&e->d_peers), sizeof(TpExchange *) * kMaxTp) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void **>(&e->h_alt), static_cast<size_t>(kBatch) * H * 2) != cudaSuccess) {
+      return fail("tensor-parallel exchange allocation");
+    }
+    cudaMemsetAsync(e->xchg, 0, sizeof(TpExchange), e->stream);
+    cudaMemsetAsync(e->d_peers, 0, sizeof(TpExchange *) * kMaxTp, e->stream);
+    cudaMemsetAsync(e->h_alt, 0, static_cast<size_t>(kBatch) * H * 2, e->stream);
   }
   std::vector<uint16_t> cos_t, sin_t;
   default_rope(e, cos_t, sin_t);
   cudaMemcpyAsync(e->rope_cos, cos_t.data(), cos_t.size() * 2, cudaMemcpyHostToDevice, e->stream);
   cudaMemcpyAsync(e->rope_sin, sin_t.data(), sin_t.size() * 2, cudaMemcpyHostToDevice, e->stream);
-  if (cudaStreamSynchronize(e->stream) != cudaSuccess) { *status = 3; destroy_engine(e); return nullptr; }
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) {
+    *status = 3;
+    return fail("initialising the resident state");
+  }
   *status = 0;
   return e;
 }
@@ -455,7 +560,7 @@ bool locate(Engine *e, const std::string &name, TensorPlace &tp) {
   };
   if (name == "model.embed_tokens.weight") return plain(e->embed, m.V, H, 0);
   if (name == "model.norm.weight") return plain(e->final_norm, 1, H, 0);
-  if (name == "lm_head.weight") return tiled(e->lm_head, m.V, H, kRowOffset, 0, H);
+  if (name == "lm_head.weight") return tiled(e->lm_head, m.Vl, H, kRowOffset, 0, H);
   const std::string prefix = "model.layers.";
   if (name.compare(0, prefix.size(), prefix) != 0) return false;
   const size_t dot = name.find('.', prefix.size());
@@ -466,13 +571,14 @@ bool locate(Engine *e, const std::string &name, TensorPlace &tp) {
   const LayerWeights &lw = e->layers[layer];
   if (key == "input_layernorm.weight") return plain(lw.w_in, 1, H, 0);
   if (key == "post_attention_layernorm.weight") return plain(lw.w_post, 1, H, 0);
-  if (key == "self_attn.q_proj.weight") return tiled(lw.qkv_w, H, H, kRowOffset, 0, H);
-  if (key == "self_attn.k_proj.weight") return tiled(lw.qkv_w, kv, H, kRowOffset, H, H);
-  if (key == "self_attn.v_proj.weight") return tiled(lw.qkv_w, kv, H, kRowOffset, H + kv, H);
-  if (key == "self_attn.q_proj.bias") return plain(lw.qkv_b, 1, H, 0);
-  if (key == "self_attn.k_proj.bias") return plain(lw.qkv_b, 1, kv, H);
-  if (key == "self_attn.v_proj.bias") return plain(lw.qkv_b, 1, kv, H + kv);
-  if (key == "self_attn.o_proj.weight") return tiled(lw.o_w, H, H, kRowOffset, 0, H);
+  const int64_t Hq = m.Hq;   // this rank's query rows (H without tensor parallelism)
+  if (key == "self_attn.q_proj.weight") return tiled(lw.qkv_w, Hq, H, kRowOffset, 0, H);
+  if (key == "self_attn.k_proj.weight") return tiled(lw.qkv_w, kv, H, kRowOffset, Hq, H);
+  if (key == "self_attn.v_proj.weight") return tiled(lw.qkv_w, kv, H, kRowOffset, Hq + kv, H);
+  if (key == "self_attn.q_proj.bias") return plain(lw.qkv_b, 1, Hq, 0);
+  if (key == "self_attn.k_proj.bias") return plain(lw.qkv_b, 1, kv, Hq);
+  if (key == "self_attn.v_proj.bias") return plain(lw.qkv_b, 1, kv, Hq + kv);
+  if (key == "self_attn.o_proj.weight") return tiled(lw.o_w, H, Hq, kRowOffset, 0, Hq);
   if (key == "mlp.gate_proj.weight") return tiled(lw.gu_w, m.I, H, kRowGate, 0, H);
   if (key == "mlp.up_proj.weight") return tiled(lw.gu_w, m.I, H, kRowUp, 0, H);
   if (key == "mlp.down_proj.weight") return tiled(lw.down_w, H, m.I, kRowOffset, 0, m.I_pad);
@@ -539,24 +645,29 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
     launch(const_cast<bf16 *>(lw.w_post), H, plain(base + 1));
     SynthMap q{};
     q.mode = kQkvRows; q.ids[0] = base + 2; q.ids[1] = base + 4; q.ids[2] = base + 6;
-    q.cols = H; q.rows0 = H; q.rows1 = kv;
+    q.cols = H; q.rows0 = m.Hq; q.rows1 = kv;
+    q.off0 = static_cast<int64_t>(m.q0) * m.d; q.off1 = static_cast<int64_t>(m.kv0) * m.d;
     SynthMap qb = q;
     qb.ids[0] = base + 3; qb.ids[1] = base + 5; qb.ids[2] = base + 7; qb.cols = 1;
     launch(const_cast<bf16 *>(lw.qkv_w), static_cast<int64_t>(m.Nqkv) * H, tile(q, H));
     launch(const_cast<bf16 *>(lw.qkv_b), m.Nqkv, qb);
-    SynthMap o = plain(base + 8);
-    launch(const_cast<bf16 *>(lw.o_w), H * H, tile(o, H));
+    SynthMap o{};
+    o.mode = kColsOff; o.ids[0] = base + 8; o.cols = H; o.dst_cols = m.Hq;
+    o.off0 = static_cast<int64_t>(m.q0) * m.d;
+    launch(const_cast<bf16 *>(lw.o_w), H * m.Hq, tile(o, m.Hq));
     SynthMap gu{};
     gu.mode = kGateUp; gu.ids[0] = base + 9; gu.ids[1] = base + 10; gu.cols = H;
+    gu.off0 = static_cast<int64_t>(e->tp_rank) * m.I;
     launch(const_cast<bf16 *>(lw.gu_w), 2LL * m.I * H, tile(gu, H));
     SynthMap dn{};
-    dn.mode = kDownPad; dn.ids[0] = base + 11; dn.cols = m.I;
+    dn.mode = kDownPad; dn.ids[0] = base + 11; dn.cols = e->cfg.intermediate; dn.rows0 = m.I;
+    dn.off0 = static_cast<int64_t>(e->tp_rank) * m.I;
     dn = tile(dn, m.I_pad);
     launch(const_cast<bf16 *>(lw.down_w), H * m.I_pad, dn);
   }
   launch(e->final_norm, H, plain(1 + kLayerTensors * L));
   SynthMap lm{};
-  lm.mode = kRowsPad; lm.ids[0] = 2 + kLayerTensors * L; lm.cols = H; lm.rows0 = m.V;
+  lm.mode = kRowsPad; lm.ids[0] = 2 + kLayerTensors * L; lm.cols = H; lm.rows0 = m.Vl; lm.off0 = m.v0;
   launch(e->lm_head, static_cast<int64_t>(m.V_pad) * H, tile(lm, H));
   cudaError_t err = cudaGetLastError();
   if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
@@ -564,7 +675,7 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
 }
 
 int64_t import_payload_bytes(const Engine *e) {
-  return 2LL * e->m.L * kBatch * e->m.bs * e->m.nkv * e->m.d * 2;
+  return 2LL * e->m.L * kBatch * e->m.bs * e->m.nkv_all * e->m.d * 2;   // every KV head of the model
 }
 
 // One epoch: H2D of the 8 inputs (+ optional import payload), one cooperative
@@ -640,6 +751,20 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   if (e->trace_on) cudaMemsetAsync(e->trace, 0, 5 * kTraceMax * sizeof(uint64_t), e->stream);
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
   p.l2_ahead = e->l2_ahead;
+  p.tp_size = e->tp_size;
+  p.tp_rank = e->tp_rank;
+  if (e->tp_size > 1) {
+    if (!e->tp_connected) {
+      e->last_error = "tensor-parallel engine used before cruise_epoch_tp_connect";
+      return -5;
+    }
+    p.tp_peer = e->d_peers;
+    p.tp_local = e->xchg;
+    p.h_alt = e->h_alt;
+  }
+  // exchange sequence numbers grow across launches (every rank launches the
+  // same epochs); a launch uses at most 8 x 142 of its 65,536
+  p.tp_seq_base = ++e->launches << 16;
   void *args[] = {&p};
   cudaEventRecord(e->ev0, e->stream);
   err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
@@ -888,6 +1013,10 @@ int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *positi
                           const int32_t *control, int64_t *history, int32_t *control_out) {
   cudaError_t err = cudaSetDevice(e->device);
   if (err != cudaSuccess) return set_err(e, err, "noalloc set device");
+  if (e->tp_size > 1) {
+    e->last_error = "cruise_epoch_run_noalloc: single-GPU engines only (no tensor parallelism)";
+    return -4;
+  }
   const NoAllocLayout l = noalloc_layout(e);
   if (l.total > kNoAllocScratchBytes) {
     e->last_error = "cruise_epoch_run_noalloc: this model needs " + std::to_string(l.total) +
@@ -949,6 +1078,7 @@ int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *positi
   p.trace = nullptr;
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
   p.l2_ahead = e->l2_ahead;
+  p.tp_size = 1;
   void *args[] = {&p};
   err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
                                     dim3(kThreads), args, e->smem, e->stream);
@@ -973,6 +1103,55 @@ using cruise::kMaxSteps;
 extern "C" {
 
 int32_t cruise_epoch_preset(const char *name, CruiseModelConfig *cfg) { return cruise::preset(name, cfg); }
+
+void *cruise_epoch_create_tp(const CruiseModelConfig *cfg, int32_t device, int32_t tp_rank, int32_t tp_size,
+                             int32_t *status) {
+  int32_t dummy = 0;
+  if (status == nullptr) status = &dummy;
+  *status = 1;
+  if (cfg == nullptr) return nullptr;
+  return cruise::create_engine(*cfg, device, status, tp_rank, tp_size);
+}
+
+int32_t cruise_epoch_tp_handle(void *engine, void *handle_out) {
+  if (engine == nullptr || handle_out == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  if (e->tp_size < 2) return -1;
+  cudaSetDevice(e->device);
+  cudaIpcMemHandle_t handle;
+  const cudaError_t err = cudaIpcGetMemHandle(&handle, e->xchg);
+  if (err != cudaSuccess) return cruise::set_err(e, err, "tp handle");
+  std::memcpy(handle_out, &handle, sizeof(handle));
+  return 0;
+}
+
+int32_t cruise_epoch_tp_connect(void *engine, const void *handles) {
+  if (engine == nullptr || handles == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  if (e->tp_size < 2 || e->tp_connected) return -1;
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  std::vector<cruise::TpExchange *> peers(cruise::kMaxTp, nullptr);
+  for (int r = 0; r < e->tp_size; ++r) {
+    if (r == e->tp_rank) {
+      peers[r] = e->xchg;
+      continue;
+    }
+    cudaIpcMemHandle_t handle;
+    std::memcpy(&handle, static_cast<const uint8_t *>(handles) + static_cast<size_t>(r) * sizeof(handle),
+                sizeof(handle));
+    void *ptr = nullptr;
+    const cudaError_t err = cudaIpcOpenMemHandle(&ptr, handle, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return cruise::set_err(e, err, "tp connect: open peer exchange block");
+    e->opened.push_back(ptr);
+    peers[r] = static_cast<cruise::TpExchange *>(ptr);
+  }
+  const cudaError_t err = cruise::copy_sync(e, e->d_peers, peers.data(), sizeof(cruise::TpExchange *) * cruise::kMaxTp,
+                                            cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) return cruise::set_err(e, err, "tp connect");
+  e->tp_connected = true;
+  return 0;
+}
 
 void *cruise_epoch_create(const CruiseModelConfig *cfg, int32_t device, int32_t *status) {
   int32_t dummy = 0;
@@ -1099,7 +1278,7 @@ int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns, int3
 }
 
 const char *cruise_epoch_last_error(void *engine) {
-  if (engine == nullptr) return "null engine";
+  if (engine == nullptr) return cruise::g_create_error.c_str();
   return static_cast<Engine *>(engine)->last_error.c_str();
 }
 
@@ -1111,16 +1290,28 @@ void *resident_epoch_create(const char *air_path, const char *graph_config, cons
   if (status == nullptr) return nullptr;
   *status = 1;
   std::lock_guard<std::mutex> lifecycle(cruise::g_lifecycle_mutex);
-  if (cruise::g_bridge_active || air_path == nullptr || external_weight_dir == nullptr) return nullptr;
+  cruise::g_create_error.clear();
+  if (cruise::g_bridge_active || air_path == nullptr || external_weight_dir == nullptr) {
+    cruise::g_create_error = cruise::g_bridge_active ? "a resident epoch is already active in this process"
+                                                     : "null model or weight path";
+    return nullptr;
+  }
   CruiseModelConfig cfg{};
-  if (cruise::preset(air_path, &cfg) != 0) { *status = 5; return nullptr; }
+  if (cruise::preset(air_path, &cfg) != 0) {
+    *status = 5;
+    cruise::g_create_error = std::string("unknown model preset ") + air_path;
+    return nullptr;
+  }
   std::array<uint8_t, cruise::kTilingBytes> tiling{};
   if (tiling_path != nullptr && tiling_path[0] != '\0') {
     std::ifstream t(tiling_path, std::ios::binary | std::ios::ate);
-    if (!t || static_cast<size_t>(t.tellg()) != tiling.size()) { *status = 2; return nullptr; }
     t.seekg(0, std::ios::beg);
-    t.read(reinterpret_cast<char *>(tiling.data()), tiling.size());
-    if (!t) { *status = 2; return nullptr; }
+    if (t) t.read(reinterpret_cast<char *>(tiling.data()), tiling.size());
+    if (!t || t.gcount() != static_cast<std::streamsize>(tiling.size()) || t.peek() != EOF) {
+      *status = 2;
+      cruise::g_create_error = "tiling file missing or not " + std::to_string(tiling.size()) + " bytes";
+      return nullptr;
+    }
   }
   Engine *e = cruise::create_engine(cfg, 0, status);
   if (e == nullptr) return nullptr;
@@ -1147,6 +1338,7 @@ void *resident_epoch_create(const char *air_path, const char *graph_config, cons
   if (rc != 0) {
     cruise::destroy_engine(e);
     *status = 4;
+    cruise::g_create_error = "loading the weights from " + weights + " failed";
     return nullptr;
   }
   auto *be = new BridgeEngine();

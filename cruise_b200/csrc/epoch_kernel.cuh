@@ -53,6 +53,11 @@ struct Gemv {
   int32_t xmode;
   int32_t xsrc_stride;
   int32_t embed_src;     // 1: the norm source is embed[token[b]] (layer 0)
+  // tensor parallelism: the norm source is xsrc + bf16(sum over ranks of the
+  // exchange partial set `reduce_set`); this CTA writes its slice of that sum
+  // to h_dst (-1: no reduction)
+  int32_t reduce_set;
+  bf16 *h_dst;
 };
 
 __host__ __device__ inline int pick_kc(int K) {
@@ -70,27 +75,35 @@ __host__ __device__ inline int64_t tiled_offset(int64_t n, int64_t k, int64_t K,
   return ((rg * (K / kc) + kk) * kRows + r) * kc + unit * 8 + (kin & 7);
 }
 
+// Residual buffers under tensor parallelism: QKV of layer l > 0 and lm_head
+// normalise h_alt + the down partials and write h; gate/up normalises h + the
+// O partials and writes h_alt.  Without it every projection reads h in place.
 __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int kind) {
   const ModelDims &m = p.m;
+  const bool tp = p.tp_size > 1;
   Gemv g{};
   g.kind = kind;
+  g.reduce_set = -1;
   if (kind == kLM) {
     g.W = p.lm_head; g.N = m.V_pad; g.K = m.H;
     g.xmode = kXNorm; g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = p.final_norm;
+    if (tp) { g.xsrc = p.h_alt; g.reduce_set = 1; g.h_dst = p.h; }
   } else {
     const LayerWeights &lw = p.layers[layer];
     switch (kind) {
       case kQKV:
         g.W = lw.qkv_w; g.bias = lw.qkv_b; g.N = m.Nqkv; g.K = m.H; g.xmode = kXNorm;
         g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = lw.w_in; g.embed_src = layer == 0;
+        if (tp && layer > 0) { g.xsrc = p.h_alt; g.reduce_set = 1; g.h_dst = p.h; }
         break;
       case kO:
-        g.W = lw.o_w; g.N = m.H; g.K = m.H; g.xmode = kXCopy; g.xsrc = p.attn;
-        g.xsrc_stride = m.H;
+        g.W = lw.o_w; g.N = m.H; g.K = m.Hq; g.xmode = kXCopy; g.xsrc = p.attn;
+        g.xsrc_stride = m.Hq;
         break;
       case kGU:
         g.W = lw.gu_w; g.N = 2 * m.I; g.K = m.H; g.xmode = kXNorm; g.xsrc = p.h;
         g.xsrc_stride = m.H; g.norm_w = lw.w_post;
+        if (tp) { g.reduce_set = 0; g.h_dst = p.h_alt; }
         break;
       default:  // kDown
         g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = p.down_xglobal ? kXGlobal : kXCopy;
@@ -294,6 +307,34 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
 
 // Slot of a position inside a row's valid range (32-bit: 0 <= t < C); -1 for
 // an invalid block-table entry.  The attention's per-position lookup.
+// Tensor-parallel rendezvous after a phase whose outputs other ranks read.
+// The grid barrier before it guarantees that every CTA of this rank finished
+// the phase and fenced its peer writes system-wide; CTA 0 then publishes `seq`
+// into every rank's flag slot of this rank, and every CTA waits until all
+// ranks' flags in its local exchange block reached `seq` (flags only grow).
+__device__ bool tp_rendezvous(const EpochParams &p, const Smem &s, uint32_t seq, uint32_t where) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    if (blockIdx.x == 0 && lane < p.tp_size) st_release_sys_u32(&p.tp_peer[lane]->flag[p.tp_rank][0], seq);
+    int ready = 1;
+    if (lane < p.tp_size) {
+      const uint32_t *flag = &p.tp_local->flag[lane][0];
+      const uint64_t deadline = globaltimer() + p.timeout_ns;
+      uint32_t polls = 0;
+      while (static_cast<int32_t>(ld_acquire_sys_u32(flag) - seq) < 0) {
+        if ((++polls & 15) == 0) {
+          if (aborted(p)) { ready = 0; break; }
+          if (globaltimer() > deadline) { raise_error(p, where); ready = 0; break; }
+        }
+      }
+    }
+    ready = __all_sync(0xffffffffu, ready);
+    if (lane == 0) s.misc[1] = ready;
+  }
+  named_sync(1, kConsumerThreads);
+  return s.misc[1] != 0;
+}
+
 __device__ __forceinline__ int slot_in_row(const ModelDims &m, const int32_t *bt, int row, int t) {
   const int logical = t / m.bs;
   if (logical >= m.bpr) return -1;
@@ -438,6 +479,106 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
 }
 
 // ---- consumer: activation prologue ------------------------------------------------------
+// RMSNorm staging under tensor parallelism: x = src + bf16(sum over ranks, in
+// rank order, of the fp32 row-parallel partials) -- the reference's
+// `hidden + materialize(mm_t(...))` with the sum split over ranks -- then the
+// RMSNorm of x into s.xs as usual.  This CTA writes its slice of x (the same
+// slice split as the embedding materialisation) to g.h_dst.
+__device__ void load_x_reduced(const EpochParams &p, const Smem &s, const Gemv &g, const bf16 *const (&rows)[kBatch]) {
+  const int tid = threadIdx.x;
+  const int K = g.K;
+  const int K8 = K / 8;
+  const int T = p.tp_size;
+  const TpExchange *xc = p.tp_local;
+  uint4 v[2][kBatch];
+  uint4 wv[2];
+  float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+    wv[j] = k8 < K8 ? __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8) : make_uint4(0, 0, 0, 0);
+  }
+  const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
+  const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      uint4 out = make_uint4(0, 0, 0, 0);
+      if (k8 < K8) {
+        const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8);
+        float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int src = 0; src < T; ++src) {
+          const float4 *pp = reinterpret_cast<const float4 *>(&xc->part[g.reduce_set][src][b][k8 * 8]);
+          const float4 a = __ldcg(pp), c = __ldcg(pp + 1);
+          sum[0] += a.x; sum[1] += a.y; sum[2] += a.z; sum[3] += a.w;
+          sum[4] += c.x; sum[5] += c.y; sum[6] += c.z; sum[7] += c.w;
+        }
+        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&hv);
+        __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&out);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 hf = __bfloat1622float2(h2[q]);
+          o2[q] = __floats2bfloat162_rn(__fadd_rn(hf.x, rbf(sum[2 * q])), __fadd_rn(hf.y, rbf(sum[2 * q + 1])));
+        }
+        if (k8 >= lo && k8 < hi)
+          *reinterpret_cast<uint4 *>(g.h_dst + static_cast<size_t>(b) * p.m.H + k8 * 8) = out;
+      }
+      v[j][b] = out;
+      const __nv_bfloat162 *x2 = reinterpret_cast<const __nv_bfloat162 *>(&out);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(x2[q]);
+        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.x, f.x));
+        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.y, f.y));
+      }
+    }
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
+  }
+  named_sync(1, kConsumerThreads);
+  if (tid < kBatch) {
+    float total = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + tid];
+    const float var = __fdiv_rn(total, static_cast<float>(K));
+    s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
+  }
+  named_sync(1, kConsumerThreads);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+    if (k8 >= K8) continue;
+    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv[j]);
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const float r = s.nrm[32 + b];
+      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
+      uint4 o;
+      __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 hf = __bfloat1622float2(h2[q]);
+        const float2 wf = __bfloat1622float2(w2[q]);
+        const float nx = rbf(__fmul_rn(hf.x, r));
+        const float ny = rbf(__fmul_rn(hf.y, r));
+        o2[q] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));
+      }
+      *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = o;
+    }
+  }
+  named_sync(1, kConsumerThreads);
+}
+
+
 // Fills s.xs[4][K] with the projection input: RMSNorm of the residual stream
 // (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU output).
 __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
@@ -461,6 +602,10 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
   for (int b = 0; b < kBatch; ++b) {
     rows[b] = g.embed_src ? p.embed + __ldcg(&p.work->token[b]) * static_cast<int64_t>(K)
                           : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
+  }
+  if (g.reduce_set >= 0) {
+    load_x_reduced(p, s, g, rows);
+    return;
   }
   uint4 v[2][kBatch];
   uint4 wv[2];   // norm weights, requested together with the activations
@@ -799,7 +944,8 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
   const int b_lane = lane & 3;
   float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f;
   int64_t pa_rg = -1, pb_rg = -1;
-  if (g.kind == kQKV || g.kind == kO || g.kind == kDown) {
+  const bool tp_partial = p.tp_size > 1 && (g.kind == kO || g.kind == kDown);
+  if (g.kind == kQKV || ((g.kind == kO || g.kind == kDown) && !tp_partial)) {
     const int64_t first_head = tr.t0 % tr.KT == 0 ? tr.t0 / tr.KT : tr.t0 / tr.KT + 1;
     auto fetch = [&](int64_t r, float &v0, float &v1) {
       const int64_t n0 = r * kRows + (lane >> 2), n1 = n0 + 8;
@@ -882,6 +1028,15 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
           // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, e0));
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, e1));
+        } else if (tp_partial) {
+          // row-parallel partial of this rank, sent to every rank (peer memory);
+          // the next RMSNorm staging adds them up (load_x_reduced)
+          const int set = g.kind == kO ? 0 : 1;
+          for (int r = 0; r < p.tp_size; ++r) {
+            float *dst = p.tp_peer[r]->part[set][p.tp_rank][b];
+            dst[n0] = v0;
+            dst[n1] = v1;
+          }
         } else if (g.kind == kO || g.kind == kDown) {
           // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
           p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(v0)));
@@ -898,15 +1053,16 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
           const float l0 = rbf(v0), l1 = rbf(v1);
           float cb = -INFINITY;
           int32_t ci = INT_MAX, cbad = 0;
-          if (n0 < m.V) {
-            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n0] = l0;
+          // rows of this rank's vocabulary shard; ids are global
+          if (n0 < m.Vl) {
+            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + m.v0 + n0] = l0;
             cbad |= !isfinite(l0);
-            if (l0 > cb) { cb = l0; ci = static_cast<int32_t>(n0); }
+            if (l0 > cb) { cb = l0; ci = static_cast<int32_t>(m.v0 + n0); }
           }
-          if (n1 < m.V) {
-            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + n1] = l1;
+          if (n1 < m.Vl) {
+            if (p.logits != nullptr) p.logits[(static_cast<size_t>(step) * kBatch + b) * m.V + m.v0 + n1] = l1;
             cbad |= !isfinite(l1);
-            if (l1 > cb) { cb = l1; ci = static_cast<int32_t>(n1); }
+            if (l1 > cb) { cb = l1; ci = static_cast<int32_t>(m.v0 + n1); }
           }
 #pragma unroll
           for (int off = 4; off < 32; off <<= 1) {   // lanes sharing b: l ^ 4, 8, 16
@@ -927,9 +1083,14 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
     p.arg_idx[blockIdx.x * kBatch + lane] = best_i;
     p.arg_bad[blockIdx.x * kBatch + lane] = bad;
   }
-  // the phase's outputs written by this warp are visible GPU-wide before the
-  // consumers may arrive at the grid barrier
-  __threadfence();
+  // the phase's outputs written by this warp are visible GPU-wide (and to the
+  // peer GPUs under tensor parallelism) before the consumers may arrive at
+  // the grid barrier
+  if (tp_partial) {
+    __threadfence_system();
+  } else {
+    __threadfence();
+  }
   __syncwarp();
   if (lane == 0) mbar_arrive(s.phase_done);
 }
@@ -1028,7 +1189,7 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
   const int vslice = tid % kSlices, vgroup = tid / kSlices;
   for (int u = blockIdx.x; u < units; u += p.grid) {
     const int b = u / m.nq, qh = u % m.nq, kvh = qh / groups;
-    bf16 *out = p.attn + static_cast<size_t>(b) * m.H + qh * D;
+    bf16 *out = p.attn + static_cast<size_t>(b) * m.Hq + qh * D;
     if (s.row_act[b] == 0) {
       for (int i = tid; i < D; i += kConsumerThreads) out[i] = tobf(0.f);
       continue;
@@ -1065,8 +1226,8 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
     }
     cp_async_commit();
     const bf16 *qsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + qh * D;
-    const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + kvh * D;
-    const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.H + m.nkv * D + kvh * D;
+    const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.Hq + kvh * D;
+    const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.Hq + m.nkv * D + kvh * D;
     const bf16 *cs = p.rope_cos + pos * D;
     const bf16 *sn = p.rope_sin + pos * D;
     if (tid < D) {
@@ -1305,6 +1466,9 @@ __device__ void adler_block(const uint8_t *data, int n, uint64_t &S1, uint64_t &
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------------
+// The register file is split over the SM's four sub-partitions (16K registers each) and ten warps put
+// three warps on two of them, so one CTA of 320 threads fits only at <= 168 registers per thread; the
+// launch bound makes ptxas hold that ceiling (a higher cap compiles but leaves zero resident CTAs).
 __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const EpochParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const Smem s = carve_smem(smem_raw, p);
@@ -1343,6 +1507,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
   uint32_t done_parity = 0;
   bool ok = true;
   const size_t block_elems = static_cast<size_t>(m.bs) * m.nkv * m.d;
+  const size_t payload_block_elems = static_cast<size_t>(m.bs) * m.nkv_all * m.d;
   const size_t layer_elems = static_cast<size_t>(m.NB) * block_elems;
 
   // 1. validation (CTA 0)
@@ -1374,10 +1539,15 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       uint4 *d4 = reinterpret_cast<uint4 *>(dst);
       const size_t n16 = block_elems * 2 / 16;
       if (j == 0) {
+        // the payload block holds every KV head of the model; this rank copies
+        // its heads [kv0, kv0 + nkv) of each slot
         const uint4 *s4 = reinterpret_cast<const uint4 *>(
             p.import_payload +
-            ((static_cast<size_t>(cache) * m.L + layer) * kBatch + b) * block_elems * 2);
-        for (size_t i = tid; i < n16; i += kConsumerThreads) d4[i] = __ldcg(s4 + i);
+            ((static_cast<size_t>(cache) * m.L + layer) * kBatch + b) * payload_block_elems * 2);
+        const size_t u_loc = static_cast<size_t>(m.nkv) * m.d / 8, u_all = static_cast<size_t>(m.nkv_all) * m.d / 8;
+        const size_t u_off = static_cast<size_t>(m.kv0) * m.d / 8;
+        for (size_t i = tid; i < n16; i += kConsumerThreads)
+          d4[i] = __ldcg(s4 + (i / u_loc) * u_all + u_off + i % u_loc);
       } else {
         for (size_t i = tid; i < n16; i += kConsumerThreads) d4[i] = make_uint4(0, 0, 0, 0);
       }
@@ -1400,16 +1570,17 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       for (int b = 0; b < kBatch; ++b)
         if (rows & (1 << b)) order[nrows++] = b;
       const int units2 = 2 * m.L * nrows;
-      const int n = static_cast<int>(block_elems * 2);
+      // the imported blocks are the payload's blocks (every KV head): the proof
+      // is computed from the device copy of the payload
+      const int n = static_cast<int>(payload_block_elems * 2);
       for (int u = blockIdx.x; u < units2; u += p.grid) {
         const int cache = u / (m.L * nrows);
         const int layer = (u / nrows) % m.L;
         const int b = order[u % nrows];
-        const bf16 *src = (cache == 0 ? p.key_cache : p.value_cache) + layer * layer_elems +
-                          static_cast<size_t>(w->bt[b * m.bpr]) * block_elems;
+        const uint8_t *src = p.import_payload +
+                             ((static_cast<size_t>(cache) * m.L + layer) * kBatch + b) * payload_block_elems * 2;
         uint64_t S1 = 0, S2 = 0;
-        adler_block(reinterpret_cast<const uint8_t *>(src), n, S1, S2,
-                    reinterpret_cast<float *>(s.xs));
+        adler_block(src, n, S1, S2, reinterpret_cast<float *>(s.xs));
         if (tid == 0) {
           w->adler[2 * u] = S1;
           w->adler[2 * u + 1] = S2;
@@ -1523,6 +1694,52 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
                                 (s.best_val[w1] == s.best_val[w0] && s.best_idx[w1] < s.best_idx[w0]);
             s.misc[4 + tid] = second ? s.best_idx[w1] : s.best_idx[w0];
             s.misc[8 + tid] = s.best_bad[w0] | s.best_bad[w1];
+            if (p.tp_size > 1) {
+              // this rank's vocabulary shard result, sent to every rank
+              TpArg a;
+              a.val = second ? s.best_val[w1] : s.best_val[w0];
+              a.idx = s.misc[4 + tid];
+              a.bad = s.misc[8 + tid];
+              a.pad = 0;
+              for (int r = 0; r < p.tp_size; ++r) p.tp_peer[r]->arg[p.tp_rank][tid] = a;
+              __threadfence_system();
+            }
+          }
+          named_sync(1, kConsumerThreads);
+        }
+        if (p.tp_size > 1) {
+          // cross-rank pass: first maximum over the ranks' shards in rank order
+          // (shards are in increasing id order, so ties keep the lowest id)
+          if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            if (lane < p.tp_size) st_release_sys_u32(&p.tp_peer[lane]->flag[p.tp_rank][0], p.tp_seq_base + seq);
+            int ready = 1;
+            if (lane < p.tp_size) {
+              const uint32_t *flag = &p.tp_local->flag[lane][0];
+              const uint64_t deadline = globaltimer() + p.timeout_ns;
+              uint32_t polls = 0;
+              while (static_cast<int32_t>(ld_acquire_sys_u32(flag) - (p.tp_seq_base + seq)) < 0) {
+                if ((++polls & 15) == 0) {
+                  if (aborted(p)) { ready = 0; break; }
+                  if (globaltimer() > deadline) { raise_error(p, 401); ready = 0; break; }
+                }
+              }
+            }
+            ready = __all_sync(0xffffffffu, ready);
+            if (lane == 0) s.misc[1] = ready;
+          }
+          named_sync(1, kConsumerThreads);
+          if (tid < kBatch && s.misc[1]) {
+            float bv = -INFINITY;
+            int32_t bi = INT_MAX, bb = 0;
+            for (int r = 0; r < p.tp_size; ++r) {
+              const int4 raw = __ldcg(reinterpret_cast<const int4 *>(&p.tp_local->arg[r][tid]));
+              const float v = __int_as_float(raw.x);
+              bb |= raw.z;
+              if (v > bv || (v == bv && raw.y < bi)) { bv = v; bi = raw.y; }
+            }
+            s.misc[4 + tid] = bi;
+            s.misc[8 + tid] = bb;
           }
           named_sync(1, kConsumerThreads);
         }
@@ -1558,6 +1775,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
         }
       }
       if (ok) ok = grid_barrier(p, s, ++barrier_index, 100 + ph);
+      if (ok && p.tp_size > 1 && (kind == kO || kind == kDown))
+        ok = tp_rendezvous(p, s, p.tp_seq_base + seq, 300 + ph);
     }
   }
   if (tid == 0) *s.prod_ctl = -1;   // producer: no more steps

@@ -48,8 +48,17 @@ enum Status : int32_t {
 };
 enum Finish : int32_t { kNone = 0, kEos = 1, kMaxStepsReason = 2, kFallback = 3, kEmpty = 4, kAlreadyFinished = 5 };
 
+// Per-rank geometry.  Without tensor parallelism the rank holds the whole
+// model; with it (tp ranks) the rank holds query heads [q0, q0 + nq), KV heads
+// [kv0, kv0 + nkv) of nkv_all, intermediate rows [i0, i0 + I) and vocabulary
+// rows [v0, v0 + Vl); the residual stream (H) and the embedding are whole.
 struct ModelDims {
   int32_t L, H, nq, nkv, d, I, I_pad, V, V_pad, Nqkv;
+  int32_t Hq;            // attention output width on this rank (nq * d)
+  int32_t Vl;            // lm_head rows on this rank (V without tensor parallelism)
+  int32_t v0;            // global id of this rank's first vocabulary row
+  int32_t kv0, nkv_all;  // first KV head of this rank, KV heads of the model
+  int32_t q0;            // first query head of this rank
   float eps;
   float sqrt_d;          // (float)sqrt(head_dim), the attention divisor
   int32_t bs, bpr, NB, C;
@@ -133,6 +142,21 @@ struct SyncState {
   uint32_t flags[kMaxCtas];    // split row-group partial published (phase seq)
 };
 
+// One rank's block of the tensor-parallel exchange, written by its peers over
+// NVLink: the fp32 row-parallel partials of the O and down projections
+// (double-buffered: set 0 for O, set 1 for down) from every rank, the lm_head
+// argmax partials from every rank, and one sequence flag per source rank.
+constexpr int kMaxTp = 8;
+struct TpArg {
+  float val;
+  int32_t idx, bad, pad;
+};
+struct TpExchange {
+  uint32_t flag[kMaxTp][32];            // flag[src]: last sequence number src published (own 128-B line)
+  TpArg arg[kMaxTp][4];                 // argmax partial of each rank per batch row
+  float part[2][kMaxTp][4][8192];       // [set][src][row][H] (H <= 8192)
+};
+
 struct EpochParams {
   ModelDims m;
   const LayerWeights *layers;  // [L] in device memory
@@ -164,7 +188,14 @@ struct EpochParams {
   uint64_t *trace;             // optional: CTA 0 globaltimer at each grid barrier (exit, entry)
   uint64_t timeout_ns;         // bound of every spin wait
   uint32_t l2_ahead;           // bytes of weights prefetched into L2 beyond the ring (0: off)
-  uint32_t pad1;
+  // tensor parallelism (tp_size 1: off).  Every rank's exchange block is
+  // mapped into every other rank (peer memory over NVLink); tp_peer[r] is rank r's.
+  int32_t tp_size, tp_rank;
+  TpExchange *const *tp_peer;  // device array [tp_size] of the ranks' exchange blocks
+  TpExchange *tp_local;
+  uint32_t tp_seq_base;        // launch-unique base of the exchange sequence numbers
+  uint32_t pad3;
+  bf16 *h_alt;                 // [4][H] second residual buffer (tensor parallelism)
 };
 
 }  // namespace cruise

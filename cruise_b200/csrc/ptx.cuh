@@ -141,6 +141,17 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *ptr) {
   return v;
 }
 
+// System-scope release store / acquire load (flags shared with peer GPUs).
+__device__ __forceinline__ void st_release_sys_u32(uint32_t *ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_release_u32(uint32_t *ptr, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }

@@ -46,7 +46,8 @@ class CudaEpochEngine:
             ctypes.byref(status),
         )
         if not self.handle or status.value != 0:
-            raise RuntimeError(f"failed to create the CUDA resident epoch, status={status.value}")
+            detail = self.library.cruise_epoch_last_error(None).decode()
+            raise RuntimeError(f"failed to create the CUDA resident epoch, status={status.value}: {detail}")
 
     # -- NativeEpochEngine ---------------------------------------------------------
     def warm_up(self) -> NativeWarmupOutput:

@@ -15,7 +15,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .model_config import BATCH, MAX_STEPS, PRESETS, ModelConfig, layer_tensor_names
+from .model_config import BATCH, MAX_STEPS, PRESETS, ModelConfig, TpShard, layer_tensor_names
 
 CONTROL_IN = 11
 CONTROL_OUT = 28
@@ -58,14 +58,20 @@ class EngineError(RuntimeError):
 
 
 class EpochEngine:
-    def __init__(self, config: ModelConfig | str, device: int = 0) -> None:
+    def __init__(self, config: ModelConfig | str, device: int = 0, tp_rank: int = 0, tp_size: int = 1) -> None:
         self.config = PRESETS[config] if isinstance(config, str) else config
         self.lib = _lib.load()
+        self.shard = TpShard.of(self.config, tp_rank, tp_size)
         status = ctypes.c_int32(-1)
         c_config = self.config.to_c()
-        self.handle = self.lib.cruise_epoch_create(ctypes.byref(c_config), device, ctypes.byref(status))
+        if tp_size > 1:
+            self.handle = self.lib.cruise_epoch_create_tp(ctypes.byref(c_config), device, tp_rank, tp_size,
+                                                          ctypes.byref(status))
+        else:
+            self.handle = self.lib.cruise_epoch_create(ctypes.byref(c_config), device, ctypes.byref(status))
         if not self.handle or status.value != 0:
-            raise EngineError(f"cruise_epoch_create failed with status {status.value}")
+            detail = self.lib.cruise_epoch_last_error(None).decode()
+            raise EngineError(f"cruise_epoch_create failed with status {status.value}: {detail}")
         self.device = device
         cos, sin = rope_tables(self.config)
         self._check(
@@ -119,9 +125,21 @@ class EpochEngine:
         for name in layer_tensor_names(self.config.num_layers):
             self.set_weight(name, weights[name])
 
+    # -- tensor parallelism -------------------------------------------------------------
+    def tp_handle(self) -> bytes:
+        """The 64-byte IPC handle of this rank's exchange block."""
+        buf = ctypes.create_string_buffer(64)
+        self._check(self.lib.cruise_epoch_tp_handle(self.handle, buf), "tp_handle")
+        return buf.raw
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        """Maps the other ranks' exchange blocks (handles in rank order)."""
+        raw = b"".join(handles)
+        self._check(self.lib.cruise_epoch_tp_connect(self.handle, raw), "tp_connect")
+
     # -- KV cache ------------------------------------------------------------------
     def read_kv(self) -> tuple[torch.Tensor, torch.Tensor]:
-        shape = self.config.kv_cache_shape
+        shape = self.shard.kv_cache_shape(self.config)
         key = np.empty(shape, dtype=np.int16)
         value = np.empty(shape, dtype=np.int16)
         self._check(

@@ -111,3 +111,73 @@ def layer_tensor_names(num_layers: int) -> list[str]:
         names.extend(f"model.layers.{layer}.{key}" for key in keys)
     names.extend(["model.norm.weight", "lm_head.weight"])
     return names
+
+
+@dataclass(frozen=True)
+class TpShard:
+    """Tensor-parallel shard of rank ``rank`` of ``size`` (the engine's
+    ``tp_geometry``): query heads [q0, q0+nq), KV heads [kv0, kv0+nkv),
+    intermediate rows [i0, i0+ni), vocabulary rows [v0, v0+nv)."""
+
+    rank: int
+    size: int
+    q0: int
+    nq: int
+    kv0: int
+    nkv: int
+    i0: int
+    ni: int
+    v0: int
+    nv: int
+
+    @staticmethod
+    def of(config: ModelConfig, rank: int, size: int) -> "TpShard":
+        if not (1 <= size <= 8 and 0 <= rank < size):
+            raise ValueError(f"rank {rank} of {size}")
+        nq, nkv = config.num_heads, config.num_kv_heads
+        grp = nq // nkv
+        if size <= nkv:
+            if nkv % size:
+                raise ValueError(f"{nkv} KV heads do not split over {size} ranks")
+            kvn = nkv // size
+            kv0 = rank * kvn
+            q0, qn = kv0 * grp, kvn * grp
+        else:
+            if size % nkv:
+                raise ValueError(f"{size} ranks do not share {nkv} KV heads evenly")
+            per = size // nkv
+            if grp < per:
+                raise ValueError("fewer query heads per KV head than ranks sharing it")
+            part, base, extra = rank % per, grp // per, grp % per
+            kv0, kvn = rank // per, 1
+            q0 = kv0 * grp + part * base + min(part, extra)
+            qn = base + (1 if part < extra else 0)
+        if config.intermediate % size or (config.intermediate // size) % 8:
+            raise ValueError(f"intermediate {config.intermediate} does not split over {size} ranks")
+        ni = config.intermediate // size
+        vs = -(-config.vocab // size)
+        v0 = rank * vs
+        nv = min(vs, config.vocab - v0)
+        return TpShard(rank, size, q0, qn, kv0, kvn, rank * ni, ni, v0, nv)
+
+    def kv_cache_shape(self, config: ModelConfig) -> tuple[int, ...]:
+        return (config.num_layers, config.num_blocks, config.block_size, self.nkv, config.head_dim)
+
+    def slice_tensor(self, config: ModelConfig, name: str, full):
+        """This rank's part of a whole checkpoint tensor (a torch tensor)."""
+        d = config.head_dim
+        key = name.split(".", 3)[-1] if name.startswith("model.layers.") else name
+        if key in ("self_attn.q_proj.weight", "self_attn.q_proj.bias"):
+            return full[self.q0 * d:(self.q0 + self.nq) * d]
+        if key in ("self_attn.k_proj.weight", "self_attn.k_proj.bias",
+                   "self_attn.v_proj.weight", "self_attn.v_proj.bias"):
+            return full[self.kv0 * d:(self.kv0 + self.nkv) * d]
+        if key == "self_attn.o_proj.weight":
+            return full[:, self.q0 * d:(self.q0 + self.nq) * d]
+        if key in ("mlp.gate_proj.weight", "mlp.up_proj.weight"):
+            return full[self.i0:self.i0 + self.ni]
+        if key == "mlp.down_proj.weight":
+            return full[:, self.i0:self.i0 + self.ni]
+        if key == "lm_head.weight":
+            return full[self.v0:self.v0 + self.nv]
+        return full

@@ -115,6 +115,25 @@ void *cruise_epoch_create(const CruiseModelConfig *cfg, int32_t device,
                           int32_t *status);
 void cruise_epoch_destroy(void *engine);
 
+/* Tensor parallelism (no counterpart in the reference; the survey's 2/4/8-GPU
+ * sharding of the same epoch).  One process per GPU creates rank `tp_rank` of
+ * `tp_size` (1..8): query heads, KV heads (shared by tp_size / KV-heads ranks
+ * when tp_size exceeds them), intermediate rows and vocabulary rows are split
+ * over the ranks; the residual stream, the embedding and the epoch control
+ * are replicated.  The O and down projections are all-reduced inside the epoch
+ * kernel through peer memory, the argmax across vocabulary shards likewise.
+ * Tensors passed to cruise_epoch_set_weight / _get_weight and the KV cache of
+ * _read_kv / _write_kv are this rank's shards; the import payload stays whole.
+ * Before the first epoch every rank exports its exchange block with
+ * cruise_epoch_tp_handle (a 64-byte cudaIpcMemHandle_t), the handles are
+ * gathered in rank order (any host channel) and passed to
+ * cruise_epoch_tp_connect.  All ranks must then run the same epochs. */
+void *cruise_epoch_create_tp(const CruiseModelConfig *cfg, int32_t device,
+                             int32_t tp_rank, int32_t tp_size,
+                             int32_t *status);
+int32_t cruise_epoch_tp_handle(void *engine, void *handle_out);
+int32_t cruise_epoch_tp_connect(void *engine, const void *handles);
+
 /* Seeded random-init weights generated on the device: every tensor element is
  * bf16(0.02-scaled Irwin-Hall(4) sum of a splitmix64 hash of (seed, tensor,
  * index)).  Returns 0 or a CUDA error code. */
@@ -183,8 +202,8 @@ int32_t cruise_epoch_run(void *engine, const int64_t *token,
  * must be serialised by the caller.
  * Returns 0 when the epoch ran (device status in control_out[3]), -1 for a
  * NULL argument, -2 when the model's scratch exceeds the 1 MiB array, -3 for
- * an import request, or a CUDA error code; cruise_epoch_last_error explains
- * -2 and -3. */
+ * an import request, -4 for a tensor-parallel engine, or a CUDA error code;
+ * cruise_epoch_last_error explains -2, -3 and -4. */
 int32_t cruise_epoch_run_noalloc(void *engine, const int64_t *token,
                                  const int64_t *position,
                                  const int32_t *seq_len, const int32_t *slot,
@@ -211,7 +230,9 @@ int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,
                                 int32_t count);
 
-/* Last CUDA error string of this engine (static storage). */
+/* Last CUDA error string of this engine (static storage).  With engine NULL:
+ * why the calling thread's last cruise_epoch_create / _create_tp returned
+ * NULL (the failing step and CUDA error), "" after a successful create. */
 const char *cruise_epoch_last_error(void *engine);
 
 #ifdef __cplusplus
