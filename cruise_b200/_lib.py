@@ -47,6 +47,9 @@ SIGNATURES = {
     ),
     "cruise_epoch_tp_handle": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p]),
     "cruise_epoch_tp_connect": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p]),
+    "cruise_epoch_tp_shard": (
+        ctypes.c_int32, [ctypes.POINTER(CruiseModelConfigC), ctypes.c_int32, ctypes.c_int32, i32p]
+    ),
     "cruise_epoch_init_synthetic": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_double]),
     "cruise_epoch_set_weight": (
         ctypes.c_int32, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_uint64]

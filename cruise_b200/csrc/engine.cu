@@ -749,7 +749,9 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   p.down_xglobal = e->down_xglobal;
   p.trace = e->trace_on ? e->trace : nullptr;
   if (e->trace_on) cudaMemsetAsync(e->trace, 0, 5 * kTraceMax * sizeof(uint64_t), e->stream);
-  p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
+  // every device-side wait gives up after 2 s; under tensor parallelism after
+  // 20 s, since a rank's first wait also covers the other ranks' launch skew
+  p.timeout_ns = e->tp_size > 1 ? 20000000000ull : 2000000000ull;
   p.l2_ahead = e->l2_ahead;
   p.tp_size = e->tp_size;
   p.tp_rank = e->tp_rank;
@@ -1150,6 +1152,15 @@ int32_t cruise_epoch_tp_connect(void *engine, const void *handles) {
                                             cudaMemcpyHostToDevice);
   if (err != cudaSuccess) return cruise::set_err(e, err, "tp connect");
   e->tp_connected = true;
+  return 0;
+}
+
+int32_t cruise_epoch_tp_shard(const CruiseModelConfig *cfg, int32_t tp_rank, int32_t tp_size, int32_t *shard_out) {
+  if (cfg == nullptr || shard_out == nullptr) return -1;
+  cruise::TpGeom g{};
+  if (!cruise::tp_geometry(*cfg, tp_rank, tp_size, g)) return -1;
+  const int32_t v[8] = {g.q0, g.nq, g.kv0, g.nkv, g.i0, g.ni, g.v0, g.nv};
+  std::memcpy(shard_out, v, sizeof(v));
   return 0;
 }
 

@@ -579,6 +579,36 @@ __device__ void load_x_reduced(const EpochParams &p, const Smem &s, const Gemv &
 }
 
 
+// The slice-only part of load_x_reduced for a CTA without tiles in the phase:
+// h_dst[b][k] = src[b][k] + bf16(sum over ranks of the partials) over this
+// CTA's slice [lo, hi) of the 8-element units, with the same rounding.
+__device__ void store_reduced_slice(const EpochParams &p, const Gemv &g) {
+  const int K8 = g.K / 8;
+  const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
+  const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
+  const TpExchange *xc = p.tp_local;
+  for (int i = threadIdx.x; i < kBatch * (hi - lo); i += kConsumerThreads) {
+    const int b = i / (hi - lo), k8 = lo + i % (hi - lo);
+    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(g.xsrc + static_cast<size_t>(b) * g.xsrc_stride) + k8);
+    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int src = 0; src < p.tp_size; ++src) {
+      const float4 *pp = reinterpret_cast<const float4 *>(&xc->part[g.reduce_set][src][b][k8 * 8]);
+      const float4 a = __ldcg(pp), c = __ldcg(pp + 1);
+      sum[0] += a.x; sum[1] += a.y; sum[2] += a.z; sum[3] += a.w;
+      sum[4] += c.x; sum[5] += c.y; sum[6] += c.z; sum[7] += c.w;
+    }
+    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&hv);
+    uint4 out;
+    __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&out);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 hf = __bfloat1622float2(h2[q]);
+      o2[q] = __floats2bfloat162_rn(__fadd_rn(hf.x, rbf(sum[2 * q])), __fadd_rn(hf.y, rbf(sum[2 * q + 1])));
+    }
+    *reinterpret_cast<uint4 *>(g.h_dst + static_cast<size_t>(b) * p.m.H + k8 * 8) = out;
+  }
+}
+
 // Fills s.xs[4][K] with the projection input: RMSNorm of the residual stream
 // (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU output).
 __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
@@ -909,7 +939,12 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
       *reinterpret_cast<uint4 *>(p.h + static_cast<size_t>(b) * p.m.H + k8 * 8) = v;
     }
   }
-  if (tr.t0 >= tr.t1) return;
+  if (tr.t0 >= tr.t1) {
+    // no tiles here; under tensor parallelism this CTA still owns its slice of
+    // the reduced residual stream that the next phases read
+    if (g.reduce_set >= 0) store_reduced_slice(p, g);
+    return;
+  }
   const bool xg = g.xmode == kXGlobal;
   if (!xg) load_x(p, s, g);
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)

@@ -122,8 +122,10 @@ class EpochEngine:
         return torch.from_numpy(out).view(torch.bfloat16)
 
     def load_weights(self, weights: dict[str, torch.Tensor]) -> None:
+        """Loads whole checkpoint tensors (this rank's shards under tensor parallelism)."""
         for name in layer_tensor_names(self.config.num_layers):
-            self.set_weight(name, weights[name])
+            full = weights[name]
+            self.set_weight(name, self.shard.slice_tensor(self.config, name, full) if self.shard.size > 1 else full)
 
     # -- tensor parallelism -------------------------------------------------------------
     def tp_handle(self) -> bytes:

@@ -158,6 +158,8 @@ class TpShard:
         vs = -(-config.vocab // size)
         v0 = rank * vs
         nv = min(vs, config.vocab - v0)
+        if nv <= 0:
+            raise ValueError(f"vocabulary {config.vocab} leaves rank {rank} of {size} no rows")
         return TpShard(rank, size, q0, qn, kv0, kvn, rank * ni, ni, v0, nv)
 
     def kv_cache_shape(self, config: ModelConfig) -> tuple[int, ...]:

@@ -132,6 +132,12 @@ void *cruise_epoch_create_tp(const CruiseModelConfig *cfg, int32_t device,
                              int32_t tp_rank, int32_t tp_size,
                              int32_t *status);
 int32_t cruise_epoch_tp_handle(void *engine, void *handle_out);
+/* The shard of rank tp_rank of tp_size without creating an engine (host only):
+ * shard_out[8] = {q0, nq, kv0, nkv, i0, ni, v0, nv} -- first query head and
+ * count, first KV head and count, intermediate rows, vocabulary rows.
+ * Returns 0, or -1 when the model does not split over tp_size ranks. */
+int32_t cruise_epoch_tp_shard(const CruiseModelConfig *cfg, int32_t tp_rank,
+                              int32_t tp_size, int32_t *shard_out);
 int32_t cruise_epoch_tp_connect(void *engine, const void *handles);
 
 /* Seeded random-init weights generated on the device: every tensor element is

@@ -39,3 +39,5 @@ def test_engine_creation_without_gpu_fails_cleanly():
     cfg = TINY.to_c()
     handle = lib.cruise_epoch_create(ctypes.byref(cfg), 0, ctypes.byref(status))
     assert not handle and status.value == 3
+    reason = lib.cruise_epoch_last_error(None).decode()
+    assert reason.startswith(("cudaSetDevice", "cudaGetDeviceProperties")), reason
