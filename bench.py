@@ -22,6 +22,11 @@ e2e      the same through the C-ABI call with host buffers: H2D of the epoch
 Multi-GPU (torchrun): each rank runs an independent B=4 cohort on its own GPU
 (data-parallel replicas, no collective on the data path); the process group is
 only used for the start/stop barrier and the max-over-ranks timing.
+With --tp the N ranks instead form one tensor-parallel group decoding a single
+B=4 cohort (strong scaling): each GPU streams its 1/N of the weights and the
+epoch kernel exchanges the O / down partials and the vocabulary argmax over
+NVLink peer memory; value counts the cohort's tokens once, and the roofline
+compares the group's shard bytes with N x the per-GPU HBM peak.
 """
 
 from __future__ import annotations
@@ -78,6 +83,17 @@ def step_bytes(cfg, contexts: list[int]) -> int:
     active row's context + KV write of the new position + embedding rows."""
     kv_token = 2 * cfg.num_layers * cfg.kv_width * 2
     return weight_bytes_per_step(cfg) + kv_token * (sum(contexts) + len(contexts)) + len(contexts) * cfg.hidden * 2
+
+
+def shard_step_bytes(cfg, shard, contexts: list[int]) -> int:
+    """step_bytes of one tensor-parallel rank: its query/KV heads, intermediate
+    and vocabulary rows, the replicated norms and its KV heads' cache."""
+    h, d, L = cfg.hidden, cfg.head_dim, cfg.num_layers
+    qkv = (shard.nq + 2 * shard.nkv) * d
+    per_layer = qkv * h + qkv + h * shard.nq * d + 3 * shard.ni * h + 2 * h
+    weights = 2 * (L * per_layer + shard.nv * h + h)
+    kv_token = 2 * L * shard.nkv * d * 2
+    return weights + kv_token * (sum(contexts) + len(contexts)) + len(contexts) * h * 2
 
 
 class ClockSampler:
@@ -188,6 +204,26 @@ class ClockSampler:
         }
 
 
+def gather_kv_shards(engine, key, value):
+    """The whole KV cache from every tensor-parallel rank's head shard (an
+    all-gather over the default process group; ranks sharing a KV head hold
+    identical copies of it)."""
+    import torch
+    import torch.distributed as dist
+
+    shard = engine.shard
+    parts: list = [None] * dist.get_world_size()
+    dist.all_gather_object(parts, (shard.kv0, shard.nkv, key, value))
+    shape = list(key.shape)
+    shape[3] = engine.config.num_kv_heads
+    full_k = torch.empty(shape, dtype=key.dtype)
+    full_v = torch.empty(shape, dtype=value.dtype)
+    for kv0, nkv, k_part, v_part in parts:
+        full_k[:, :, :, kv0:kv0 + nkv] = k_part
+        full_v[:, :, :, kv0:kv0 + nkv] = v_part
+    return full_k, full_v
+
+
 def setup_cohort(engine, cfg, seed: int, k: int):
     """Device prefill of a seeded B=4 cohort, then the one-shot import epoch."""
     from scenario import decode_inputs, import_payload, make_scenario, prefill_epochs
@@ -198,6 +234,8 @@ def setup_cohort(engine, cfg, seed: int, k: int):
         out = engine.run(**inputs)
         assert out.status == 0, f"prefill epoch status {out.status}"
     key, value = engine.read_kv()
+    if engine.shard.size > 1:
+        key, value = gather_kv_shards(engine, key, value)
     payload = import_payload(key, value, sc)
     inputs = decode_inputs(sc, cfg.block_size, importing=True)
     out = engine.run(**inputs, import_payload=payload)
@@ -246,9 +284,11 @@ class Cohort:
         return int(self.cfg.capacity - self.position.max() - 1)
 
 
-def reduce_over_ranks(dev_s: float, tokens: int, wall_s: float, device) -> tuple[float, float, float]:
+def reduce_over_ranks(dev_s: float, tokens: int, wall_s: float, device,
+                      sum_tokens: bool = True) -> tuple[float, float, float]:
     """(max device seconds, total tokens, max wall seconds) over the ranks of
-    the default process group (identity without one)."""
+    the default process group (identity without one).  A tensor-parallel group
+    decodes one cohort: its tokens are counted once (sum_tokens=False)."""
     import torch
     import torch.distributed as dist
 
@@ -258,7 +298,7 @@ def reduce_over_ranks(dev_s: float, tokens: int, wall_s: float, device) -> tuple
     times = torch.tensor([dev_s, wall_s], dtype=torch.float64, device=where)
     total = torch.tensor([float(tokens)], dtype=torch.float64, device=where)
     dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    dist.all_reduce(total, op=dist.ReduceOp.SUM)
+    dist.all_reduce(total, op=dist.ReduceOp.SUM if sum_tokens else dist.ReduceOp.MAX)
     return float(times[0]), float(total[0]), float(times[1])
 
 
@@ -281,11 +321,19 @@ def run_gpu(args) -> None:
         # reduced geometry for profiler captures only (never a bench line)
         cfg = cfg.with_(num_layers=args.layers or cfg.num_layers, vocab=args.vocab or cfg.vocab,
                         configured_eos=(args.vocab or cfg.vocab) - 1)
-    engine = EpochEngine(cfg, device=device)
+    tp = args.tp and world > 1
+    if tp:
+        # one cohort sharded over all ranks (one GPU each); the kernel exchanges
+        # the row-parallel partials and the vocabulary argmax over peer memory
+        from cruise_b200.tp import create_tp_engine
+
+        engine = create_tp_engine(cfg, device=device)
+    else:
+        engine = EpochEngine(cfg, device=device)
     t0 = time.perf_counter()
     engine.init_synthetic(seed=0)
     synth_s = time.perf_counter() - t0
-    sc, first = setup_cohort(engine, cfg, seed=1000 + rank, k=args.k)
+    sc, first = setup_cohort(engine, cfg, seed=1000 + (0 if tp else rank), k=args.k)
     cohort = Cohort(engine, cfg, sc, first)
     need = (args.warmup + args.steps + (1 if args.trace else 0)) * args.k
     if cohort.room() < need:
@@ -313,19 +361,23 @@ def run_gpu(args) -> None:
             contexts0 = [int(p) for p in inputs["position"]]
             for s in range(out.model_calls):
                 ctx = [c + s for c, e in zip(contexts0, executed) if e > s]
-                step_bytes_total += step_bytes(cfg, ctx)
+                step_bytes_total += shard_step_bytes(cfg, engine.shard, ctx) * world if tp else step_bytes(cfg, ctx)
         wall = time.perf_counter() - wall0
     barrier()
     dev_s = sum(device_us) / 1e6
     model_calls = args.steps * args.k
-    t_max, tok_total, e2e_wall = reduce_over_ranks(dev_s, tokens, wall, device=device if world > 1 else None)
+    t_max, tok_total, e2e_wall = reduce_over_ranks(dev_s, tokens, wall, device=device if world > 1 else None,
+                                                   sum_tokens=not tp)
     value = tok_total / t_max
     e2e_tokens = tok_total
-    if args.trace and rank == 0:
-        print_trace(engine, cohort, cfg, args.k)
+    if args.trace and (rank == 0 or tp):
+        # a tensor-parallel group runs the traced epoch on every rank
+        print_trace(engine, cohort, cfg, args.k, show=rank == 0)
     peak, peak_kind = hbm_peak()
-    per_epoch_us = dev_s * 1e6 / args.steps
-    achieved_gbs = step_bytes_total / dev_s / 1e9
+    per_epoch_us = t_max * 1e6 / args.steps
+    achieved_gbs = step_bytes_total / (t_max if tp else dev_s) / 1e9
+    if tp:
+        peak = peak * world   # the group's aggregate HBM bandwidth
     clock = clocks.summary()
     if rank == 0:
         line = {
@@ -338,7 +390,7 @@ def run_gpu(args) -> None:
             "ms_per_step": round(per_epoch_us / 1e3, 4),
             "us_per_decode_step": round(per_epoch_us / args.k, 2),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded random-init weights generated on the device; seeded prompts)",
@@ -346,21 +398,23 @@ def run_gpu(args) -> None:
                 "workload": "configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
                             "one-shot H2D KV import of the device-prefilled prompts (2-5 tokens)" % args.k,
                 "model": "Qwen2.5-7B architecture (28 layers, hidden 3584, 28/4 heads x 128, I 18944, V 152064)",
-                "global_batch": 4 * world,
+                "global_batch": 4 if tp else 4 * world,
                 "epoch_k": args.k,
                 "kv": "paged, block 128, 2 blocks per row",
-                "parallelism": f"dp{world} (independent cohorts)" if world > 1 else "single GPU",
+                "parallelism": (f"tp{world} (one cohort sharded over {world} GPUs)" if tp else
+                                f"dp{world} (independent cohorts)" if world > 1 else "single GPU"),
                 "l2": "no flush: every step streams 14.1 GB of weights, > 126 MB L2",
             },
             "roofline": {
                 "bound": "hbm",
                 "achieved": round(achieved_gbs, 1),
                 "peak": peak,
-                "peak_kind": peak_kind,
+                "peak_kind": f"{peak_kind}, x{world} GPUs (aggregate)" if tp else peak_kind,
                 "unit": "GB/s",
                 "frac": round(achieved_gbs / peak, 4),
                 "traffic": (PROFILED_TRAFFIC["bytes_per_launch"] // PROFILED_TRAFFIC["steps_per_launch"]
-                            if args.k == PROFILED_TRAFFIC["k"] and not args.layers and not args.vocab else None),
+                            if args.k == PROFILED_TRAFFIC["k"] and not args.layers and not args.vocab and not tp
+                            else None),
                 "traffic_unit": "bytes per decode step (ncu dram read + write)",
                 "kernel": "resident_epoch_kernel",
                 "bytes_per_decode_step": step_bytes_total // model_calls,
@@ -372,7 +426,7 @@ def run_gpu(args) -> None:
                 "d2h_bytes_per_step": EPOCH_D2H_BYTES,
                 "host_control_ms_per_epoch": round(wall * 1e3 / args.steps, 4),
             },
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * world,   # one epoch kernel per step on every rank
             "clocks": clock,
             "setup": {"weight_synthesis_s": round(synth_s, 2)},
         }
@@ -387,10 +441,11 @@ def run_gpu(args) -> None:
 PHASE_NAMES = ("qkv", "attention", "o_proj", "gate_up", "down")
 
 
-def print_trace(engine, cohort, cfg, k) -> None:
+def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
     """One traced epoch: per phase kind, the time between grid barriers and its
     parts on CTA 0 (activation staging, tile stream, epilogue drain, wait for the
-    last CTA, barrier release), summed over layers and steps."""
+    last CTA, barrier release; under tensor parallelism also how much of the
+    epilogue waited for the other ranks' partials), summed over layers and steps."""
     engine.set_trace(True)
     out, _ = cohort.step()
     engine.set_trace(False)
@@ -398,16 +453,17 @@ def print_trace(engine, cohort, cfg, k) -> None:
     phases = 5 * L + 2
     count = 2 + out.model_calls * phases + 1
     tr = engine.read_trace(count).astype(np.int64)
-    exit_ns, entry_ns, xready, tiles, last = tr
+    exit_ns, entry_ns, xready, tiles, last, tp_wait = tr
+    end_ns = exit_ns   # a phase ends when CTA 0 leaves its grid barrier
     first = 2   # validation and continuity barriers precede the loop
     acc = {}
     for step in range(out.model_calls):
         for ph in range(phases):
             j = first + step * phases + ph + 1
             name = "lm_head" if ph == 5 * L else "control" if ph > 5 * L else PHASE_NAMES[ph % 5]
-            a = acc.setdefault(name, np.zeros(6))
-            start = exit_ns[j - 1]
-            a[0] += exit_ns[j] - start
+            a = acc.setdefault(name, np.zeros(7))
+            start = end_ns[j - 1]
+            a[0] += end_ns[j] - start
             if xready[j]:
                 a[1] += xready[j] - start
                 a[2] += tiles[j] - xready[j]
@@ -416,17 +472,21 @@ def print_trace(engine, cohort, cfg, k) -> None:
                 a[3] += entry_ns[j] - start
             a[4] += max(last[j] - entry_ns[j], 0)
             a[5] += exit_ns[j] - max(last[j], entry_ns[j])
-    h, kv, i = cfg.hidden, cfg.kv_width, cfg.intermediate
-    wbytes = {"qkv": (h + 2 * kv) * h * 2 * L, "o_proj": h * h * 2 * L, "gate_up": 2 * i * h * 2 * L,
-              "down": h * i * 2 * L, "lm_head": cfg.vocab * h * 2}
+            a[6] += tp_wait[j]   # part of the epilogue: waiting for other ranks' partials
+    if not show:
+        return
+    sh, h, d = engine.shard, cfg.hidden, cfg.head_dim   # this rank's shard (the whole model on one GPU)
+    wbytes = {"qkv": (sh.nq + 2 * sh.nkv) * d * h * 2 * L, "o_proj": h * sh.nq * d * 2 * L,
+              "gate_up": 2 * sh.ni * h * 2 * L, "down": h * sh.ni * 2 * L, "lm_head": sh.nv * h * 2}
     calls = out.model_calls
     print(f"trace: epoch {out.device_us:.1f} us, {calls} steps; per step, us "
-          f"[total | x-staging  tiles  epilogue | wait-last-CTA  release] and weight GB/s", file=sys.stderr)
+          f"[total | x-staging  tiles  epilogue | wait-last-CTA  release | epilogue tp-wait] and weight GB/s",
+          file=sys.stderr)
     for name in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "control"):
-        a = acc.get(name, np.zeros(6)) / calls / 1e3
+        a = acc.get(name, np.zeros(7)) / calls / 1e3
         bw = wbytes.get(name, 0) / (a[0] * 1e3) if name in wbytes and a[0] else 0.0
-        print(f"  {name:9s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} {a[5]:7.1f}   "
-              f"{bw:6.0f}", file=sys.stderr)
+        print(f"  {name:9s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} {a[5]:7.1f} "
+              f"{a[6]:7.1f}   {bw:6.0f}", file=sys.stderr)
 
 
 SAMPLE_LAYERS = (1, 5)
@@ -568,6 +628,8 @@ def main() -> None:
     parser.add_argument("--trace", action="store_true", help="per-phase timing of one extra epoch (stderr)")
     parser.add_argument("--layers", type=int, default=0, help="profiling only: truncate the model to N layers")
     parser.add_argument("--vocab", type=int, default=0, help="profiling only: vocabulary size")
+    parser.add_argument("--tp", action="store_true",
+                        help="under torchrun: the ranks form one tensor-parallel group decoding one cohort")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -203,7 +203,6 @@ struct Engine {
   std::vector<void *> opened;              // peer blocks opened through IPC
   bool tp_connected = false;
   uint32_t launches = 0;                   // epochs launched (exchange sequence base)
-  bf16 *h_alt = nullptr;
 };
 
 // Every host<->device copy runs on the engine's own (non-blocking) stream and is
@@ -249,7 +248,8 @@ struct TpGeom {
 };
 
 bool tp_geometry(const CruiseModelConfig &c, int rank, int size, TpGeom &g) {
-  if (size < 1 || size > kMaxTp || rank < 0 || rank >= size) return false;
+  // 1, 2, 4 or 8 ranks (the kernel's cross-rank reduction is unrolled for those)
+  if ((size != 1 && size != 2 && size != 4 && size != 8) || rank < 0 || rank >= size) return false;
   const int nq = c.num_heads, nkv = c.num_kv_heads, grp = nq / nkv;
   if (size <= nkv) {
     if (nkv % size != 0) return false;
@@ -291,7 +291,11 @@ void fill_dims(Engine *e) {
   m.nkv_all = c.num_kv_heads;
   m.Hq = g.nq * c.head_dim;
   m.I = g.ni;
-  m.I_pad = static_cast<int32_t>(align_up(g.ni, 64));
+  // intermediate columns zero-padded to a multiple of 512 (the down projection's
+  // 512-wide tiles and its activation read straight from L2) when that adds at
+  // most a tenth to the down weights, else to a multiple of 64
+  const int64_t pad512 = static_cast<int64_t>(align_up(g.ni, 512));
+  m.I_pad = static_cast<int32_t>(pad512 * 10 <= static_cast<int64_t>(g.ni) * 11 ? pad512 : align_up(g.ni, 64));
   m.V = c.vocab;
   m.v0 = g.v0;
   m.Vl = g.nv;
@@ -341,7 +345,6 @@ void destroy_engine(Engine *e) {
   for (void *ptr : e->opened) cudaIpcCloseMemHandle(ptr);
   cudaFree(e->d_peers);
   cudaFree(e->xchg);
-  cudaFree(e->h_alt);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
@@ -487,7 +490,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
   const size_t o_ai = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ab = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_lg = take2(static_cast<size_t>(kMaxSteps) * kBatch * m.V * 4);
-  const size_t o_trace = take2(5 * kTraceMax * sizeof(uint64_t));
+  const size_t o_trace = take2(kTraceSeries * kTraceMax * sizeof(uint64_t));
   const size_t o_io = take2(sizeof(EpochIO)), o_res = take2(sizeof(ResidentState));
   const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sizeof(SyncState));
   if (cudaMalloc(&e->state, st) != cudaSuccess) return fail("state allocation");
@@ -517,13 +520,11 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
   if (e->tp_size > 1) {
     // the exchange block is its own allocation so that it can be exported by IPC
     if (cudaMalloc(reinterpret_cast<void **>(&e->xchg), sizeof(TpExchange)) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void **>(&e->d_peers), sizeof(TpExchange *) * kMaxTp) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void **>(&e->h_alt), static_cast<size_t>(kBatch) * H * 2) != cudaSuccess) {
+        cudaMalloc(reinterpret_cast<void **>(&e->d_peers), sizeof(TpExchange *) * kMaxTp) != cudaSuccess) {
       return fail("tensor-parallel exchange allocation");
     }
     cudaMemsetAsync(e->xchg, 0, sizeof(TpExchange), e->stream);
     cudaMemsetAsync(e->d_peers, 0, sizeof(TpExchange *) * kMaxTp, e->stream);
-    cudaMemsetAsync(e->h_alt, 0, static_cast<size_t>(kBatch) * H * 2, e->stream);
   }
   std::vector<uint16_t> cos_t, sin_t;
   default_rope(e, cos_t, sin_t);
@@ -748,7 +749,7 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   p.xs_stride = e->xs_stride;
   p.down_xglobal = e->down_xglobal;
   p.trace = e->trace_on ? e->trace : nullptr;
-  if (e->trace_on) cudaMemsetAsync(e->trace, 0, 5 * kTraceMax * sizeof(uint64_t), e->stream);
+  if (e->trace_on) cudaMemsetAsync(e->trace, 0, kTraceSeries * kTraceMax * sizeof(uint64_t), e->stream);
   // every device-side wait gives up after 2 s; under tensor parallelism after
   // 20 s, since a rank's first wait also covers the other ranks' launch skew
   p.timeout_ns = e->tp_size > 1 ? 20000000000ull : 2000000000ull;
@@ -762,7 +763,6 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
     }
     p.tp_peer = e->d_peers;
     p.tp_local = e->xchg;
-    p.h_alt = e->h_alt;
   }
   // exchange sequence numbers grow across launches (every rank launches the
   // same epochs); a launch uses at most 8 x 142 of its 65,536
@@ -1278,7 +1278,7 @@ int32_t cruise_epoch_set_trace(void *engine, int32_t enable) {
 }
 
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns, int32_t count) {
-  if (engine == nullptr || ns == nullptr || series < 0 || series > 4 || count < 0 || count > cruise::kTraceMax)
+  if (engine == nullptr || ns == nullptr || series < 0 || series >= cruise::kTraceSeries || count < 0 || count > cruise::kTraceMax)
     return -1;
   Engine *e = static_cast<Engine *>(engine);
   std::lock_guard<std::mutex> lock(e->execute_mutex);

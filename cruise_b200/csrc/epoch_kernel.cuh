@@ -53,11 +53,6 @@ struct Gemv {
   int32_t xmode;
   int32_t xsrc_stride;
   int32_t embed_src;     // 1: the norm source is embed[token[b]] (layer 0)
-  // tensor parallelism: the norm source is xsrc + bf16(sum over ranks of the
-  // exchange partial set `reduce_set`); this CTA writes its slice of that sum
-  // to h_dst (-1: no reduction)
-  int32_t reduce_set;
-  bf16 *h_dst;
 };
 
 __host__ __device__ inline int pick_kc(int K) {
@@ -75,26 +70,22 @@ __host__ __device__ inline int64_t tiled_offset(int64_t n, int64_t k, int64_t K,
   return ((rg * (K / kc) + kk) * kRows + r) * kc + unit * 8 + (kin & 7);
 }
 
-// Residual buffers under tensor parallelism: QKV of layer l > 0 and lm_head
-// normalise h_alt + the down partials and write h; gate/up normalises h + the
-// O partials and writes h_alt.  Without it every projection reads h in place.
+// The projection of a phase.  Under tensor parallelism the shapes are this
+// rank's shard (O reads Hq attention columns, down I_pad columns of its rows);
+// the residual stream h is whole on every rank.
 __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int kind) {
   const ModelDims &m = p.m;
-  const bool tp = p.tp_size > 1;
   Gemv g{};
   g.kind = kind;
-  g.reduce_set = -1;
   if (kind == kLM) {
     g.W = p.lm_head; g.N = m.V_pad; g.K = m.H;
     g.xmode = kXNorm; g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = p.final_norm;
-    if (tp) { g.xsrc = p.h_alt; g.reduce_set = 1; g.h_dst = p.h; }
   } else {
     const LayerWeights &lw = p.layers[layer];
     switch (kind) {
       case kQKV:
         g.W = lw.qkv_w; g.bias = lw.qkv_b; g.N = m.Nqkv; g.K = m.H; g.xmode = kXNorm;
         g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = lw.w_in; g.embed_src = layer == 0;
-        if (tp && layer > 0) { g.xsrc = p.h_alt; g.reduce_set = 1; g.h_dst = p.h; }
         break;
       case kO:
         g.W = lw.o_w; g.N = m.H; g.K = m.Hq; g.xmode = kXCopy; g.xsrc = p.attn;
@@ -103,7 +94,6 @@ __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int k
       case kGU:
         g.W = lw.gu_w; g.N = 2 * m.I; g.K = m.H; g.xmode = kXNorm; g.xsrc = p.h;
         g.xsrc_stride = m.H; g.norm_w = lw.w_post;
-        if (tp) { g.reduce_set = 0; g.h_dst = p.h_alt; }
         break;
       default:  // kDown
         g.W = lw.down_w; g.N = m.H; g.K = m.I_pad; g.xmode = p.down_xglobal ? kXGlobal : kXCopy;
@@ -305,36 +295,26 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
   return s.misc[0] != 0;
 }
 
-// Slot of a position inside a row's valid range (32-bit: 0 <= t < C); -1 for
-// an invalid block-table entry.  The attention's per-position lookup.
-// Tensor-parallel rendezvous after a phase whose outputs other ranks read.
-// The grid barrier before it guarantees that every CTA of this rank finished
-// the phase and fenced its peer writes system-wide; CTA 0 then publishes `seq`
-// into every rank's flag slot of this rank, and every CTA waits until all
-// ranks' flags in its local exchange block reached `seq` (flags only grow).
-__device__ bool tp_rendezvous(const EpochParams &p, const Smem &s, uint32_t seq, uint32_t where) {
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    if (blockIdx.x == 0 && lane < p.tp_size) st_release_sys_u32(&p.tp_peer[lane]->flag[p.tp_rank][0], seq);
-    int ready = 1;
-    if (lane < p.tp_size) {
-      const uint32_t *flag = &p.tp_local->flag[lane][0];
-      const uint64_t deadline = globaltimer() + p.timeout_ns;
-      uint32_t polls = 0;
-      while (static_cast<int32_t>(ld_acquire_sys_u32(flag) - seq) < 0) {
-        if ((++polls & 15) == 0) {
-          if (aborted(p)) { ready = 0; break; }
-          if (globaltimer() > deadline) { raise_error(p, where); ready = 0; break; }
-        }
+// Tensor parallelism: rank `src`'s partial in this rank's exchange block,
+// once the word carries `tag` (the phase's sequence number).  A wait that runs
+// out raises the epoch error and returns 0, so the kernel winds down.
+__device__ __forceinline__ float tp_recv(const EpochParams &p, const uint64_t *word, uint32_t tag) {
+  uint64_t v = ld_relaxed_sys_u64(word);
+  if (static_cast<uint32_t>(v >> 32) != tag) {
+    const uint64_t deadline = globaltimer() + p.timeout_ns;
+    uint32_t polls = 0;
+    while (static_cast<uint32_t>((v = ld_relaxed_sys_u64(word)) >> 32) != tag) {
+      if ((++polls & 15) == 0) {
+        if (aborted(p)) return 0.f;
+        if (globaltimer() > deadline) { raise_error(p, 300); return 0.f; }
       }
     }
-    ready = __all_sync(0xffffffffu, ready);
-    if (lane == 0) s.misc[1] = ready;
   }
-  named_sync(1, kConsumerThreads);
-  return s.misc[1] != 0;
+  return __uint_as_float(static_cast<uint32_t>(v));
 }
 
+// Slot of a position inside a row's valid range (32-bit: 0 <= t < C); -1 for
+// an invalid block-table entry.  The attention's per-position lookup.
 __device__ __forceinline__ int slot_in_row(const ModelDims &m, const int32_t *bt, int row, int t) {
   const int logical = t / m.bs;
   if (logical >= m.bpr) return -1;
@@ -479,136 +459,6 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
 }
 
 // ---- consumer: activation prologue ------------------------------------------------------
-// RMSNorm staging under tensor parallelism: x = src + bf16(sum over ranks, in
-// rank order, of the fp32 row-parallel partials) -- the reference's
-// `hidden + materialize(mm_t(...))` with the sum split over ranks -- then the
-// RMSNorm of x into s.xs as usual.  This CTA writes its slice of x (the same
-// slice split as the embedding materialisation) to g.h_dst.
-__device__ void load_x_reduced(const EpochParams &p, const Smem &s, const Gemv &g, const bf16 *const (&rows)[kBatch]) {
-  const int tid = threadIdx.x;
-  const int K = g.K;
-  const int K8 = K / 8;
-  const int T = p.tp_size;
-  const TpExchange *xc = p.tp_local;
-  uint4 v[2][kBatch];
-  uint4 wv[2];
-  float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int k8 = tid + j * kConsumerThreads;
-    wv[j] = k8 < K8 ? __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8) : make_uint4(0, 0, 0, 0);
-  }
-  const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
-  const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int k8 = tid + j * kConsumerThreads;
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      uint4 out = make_uint4(0, 0, 0, 0);
-      if (k8 < K8) {
-        const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(rows[b]) + k8);
-        float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int src = 0; src < T; ++src) {
-          const float4 *pp = reinterpret_cast<const float4 *>(&xc->part[g.reduce_set][src][b][k8 * 8]);
-          const float4 a = __ldcg(pp), c = __ldcg(pp + 1);
-          sum[0] += a.x; sum[1] += a.y; sum[2] += a.z; sum[3] += a.w;
-          sum[4] += c.x; sum[5] += c.y; sum[6] += c.z; sum[7] += c.w;
-        }
-        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&hv);
-        __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&out);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 hf = __bfloat1622float2(h2[q]);
-          o2[q] = __floats2bfloat162_rn(__fadd_rn(hf.x, rbf(sum[2 * q])), __fadd_rn(hf.y, rbf(sum[2 * q + 1])));
-        }
-        if (k8 >= lo && k8 < hi)
-          *reinterpret_cast<uint4 *>(g.h_dst + static_cast<size_t>(b) * p.m.H + k8 * 8) = out;
-      }
-      v[j][b] = out;
-      const __nv_bfloat162 *x2 = reinterpret_cast<const __nv_bfloat162 *>(&out);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(x2[q]);
-        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.x, f.x));
-        ss[b] = __fadd_rn(ss[b], __fmul_rn(f.y, f.y));
-      }
-    }
-  }
-  const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-  for (int b = 0; b < kBatch; ++b) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], off);
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
-  }
-  named_sync(1, kConsumerThreads);
-  if (tid < kBatch) {
-    float total = 0.f;
-    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + tid];
-    const float var = __fdiv_rn(total, static_cast<float>(K));
-    s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
-  }
-  named_sync(1, kConsumerThreads);
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int k8 = tid + j * kConsumerThreads;
-    if (k8 >= K8) continue;
-    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv[j]);
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const float r = s.nrm[32 + b];
-      const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
-      uint4 o;
-      __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 hf = __bfloat1622float2(h2[q]);
-        const float2 wf = __bfloat1622float2(w2[q]);
-        const float nx = rbf(__fmul_rn(hf.x, r));
-        const float ny = rbf(__fmul_rn(hf.y, r));
-        o2[q] = __floats2bfloat162_rn(__fmul_rn(nx, wf.x), __fmul_rn(ny, wf.y));
-      }
-      *reinterpret_cast<uint4 *>(s.xs + static_cast<size_t>(b) * p.xs_stride + k8 * 8) = o;
-    }
-  }
-  named_sync(1, kConsumerThreads);
-}
-
-
-// The slice-only part of load_x_reduced for a CTA without tiles in the phase:
-// h_dst[b][k] = src[b][k] + bf16(sum over ranks of the partials) over this
-// CTA's slice [lo, hi) of the 8-element units, with the same rounding.
-__device__ void store_reduced_slice(const EpochParams &p, const Gemv &g) {
-  const int K8 = g.K / 8;
-  const int lo = static_cast<int>(static_cast<int64_t>(K8) * blockIdx.x / p.grid);
-  const int hi = static_cast<int>(static_cast<int64_t>(K8) * (blockIdx.x + 1) / p.grid);
-  const TpExchange *xc = p.tp_local;
-  for (int i = threadIdx.x; i < kBatch * (hi - lo); i += kConsumerThreads) {
-    const int b = i / (hi - lo), k8 = lo + i % (hi - lo);
-    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(g.xsrc + static_cast<size_t>(b) * g.xsrc_stride) + k8);
-    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int src = 0; src < p.tp_size; ++src) {
-      const float4 *pp = reinterpret_cast<const float4 *>(&xc->part[g.reduce_set][src][b][k8 * 8]);
-      const float4 a = __ldcg(pp), c = __ldcg(pp + 1);
-      sum[0] += a.x; sum[1] += a.y; sum[2] += a.z; sum[3] += a.w;
-      sum[4] += c.x; sum[5] += c.y; sum[6] += c.z; sum[7] += c.w;
-    }
-    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&hv);
-    uint4 out;
-    __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&out);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 hf = __bfloat1622float2(h2[q]);
-      o2[q] = __floats2bfloat162_rn(__fadd_rn(hf.x, rbf(sum[2 * q])), __fadd_rn(hf.y, rbf(sum[2 * q + 1])));
-    }
-    *reinterpret_cast<uint4 *>(g.h_dst + static_cast<size_t>(b) * p.m.H + k8 * 8) = out;
-  }
-}
-
 // Fills s.xs[4][K] with the projection input: RMSNorm of the residual stream
 // (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU output).
 __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
@@ -627,24 +477,20 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
   // One pass over L2: each thread keeps its (at most 2 x 8) elements of every
   // row in registers (K <= 4096), reduces the fp32 sums of squares, then
   // normalises from registers.
+  uint4 wv[2];   // norm weights, requested together with the activations
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k8 = tid + j * kConsumerThreads;
+    wv[j] = k8 < K8 ? __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8) : make_uint4(0, 0, 0, 0);
+  }
   const bf16 *rows[kBatch];
 #pragma unroll
   for (int b = 0; b < kBatch; ++b) {
     rows[b] = g.embed_src ? p.embed + __ldcg(&p.work->token[b]) * static_cast<int64_t>(K)
                           : g.xsrc + static_cast<size_t>(b) * g.xsrc_stride;
   }
-  if (g.reduce_set >= 0) {
-    load_x_reduced(p, s, g, rows);
-    return;
-  }
   uint4 v[2][kBatch];
-  uint4 wv[2];   // norm weights, requested together with the activations
   float ss[kBatch] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int k8 = tid + j * kConsumerThreads;
-    wv[j] = k8 < K8 ? __ldg(reinterpret_cast<const uint4 *>(g.norm_w) + k8) : make_uint4(0, 0, 0, 0);
-  }
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int k8 = tid + j * kConsumerThreads;
@@ -939,12 +785,7 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
       *reinterpret_cast<uint4 *>(p.h + static_cast<size_t>(b) * p.m.H + k8 * 8) = v;
     }
   }
-  if (tr.t0 >= tr.t1) {
-    // no tiles here; under tensor parallelism this CTA still owns its slice of
-    // the reduced residual stream that the next phases read
-    if (g.reduce_set >= 0) store_reduced_slice(p, g);
-    return;
-  }
+  if (tr.t0 >= tr.t1) return;
   const bool xg = g.xmode == kXGlobal;
   if (!xg) load_x(p, s, g);
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
@@ -964,12 +805,14 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
 // them (the segment's row group started on the previous CTA), or adds the next
 // CTA's published part (the row group continues there) and runs the epilogue.
 __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, RingCursor &red,
-                            uint32_t seq, int step) {
+                            uint32_t seq, int step, uint32_t trace_slot) {
   const int lane = threadIdx.x & 31;
   const ModelDims &m = p.m;
   const TileRange tr = tile_range(g, blockIdx.x, p.grid);
   float best = -INFINITY;
   int32_t best_i = INT_MAX, bad = 0;
+  uint64_t tp_wait_ns = 0;   // traced: time this warp waited for other ranks' partials
+
   int64_t seg_start = tr.t0;
   int64_t rg = tr.t0 / tr.KT;
   int kk = static_cast<int>(tr.t0 % tr.KT);
@@ -980,7 +823,9 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
   float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f;
   int64_t pa_rg = -1, pb_rg = -1;
   const bool tp_partial = p.tp_size > 1 && (g.kind == kO || g.kind == kDown);
-  if (g.kind == kQKV || ((g.kind == kO || g.kind == kDown) && !tp_partial)) {
+  // lane r < tp_size holds rank r's exchange block (shuffled to every lane per send)
+  TpExchange *const peer_mine = tp_partial && lane < p.tp_size ? p.tp_peer[lane] : nullptr;
+  if (g.kind == kQKV || g.kind == kO || g.kind == kDown) {
     const int64_t first_head = tr.t0 % tr.KT == 0 ? tr.t0 / tr.KT : tr.t0 / tr.KT + 1;
     auto fetch = [&](int64_t r, float &v0, float &v1) {
       const int64_t n0 = r * kRows + (lane >> 2), n1 = n0 + 8;
@@ -1064,14 +909,37 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, e0));
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, e1));
         } else if (tp_partial) {
-          // row-parallel partial of this rank, sent to every rank (peer memory);
-          // the next RMSNorm staging adds them up (load_x_reduced)
+          // Row-parallel output under tensor parallelism: every rank's finisher
+          // of this row group holds a partial over its K shard.  Send ours to
+          // the other ranks as tagged words, read theirs (each word valid once
+          // it carries this phase's tag), then hidden = residual +
+          // materialize(sum over ranks in rank order) -- the reference's
+          // (:380-386, :399-403) with the sum split over ranks.
           const int set = g.kind == kO ? 0 : 1;
+          const uint32_t tag = p.tp_seq_base + seq;
+          const uint64_t hi = static_cast<uint64_t>(tag) << 32;
+          const uint64_t w0 = hi | __float_as_uint(v0), w1 = hi | __float_as_uint(v1);
           for (int r = 0; r < p.tp_size; ++r) {
-            float *dst = p.tp_peer[r]->part[set][p.tp_rank][b];
-            dst[n0] = v0;
-            dst[n1] = v1;
+            TpExchange *peer = reinterpret_cast<TpExchange *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(peer_mine), r));
+            if (r == p.tp_rank) continue;
+            st_relaxed_sys_u64(&peer->part[set][p.tp_rank][n0][b], w0);
+            st_relaxed_sys_u64(&peer->part[set][p.tp_rank][n1][b], w1);
           }
+          const uint64_t wait0 = p.trace != nullptr ? globaltimer() : 0;
+          float sum0 = 0.f, sum1 = 0.f;
+          for (int r = 0; r < p.tp_size; ++r) {
+            float a0 = v0, a1 = v1;   // this rank's own partial
+            if (r != p.tp_rank) {
+              a0 = tp_recv(p, &p.tp_local->part[set][r][n0][b], tag);
+              a1 = tp_recv(p, &p.tp_local->part[set][r][n1][b], tag);
+            }
+            sum0 = __fadd_rn(sum0, a0);
+            sum1 = __fadd_rn(sum1, a1);
+          }
+          if (p.trace != nullptr) tp_wait_ns += globaltimer() - wait0;
+          p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(sum0)));
+          p.h[static_cast<size_t>(b) * m.H + n1] = tobf(__fadd_rn(e1, rbf(sum1)));
         } else if (g.kind == kO || g.kind == kDown) {
           // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
           p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(v0)));
@@ -1118,14 +986,11 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
     p.arg_idx[blockIdx.x * kBatch + lane] = best_i;
     p.arg_bad[blockIdx.x * kBatch + lane] = bad;
   }
-  // the phase's outputs written by this warp are visible GPU-wide (and to the
-  // peer GPUs under tensor parallelism) before the consumers may arrive at
-  // the grid barrier
-  if (tp_partial) {
-    __threadfence_system();
-  } else {
-    __threadfence();
-  }
+  if (tp_partial && p.trace != nullptr && blockIdx.x == 0 && lane == 0 && trace_slot < kTraceMax)
+    p.trace[5 * kTraceMax + trace_slot] = tp_wait_ns;
+  // the phase's outputs written by this warp are visible GPU-wide before the
+  // consumers may arrive at the grid barrier
+  __threadfence();
   __syncwarp();
   if (lane == 0) mbar_arrive(s.phase_done);
 }
@@ -1157,7 +1022,8 @@ __device__ void epilogue_main(const EpochParams &p, const Smem &s) {
       started = __shfl_sync(0xffffffffu, started ? 1 : 0, 0) != 0;
       if (!started) return;
       const Gemv g = make_gemv(p, ph / 5, kind);
-      gemv_finish(p, s, g, red, static_cast<uint32_t>(seq), step);
+      gemv_finish(p, s, g, red, static_cast<uint32_t>(seq), step,
+                  static_cast<uint32_t>(*reinterpret_cast<volatile int32_t *>(&s.misc[12])));
     }
   }
 }
@@ -1688,7 +1554,11 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
       const int kind = gemv_kind_of_phase(ph, L);
       if (kind >= 0) {
         const Gemv g = make_gemv(p, ph / 5, kind);
-        if (tid == 0) *s.phase_started = static_cast<int>(seq);
+        if (tid == 0) {
+          s.misc[12] = static_cast<int32_t>(barrier_index + 1);   // the phase's trace slot
+          __threadfence_block();
+          *s.phase_started = static_cast<int>(seq);
+        }
         gemv_consume(p, s, g, ring, red, barrier_index + 1);
         // the epilogue warp has written every output of the phase
         if (tid == 0) wait_bar(p, s.phase_done, done_parity, nullptr, 1004);
@@ -1810,8 +1680,6 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
         }
       }
       if (ok) ok = grid_barrier(p, s, ++barrier_index, 100 + ph);
-      if (ok && p.tp_size > 1 && (kind == kO || kind == kDown))
-        ok = tp_rendezvous(p, s, p.tp_seq_base + seq, 300 + ph);
     }
   }
   if (tid == 0) *s.prod_ctl = -1;   // producer: no more steps

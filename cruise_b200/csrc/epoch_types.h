@@ -29,6 +29,7 @@ constexpr int kRedSlots = 4;                           // row-group partial-sum 
 constexpr int kMaxCtas = 1024;
 constexpr int kMaxStages = 8;
 constexpr int kTraceMax = 2048;       // grid barriers recorded per launch
+constexpr int kTraceSeries = 6;      // globaltimer series per grid barrier (see cruise_epoch_read_trace)
 
 // statuses and finish reasons of the reference controller (:51-74)
 enum Status : int32_t {
@@ -151,10 +152,15 @@ struct TpArg {
   float val;
   int32_t idx, bad, pad;
 };
+constexpr int kTpRows = 8192;          // widest hidden size a tensor-parallel exchange holds
+
 struct TpExchange {
   uint32_t flag[kMaxTp][32];            // flag[src]: last sequence number src published (own 128-B line)
   TpArg arg[kMaxTp][4];                 // argmax partial of each rank per batch row
-  float part[2][kMaxTp][4][8192];       // [set][src][row][H] (H <= 8192)
+  // [set][src][n][b]: rank src's fp32 partial of output row n, batch row b, in
+  // the low half of the word and the sequence number of its phase in the high
+  // half (H <= kTpRows); set 0 holds the O projection, set 1 the down projection
+  uint64_t part[2][kMaxTp][kTpRows][4];
 };
 
 struct EpochParams {
@@ -195,7 +201,6 @@ struct EpochParams {
   TpExchange *tp_local;
   uint32_t tp_seq_base;        // launch-unique base of the exchange sequence numbers
   uint32_t pad3;
-  bf16 *h_alt;                 // [4][H] second residual buffer (tensor parallelism)
 };
 
 }  // namespace cruise

@@ -152,6 +152,19 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *ptr) {
   return v;
 }
 
+// Self-validating exchange words: a naturally aligned 64-bit access is
+// single-copy atomic, so a reader that sees the expected tag in the high half
+// also sees the value written with it (no fence or separate flag).
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *ptr, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *ptr) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_release_u32(uint32_t *ptr, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }

@@ -218,10 +218,11 @@ class EpochEngine:
         self.lib.cruise_epoch_set_trace(self.handle, 1 if enable else 0)
 
     def read_trace(self, count: int) -> np.ndarray:
-        """[5, count] globaltimer ns per grid barrier of the last epoch: CTA 0
-        exit, CTA 0 entry, activations staged, last tile consumed, last arrival."""
-        out = np.zeros((5, count), dtype=np.uint64)
-        for series in range(5):
+        """[6, count] globaltimer ns per grid barrier of the last epoch: CTA 0
+        exit, CTA 0 entry, activations staged, last tile consumed, last arrival,
+        and (a duration) CTA 0's wait for other tensor-parallel ranks (or 0)."""
+        out = np.zeros((6, count), dtype=np.uint64)
+        for series in range(6):
             self._check(
                 self.lib.cruise_epoch_read_trace(self.handle, series, _ptr(out[series], ctypes.c_uint64), count),
                 "read_trace",

@@ -132,8 +132,8 @@ class TpShard:
 
     @staticmethod
     def of(config: ModelConfig, rank: int, size: int) -> "TpShard":
-        if not (1 <= size <= 8 and 0 <= rank < size):
-            raise ValueError(f"rank {rank} of {size}")
+        if size not in (1, 2, 4, 8) or not 0 <= rank < size:
+            raise ValueError(f"rank {rank} of {size} (tensor parallelism over 1, 2, 4 or 8 ranks)")
         nq, nkv = config.num_heads, config.num_kv_heads
         grp = nq // nkv
         if size <= nkv:

@@ -117,7 +117,7 @@ void cruise_epoch_destroy(void *engine);
 
 /* Tensor parallelism (no counterpart in the reference; the survey's 2/4/8-GPU
  * sharding of the same epoch).  One process per GPU creates rank `tp_rank` of
- * `tp_size` (1..8): query heads, KV heads (shared by tp_size / KV-heads ranks
+ * `tp_size` (1, 2, 4 or 8): query heads, KV heads (shared by tp_size / KV-heads ranks
  * when tp_size exceeds them), intermediate rows and vocabulary rows are split
  * over the ranks; the residual stream, the embedding and the epoch control
  * are replicated.  The O and down projections are all-reduced inside the epoch
@@ -225,12 +225,15 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us,
 
 /* Phase trace (tracing / profiling aid): when enabled, each epoch records, per
  * grid barrier j (1-based, in launch order; at most 2048 per epoch), globaltimer
- * nanoseconds in five series:
+ * nanoseconds in six series:
  *   0  CTA 0 left barrier j (every CTA had arrived)
  *   1  CTA 0 arrived at barrier j (finished its share of the phase)
  *   2  CTA 0 had staged the phase's activations (projection phases)
  *   3  CTA 0's warp 0 consumed its last weight tile (projection phases)
  *   4  the last CTA arrived at barrier j
+ *   5  not a time stamp: nanoseconds CTA 0's epilogue waited for the other
+ *      ranks' partials in phase j (O and down of a tensor-parallel engine;
+ *      0 otherwise)
  * cruise_epoch_read_trace copies `count` entries of one series. */
 int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,

@@ -133,3 +133,48 @@ def test_two_rank_handle_exchange():
     for rank in range(world):
         assert results[rank] == expect
         assert results[f"short{rank}"] and results[f"size{rank}"]
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_shard_step_bytes_partition_the_step(size):
+    import bench
+
+    cfg = QWEN25_7B
+    ctx = [5, 17, 130, 2]
+    shards = [TpShard.of(cfg, r, size) for r in range(size)]
+    total = sum(bench.shard_step_bytes(cfg, s, ctx) for s in shards)
+    # replicated on every rank: the norms and the embedding rows
+    replicated = 2 * (cfg.num_layers * 2 * cfg.hidden + cfg.hidden) + len(ctx) * cfg.hidden * 2
+    # ranks sharing a KV head (size > KV heads) each stream its K/V weights and cache
+    dup = max(1, size // cfg.num_kv_heads)
+    kv_w = cfg.num_layers * 2 * (cfg.kv_width * cfg.hidden + cfg.kv_width) * 2
+    kv_c = 2 * cfg.num_layers * cfg.kv_width * 2 * (sum(ctx) + len(ctx))
+    assert total == bench.step_bytes(cfg, ctx) + (size - 1) * replicated + (dup - 1) * (kv_w + kv_c)
+
+
+def _gather_worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import bench
+
+    class _Engine:
+        config = QWEN25_7B
+        shard = TpShard.of(QWEN25_7B, rank, world)
+
+    full = torch.arange(2 * 3 * 2 * 4 * 5, dtype=torch.float32).reshape(2, 3, 2, 4, 5)
+    s = _Engine.shard
+    key, value = bench.gather_kv_shards(_Engine(), full[:, :, :, s.kv0:s.kv0 + s.nkv].clone(),
+                                        -full[:, :, :, s.kv0:s.kv0 + s.nkv].clone())
+    results[rank] = bool(torch.equal(key, full) and torch.equal(value, -full))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_kv_shards_gather_to_the_whole_cache(world):
+    port = _free_port()
+    manager = mp.Manager()
+    results = manager.dict()
+    mp.spawn(_gather_worker, args=(world, port, results), nprocs=world, join=True)
+    assert all(results[r] for r in range(world))
