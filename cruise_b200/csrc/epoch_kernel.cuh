@@ -811,7 +811,6 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
   const TileRange tr = tile_range(g, blockIdx.x, p.grid);
   float best = -INFINITY;
   int32_t best_i = INT_MAX, bad = 0;
-  uint64_t tp_wait_ns = 0;   // traced: time this warp waited for other ranks' partials
 
   int64_t seg_start = tr.t0;
   int64_t rg = tr.t0 / tr.KT;
@@ -910,36 +909,19 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, e1));
         } else if (tp_partial) {
           // Row-parallel output under tensor parallelism: every rank's finisher
-          // of this row group holds a partial over its K shard.  Send ours to
-          // the other ranks as tagged words, read theirs (each word valid once
-          // it carries this phase's tag), then hidden = residual +
-          // materialize(sum over ranks in rank order) -- the reference's
-          // (:380-386, :399-403) with the sum split over ranks.
+          // of this row group holds a partial over its K shard.  Publish ours
+          // to every rank (this one included) as tagged words; the residual
+          // update waits until the phase's last row group was sent (below), so
+          // no rank's sends wait on another rank.
           const int set = g.kind == kO ? 0 : 1;
-          const uint32_t tag = p.tp_seq_base + seq;
-          const uint64_t hi = static_cast<uint64_t>(tag) << 32;
+          const uint64_t hi = static_cast<uint64_t>(p.tp_seq_base + seq) << 32;
           const uint64_t w0 = hi | __float_as_uint(v0), w1 = hi | __float_as_uint(v1);
           for (int r = 0; r < p.tp_size; ++r) {
             TpExchange *peer = reinterpret_cast<TpExchange *>(
                 __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(peer_mine), r));
-            if (r == p.tp_rank) continue;
             st_relaxed_sys_u64(&peer->part[set][p.tp_rank][n0][b], w0);
             st_relaxed_sys_u64(&peer->part[set][p.tp_rank][n1][b], w1);
           }
-          const uint64_t wait0 = p.trace != nullptr ? globaltimer() : 0;
-          float sum0 = 0.f, sum1 = 0.f;
-          for (int r = 0; r < p.tp_size; ++r) {
-            float a0 = v0, a1 = v1;   // this rank's own partial
-            if (r != p.tp_rank) {
-              a0 = tp_recv(p, &p.tp_local->part[set][r][n0][b], tag);
-              a1 = tp_recv(p, &p.tp_local->part[set][r][n1][b], tag);
-            }
-            sum0 = __fadd_rn(sum0, a0);
-            sum1 = __fadd_rn(sum1, a1);
-          }
-          if (p.trace != nullptr) tp_wait_ns += globaltimer() - wait0;
-          p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(sum0)));
-          p.h[static_cast<size_t>(b) * m.H + n1] = tobf(__fadd_rn(e1, rbf(sum1)));
         } else if (g.kind == kO || g.kind == kDown) {
           // hidden = residual + materialize(mm_t(x, W))  (:380-386, :399-403)
           p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(v0)));
@@ -986,8 +968,39 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
     p.arg_idx[blockIdx.x * kBatch + lane] = best_i;
     p.arg_bad[blockIdx.x * kBatch + lane] = bad;
   }
-  if (tp_partial && p.trace != nullptr && blockIdx.x == 0 && lane == 0 && trace_slot < kTraceMax)
-    p.trace[5 * kTraceMax + trace_slot] = tp_wait_ns;
+  if (tp_partial) {
+    // hidden = residual + materialize(sum over ranks in rank order) for every
+    // row group this CTA finished -- the reference's (:380-386, :399-403) with
+    // the sum split over ranks; each word is valid once it carries the tag
+    const int set = g.kind == kO ? 0 : 1;
+    const uint32_t tag = p.tp_seq_base + seq;
+    const uint64_t wait0 = p.trace != nullptr ? globaltimer() : 0;
+    const int b = b_lane;
+    const int64_t first_head = tr.t0 % tr.KT == 0 ? tr.t0 / tr.KT : tr.t0 / tr.KT + 1;
+    for (int64_t r = first_head; tr.t0 < tr.t1 && r * tr.KT < tr.t1; ++r) {
+      const int64_t n0 = r * kRows + (lane >> 2), n1 = n0 + 8;
+      float sum0 = 0.f, sum1 = 0.f;
+      for (int src = 0; src < p.tp_size; ++src) {
+        sum0 = __fadd_rn(sum0, tp_recv(p, &p.tp_local->part[set][src][n0][b], tag));
+        sum1 = __fadd_rn(sum1, tp_recv(p, &p.tp_local->part[set][src][n1][b], tag));
+      }
+      float e0, e1;
+      if (r == pa_rg) {
+        e0 = pa0;
+        e1 = pa1;
+      } else if (r == pb_rg) {
+        e0 = pb0;
+        e1 = pb1;
+      } else {
+        e0 = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n0));
+        e1 = bf(__ldcg(p.h + static_cast<size_t>(b) * m.H + n1));
+      }
+      p.h[static_cast<size_t>(b) * m.H + n0] = tobf(__fadd_rn(e0, rbf(sum0)));
+      p.h[static_cast<size_t>(b) * m.H + n1] = tobf(__fadd_rn(e1, rbf(sum1)));
+    }
+    if (p.trace != nullptr && blockIdx.x == 0 && lane == 0 && trace_slot < kTraceMax)
+      p.trace[5 * kTraceMax + trace_slot] = globaltimer() - wait0;
+  }
   // the phase's outputs written by this warp are visible GPU-wide before the
   // consumers may arrive at the grid barrier
   __threadfence();
