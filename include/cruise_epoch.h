@@ -115,7 +115,7 @@ void *cruise_epoch_create(const CruiseModelConfig *cfg, int32_t device,
                           int32_t *status);
 void cruise_epoch_destroy(void *engine);
 
-/* Tensor parallelism (no counterpart in the reference; the survey's 2/4/8-GPU
+/* Tensor parallelism (no counterpart in the reference: its 2/4/8-device
  * sharding of the same epoch).  One process per GPU creates rank `tp_rank` of
  * `tp_size` (1, 2, 4 or 8): query heads, KV heads (shared by tp_size / KV-heads ranks
  * when tp_size exceeds them), intermediate rows and vocabulary rows are split
@@ -123,11 +123,15 @@ void cruise_epoch_destroy(void *engine);
  * are replicated.  The O and down projections are all-reduced inside the epoch
  * kernel through peer memory, the argmax across vocabulary shards likewise.
  * Tensors passed to cruise_epoch_set_weight / _get_weight and the KV cache of
- * _read_kv / _write_kv are this rank's shards; the import payload stays whole.
+ * _read_kv / _write_kv are this rank's shards, the logits of cruise_epoch_run
+ * hold this rank's vocabulary rows at their global positions; the import
+ * payload stays whole and history / control output are the same on every rank.
  * Before the first epoch every rank exports its exchange block with
  * cruise_epoch_tp_handle (a 64-byte cudaIpcMemHandle_t), the handles are
  * gathered in rank order (any host channel) and passed to
- * cruise_epoch_tp_connect.  All ranks must then run the same epochs. */
+ * cruise_epoch_tp_connect.  All ranks must then run the same epochs; a rank
+ * that does not makes the others' epoch end with status 207 (device waits are
+ * bounded at 20 s under tensor parallelism). */
 void *cruise_epoch_create_tp(const CruiseModelConfig *cfg, int32_t device,
                              int32_t tp_rank, int32_t tp_size,
                              int32_t *status);

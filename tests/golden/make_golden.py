@@ -3,7 +3,7 @@
 
 Run in the container that holds the reference checkout (default path below):
 
-    python tests/golden/make_golden.py [--reference /path/to/Cruise]
+    python tests/golden/make_golden.py --reference /path/to/Cruise
 
 It imports ``PagedQwenDecoderStep`` from
 ``history/attempts/g4c-attempt69c-b4-air/batched_decoder_step.py`` unmodified,
@@ -94,7 +94,7 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True, help="checkout of the reference project")
     parser.add_argument("--output", type=Path, default=REPO / "tests/golden/decoder_tiny.npz")
     args = parser.parse_args()
     torch.set_num_threads(8)
