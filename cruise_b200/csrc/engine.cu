@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <array>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -202,7 +203,10 @@ struct Engine {
   TpExchange **d_peers = nullptr;          // device array of every rank's block
   std::vector<void *> opened;              // peer blocks opened through IPC
   bool tp_connected = false;
-  uint32_t launches = 0;                   // epochs launched (exchange sequence base)
+  std::atomic<uint32_t> launches{0};       // epochs launched (exchange sequence base, egress launch id)
+  StreamRing *h_stream = nullptr;          // host-mapped egress ring (allocated on first enable)
+  StreamRing *d_stream = nullptr;          // its device view
+  bool stream_on = false;
 };
 
 // Every host<->device copy runs on the engine's own (non-blocking) stream and is
@@ -346,6 +350,7 @@ void destroy_engine(Engine *e) {
   cudaFree(e->d_peers);
   cudaFree(e->xchg);
   if (e->h_io) cudaFreeHost(e->h_io);
+  if (e->h_stream) cudaFreeHost(e->h_stream);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -766,7 +771,9 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   }
   // exchange sequence numbers grow across launches (every rank launches the
   // same epochs); a launch uses at most 8 x 142 of its 65,536
-  p.tp_seq_base = ++e->launches << 16;
+  p.launch_id = ++e->launches;
+  p.tp_seq_base = p.launch_id << 16;
+  p.stream = e->stream_on ? e->d_stream : nullptr;
   void *args[] = {&p};
   cudaEventRecord(e->ev0, e->stream);
   err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
@@ -1275,6 +1282,46 @@ int32_t cruise_epoch_set_trace(void *engine, int32_t enable) {
   if (engine == nullptr) return -1;
   static_cast<Engine *>(engine)->trace_on = enable != 0;
   return 0;
+}
+
+int32_t cruise_epoch_stream_enable(void *engine, int32_t enable) {
+  if (engine == nullptr) return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  if (enable != 0 && e->h_stream == nullptr) {
+    cudaSetDevice(e->device);
+    void *host = nullptr, *dev = nullptr;
+    cudaError_t err = cudaHostAlloc(&host, sizeof(cruise::StreamRing), cudaHostAllocMapped);
+    if (err == cudaSuccess) err = cudaHostGetDevicePointer(&dev, host, 0);
+    if (err != cudaSuccess) {
+      if (host != nullptr) cudaFreeHost(host);
+      return cruise::set_err(e, err, "stream ring");
+    }
+    std::memset(host, 0, sizeof(cruise::StreamRing));
+    e->h_stream = static_cast<cruise::StreamRing *>(host);
+    e->d_stream = static_cast<cruise::StreamRing *>(dev);
+  }
+  e->stream_on = enable != 0;
+  return 0;
+}
+
+uint32_t cruise_epoch_stream_next_id(void *engine) {
+  if (engine == nullptr) return 0;
+  return static_cast<Engine *>(engine)->launches.load() + 1;
+}
+
+int32_t cruise_epoch_stream_poll(void *engine, uint32_t launch_id, int64_t *tokens_out) {
+  if (engine == nullptr || tokens_out == nullptr) return -1;
+  const Engine *e = static_cast<const Engine *>(engine);
+  if (e->h_stream == nullptr) return -1;
+  // no lock: the epoch that publishes holds the engine's mutex while it runs
+  const uint64_t published = *reinterpret_cast<const volatile uint64_t *>(&e->h_stream->published);
+  std::atomic_thread_fence(std::memory_order_acquire);
+  if (static_cast<uint32_t>(published >> 32) != launch_id) return 0;
+  const int32_t steps = std::min(static_cast<int32_t>(published & 0xFFFFFFFFu), cruise::kMaxSteps);
+  for (int i = 0; i < steps * cruise::kBatch; ++i)
+    tokens_out[i] = reinterpret_cast<const volatile int64_t *>(&e->h_stream->tokens[0][0])[i];
+  return steps;
 }
 
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns, int32_t count) {

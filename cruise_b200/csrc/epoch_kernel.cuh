@@ -1690,6 +1690,14 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
           int any = 0;
           for (int b = 0; b < kBatch; ++b) any |= w->active[b];
           w->stop = (w->status != kOk || calls >= w->max_steps || any == 0) ? 1 : 0;
+          if (p.stream != nullptr && w->status == kOk) {
+            // streaming egress: this step's tokens, then the step count
+            for (int b = 0; b < kBatch; ++b)
+              *reinterpret_cast<volatile int64_t *>(&p.stream->tokens[st][b]) = io->history[st * kBatch + b];
+            __threadfence_system();
+            *reinterpret_cast<volatile uint64_t *>(&p.stream->published) =
+                (static_cast<uint64_t>(p.launch_id) << 32) | static_cast<uint32_t>(calls);
+          }
         }
       }
       if (ok) ok = grid_barrier(p, s, ++barrier_index, 100 + ph);

@@ -79,6 +79,14 @@ struct LayerWeights {
   const bf16 *down_w;          // tiled [H][I_pad]  columns >= I are zero
 };
 
+// Streaming egress, in host-mapped pinned memory: after each decode step of an
+// epoch the kernel writes that step's tokens (-1 for rows that did not run),
+// then `published` = launch id << 32 | steps so far.
+struct StreamRing {
+  int64_t tokens[kMaxSteps][kBatch];
+  uint64_t published;
+};
+
 // One host->device and one device->host copy per epoch (the 8-in / 2-out ABI).
 struct EpochIO {
   int64_t token[kBatch];
@@ -200,6 +208,8 @@ struct EpochParams {
   TpExchange *const *tp_peer;  // device array [tp_size] of the ranks' exchange blocks
   TpExchange *tp_local;
   uint32_t tp_seq_base;        // launch-unique base of the exchange sequence numbers
+  uint32_t launch_id;          // epochs launched by this engine, this one included
+  StreamRing *stream;          // device view of the host-mapped egress ring (nullptr: off)
   uint32_t pad3;
 };
 

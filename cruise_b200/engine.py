@@ -9,7 +9,10 @@ the 28-word control output.  PyTorch is used only for host tensors.
 from __future__ import annotations
 
 import ctypes
+import threading
+import time
 from dataclasses import dataclass
+from typing import Callable
 
 import numpy as np
 import torch
@@ -213,6 +216,43 @@ class EpochEngine:
         launches = ctypes.c_int32(0)
         self.lib.cruise_epoch_last_timing(self.handle, ctypes.byref(device_us), ctypes.byref(launches))
         return EpochOutput(history, control_out, logits, float(device_us.value))
+
+    # -- streaming egress ------------------------------------------------------------
+    def run_streaming(self, on_step: Callable[[int, np.ndarray], None], poll_s: float = 5e-5,
+                      **run_kwargs) -> EpochOutput:
+        """One epoch exactly like :meth:`run`, while this thread hands every
+        decode step's tokens (int64[4], -1 for rows that did not run) to
+        ``on_step(step, tokens)`` in step order as soon as the device published
+        them -- before the epoch ends.  The epoch itself runs on a helper
+        thread (the C call releases the GIL)."""
+        self._check(self.lib.cruise_epoch_stream_enable(self.handle, 1), "stream_enable")
+        launch = self.lib.cruise_epoch_stream_next_id(self.handle)
+        result: dict = {}
+
+        def epoch() -> None:
+            try:
+                result["out"] = self.run(**run_kwargs)
+            except BaseException as exc:   # re-raised on the caller's thread
+                result["err"] = exc
+
+        worker = threading.Thread(target=epoch, name="cruise-epoch", daemon=True)
+        worker.start()
+        tokens = np.empty((MAX_STEPS, BATCH), dtype=np.int64)
+        seen = 0
+        while True:
+            running = worker.is_alive()
+            n = self.lib.cruise_epoch_stream_poll(self.handle, launch, tokens.ctypes.data)
+            while seen < n:
+                on_step(seen, tokens[seen].copy())
+                seen += 1
+            if not running:
+                break
+            time.sleep(poll_s)
+        worker.join()
+        self._check(self.lib.cruise_epoch_stream_enable(self.handle, 0), "stream_enable")
+        if "err" in result:
+            raise result["err"]
+        return result["out"]
 
     def set_trace(self, enable: bool) -> None:
         self.lib.cruise_epoch_set_trace(self.handle, 1 if enable else 0)

@@ -243,6 +243,20 @@ int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,
                                 int32_t count);
 
+/* Streaming token egress (a reference evaluation item: stream without K=1).
+ * With streaming enabled, every decode step of an epoch publishes that step's
+ * four tokens (-1 for rows that did not run) to host-mapped pinned memory as
+ * soon as the device decided them, while cruise_epoch_run still waits for the
+ * epoch.  cruise_epoch_stream_next_id gives the id the next epoch of this
+ * engine will carry; another host thread then calls cruise_epoch_stream_poll
+ * with it: returns how many steps of that epoch were published so far (0
+ * before the first) and copies their tokens, step-major, into tokens_out
+ * [8][4]; -1 if streaming was never enabled.  Poll takes no lock. */
+int32_t cruise_epoch_stream_enable(void *engine, int32_t enable);
+uint32_t cruise_epoch_stream_next_id(void *engine);
+int32_t cruise_epoch_stream_poll(void *engine, uint32_t launch_id,
+                                 int64_t *tokens_out);
+
 /* Last CUDA error string of this engine (static storage).  With engine NULL:
  * why the calling thread's last cruise_epoch_create / _create_tp returned
  * NULL (the failing step and CUDA error), "" after a successful create. */
