@@ -53,7 +53,7 @@ METRIC = "Qwen2.5-7B-arch B=4 epoch: decode tok/s, µs/step, % HBM roofline"
 # 7B geometry), dram__bytes_read.sum + dram__bytes_write.sum from a one-pass ncu
 # capture of this bench command; reported per decode step beside the
 # algorithmic bytes.  It applies to the default K only.
-PROFILED_TRAFFIC = {"k": 2, "bytes_per_launch": 28298194688 + 21556480, "steps_per_launch": 2}
+PROFILED_TRAFFIC = {"k": 2, "bytes_per_launch": 28301151744 + 21519616, "steps_per_launch": 2}
 KV_BYTES_PER_TOKEN = 28 * 4 * 128 * 2 * 2   # K and V over all layers, one position
 FALLBACK_HBM_GBS = 6650.0
 EPOCH_H2D_BYTES = 616   # EpochIO inputs (8-in ABI + forced-token table), one copy per epoch
