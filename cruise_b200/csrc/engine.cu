@@ -207,6 +207,7 @@ struct Engine {
   StreamRing *h_stream = nullptr;          // host-mapped egress ring (allocated on first enable)
   StreamRing *d_stream = nullptr;          // its device view
   bool stream_on = false;
+  uint64_t tp_timeout_ns = 20000000000ull;   // device waits on other ranks (CRUISE_TP_TIMEOUT_MS)
 };
 
 // Every host<->device copy runs on the engine's own (non-blocking) stream and is
@@ -410,6 +411,10 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
   e->down_xglobal = pick_kc(m.I_pad) == 64 * kConsumerWarps;
   const int kmax = e->down_xglobal ? m.H : std::max(m.H, m.I_pad);
   e->xs_stride = kmax + 8;
+  if (const char *env = std::getenv("CRUISE_TP_TIMEOUT_MS")) {
+    const long ms = std::strtol(env, nullptr, 10);
+    if (ms > 0) e->tp_timeout_ns = static_cast<uint64_t>(std::min(ms, 600000L)) * 1000000ull;
+  }
   {
     const char *env = std::getenv("CRUISE_L2_AHEAD_KB");
     const long kb = env != nullptr ? std::strtol(env, nullptr, 10) : kDefaultL2AheadKb;
@@ -756,8 +761,9 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   p.trace = e->trace_on ? e->trace : nullptr;
   if (e->trace_on) cudaMemsetAsync(e->trace, 0, kTraceSeries * kTraceMax * sizeof(uint64_t), e->stream);
   // every device-side wait gives up after 2 s; under tensor parallelism after
-  // 20 s, since a rank's first wait also covers the other ranks' launch skew
-  p.timeout_ns = e->tp_size > 1 ? 20000000000ull : 2000000000ull;
+  // 20 s by default (CRUISE_TP_TIMEOUT_MS at creation), since a rank's first
+  // wait also covers the other ranks' launch skew
+  p.timeout_ns = e->tp_size > 1 ? e->tp_timeout_ns : 2000000000ull;
   p.l2_ahead = e->l2_ahead;
   p.tp_size = e->tp_size;
   p.tp_rank = e->tp_rank;
@@ -792,6 +798,14 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   e->last_launches = 1;
   std::memcpy(history, io->history, sizeof(io->history));
   std::memcpy(control_out, io->control_out, sizeof(io->control_out));
+  if (control_out[3] == kModelError) {
+    // which device-side wait gave up (sites: 1-4 prologue barriers, 100+phase
+    // grid barriers, 300 tensor-parallel partials, 401 tensor-parallel argmax,
+    // 900/1001-1004 pipeline waits)
+    uint32_t words[2] = {0, 0};
+    if (copy_sync(e, words, &e->d_sync->error, sizeof(words), cudaMemcpyDeviceToHost) == cudaSuccess && words[0])
+      e->last_error = "epoch ended by a device-side wait that gave up (site " + std::to_string(words[1]) + ")";
+  }
   return 0;
 }
 
