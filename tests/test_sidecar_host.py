@@ -1,7 +1,9 @@
 """The sidecar server and client without a GPU: wire layout, startup handshake,
 exit codes and the client's checks.  Engine creation fails on a CPU host (no
 CUDA device), which the server must report as startup status 100 + 3 and exit
-with the same code -- that path exercises the real socket and message layout."""
+with the same code -- that path exercises the real socket and message layout.
+The client-side wire tests follow the reference's tests/test_sidecar_protocol.py
+(round trip, reserved warm-up generation, device IPC reported as an import)."""
 
 from __future__ import annotations
 
@@ -102,3 +104,90 @@ def test_transfer_checks_against_the_plan():
         sc.SidecarEpochEngine._check_transfer(plan, 0b10, (0, 3, 0, 0), "x")
     assert sc._by_row(plan, "token_id", 0) == [5, 5, 0, 0]
     assert sc._by_row(plan, "eos_token_id", 7) == [4095, 4095, 7, 7]
+
+
+def test_request_and_response_round_trip():
+    from cruise_b200.contract import EpochCommitState
+
+    request = sc.REQUEST.pack(sc.REQUEST_MAGIC, sc.SIDECAR_PROTOCOL_VERSION, sc.EXECUTE, 2, 4, 0, *range(4),
+                              *range(4), *([1] * 4), *([151645] * 4), *([1, 2, 0, 0]))
+    assert sc.REQUEST.unpack(request)[:5] == (sc.REQUEST_MAGIC, sc.SIDECAR_PROTOCOL_VERSION, sc.EXECUTE, 2, 4)
+    response = sc.RESPONSE.pack(sc.RESPONSE_MAGIC, 0, 0, 4, 1, 1, EpochCommitState.COMMITTED, 0x12345678, 123, 45,
+                                260, 368, *([4, 4, 0, 0]), *([1, 2, 0, 0]), *range(32))
+    values = sc.RESPONSE.unpack(response)
+    assert values[:12] == (sc.RESPONSE_MAGIC, 0, 0, 4, 1, 1, EpochCommitState.COMMITTED, 0x12345678, 123, 45, 260,
+                           368)
+
+
+class _RecordingSocket:
+    def __init__(self):
+        self.payloads = []
+
+    def sendall(self, payload):
+        self.payloads.append(payload)
+
+
+def _wired_client(response: tuple) -> sc.SidecarEpochEngine:
+    """A client whose socket records requests and whose reply is `response`."""
+    from cruise_b200.model_config import QWEN25_7B
+
+    engine = sc.SidecarEpochEngine.__new__(sc.SidecarEpochEngine)
+    engine.socket = _RecordingSocket()
+    engine.config = QWEN25_7B
+    engine._receive = lambda: response
+    return engine
+
+
+def test_warmup_uses_the_reserved_generation():
+    from cruise_b200.contract import EpochCommitState
+
+    reply = sc.RESPONSE.unpack(sc.RESPONSE.pack(sc.RESPONSE_MAGIC, 0, 0, 1, 1, 1, EpochCommitState.COMMITTED, 0, 1, 1,
+                                                260, 368, 1, 0, 0, 0, sc.WARMUP_GENERATION, 0, 0, 0,
+                                                5, *([-1] * 31)))
+    engine = _wired_client(reply)
+    out = engine.warm_up()
+    assert out.model_calls == 1 and out.commit_state == EpochCommitState.COMMITTED
+    sent = sc.REQUEST.unpack(engine.socket.payloads[0])
+    assert sent[:5] == (sc.REQUEST_MAGIC, sc.SIDECAR_PROTOCOL_VERSION, sc.WARM_UP, 1, 1)
+    assert sent[-4:] == (sc.WARMUP_GENERATION, 0, 0, 0) and sent[6] == sc.WARMUP_TOKEN
+
+
+def test_device_ipc_execute_is_reported_as_kv_import():
+    from cruise_b200.contract import CONTRACT_VERSION, EpochCommitState, ResidentEpochPlan, ResidentEpochRequest
+    from cruise_b200.kv_transfer import IPC_METADATA_BYTES
+
+    reply = sc.RESPONSE.unpack(sc.RESPONSE.pack(sc.RESPONSE_MAGIC, 0, 0, 1, 1, 1, EpochCommitState.COMMITTED,
+                                                0x12345678, 123, 45, 3776, 368, 1, 0, 0, 0, 7, 0, 0, 0,
+                                                42, *([-1] * 31)))
+    engine = _wired_client(reply)
+    plan = ResidentEpochPlan(
+        version=CONTRACT_VERSION, graph_batch_size=4, max_steps=1, logical_capacity=8,
+        requests=(ResidentEpochRequest(req_id="request-0", row=0, generation=7, token_id=11, position=1,
+                                       sequence_length=2, eos_token_id=151645, scheduler_block_ids=(0,),
+                                       device_block_ids=(0, 1), kv_import_required=True),),
+        active_mask=(1, 0, 0, 0))
+    metadata = b"\0" * IPC_METADATA_BYTES
+    out = engine._execute(plan, sc.DEVICE_IPC_EXECUTE, 9, metadata)
+    assert out.kv_imported and out.kv_import_checksum == 0x12345678 and out.kv_transfer_mode == "device_ipc"
+    assert out.token_ids == {"request-0": [42]} and out.row_generations == (7, 0, 0, 0)
+    assert len(engine.socket.payloads) == 1 and engine.socket.payloads[0][sc.REQUEST.size:] == metadata
+    sent = sc.REQUEST.unpack(engine.socket.payloads[0][: sc.REQUEST.size])
+    assert sent[2] == sc.DEVICE_IPC_EXECUTE and sent[5] == 9
+
+
+def test_transport_errors_keep_the_commit_state():
+    from cruise_b200.contract import EpochCommitState, ResidentEpochExecutionError
+
+    reply = sc.RESPONSE.unpack(sc.RESPONSE.pack(sc.RESPONSE_MAGIC, 12, -1, 0, 0, 0, EpochCommitState.PREPARED, 0,
+                                                0, 0, 0, 0, *([0] * 8), *([-1] * 32)))
+    engine = _wired_client(reply)
+    from cruise_b200.contract import CONTRACT_VERSION, ResidentEpochPlan, ResidentEpochRequest
+
+    plan = ResidentEpochPlan(
+        version=CONTRACT_VERSION, graph_batch_size=4, max_steps=1, logical_capacity=8,
+        requests=(ResidentEpochRequest(req_id="a", row=0, generation=1, token_id=1, position=0, sequence_length=1,
+                                       eos_token_id=151645, scheduler_block_ids=(0,), device_block_ids=(0, 1)),),
+        active_mask=(1, 0, 0, 0))
+    with pytest.raises(ResidentEpochExecutionError) as caught:
+        engine.execute(plan)
+    assert caught.value.status == 12 and caught.value.commit_state == EpochCommitState.PREPARED
