@@ -617,6 +617,86 @@ def random_weights(cfg, layers: int, seed: int) -> dict:
             for name, shape in tensor_shapes(ocfg).items()}
 
 
+def forced_epochs_all_rows(sc, cfg, generation_offset: int):
+    """Teacher-forced epochs writing the KV of every prompt token but the last,
+    all rows of the cohort in the same epochs (8 positions per epoch)."""
+    from scenario import BATCH, MAX_STEPS, compute_slot
+
+    longest = max(len(p) for p in sc.prompts)
+    eos = next(t for t in range(cfg.vocab - 1, -1, -1) if all(t not in p for p in sc.prompts))
+    gens = [g + generation_offset if g else 0 for g in sc.generations]
+    for done in range(0, longest - 1, MAX_STEPS):
+        token = np.zeros(BATCH, dtype=np.int64)
+        position = np.zeros(BATCH, dtype=np.int64)
+        seq_len = np.zeros(BATCH, dtype=np.int32)
+        active = np.zeros(BATCH, dtype=np.int32)
+        forced = np.full((MAX_STEPS, BATCH), -1, dtype=np.int64)
+        steps = 0
+        for row, prompt in enumerate(sc.prompts):
+            if len(prompt) - 1 <= done:
+                continue
+            n = min(MAX_STEPS, len(prompt) - 1 - done)
+            steps = max(steps, n)
+            token[row], position[row], seq_len[row], active[row] = prompt[done], done, done + 1, 1
+            forced[:n, row] = prompt[done + 1: done + 1 + n]
+        slot = np.array([compute_slot(sc.block_table, cfg.block_size, r, int(position[r])) for r in range(BATCH)],
+                        dtype=np.int32)
+        row_gens = [gens[r] if active[r] else 0 for r in range(BATCH)]
+        control = np.array([steps, eos, eos, eos, eos, 0, 0, *row_gens], dtype=np.int32)
+        yield dict(token=token, position=position, seq_len=seq_len, slot=slot, active=active,
+                   block_table=sc.block_table.reshape(-1), control=control, forced=forced)
+
+
+def run_prefill(args) -> None:
+    """Prefill of a 4-row cohort of 120-token prompts on the 7B model: the
+    batched device prefill (cruise_epoch_prefill + the import epoch) against the
+    teacher-forced prefill epochs (one token per row per step).  Prints one
+    JSON line; not part of the default decode benchmark."""
+    import torch
+
+    from cruise_b200.engine import EpochEngine
+    from cruise_b200.model_config import QWEN25_7B
+    from scenario import decode_inputs, make_scenario
+
+    cfg = QWEN25_7B
+    engine = EpochEngine(cfg)
+    engine.init_synthetic(seed=0)
+    length = 120
+    sc = make_scenario(vocab=cfg.vocab, seed=77, active_rows=(1, 1, 1, 1), prompt_len=(length, length), k=2,
+                       budget=(2, 2), eos=cfg.configured_eos, token_high=151643)
+    tokens = sum(len(p) - 1 for p in sc.prompts)
+    engine.prefill(sc.prompts)   # first call builds the untiled weights
+    batched = []
+    for _ in range(max(3, args.steps)):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        engine.prefill(sc.prompts)
+        batched.append((time.perf_counter() - t0) * 1e3)
+    out = engine.run(**decode_inputs(sc, cfg.block_size, importing=True))
+    assert out.status == 0, out.status
+    # the same prompts again as teacher-forced epochs (all four rows together,
+    # 8 tokens per row per epoch), under new generations
+    forced_dev, forced_wall = 0.0, time.perf_counter()
+    epochs = 0
+    for inputs in forced_epochs_all_rows(sc, cfg, generation_offset=10):
+        o = engine.run(**inputs)
+        assert o.status == 0, o.status
+        forced_dev += o.device_us / 1e3
+        epochs += 1
+    forced_wall = (time.perf_counter() - forced_wall) * 1e3
+    engine.close()
+    ms = statistics.median(batched)
+    print(json.dumps({
+        "metric": "prefill of a B=4 cohort of 120-token prompts (7B arch), ms", "unit": "ms",
+        "higher_is_better": False, "data": "synthetic (seeded weights and prompts)", "dtype": "bf16",
+        "batched_device_prefill_ms": round(ms, 3), "prompt_tokens_prefilled": tokens,
+        "batched_tok_per_s": round(tokens / ms * 1e3, 1),
+        "teacher_forced_epochs": epochs, "teacher_forced_device_ms": round(forced_dev, 3),
+        "teacher_forced_wall_ms": round(forced_wall, 3), "speedup_vs_teacher_forced": round(forced_wall / ms, 1),
+        "batched_includes": "host token upload, all 28 layers (cuBLAS GEMMs + prefill kernels), sync",
+    }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -630,10 +710,14 @@ def main() -> None:
     parser.add_argument("--vocab", type=int, default=0, help="profiling only: vocabulary size")
     parser.add_argument("--tp", action="store_true",
                         help="under torchrun: the ranks form one tensor-parallel group decoding one cohort")
+    parser.add_argument("--prefill", action="store_true",
+                        help="measure the batched device prefill instead of the decode epochs")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.prefill:
+        run_prefill(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

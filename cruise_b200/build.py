@@ -58,12 +58,19 @@ def build_server() -> Path:
     return SERVER
 
 
+def link_flags() -> list[str]:
+    """cuBLAS (the prefill GEMMs) from the toolkit next to nvcc, found there at run time."""
+    lib = Path(nvcc()).resolve().parent.parent / "lib64"
+    return [f"-L{lib}", "-lcublas", "-Xlinker", f"-rpath={lib}"]
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         return LIBRARY
     if force or not _fresh(LIBRARY, SOURCES):
         tmp = LIBRARY.with_suffix(f".so.tmp{os.getpid()}")
-        cmd = [nvcc(), *NVCC_FLAGS, *(["-Xptxas", "-v"] if verbose else []), "-o", str(tmp), *map(str, SOURCES)]
+        cmd = [nvcc(), *NVCC_FLAGS, *(["-Xptxas", "-v"] if verbose else []), "-o", str(tmp), *map(str, SOURCES),
+               *link_flags()]
         subprocess.run(cmd, check=True)
         os.replace(tmp, LIBRARY)
     build_server()

@@ -2,6 +2,7 @@
 // (include/cruise_epoch.h): device memory, seeded weight synthesis, weight
 // loading, the one-launch epoch, and the reference-compatible bridge
 // resident_epoch_create / _execute / _destroy.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -21,6 +22,7 @@
 
 #include "../../include/cruise_epoch.h"
 #include "epoch_kernel.cuh"
+#include "prefill.cuh"
 
 namespace cruise {
 namespace {
@@ -159,6 +161,23 @@ struct Region {
   int64_t elems = 0;
 };
 
+// Untiled projection weights and activation buffers of the batched prefill,
+// built on the first cruise_epoch_prefill (the decode epoch never needs them).
+struct PrefillLayer {
+  const bf16 *qkv_w, *qkv_b, *o_w, *gu_w, *down_w;   // [Nqkv][H], [Nqkv], [H][Hq], [2I][H], [H][I]
+};
+struct PrefillState {
+  cublasHandle_t blas = nullptr;
+  void *weights = nullptr;
+  std::vector<PrefillLayer> layers;
+  void *work = nullptr;
+  int max_tokens = 0;
+  bf16 *h = nullptr, *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+  float *acc = nullptr;
+  int64_t *tok = nullptr;
+  int32_t *row = nullptr, *pos = nullptr;
+};
+
 struct Engine {
   CruiseModelConfig cfg{};
   ModelDims m{};
@@ -207,6 +226,8 @@ struct Engine {
   StreamRing *h_stream = nullptr;          // host-mapped egress ring (allocated on first enable)
   StreamRing *d_stream = nullptr;          // its device view
   bool stream_on = false;
+  PrefillState *prefill = nullptr;
+  bool payload_ready = false;   // d_payload holds a prefilled cohort for the next import epoch
   uint64_t tp_timeout_ns = 20000000000ull;   // device waits on other ranks (CRUISE_TP_TIMEOUT_MS)
 };
 
@@ -352,6 +373,12 @@ void destroy_engine(Engine *e) {
   cudaFree(e->xchg);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->h_stream) cudaFreeHost(e->h_stream);
+  if (e->prefill != nullptr) {
+    if (e->prefill->blas != nullptr) cublasDestroy(e->prefill->blas);
+    cudaFree(e->prefill->weights);
+    cudaFree(e->prefill->work);
+    delete e->prefill;
+  }
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -634,6 +661,167 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
   return set_err(e, err, name.c_str());
 }
 
+// ---- batched device prefill ---------------------------------------------------------------------
+int64_t import_payload_bytes(const Engine *e);
+
+// y[T][N] (fp32) = x[T][K] . W[N][K]^T, both bf16 row-major (cuBLAS is column-major: y^T = W x^T).
+cublasStatus_t prefill_gemm(cublasHandle_t blas, const bf16 *x, const bf16 *w, float *y, int T, int N, int K) {
+  const float one = 1.0f, zero = 0.0f;
+  return cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16BF, K, x, CUDA_R_16BF, K, &zero, y,
+                      CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+// Builds the untiled weights (once) and buffers for kBatch * block_size tokens.
+int32_t prefill_prepare(Engine *e) {
+  if (e->prefill != nullptr) return 0;
+  const ModelDims &m = e->m;
+  const int64_t H = m.H, kv = static_cast<int64_t>(m.nkv) * m.d, Hq = m.Hq, I = m.I, N = m.Nqkv;
+  auto *ps = new PrefillState();
+  e->prefill = ps;
+  if (cublasCreate(&ps->blas) != CUBLAS_STATUS_SUCCESS) {
+    ps->blas = nullptr;
+    e->last_error = "prefill: cublasCreate failed";
+    return -2;
+  }
+  cublasSetStream(ps->blas, e->stream);
+  const int64_t per_layer = N * H + N + H * Hq + 2 * I * H + H * I;
+  cudaError_t err = cudaMalloc(&ps->weights, static_cast<size_t>(per_layer) * m.L * 2);
+  if (err != cudaSuccess) return set_err(e, err, "prefill weights");
+  bf16 *w = static_cast<bf16 *>(ps->weights);
+  auto untile = [&](const std::string &name, bf16 *dst) -> bool {
+    TensorPlace tp;
+    if (!locate(e, name, tp)) return false;
+    if (!tp.tiled) {
+      return cudaMemcpyAsync(dst, tp.base + tp.offset, static_cast<size_t>(tp.rows * tp.cols) * 2,
+                             cudaMemcpyDeviceToDevice, e->stream) == cudaSuccess;
+    }
+    const int64_t count = tp.rows * tp.cols;
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148LL * 64));
+    tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
+                                                    reinterpret_cast<uint16_t *>(dst), tp.rows, tp.cols,
+                                                    tp.row_map, tp.offset, tp.K, pick_kc(static_cast<int>(tp.K)), 0);
+    return cudaGetLastError() == cudaSuccess;
+  };
+  for (int l = 0; l < m.L; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    bf16 *qkv_w = w, *qkv_b = qkv_w + N * H, *o_w = qkv_b + N, *gu_w = o_w + H * Hq, *down_w = gu_w + 2 * I * H;
+    w = down_w + H * I;
+    const bool ok = untile(p + "self_attn.q_proj.weight", qkv_w) && untile(p + "self_attn.k_proj.weight", qkv_w + Hq * H) &&
+                    untile(p + "self_attn.v_proj.weight", qkv_w + (Hq + kv) * H) &&
+                    untile(p + "self_attn.q_proj.bias", qkv_b) && untile(p + "self_attn.k_proj.bias", qkv_b + Hq) &&
+                    untile(p + "self_attn.v_proj.bias", qkv_b + Hq + kv) && untile(p + "self_attn.o_proj.weight", o_w) &&
+                    untile(p + "mlp.gate_proj.weight", gu_w) && untile(p + "mlp.up_proj.weight", gu_w + I * H) &&
+                    untile(p + "mlp.down_proj.weight", down_w);
+    if (!ok) return set_err(e, cudaErrorInvalidValue, "prefill weight layout");
+    ps->layers.push_back(PrefillLayer{qkv_w, qkv_b, o_w, gu_w, down_w});
+  }
+  // activations for every prompt token of a cohort: at most block_size per row
+  const int T = kBatch * m.bs;
+  ps->max_tokens = T;
+  const int64_t widest = std::max<int64_t>(std::max<int64_t>(N, 2 * I), H);
+  size_t bytes = 0;
+  auto take = [&](size_t n) { const size_t off = bytes; bytes = align_up(bytes + n, 256); return off; };
+  const size_t o_h = take(T * H * 2), o_x = take(T * H * 2), o_q = take(T * Hq * 2), o_attn = take(T * Hq * 2);
+  const size_t o_act = take(T * I * 2), o_acc = take(T * widest * 4), o_tok = take(T * 8), o_row = take(T * 4),
+               o_pos = take(T * 4);
+  err = cudaMalloc(&ps->work, bytes);
+  if (err != cudaSuccess) return set_err(e, err, "prefill buffers");
+  uint8_t *b = static_cast<uint8_t *>(ps->work);
+  ps->h = reinterpret_cast<bf16 *>(b + o_h);
+  ps->x = reinterpret_cast<bf16 *>(b + o_x);
+  ps->q = reinterpret_cast<bf16 *>(b + o_q);
+  ps->attn = reinterpret_cast<bf16 *>(b + o_attn);
+  ps->act = reinterpret_cast<bf16 *>(b + o_act);
+  ps->acc = reinterpret_cast<float *>(b + o_acc);
+  ps->tok = reinterpret_cast<int64_t *>(b + o_tok);
+  ps->row = reinterpret_cast<int32_t *>(b + o_row);
+  ps->pos = reinterpret_cast<int32_t *>(b + o_pos);
+  return set_err(e, cudaStreamSynchronize(e->stream), "prefill preparation");
+}
+
+// The K/V of prompt tokens 0..len-2 of every row (the decode epoch starts at
+// position len-1) into the import staging buffer, layer by layer for all tokens.
+int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32_t stride) {
+  const ModelDims &m = e->m;
+  if (e->tp_size > 1) {
+    e->last_error = "cruise_epoch_prefill: single-GPU engines only (no tensor parallelism)";
+    return -4;
+  }
+  if (m.bs > 128 || m.d > 128 || m.d % 32 != 0) {
+    e->last_error = "cruise_epoch_prefill: block size and head size must be at most 128";
+    return -1;
+  }
+  std::vector<int64_t> tok;
+  std::vector<int32_t> row, pos;
+  for (int r = 0; r < kBatch; ++r) {
+    if (lens[r] < 0 || lens[r] > m.bs || lens[r] > stride) {
+      e->last_error = "cruise_epoch_prefill: prompt lengths must lie in [0, block_size]";
+      return -1;
+    }
+    for (int t = 0; t + 1 < lens[r]; ++t) {
+      const int64_t id = tokens[static_cast<int64_t>(r) * stride + t];
+      if (id < 0 || id >= m.V) {
+        e->last_error = "cruise_epoch_prefill: token id outside the vocabulary";
+        return -1;
+      }
+      tok.push_back(id);
+      row.push_back(r);
+      pos.push_back(t);
+    }
+  }
+  int32_t rc = prefill_prepare(e);
+  if (rc != 0) return rc;
+  PrefillState *ps = e->prefill;
+  const size_t payload_bytes = static_cast<size_t>(import_payload_bytes(e));
+  cudaError_t err = cudaSuccess;
+  if (e->d_payload == nullptr) {
+    err = cudaMalloc(&e->d_payload, payload_bytes);
+    if (err != cudaSuccess) return set_err(e, err, "import staging");
+    e->payload_bytes = payload_bytes;
+  }
+  err = cudaMemsetAsync(e->d_payload, 0, payload_bytes, e->stream);
+  const int T = static_cast<int>(tok.size());
+  if (err == cudaSuccess && T > 0) {
+    err = cudaMemcpyAsync(ps->tok, tok.data(), T * 8, cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(ps->row, row.data(), T * 4, cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(ps->pos, pos.data(), T * 4, cudaMemcpyHostToDevice, e->stream);
+  }
+  if (err != cudaSuccess) return set_err(e, err, "prefill inputs");
+  bf16 *payload = reinterpret_cast<bf16 *>(e->d_payload);
+  const int H = m.H, I = m.I;
+  const unsigned ew = 148 * 8;   // grid of the elementwise kernels
+  bool blas_ok = true;
+  if (T > 0) {
+    prefill::embed_rows<<<T, 128, 0, e->stream>>>(e->embed, ps->tok, ps->h, H);
+    for (int l = 0; l < m.L && blas_ok; ++l) {
+      const LayerWeights &lw = e->layers[l];
+      const PrefillLayer &pl = ps->layers[l];
+      prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, lw.w_in, ps->x, H, m.eps);
+      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
+      prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, pl.qkv_b, e->rope_cos, e->rope_sin, ps->row, ps->pos,
+                                                        ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
+      prefill::causal_attention<<<dim3(T, m.nq), 128, 0, e->stream>>>(ps->q, payload, ps->row, ps->pos, ps->attn, l,
+                                                                      m.L, m.nq, m.nkv, m.d, m.bs, m.sqrt_d);
+      blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, ps->acc, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
+      prefill::add_residual<<<ew, 256, 0, e->stream>>>(ps->acc, ps->h, static_cast<int64_t>(T) * H);
+      prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, lw.w_post, ps->x, H, m.eps);
+      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.gu_w, ps->acc, T, 2 * I, H) == CUBLAS_STATUS_SUCCESS;
+      prefill::swiglu<<<ew, 256, 0, e->stream>>>(ps->acc, ps->act, T, I);
+      blas_ok &= prefill_gemm(ps->blas, ps->act, pl.down_w, ps->acc, T, H, I) == CUBLAS_STATUS_SUCCESS;
+      prefill::add_residual<<<ew, 256, 0, e->stream>>>(ps->acc, ps->h, static_cast<int64_t>(T) * H);
+    }
+  }
+  if (!blas_ok) {
+    e->last_error = "prefill: cuBLAS GEMM failed";
+    return -2;
+  }
+  err = cudaGetLastError();
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "prefill");
+  e->payload_ready = true;
+  return 0;
+}
+
 int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
   const ModelDims &m = e->m;
   const double sigma = 2.0 * std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
@@ -713,6 +901,17 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   }
   const bool importing = (control[2 + kBatch] & kImportFlag) != 0;
   cudaError_t err = cudaSuccess;
+  if (importing && payload == nullptr && payload_bytes == 0) {
+    // the cohort cruise_epoch_prefill left in the device staging buffer
+    if (!e->payload_ready) {
+      e->last_error = "import without a payload and no prefilled cohort on the device";
+      return -1;
+    }
+    payload = e->d_payload;
+    payload_bytes = static_cast<uint64_t>(import_payload_bytes(e));
+    payload_on_device = true;
+    e->payload_ready = false;
+  }
   if (importing) {
     if (payload == nullptr || payload_bytes != static_cast<uint64_t>(import_payload_bytes(e))) return -1;
     if (!payload_on_device) {
@@ -723,6 +922,7 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
       }
       err = cudaMemcpyAsync(e->d_payload, payload, payload_bytes, cudaMemcpyHostToDevice, e->stream);
       if (err != cudaSuccess) return set_err(e, err, "import payload copy");
+      e->payload_ready = false;   // a prefilled cohort in the staging buffer is overwritten
     }
   }
   const size_t in_bytes = offsetof(EpochIO, history);
@@ -1296,6 +1496,16 @@ int32_t cruise_epoch_set_trace(void *engine, int32_t enable) {
   if (engine == nullptr) return -1;
   static_cast<Engine *>(engine)->trace_on = enable != 0;
   return 0;
+}
+
+int32_t cruise_epoch_prefill(void *engine, const int64_t *prompt_tokens, const int32_t *prompt_lens,
+                             int32_t stride) {
+  if (engine == nullptr || prompt_lens == nullptr || (prompt_tokens == nullptr && stride != 0) || stride < 0)
+    return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  return cruise::prefill_run(e, prompt_tokens, prompt_lens, stride);
 }
 
 int32_t cruise_epoch_stream_enable(void *engine, int32_t enable) {

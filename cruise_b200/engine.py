@@ -217,6 +217,26 @@ class EpochEngine:
         self.lib.cruise_epoch_last_timing(self.handle, ctypes.byref(device_us), ctypes.byref(launches))
         return EpochOutput(history, control_out, logits, float(device_us.value))
 
+    # -- batched device prefill -------------------------------------------------------
+    def prefill(self, prompts) -> None:
+        """Runs up to four prompts (row r <- prompts[r]; an empty prompt leaves the
+        row alone) through the model on the GPU and keeps the K/V of all but
+        each prompt's last token as the device-side import payload: the next
+        :meth:`run` with the import flag and no ``import_payload`` imports it
+        and decodes from the last prompt token (see tests/scenario.py:
+        decode_inputs(importing=True))."""
+        prompts = [list(map(int, p)) for p in prompts] + [[]] * (BATCH - len(prompts))
+        if len(prompts) != BATCH:
+            raise ValueError(f"at most {BATCH} prompts")
+        stride = max(1, max(len(p) for p in prompts))
+        tokens = np.zeros((BATCH, stride), dtype=np.int64)
+        lens = np.zeros(BATCH, dtype=np.int32)
+        for r, prompt in enumerate(prompts):
+            tokens[r, : len(prompt)] = prompt
+            lens[r] = len(prompt)
+        self._check(self.lib.cruise_epoch_prefill(self.handle, tokens.ctypes.data, lens.ctypes.data, stride),
+                    "prefill")
+
     # -- streaming egress ------------------------------------------------------------
     def run_streaming(self, on_step: Callable[[int, np.ndarray], None], poll_s: float = 5e-5,
                       **run_kwargs) -> EpochOutput:

@@ -174,7 +174,8 @@ int32_t cruise_epoch_write_kv(void *engine, const void *key_host,
  * slot i32[4], active i32[4], block_table i32[4*blocks_per_row], tiling
  * u8[72] (may be NULL), control i32[11] = [K, eos x4, sampling, variant
  * (|0x100|mask to import), generation x4].  import_payload: when importing,
- * [K|V][layers][4 rows][block_size][kv_heads][head_dim] bf16 on the host.
+ * [K|V][layers][4 rows][block_size][kv_heads][head_dim] bf16 on the host, or
+ * NULL with import_bytes 0 to import what cruise_epoch_prefill computed.
  * forced_tokens: NULL for greedy decoding, or i64[8][4] step-major where an
  * entry >= 0 replaces the argmax of that row at that step (teacher forcing:
  * the device prefill of a prompt runs as forced epochs).
@@ -242,6 +243,23 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us,
 int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,
                                 int32_t count);
+
+/* Batched device prefill (the reference prefills on the host and imports the
+ * KV; here the prompts run through the model on the GPU in one pass per
+ * layer).  prompt_tokens is [4][stride] (row-major), prompt_lens[r] in
+ * [0, block_size] (0: row not prefilled).  Computes the K and V of tokens
+ * 0..len-2 of every row at positions 0..len-2 into the engine's import
+ * staging buffer -- [K|V][layers][4][block_size][kv_heads][head_dim], the
+ * import payload format -- and keeps it there: the next cruise_epoch_run with
+ * the import flag and import_payload NULL / import_bytes 0 imports it (one-shot
+ * device import with the Adler-32 proof) and decodes from position len-1 with
+ * token prompt[len-1].  The projections run as cuBLAS bf16 GEMMs on an
+ * untiled copy of the layer weights made on the first call (kept until
+ * destroy); attention, norms, rope and SwiGLU follow the decoder step's
+ * rounding points.  0, -1 bad arguments, -2 library failure, -4 tensor-
+ * parallel engine, or a CUDA error code. */
+int32_t cruise_epoch_prefill(void *engine, const int64_t *prompt_tokens,
+                             const int32_t *prompt_lens, int32_t stride);
 
 /* Streaming token egress (a reference evaluation item: stream without K=1).
  * With streaming enabled, every decode step of an epoch publishes that step's
