@@ -789,6 +789,20 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
   if (err != cudaSuccess) return set_err(e, err, "prefill inputs");
   bf16 *payload = reinterpret_cast<bf16 *>(e->d_payload);
   const int H = m.H, I = m.I;
+  // attention: one CTA per (16-position chunk, KV head, row) over the packed tokens
+  prefill::RowSpans spans{};
+  int longest = 0;
+  for (int r = 0, start = 0; r < kBatch; ++r) {
+    spans.start[r] = start;
+    spans.count[r] = std::max(lens[r] - 1, 0);
+    start += spans.count[r];
+    longest = std::max(longest, spans.count[r]);
+  }
+  const dim3 attn_grid((longest + prefill::kAttnChunk - 1) / prefill::kAttnChunk, m.nkv, kBatch);
+  const size_t attn_smem = prefill::attention_smem_bytes(m.bs, m.d, m.nq / m.nkv);
+  if (T > 0 && cudaFuncSetAttribute(prefill::causal_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(attn_smem)) != cudaSuccess)
+    return set_err(e, cudaGetLastError(), "prefill attention shared memory");
   const unsigned ew = 148 * 8;   // grid of the elementwise kernels
   bool blas_ok = true;
   if (T > 0) {
@@ -800,8 +814,8 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
       prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, pl.qkv_b, e->rope_cos, e->rope_sin, ps->row, ps->pos,
                                                         ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
-      prefill::causal_attention<<<dim3(T, m.nq), 128, 0, e->stream>>>(ps->q, payload, ps->row, ps->pos, ps->attn, l,
-                                                                      m.L, m.nq, m.nkv, m.d, m.bs, m.sqrt_d);
+      prefill::causal_attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(
+          ps->q, payload, spans, ps->attn, l, m.L, m.nq, m.nkv, m.d, m.bs, m.sqrt_d);
       blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, ps->acc, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
       prefill::add_residual<<<ew, 256, 0, e->stream>>>(ps->acc, ps->h, static_cast<int64_t>(T) * H);
       prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, lw.w_post, ps->x, H, m.eps);

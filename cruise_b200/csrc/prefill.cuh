@@ -108,42 +108,111 @@ __global__ void qkv_rope_store(const float *acc, const bf16 *bias, const bf16 *c
   }
 }
 
-// Causal attention of one (token, query head), reading the row's K and V from
-// the payload (positions 0..pos, the token's own included): scores
-// bf16(bf16(q.k) / sqrt(d)) (:356-367), softmax in fp32 rounded to bf16
-// (:368-377), output bf16(sum_j p_j v_j) (fp32 accumulation, positions in
-// ascending order).  grid (T, nq), 128 threads; positions <= block_size <= 128
-// per pass, dims d <= 128.
-__global__ void causal_attention(const bf16 *q, const bf16 *payload, const int32_t *tok_row,
-                                 const int32_t *tok_pos, bf16 *out, int layer, int L, int nq, int nkv, int d,
-                                 int bs, float sqrt_d) {
-  __shared__ float qs[128];
-  __shared__ float p[128];
-  __shared__ float scratch[32];
-  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int row = tok_row[t], n = tok_pos[t] + 1;
-  const int kvh = h / (nq / nkv), kvw = nkv * d;
+// Tokens of the cohort in the order the host packs them: row by row, each
+// row's positions 0..count-1 consecutive from `start`.
+struct RowSpans {
+  int32_t start[kBatch];
+  int32_t count[kBatch];
+};
+
+constexpr int kAttnChunk = 16;     // query positions per CTA
+constexpr int kAttnWarps = 8;
+constexpr int kKeyStride = 130;    // bf16 per staged K row: 65 words, so 32 lanes reading 32 keys hit 32 banks
+
+__host__ __device__ inline size_t attention_smem_bytes(int bs, int d, int groups) {
+  return static_cast<size_t>(bs) * kKeyStride * 2 + static_cast<size_t>(bs) * d * 2 +
+         static_cast<size_t>(kAttnChunk) * groups * d * 4 + static_cast<size_t>(kAttnWarps) * bs * 4;
+}
+
+// Causal attention of the query heads sharing one KV head, for a chunk of a
+// row's prompt positions: grid (chunks, kv heads, rows), kAttnWarps warps.
+// The row's K and V up to the chunk's last position are staged in shared
+// memory once and read by every (position, head) pair of the chunk; a warp
+// takes one pair at a time: scores bf16(bf16(q.k) / sqrt(d)) with a lane per
+// key (:356-367), softmax in fp32 rounded to bf16 (:368-377), then
+// bf16(sum_j p_j v_j) with a lane per d/32 dims, positions ascending.
+// Requires block_size <= 128 and d a multiple of 32, d <= 128.
+__global__ void causal_attention(const bf16 *q, const bf16 *payload, RowSpans spans, bf16 *out, int layer, int L,
+                                 int nq, int nkv, int d, int bs, float sqrt_d) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int chunk = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+  const int count = spans.count[row];
+  const int p0 = chunk * kAttnChunk;
+  if (p0 >= count) return;
+  const int p1 = min(count, p0 + kAttnChunk);   // positions [p0, p1)
+  const int groups = nq / nkv, kvw = nkv * d;
+  bf16 *ks = reinterpret_cast<bf16 *>(smem);
+  bf16 *vs = ks + static_cast<size_t>(bs) * kKeyStride;
+  float *qs = reinterpret_cast<float *>(vs + static_cast<size_t>(bs) * d);
+  float *ps = qs + static_cast<size_t>(kAttnChunk) * groups * d;
   const int64_t block_elems = static_cast<int64_t>(bs) * kvw;
-  const bf16 *keys = payload + (static_cast<int64_t>(layer) * kBatch + row) * block_elems + kvh * d;
-  const bf16 *vals = keys + static_cast<int64_t>(L) * kBatch * block_elems;
-  if (tid < d) qs[tid] = f(q[static_cast<int64_t>(t) * nq * d + h * d + tid]);
-  __syncthreads();
-  float s = -INFINITY;
-  if (tid < n) {
-    const bf16 *k = keys + static_cast<int64_t>(tid) * kvw;
-    float dot = 0.f;
-    for (int i = 0; i < d; ++i) dot = fmaf(qs[i], f(k[i]), dot);
-    s = r(__fdiv_rn(r(dot), sqrt_d));
+  const bf16 *kg = payload + (static_cast<int64_t>(layer) * kBatch + row) * block_elems + kvh * d;
+  const bf16 *vg = kg + static_cast<int64_t>(L) * kBatch * block_elems;
+  // stage K and V of positions 0..p1-1 (2-element words) and the chunk's queries
+  const int half_d = d / 2;
+  for (int i = threadIdx.x; i < p1 * half_d; i += blockDim.x) {
+    const int j = i / half_d, w = i % half_d;
+    reinterpret_cast<uint32_t *>(ks + static_cast<size_t>(j) * kKeyStride)[w] =
+        reinterpret_cast<const uint32_t *>(kg + static_cast<int64_t>(j) * kvw)[w];
+    reinterpret_cast<uint32_t *>(vs + static_cast<size_t>(j) * d)[w] =
+        reinterpret_cast<const uint32_t *>(vg + static_cast<int64_t>(j) * kvw)[w];
   }
-  const float mx = block_max(s, scratch);
-  const float e = tid < n ? expf(__fsub_rn(s, mx)) : 0.f;
-  const float sum = block_sum(e, scratch);
-  p[tid] = tid < n ? r(__fdiv_rn(e, sum)) : 0.f;
+  const int pairs = (p1 - p0) * groups;
+  for (int i = threadIdx.x; i < pairs * d; i += blockDim.x) {
+    const int pair = i / d, k = i % d;
+    const int t = spans.start[row] + p0 + pair / groups, h = kvh * groups + pair % groups;
+    qs[i] = f(q[static_cast<int64_t>(t) * nq * d + h * d + k]);
+  }
   __syncthreads();
-  if (tid < d) {
-    float o = 0.f;
-    for (int j = 0; j < n; ++j) o = fmaf(p[j], f(vals[static_cast<int64_t>(j) * kvw + tid]), o);
-    out[static_cast<int64_t>(t) * nq * d + h * d + tid] = b(o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float *pw = ps + static_cast<size_t>(warp) * bs;
+  const int dims = d / 32;
+  for (int pair = warp; pair < pairs; pair += kAttnWarps) {
+    const int pos = p0 + pair / groups, h = kvh * groups + pair % groups;
+    const int n = pos + 1;   // keys 0..pos
+    const float *qv = qs + static_cast<size_t>(pair) * d;
+    float sc[4], mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = lane + 32 * i;
+      sc[i] = -INFINITY;
+      if (j < n) {
+        const uint32_t *kr = reinterpret_cast<const uint32_t *>(ks + static_cast<size_t>(j) * kKeyStride);
+        float dot = 0.f;
+        for (int w = 0; w < half_d; ++w) {
+          const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162 *>(kr + w);
+          dot = fmaf(qv[2 * w], __low2float(k2), dot);
+          dot = fmaf(qv[2 * w + 1], __high2float(k2), dot);
+        }
+        sc[i] = r(__fdiv_rn(r(dot), sqrt_d));
+        mx = fmaxf(mx, sc[i]);
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float e[4], sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      e[i] = lane + 32 * i < n ? expf(__fsub_rn(sc[i], mx)) : 0.f;
+      sum += e[i];
+    }
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (lane + 32 * i < n) pw[lane + 32 * i] = r(__fdiv_rn(e[i], sum));
+    __syncwarp();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < n; ++j) {
+      const float pj = pw[j];
+      const bf16 *vr = vs + static_cast<size_t>(j) * d + lane * dims;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < dims) acc[c] = fmaf(pj, f(vr[c]), acc[c]);
+    }
+    bf16 *dst = out + static_cast<int64_t>(spans.start[row] + pos) * nq * d + h * d + lane * dims;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (c < dims) dst[c] = b(acc[c]);
+    __syncwarp();
   }
 }
 
