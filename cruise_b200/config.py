@@ -4,7 +4,8 @@ Environment names are the reference's operator surface:
 ``VLLM_ASCEND_RESIDENT_EPOCH_STEPS`` (K per epoch, one of 1/2/4/8) and
 ``VLLM_ASCEND_RESIDENT_EPOCH_CAPACITY`` (logical tokens per row).  The
 reference fixes capacity at 8 tokens; here it defaults to the paged layout's
-``blocks_per_row * block_size`` (256 for the 7B preset).
+``blocks_per_row * block_size`` of the served preset
+(``VLLM_ASCEND_RESIDENT_EPOCH_MODEL``; 256 for the 7B preset).
 """
 
 from __future__ import annotations
@@ -36,9 +37,17 @@ class ResidentEpochConfig:
 
     @classmethod
     def from_env(cls) -> "ResidentEpochConfig":
+        """The paged geometry of the served preset (VLLM_ASCEND_RESIDENT_EPOCH_MODEL,
+        default the 7B one) with the step and capacity overrides."""
+        from .model_config import PRESETS
+
+        preset = PRESETS[os.getenv("VLLM_ASCEND_RESIDENT_EPOCH_MODEL", "qwen2.5-7b")]
         config = cls(
             max_steps=_env_int("VLLM_ASCEND_RESIDENT_EPOCH_STEPS", 8),
-            logical_capacity=_env_int("VLLM_ASCEND_RESIDENT_EPOCH_CAPACITY", 256),
+            logical_capacity=_env_int("VLLM_ASCEND_RESIDENT_EPOCH_CAPACITY", preset.capacity),
+            physical_blocks=preset.num_blocks,
+            blocks_per_request=preset.blocks_per_row,
+            block_size=preset.block_size,
         )
         config.validate()
         return config

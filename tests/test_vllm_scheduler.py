@@ -1,0 +1,283 @@
+"""The resident epoch scheduler and dedicated worker inside vLLM 0.22's real V1
+scheduler (CPU; no model runs).  Scenarios follow the reference's
+tests/test_real_scheduler.py: fixed-graph plans for 1-4 greedy requests, the
+host-prefill -> import -> device-owned transition, continuous admission with
+an isolated host lane, rejection reasons, and the scheduler -> worker ->
+scheduler control path through a deterministic native engine."""
+
+from __future__ import annotations
+
+import json
+
+import pytest
+
+vllm = pytest.importorskip("vllm")
+
+from vllm import SamplingParams  # noqa: E402
+from vllm.sampling_params import RequestOutputKind  # noqa: E402
+from vllm.v1.outputs import ModelRunnerOutput  # noqa: E402
+from vllm.v1.request import Request, RequestStatus  # noqa: E402
+
+from cruise_b200.config import ResidentEpochConfig  # noqa: E402
+from cruise_b200.contract import CONTRACT_VERSION, ResidentEpochResult, attach_result, get_plan  # noqa: E402
+from cruise_b200.model_config import QWEN25_7B  # noqa: E402
+
+EOS = QWEN25_7B.configured_eos
+
+
+def hf_config_dir(tmp_path, preset=QWEN25_7B):
+    """A Hugging Face config directory with an engine preset's geometry."""
+    path = tmp_path / f"{preset.name}-config"
+    path.mkdir(exist_ok=True)
+    (path / "config.json").write_text(json.dumps({
+        "architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2", "hidden_size": preset.hidden,
+        "intermediate_size": preset.intermediate, "num_hidden_layers": preset.num_layers,
+        "num_attention_heads": preset.num_heads, "num_key_value_heads": preset.num_kv_heads,
+        "vocab_size": preset.vocab, "max_position_embeddings": 32768, "rms_norm_eps": 1e-6,
+        "rope_theta": 1000000.0, "torch_dtype": "bfloat16", "tie_word_embeddings": False,
+        "hidden_act": "silu", "eos_token_id": preset.configured_eos,
+    }))
+    return path
+
+
+def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_model_len=256, adopt=True):
+    """vLLM's own V1 scheduler for the preset, turned into the resident one."""
+    from vllm.config import CacheConfig, DeviceConfig, ModelConfig, SchedulerConfig, VllmConfig
+    from vllm.v1.core.sched.scheduler import Scheduler
+    from vllm.v1.kv_cache_interface import FullAttentionSpec, KVCacheConfig, KVCacheGroupSpec
+    from vllm.v1.structured_output import StructuredOutputManager
+    import torch
+
+    from cruise_b200.scheduler import ResidentEpochScheduler
+
+    model = ModelConfig(model=str(hf_config_dir(tmp_path, preset)), skip_tokenizer_init=True,
+                        max_model_len=max_model_len, dtype="bfloat16")
+    cache = CacheConfig(block_size=preset.block_size)
+    cache.num_gpu_blocks = 16
+    sched = SchedulerConfig(max_num_seqs=batch_size, max_num_batched_tokens=512, max_model_len=max_model_len,
+                            is_encoder_decoder=False, async_scheduling=False)
+    vc = VllmConfig(model_config=model, cache_config=cache, scheduler_config=sched,
+                    device_config=DeviceConfig(device="cuda"))
+    spec = FullAttentionSpec(block_size=preset.block_size, num_kv_heads=preset.num_kv_heads,
+                             head_size=preset.head_dim, dtype=torch.bfloat16)
+    kv = KVCacheConfig(num_blocks=16, kv_cache_tensors=[],
+                       kv_cache_groups=[KVCacheGroupSpec([f"model.layers.{i}.self_attn" for i in
+                                                          range(preset.num_layers)], spec)])
+    cls = Scheduler if adopt else ResidentEpochScheduler
+    scheduler = cls(vllm_config=vc, kv_cache_config=kv, log_stats=False,
+                    structured_output_manager=StructuredOutputManager(vc), block_size=preset.block_size)
+    if adopt:
+        ResidentEpochScheduler.adopt(scheduler, config or ResidentEpochConfig(
+            logical_capacity=min(256, 2 * preset.block_size), block_size=preset.block_size))
+    return scheduler
+
+
+def request(req_id, prompt, max_tokens, temperature=0.0):
+    params = SamplingParams(temperature=temperature, max_tokens=max_tokens)
+    params.update_from_generation_config({}, EOS)
+    return Request(request_id=req_id, client_index=0, prompt_token_ids=list(prompt), sampling_params=params,
+                   pooling_params=None)
+
+
+def host_step(scheduler, output, tokens):
+    ids = list(tokens)
+    scheduler.update_from_output(output, ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
+                                                           sampled_token_ids=[tokens[r] for r in ids]))
+
+
+def commit_device_epoch(scheduler, output, tokens):
+    plan = get_plan(output)
+    assert plan is not None
+    ids = list(plan.req_ids)
+    runner = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
+                               sampled_token_ids=[tokens[r] for r in ids])
+    importing = any(r.kv_import_required for r in plan.requests)
+    attach_result(runner, ResidentEpochResult(
+        version=CONTRACT_VERSION, route="device", status=0, model_calls=plan.max_steps,
+        computed_steps={r: len(tokens[r]) for r in ids}, row_generations=plan.row_generations,
+        kv_imported=importing, kv_import_checksum=1 if importing else 0, kv_snapshot_checksum=1 if importing else 0))
+    scheduler.update_from_output(output, runner)
+    return plan
+
+
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
+def test_fixed_graph_plan_and_commit(tmp_path, batch):
+    scheduler = make_scheduler(tmp_path, batch)
+    reqs = [request(str(i), [5 + i], max_tokens=8) for i in range(batch)]
+    for r in reqs:
+        scheduler.add_request(r)
+    output = scheduler.schedule()
+    plan = get_plan(output)
+    assert plan is not None and plan.graph_batch_size == 4 and plan.max_steps == 8
+    assert plan.active_mask == (1,) * batch + (0,) * (4 - batch)
+    assert all(v == 1 for v in output.num_scheduled_tokens.values())
+    assert all(len(r.scheduler_block_ids) == 1 for r in plan.requests)
+    assert [r.generation for r in plan.requests] == list(range(1, batch + 1))
+    commit_device_epoch(scheduler, output, {r: [100 + s for s in range(8)] for r in plan.req_ids})
+    for r in reqs:
+        assert (r.num_computed_tokens, r.num_tokens, r.num_output_tokens) == (8, 9, 8)
+        assert r.status == RequestStatus.FINISHED_LENGTH_CAPPED
+
+
+def test_unsupported_sampling_stays_on_the_host_path(tmp_path):
+    scheduler = make_scheduler(tmp_path, 1)
+    scheduler.add_request(request("0", [5], max_tokens=8, temperature=0.8))
+    output = scheduler.schedule()
+    assert get_plan(output) is None and scheduler.last_rejection == "non-greedy-temperature"
+    assert scheduler.num_lookahead_tokens == 0
+
+
+def test_delta_output_kind_allows_a_multi_token_epoch(tmp_path):
+    scheduler = make_scheduler(tmp_path, 2, ResidentEpochConfig(max_steps=4))
+    reqs = [request(str(i), [5 + i], max_tokens=6) for i in range(2)]
+    reqs[1].sampling_params.output_kind = RequestOutputKind.DELTA
+    for r in reqs:
+        scheduler.add_request(r)
+    plan = get_plan(scheduler.schedule())
+    assert plan is not None and plan.max_steps == 4
+
+
+def test_host_prefill_transitions_to_device_owned_decode(tmp_path):
+    scheduler = make_scheduler(tmp_path, 1)
+    r = request("0", [5, 6, 7], max_tokens=4)
+    scheduler.add_request(r)
+    prefill = scheduler.schedule()
+    assert get_plan(prefill) is None and scheduler.last_rejection == "not-single-token-decode"
+    host_step(scheduler, prefill, {"0": [101]})
+    assert (r.num_computed_tokens, r.num_output_tokens) == (3, 1)
+    first = scheduler.schedule()
+    plan = get_plan(first)
+    assert plan is not None and plan.max_steps == 2            # 3 tokens left -> K = 2
+    q = plan.requests[0]
+    assert (q.position, q.sequence_length, q.token_id, q.state_owner, q.kv_import_required) == (3, 4, 101, "host", True)
+    commit_device_epoch(scheduler, first, {"0": [102, 103]})
+    assert "0" in scheduler.resident.device_owned
+    nxt = get_plan(scheduler.schedule())
+    assert nxt.requests[0].state_owner == "device" and not nxt.requests[0].kv_import_required
+
+
+def test_continuous_admission_isolates_host_prefill_and_reuses_rows(tmp_path):
+    scheduler = make_scheduler(tmp_path, 2, ResidentEpochConfig(max_steps=2))
+    a = request("A", [9707, 11], max_tokens=7)
+    scheduler.add_request(a)
+    prefill_a = scheduler.schedule()
+    assert get_plan(prefill_a) is None
+    host_step(scheduler, prefill_a, {"A": [101]})
+    plan_a = commit_device_epoch(scheduler, scheduler.schedule(), {"A": [102, 103]})
+    assert plan_a.max_steps == 2
+
+    b = request("B", [9707, 11, 358], max_tokens=2)
+    scheduler.add_request(b)
+    prefill_b = scheduler.schedule()
+    assert get_plan(prefill_b) is None and prefill_b.num_scheduled_tokens == {"B": 3}
+    assert scheduler.last_rejection == "host-prefill-admission"
+    assert [x.request_id for x in scheduler.running] == ["A", "B"]   # A paused, not dropped
+    host_step(scheduler, prefill_b, {"B": [201]})
+    import_b = scheduler.schedule()
+    plan_b = get_plan(import_b)
+    assert plan_b.max_steps == 1
+    assert [(q.req_id, q.row, q.generation) for q in plan_b.requests] == [("A", 0, 1), ("B", 1, 2)]
+    assert [(q.state_owner, q.kv_import_required) for q in plan_b.requests] == [("device", False), ("host", True)]
+    commit_device_epoch(scheduler, import_b, {"A": [104], "B": [202]})
+    assert b.status == RequestStatus.FINISHED_LENGTH_CAPPED
+
+    c = request("C", [9707, 11, 358, 374], max_tokens=2)
+    scheduler.add_request(c)
+    prefill_c = scheduler.schedule()
+    assert prefill_c.num_scheduled_tokens == {"C": 4} and scheduler.last_rejection == "host-prefill-admission"
+    host_step(scheduler, prefill_c, {"C": [301]})
+    plan_c = get_plan(import_c := scheduler.schedule())
+    # C takes B's released row under a new generation
+    assert [(q.req_id, q.row, q.generation) for q in plan_c.requests] == [("A", 0, 1), ("C", 1, 3)]
+    commit_device_epoch(scheduler, import_c, {"A": [105], "C": [302]})
+    finish = get_plan(finish_a := scheduler.schedule())
+    assert finish.req_ids == ("A",) and finish.max_steps == 2
+    commit_device_epoch(scheduler, finish_a, {"A": [106, 107]})
+    assert a.status == RequestStatus.FINISHED_LENGTH_CAPPED
+
+
+def test_unsupported_admission_runs_in_the_host_lane(tmp_path):
+    scheduler = make_scheduler(tmp_path, 2, ResidentEpochConfig(max_steps=2))
+    a = request("A", [9707, 11], max_tokens=7)
+    scheduler.add_request(a)
+    prefill_a = scheduler.schedule()
+    host_step(scheduler, prefill_a, {"A": [101]})
+    commit_device_epoch(scheduler, scheduler.schedule(), {"A": [102, 103]})
+    u = request("u", [9707, 11], max_tokens=2, temperature=0.8)
+    scheduler.add_request(u)
+    out = scheduler.schedule()
+    assert get_plan(out) is None and out.num_scheduled_tokens == {"u": 2}
+    assert scheduler.last_rejection == "host-prefill-admission"
+    host_step(scheduler, out, {"u": [201]})
+    out = scheduler.schedule()
+    assert get_plan(out) is None and out.num_scheduled_tokens == {"u": 1}
+    assert scheduler.last_rejection == "unsupported-host-isolation"
+    host_step(scheduler, out, {"u": [202]})
+    assert u.status == RequestStatus.FINISHED_LENGTH_CAPPED
+    resume = get_plan(scheduler.schedule())
+    assert resume.req_ids == ("A",) and resume.requests[0].state_owner == "device"
+    assert resume.requests[0].generation == 1
+
+
+def test_two_prefills_beside_a_device_owned_request(tmp_path):
+    scheduler = make_scheduler(tmp_path, 3, ResidentEpochConfig(max_steps=2))
+    scheduler.add_request(request("A", [9707, 11], max_tokens=7))
+    prefill_a = scheduler.schedule()
+    host_step(scheduler, prefill_a, {"A": [101]})
+    commit_device_epoch(scheduler, scheduler.schedule(), {"A": [102, 103]})
+    scheduler.add_request(request("B", [9707, 11, 358], max_tokens=3))
+    scheduler.add_request(request("C", [9707, 11, 358, 374], max_tokens=3))
+    out = scheduler.schedule()
+    assert get_plan(out) is None and out.num_scheduled_tokens == {"B": 3, "C": 4}
+    host_step(scheduler, out, {"B": [201], "C": [301]})
+    plan = get_plan(scheduler.schedule())
+    assert plan.req_ids == ("A", "B", "C")
+    assert [q.state_owner for q in plan.requests] == ["device", "host", "host"]
+    assert [q.kv_import_required for q in plan.requests] == [False, True, True]
+
+
+def test_scheduler_to_dedicated_worker_control_path(tmp_path, monkeypatch):
+    from cruise_b200.worker import ResidentEpochWorker
+
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_BACKEND_FACTORY", "cruise_b200.testing:create_test_engine")
+    scheduler = make_scheduler(tmp_path, 4)
+    reqs = [request(str(i), [5 + i], max_tokens=4) for i in range(4)]
+    for r in reqs:
+        scheduler.add_request(r)
+    output = scheduler.schedule()
+    assert get_plan(output) is not None
+    worker = ResidentEpochWorker(vllm_config=scheduler.vllm_config, local_rank=0, rank=0,
+                                 distributed_init_method="tcp://127.0.0.1:1", is_driver_worker=True)
+    worker.load_model()
+    times = worker.compile_or_warm_up_model()
+    assert times.language_model > 0 and worker.warmup_output.model_calls == 1
+    assert len(worker.get_kv_cache_spec()) == QWEN25_7B.num_layers
+    page = 2 * QWEN25_7B.block_size * QWEN25_7B.num_kv_heads * QWEN25_7B.head_dim * 2
+    assert worker.determine_available_memory() == 8 * QWEN25_7B.num_layers * page
+    scheduler.update_from_output(output, worker.execute_model(output))
+    worker.shutdown()
+    for r in reqs:
+        assert (r.num_computed_tokens, r.num_output_tokens) == (4, 4)
+        assert r.status == RequestStatus.FINISHED_LENGTH_CAPPED
+
+
+def test_models_without_an_engine_preset_are_refused(tmp_path):
+    from dataclasses import replace
+
+    from cruise_b200.scheduler import native_model_rejection
+    from types import SimpleNamespace
+
+    good = SimpleNamespace(model_type="qwen2", num_hidden_layers=28, hidden_size=3584, num_attention_heads=28,
+                           num_key_value_heads=4, intermediate_size=18944, vocab_size=152064)
+    assert native_model_rejection(good) is None
+    assert "vocab_size=151936" in native_model_rejection(replace_ns(good, vocab_size=151936))
+    assert native_model_rejection(replace_ns(good, model_type="llama")).startswith("model_type")
+    with pytest.raises(ValueError, match="native graph mismatch"):
+        make_scheduler(tmp_path, 1, preset=replace(QWEN25_7B, vocab=151936, name="other"), adopt=False)
+    make_scheduler(tmp_path, 1, adopt=False)   # the 7B preset itself is accepted
+
+
+def replace_ns(ns, **changes):
+    from types import SimpleNamespace
+
+    return SimpleNamespace(**{**vars(ns), **changes})
