@@ -48,10 +48,11 @@ def test_vllm_scheduler_runs_cohorts_on_the_engine(cuda_ok, tmp_path, monkeypatc
     oracle = OracleEpochController(OracleDecoder(ORACLE_TINY, seeded_weights(ORACLE_TINY, 0)))
 
     # three requests now, a fourth joins after the first epoch; budgets differ
-    reqs = [request(f"q{i}", [11 + 97 * i], max_tokens=m) for i, m in enumerate((13, 6, 9))]
+    eos = TINY.configured_eos
+    reqs = [request(f"q{i}", [11 + 97 * i], max_tokens=m, eos=eos) for i, m in enumerate((13, 6, 9))]
     for r in reqs:
         scheduler.add_request(r)
-    late = request("q3", [777], max_tokens=5)
+    late = request("q3", [777], max_tokens=5, eos=eos)
     epochs = 0
     while scheduler.has_unfinished_requests() or late is not None:
         output = scheduler.schedule()

@@ -72,9 +72,9 @@ def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_mode
     return scheduler
 
 
-def request(req_id, prompt, max_tokens, temperature=0.0):
+def request(req_id, prompt, max_tokens, temperature=0.0, eos=EOS):
     params = SamplingParams(temperature=temperature, max_tokens=max_tokens)
-    params.update_from_generation_config({}, EOS)
+    params.update_from_generation_config({}, eos)
     return Request(request_id=req_id, client_index=0, prompt_token_ids=list(prompt), sampling_params=params,
                    pooling_params=None)
 
