@@ -224,11 +224,11 @@ def gather_kv_shards(engine, key, value):
     return full_k, full_v
 
 
-def setup_cohort(engine, cfg, seed: int, k: int):
+def setup_cohort(engine, cfg, seed: int, k: int, prompt_max: int = 5):
     """Device prefill of a seeded B=4 cohort, then the one-shot import epoch."""
     from scenario import decode_inputs, import_payload, make_scenario, prefill_epochs
 
-    sc = make_scenario(vocab=cfg.vocab, seed=seed, active_rows=(1, 1, 1, 1), prompt_len=(2, 5),
+    sc = make_scenario(vocab=cfg.vocab, seed=seed, active_rows=(1, 1, 1, 1), prompt_len=(2, prompt_max),
                        budget=(2, 8), k=k, eos=cfg.configured_eos, token_high=min(151643, cfg.vocab - 1))
     for inputs in prefill_epochs(sc, cfg.block_size, cfg.vocab):
         out = engine.run(**inputs)
@@ -333,7 +333,7 @@ def run_gpu(args) -> None:
     t0 = time.perf_counter()
     engine.init_synthetic(seed=0)
     synth_s = time.perf_counter() - t0
-    sc, first = setup_cohort(engine, cfg, seed=1000 + (0 if tp else rank), k=args.k)
+    sc, first = setup_cohort(engine, cfg, seed=1000 + (0 if tp else rank), k=args.k, prompt_max=args.prompt_max)
     cohort = Cohort(engine, cfg, sc, first)
     need = (args.warmup + args.steps + (1 if args.trace else 0)) * args.k
     if cohort.room() < need:
@@ -396,7 +396,8 @@ def run_gpu(args) -> None:
             "data": "synthetic (seeded random-init weights generated on the device; seeded prompts)",
             "config": {
                 "workload": "configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
-                            "one-shot H2D KV import of the device-prefilled prompts (2-5 tokens)" % args.k,
+                            "one-shot H2D KV import of the device-prefilled prompts (2-%d tokens)"
+                            % (args.k, args.prompt_max),
                 "model": "Qwen2.5-7B architecture (28 layers, hidden 3584, 28/4 heads x 128, I 18944, V 152064)",
                 "global_batch": 4 if tp else 4 * world,
                 "epoch_k": args.k,
@@ -710,6 +711,8 @@ def main() -> None:
     parser.add_argument("--vocab", type=int, default=0, help="profiling only: vocabulary size")
     parser.add_argument("--tp", action="store_true",
                         help="under torchrun: the ranks form one tensor-parallel group decoding one cohort")
+    parser.add_argument("--prompt-max", type=int, default=5,
+                        help="longest prompt of the seeded cohort (2..block_size; configs[4] uses 120)")
     parser.add_argument("--prefill", action="store_true",
                         help="measure the batched device prefill instead of the decode epochs")
     args = parser.parse_args()
