@@ -2,12 +2,26 @@
 (src/vllm_ascend_resident_epoch/eligibility.py:4-47).
 
 Returns the first reason a vLLM request falls outside the device epoch's
-support envelope (greedy sampling with EOS only), or None.
+support envelope (greedy sampling with EOS only), or None.  One extension
+over the reference: a request served without a tokenizer has no EOS id in
+vLLM and carries the model's generation-config EOS as its single stop token
+id; that token then acts as the request's EOS (``effective_eos``).
 """
 
 from __future__ import annotations
 
 from typing import Any
+
+
+def effective_eos(params: Any) -> int | None:
+    """The one token that ends a greedy request on the device: its EOS id; or,
+    for a request served without a tokenizer (vLLM then has no EOS id and
+    carries the model's generation-config EOS as the single stop token id),
+    that stop token.  None when anything else could also stop it."""
+    stop_ids = set(params.stop_token_ids or ())
+    if params.eos_token_id is not None:
+        return int(params.eos_token_id) if not stop_ids else None
+    return int(next(iter(stop_ids))) if len(stop_ids) == 1 else None
 
 
 def request_rejection_reason(request: Any) -> str | None:
@@ -35,8 +49,8 @@ def request_rejection_reason(request: Any) -> str | None:
         ),
         (params.min_tokens != 0, "min-tokens"),
         (bool(params.ignore_eos), "ignore-eos"),
-        (params.eos_token_id is None, "missing-eos"),
-        (bool(params.stop) or bool(params.stop_token_ids), "extra-stop-condition"),
+        (params.eos_token_id is None and not params.stop_token_ids, "missing-eos"),
+        (bool(params.stop) or effective_eos(params) is None, "extra-stop-condition"),
         (params.logprobs is not None or params.prompt_logprobs is not None, "logprobs"),
         (bool(params.logit_bias) or bool(params.allowed_token_ids), "logit-processor"),
         (bool(params.bad_words), "bad-words"),

@@ -31,7 +31,7 @@ from vllm.v1.outputs import ModelRunnerOutput
 
 from .config import ResidentEpochConfig, epoch_steps
 from .contract import CONTRACT_VERSION, ResidentEpochPlan, ResidentEpochRequest, attach_plan, get_plan, get_result
-from .eligibility import request_rejection_reason
+from .eligibility import effective_eos, request_rejection_reason
 from .model_config import PRESETS
 
 
@@ -167,6 +167,8 @@ class ResidentEpochScheduler(Scheduler):
         self.last_rejection, self.last_plan, self.last_result = rejection, plan, None
         if plan is not None:
             attach_plan(output, plan)
+        else:
+            output.resident_epoch_rejection = rejection   # why this step stays on the host
         return output
 
     def _make_plan(self, output: Any) -> tuple[ResidentEpochPlan | None, str | None]:
@@ -225,7 +227,7 @@ class ResidentEpochScheduler(Scheduler):
             planned.append(ResidentEpochRequest(
                 req_id=request.request_id, row=row, generation=self.resident.generations[request.request_id],
                 token_id=int(request.all_token_ids[position]), position=position, sequence_length=position + 1,
-                eos_token_id=int(params.eos_token_id), scheduler_block_ids=blocks,
+                eos_token_id=effective_eos(params), scheduler_block_ids=blocks,
                 device_block_ids=(row * cfg.blocks_per_request, row * cfg.blocks_per_request + 1),
                 state_owner="device" if owned else "host",
                 kv_import_required=request.num_prompt_tokens > 1 and not owned,

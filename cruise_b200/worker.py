@@ -100,10 +100,33 @@ class ResidentEpochWorker(WorkerBase):
         if plan is None:
             if scheduler_output.total_num_scheduled_tokens == 0:
                 return ModelRunnerOutput(req_ids=[], req_id_to_index={}, sampled_token_ids=[])
-            raise RuntimeError("dedicated resident epoch worker received a request outside the native envelope")
+            reason = getattr(scheduler_output, "resident_epoch_rejection", None)
+            raise RuntimeError("dedicated resident epoch worker received a request outside the native envelope"
+                               f" (scheduler: {reason})")
         if self.backend is None:
             raise RuntimeError("resident epoch backend is not loaded")
         return self.backend.execute(plan)
+
+    def get_supported_tasks(self) -> tuple[str, ...]:
+        return ("generate",)
+
+    def get_kv_connector_handshake_metadata(self) -> dict | None:
+        return None   # the engine's KV cache is not shared through a vLLM connector
+
+    def reset_mm_cache(self) -> None:
+        return None
+
+    def reset_encoder_cache(self) -> None:
+        return None
+
+    def execute_dummy_batch(self) -> None:
+        return None   # nothing to keep in step with: the engine has no collective with other workers
+
+    def take_draft_token_ids(self):
+        return None
+
+    def profile(self, is_start: bool = True, profile_prefix: str | None = None) -> None:
+        return None   # the engine's own trace: cruise_epoch_set_trace / bench.py --trace
 
     def sample_tokens(self, grammar_output: Any):
         raise RuntimeError("the resident epoch worker returns sampled tokens with execute_model")

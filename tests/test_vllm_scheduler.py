@@ -37,6 +37,8 @@ def hf_config_dir(tmp_path, preset=QWEN25_7B):
         "rope_theta": 1000000.0, "torch_dtype": "bfloat16", "tie_word_embeddings": False,
         "hidden_act": "silu", "eos_token_id": preset.configured_eos,
     }))
+    # the EOS vLLM gives requests when it has no tokenizer comes from here
+    (path / "generation_config.json").write_text(json.dumps({"eos_token_id": preset.configured_eos}))
     return path
 
 
@@ -281,3 +283,43 @@ def replace_ns(ns, **changes):
     from types import SimpleNamespace
 
     return SimpleNamespace(**{**vars(ns), **changes})
+
+
+def test_worker_names_the_rejection_of_a_host_step(tmp_path, monkeypatch):
+    from cruise_b200.worker import ResidentEpochWorker
+
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_BACKEND_FACTORY", "cruise_b200.testing:create_test_engine")
+    scheduler = make_scheduler(tmp_path, 1)
+    scheduler.add_request(request("0", [5], max_tokens=8, temperature=0.8))
+    output = scheduler.schedule()
+    worker = ResidentEpochWorker(vllm_config=scheduler.vllm_config, local_rank=0, rank=0,
+                                 distributed_init_method="tcp://127.0.0.1:1", is_driver_worker=True)
+    worker.load_model()
+    with pytest.raises(RuntimeError, match="scheduler: non-greedy-temperature"):
+        worker.execute_model(output)
+    assert worker.get_supported_tasks() == ("generate",)
+    worker.shutdown()
+
+
+def test_eos_from_a_single_stop_token_without_tokenizer(tmp_path):
+    from cruise_b200.eligibility import effective_eos, request_rejection_reason
+
+    scheduler = make_scheduler(tmp_path, 2)
+    plain = request("p", [5], max_tokens=4)
+    tokenizerless = Request(request_id="t", client_index=0, prompt_token_ids=[6], pooling_params=None,
+                            sampling_params=SamplingParams(temperature=0.0, max_tokens=4))
+    tokenizerless.sampling_params.update_from_generation_config({"eos_token_id": 77}, None)
+    assert tokenizerless.sampling_params.eos_token_id is None and effective_eos(tokenizerless.sampling_params) == 77
+    for r in (plain, tokenizerless):
+        scheduler.add_request(r)
+    plan = get_plan(scheduler.schedule())
+    assert plan is not None and [q.eos_token_id for q in plan.requests] == [EOS, 77]
+    both = request("b", [7], max_tokens=4)
+    both.sampling_params.stop_token_ids = [9]
+    assert request_rejection_reason(both) == "extra-stop-condition"
+    two = Request(request_id="2", client_index=0, prompt_token_ids=[6], pooling_params=None,
+                  sampling_params=SamplingParams(temperature=0.0, max_tokens=4, stop_token_ids=[3, 4]))
+    assert request_rejection_reason(two) == "extra-stop-condition"
+    none = Request(request_id="n", client_index=0, prompt_token_ids=[6], pooling_params=None,
+                   sampling_params=SamplingParams(temperature=0.0, max_tokens=4))
+    assert request_rejection_reason(none) == "missing-eos"
