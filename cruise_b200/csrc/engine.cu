@@ -747,8 +747,8 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     e->last_error = "cruise_epoch_prefill: single-GPU engines only (no tensor parallelism)";
     return -4;
   }
-  if (m.bs > 128 || m.d > 128 || m.d % 32 != 0) {
-    e->last_error = "cruise_epoch_prefill: block size and head size must be at most 128";
+  if (m.bs > prefill::kMaxKeys || (m.d != 64 && m.d != 128) || m.nq / m.nkv * prefill::kAttnChunk > prefill::kMaxKeys) {
+    e->last_error = "cruise_epoch_prefill: needs block size <= 128, head size 64 or 128, <= 8 query heads per KV head";
     return -1;
   }
   std::vector<int64_t> tok;
@@ -800,7 +800,8 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
   }
   const dim3 attn_grid((longest + prefill::kAttnChunk - 1) / prefill::kAttnChunk, m.nkv, kBatch);
   const size_t attn_smem = prefill::attention_smem_bytes(m.bs, m.d, m.nq / m.nkv);
-  if (T > 0 && cudaFuncSetAttribute(prefill::causal_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  auto *attention = m.d == 128 ? prefill::causal_attention_mma<128> : prefill::causal_attention_mma<64>;
+  if (T > 0 && cudaFuncSetAttribute(attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(attn_smem)) != cudaSuccess)
     return set_err(e, cudaGetLastError(), "prefill attention shared memory");
   const unsigned ew = 148 * 8;   // grid of the elementwise kernels
@@ -814,8 +815,8 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
       prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, pl.qkv_b, e->rope_cos, e->rope_sin, ps->row, ps->pos,
                                                         ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
-      prefill::causal_attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(
-          ps->q, payload, spans, ps->attn, l, m.L, m.nq, m.nkv, m.d, m.bs, m.sqrt_d);
+      attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(ps->q, payload, spans, ps->attn, l,
+                                                                                m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
       blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, ps->acc, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
       prefill::add_residual<<<ew, 256, 0, e->stream>>>(ps->acc, ps->h, static_cast<int64_t>(T) * H);
       prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, lw.w_post, ps->x, H, m.eps);

@@ -117,102 +117,194 @@ struct RowSpans {
 
 constexpr int kAttnChunk = 16;     // query positions per CTA
 constexpr int kAttnWarps = 8;
-constexpr int kKeyStride = 130;    // bf16 per staged K row: 65 words, so 32 lanes reading 32 keys hit 32 banks
+constexpr int kMaxKeys = 128;      // block_size bound: keys (and query rows) per CTA
+
+__host__ __device__ inline int attention_row_stride(int d) { return d + 8; }   // bf16; 16-byte pad per row
 
 __host__ __device__ inline size_t attention_smem_bytes(int bs, int d, int groups) {
-  return static_cast<size_t>(bs) * kKeyStride * 2 + static_cast<size_t>(bs) * d * 2 +
-         static_cast<size_t>(kAttnChunk) * groups * d * 4 + static_cast<size_t>(kAttnWarps) * bs * 4;
+  (void)bs;
+  (void)groups;
+  return static_cast<size_t>(3) * kMaxKeys * attention_row_stride(d) * 2;   // Q rows, K rows, V rows
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t (&r)[2], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_u32(p)));
+}
+
+// c += a (16x16 bf16, row) * b (16x8 bf16, col), fp32 accumulators
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
 }
 
 // Causal attention of the query heads sharing one KV head, for a chunk of a
-// row's prompt positions: grid (chunks, kv heads, rows), kAttnWarps warps.
-// The row's K and V up to the chunk's last position are staged in shared
-// memory once and read by every (position, head) pair of the chunk; a warp
-// takes one pair at a time: scores bf16(bf16(q.k) / sqrt(d)) with a lane per
-// key (:356-367), softmax in fp32 rounded to bf16 (:368-377), then
-// bf16(sum_j p_j v_j) with a lane per d/32 dims, positions ascending.
-// Requires block_size <= 128 and d a multiple of 32, d <= 128.
-__global__ void causal_attention(const bf16 *q, const bf16 *payload, RowSpans spans, bf16 *out, int layer, int L,
-                                 int nq, int nkv, int d, int bs, float sqrt_d) {
+// row's prompt positions, on the tensor cores: grid (chunks, kv heads, rows),
+// kAttnWarps warps.  The chunk's query rows (position-major, head-minor), the
+// row's K and V up to the chunk's last position are staged in shared memory;
+// warp w takes query rows [16w, 16w + 16) through
+//   S = Q K^T (m16n8k16 bf16 MMAs, fp32 sums) -> scores bf16(bf16(S) / sqrt(d))
+//   with the causal mask (:356-367) -> softmax in fp32 rounded to bf16
+//   (:368-377) -> O = P V (the probabilities feed the second MMA straight from
+//   the accumulator layout) -> bf16(O).
+// Requires block_size <= 128 and d in {64, 128}.
+template <int D>
+__global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
+    const bf16 *q, const bf16 *payload, RowSpans spans, bf16 *out, int layer, int L, int nq, int nkv, int bs,
+    float sqrt_d) {
   extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int S = D + 8;   // shared-memory row stride (bf16)
   const int chunk = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int count = spans.count[row];
   const int p0 = chunk * kAttnChunk;
   if (p0 >= count) return;
-  const int p1 = min(count, p0 + kAttnChunk);   // positions [p0, p1)
-  const int groups = nq / nkv, kvw = nkv * d;
-  bf16 *ks = reinterpret_cast<bf16 *>(smem);
-  bf16 *vs = ks + static_cast<size_t>(bs) * kKeyStride;
-  float *qs = reinterpret_cast<float *>(vs + static_cast<size_t>(bs) * d);
-  float *ps = qs + static_cast<size_t>(kAttnChunk) * groups * d;
+  const int p1 = min(count, p0 + kAttnChunk);   // positions [p0, p1) query keys [0, p1)
+  const int groups = nq / nkv, kvw = nkv * D;
+  const int rows = (p1 - p0) * groups;          // query rows of this CTA
+  const int keys = (p1 + 15) & ~15;             // keys padded to the MMA k-step
+  bf16 *qs = reinterpret_cast<bf16 *>(smem);
+  bf16 *ks = qs + kMaxKeys * S;
+  bf16 *vs = ks + kMaxKeys * S;
   const int64_t block_elems = static_cast<int64_t>(bs) * kvw;
-  const bf16 *kg = payload + (static_cast<int64_t>(layer) * kBatch + row) * block_elems + kvh * d;
+  const bf16 *kg = payload + (static_cast<int64_t>(layer) * kBatch + row) * block_elems + kvh * D;
   const bf16 *vg = kg + static_cast<int64_t>(L) * kBatch * block_elems;
-  // stage K and V of positions 0..p1-1 (2-element words) and the chunk's queries
-  const int half_d = d / 2;
-  for (int i = threadIdx.x; i < p1 * half_d; i += blockDim.x) {
-    const int j = i / half_d, w = i % half_d;
-    reinterpret_cast<uint32_t *>(ks + static_cast<size_t>(j) * kKeyStride)[w] =
-        reinterpret_cast<const uint32_t *>(kg + static_cast<int64_t>(j) * kvw)[w];
-    reinterpret_cast<uint32_t *>(vs + static_cast<size_t>(j) * d)[w] =
-        reinterpret_cast<const uint32_t *>(vg + static_cast<int64_t>(j) * kvw)[w];
+  // stage K / V rows [0, keys) (zero beyond p1) and Q rows [0, 16 * ceil(rows / 16)) (zero beyond rows)
+  constexpr int U = D / 8;   // 16-byte units per row
+  for (int i = threadIdx.x; i < keys * U; i += blockDim.x) {
+    const int j = i / U, u = i % U;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (j < p1) {
+      kv = *reinterpret_cast<const uint4 *>(kg + static_cast<int64_t>(j) * kvw + u * 8);
+      vv = *reinterpret_cast<const uint4 *>(vg + static_cast<int64_t>(j) * kvw + u * 8);
+    }
+    *reinterpret_cast<uint4 *>(ks + j * S + u * 8) = kv;
+    *reinterpret_cast<uint4 *>(vs + j * S + u * 8) = vv;
   }
-  const int pairs = (p1 - p0) * groups;
-  for (int i = threadIdx.x; i < pairs * d; i += blockDim.x) {
-    const int pair = i / d, k = i % d;
-    const int t = spans.start[row] + p0 + pair / groups, h = kvh * groups + pair % groups;
-    qs[i] = f(q[static_cast<int64_t>(t) * nq * d + h * d + k]);
+  const int qrows = (rows + 15) & ~15;
+  for (int i = threadIdx.x; i < qrows * U; i += blockDim.x) {
+    const int r = i / U, u = i % U;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < rows) {
+      const int t = spans.start[row] + p0 + r / groups, h = kvh * groups + r % groups;
+      v = *reinterpret_cast<const uint4 *>(q + static_cast<int64_t>(t) * nq * D + h * D + u * 8);
+    }
+    *reinterpret_cast<uint4 *>(qs + r * S + u * 8) = v;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float *pw = ps + static_cast<size_t>(warp) * bs;
-  const int dims = d / 32;
-  for (int pair = warp; pair < pairs; pair += kAttnWarps) {
-    const int pos = p0 + pair / groups, h = kvh * groups + pair % groups;
-    const int n = pos + 1;   // keys 0..pos
-    const float *qv = qs + static_cast<size_t>(pair) * d;
-    float sc[4], mx = -INFINITY;
+  const int m0 = warp * 16;
+  if (m0 >= rows) return;
+  const int g = lane >> 2, tq = lane & 3;
+  // S = Q K^T: 16 query rows x up to 128 keys (16 n-tiles of 8)
+  float sc[16][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int j = lane + 32 * i;
-      sc[i] = -INFINITY;
-      if (j < n) {
-        const uint32_t *kr = reinterpret_cast<const uint32_t *>(ks + static_cast<size_t>(j) * kKeyStride);
-        float dot = 0.f;
-        for (int w = 0; w < half_d; ++w) {
-          const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162 *>(kr + w);
-          dot = fmaf(qv[2 * w], __low2float(k2), dot);
-          dot = fmaf(qv[2 * w + 1], __high2float(k2), dot);
-        }
-        sc[i] = r(__fdiv_rn(r(dot), sqrt_d));
-        mx = fmaxf(mx, sc[i]);
+  for (int nt = 0; nt < 16; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+  const int ntiles = keys / 8;
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t a[4];
+    ldsm_x4(a, qs + (m0 + (lane & 15)) * S + kk * 16 + (lane >> 4) * 8);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      if (nt < ntiles) {
+        uint32_t bfrag[2];
+        ldsm_x2(bfrag, ks + (nt * 8 + (lane & 7)) * S + kk * 16 + ((lane >> 3) & 1) * 8);
+        mma16816(sc[nt], a, bfrag);
       }
     }
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float e[4], sum = 0.f;
+  }
+  // scores, causal mask, softmax per query row (rows g and g + 8 of the warp's tile)
+  const int rA = m0 + g, rB = rA + 8;
+  const int posA = rA < rows ? p0 + rA / groups : -1, posB = rB < rows ? p0 + rB / groups : -1;
+  float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      e[i] = lane + 32 * i < n ? expf(__fsub_rn(sc[i], mx)) : 0.f;
-      sum += e[i];
+  for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int key = nt * 8 + tq * 2 + j;
+      const bool inA = nt < ntiles && key <= posA, inB = nt < ntiles && key <= posB;
+      sc[nt][j] = inA ? r(__fdiv_rn(r(sc[nt][j]), sqrt_d)) : -INFINITY;
+      sc[nt][2 + j] = inB ? r(__fdiv_rn(r(sc[nt][2 + j]), sqrt_d)) : -INFINITY;
+      mxA = fmaxf(mxA, sc[nt][j]);
+      mxB = fmaxf(mxB, sc[nt][2 + j]);
     }
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+  mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+  mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+  mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+  if (posA < 0) mxA = 0.f;   // padding rows: no keys, all probabilities 0
+  if (posB < 0) mxB = 0.f;
+  float sumA = 0.f, sumB = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (lane + 32 * i < n) pw[lane + 32 * i] = r(__fdiv_rn(e[i], sum));
-    __syncwarp();
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < n; ++j) {
-      const float pj = pw[j];
-      const bf16 *vr = vs + static_cast<size_t>(j) * d + lane * dims;
+  for (int nt = 0; nt < 16; ++nt) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (c < dims) acc[c] = fmaf(pj, f(vr[c]), acc[c]);
+    for (int j = 0; j < 2; ++j) {
+      sc[nt][j] = sc[nt][j] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][j], mxA));
+      sc[nt][2 + j] = sc[nt][2 + j] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][2 + j], mxB));
+      sumA += sc[nt][j];
+      sumB += sc[nt][2 + j];
     }
-    bf16 *dst = out + static_cast<int64_t>(spans.start[row] + pos) * nq * d + h * d + lane * dims;
+  }
+  sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
+  sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
+  sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
+  sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+  if (posA < 0) sumA = 1.f;
+  if (posB < 0) sumB = 1.f;
+  // O = P V: P (16 x keys) as the A operand straight from the accumulator tiles
+  float o[D / 8][4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-      if (c < dims) dst[c] = b(acc[c]);
-    __syncwarp();
+  for (int nt = 0; nt < D / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+#pragma unroll
+  for (int kj = 0; kj < 8; ++kj) {
+    if (kj * 16 < keys) {
+      uint32_t a[4];
+      a[0] = pack_bf16(r(__fdiv_rn(sc[2 * kj][0], sumA)), r(__fdiv_rn(sc[2 * kj][1], sumA)));
+      a[1] = pack_bf16(r(__fdiv_rn(sc[2 * kj][2], sumB)), r(__fdiv_rn(sc[2 * kj][3], sumB)));
+      a[2] = pack_bf16(r(__fdiv_rn(sc[2 * kj + 1][0], sumA)), r(__fdiv_rn(sc[2 * kj + 1][1], sumA)));
+      a[3] = pack_bf16(r(__fdiv_rn(sc[2 * kj + 1][2], sumB)), r(__fdiv_rn(sc[2 * kj + 1][3], sumB)));
+#pragma unroll
+      for (int nt = 0; nt < D / 8; ++nt) {
+        uint32_t bfrag[2];
+        ldsm_x2_trans(bfrag, vs + (kj * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * S + nt * 8);
+        mma16816(o[nt], a, bfrag);
+      }
+    }
+  }
+  // bf16(O) to the token's head slice
+  const int64_t tA = spans.start[row] + posA, tB = spans.start[row] + posB;
+  const int hA = kvh * groups + rA % groups, hB = kvh * groups + rB % groups;
+#pragma unroll
+  for (int nt = 0; nt < D / 8; ++nt) {
+    const int dim = nt * 8 + tq * 2;
+    if (posA >= 0)
+      *reinterpret_cast<__nv_bfloat162 *>(out + tA * nq * D + hA * D + dim) = __floats2bfloat162_rn(o[nt][0], o[nt][1]);
+    if (posB >= 0)
+      *reinterpret_cast<__nv_bfloat162 *>(out + tB * nq * D + hB * D + dim) = __floats2bfloat162_rn(o[nt][2], o[nt][3]);
   }
 }
 
