@@ -27,6 +27,11 @@ B=4 cohort (strong scaling): each GPU streams its 1/N of the weights and the
 epoch kernel exchanges the O / down partials and the vocabulary argmax over
 NVLink peer memory; value counts the cohort's tokens once, and the roofline
 compares the group's shard bytes with N x the per-GPU HBM peak.
+
+Other options: --k (epoch length), --prompt-max (longest seeded prompt; the
+box-scale variant uses 120), --trace (per-phase CTA-0 timeline of one extra
+epoch on stderr), --prefill (a separate measurement: the batched device
+prefill of a 4 x 120-token cohort against teacher-forced epochs).
 """
 
 from __future__ import annotations
