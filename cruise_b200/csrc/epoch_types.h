@@ -163,7 +163,7 @@ struct TpArg {
 constexpr int kTpRows = 8192;          // widest hidden size a tensor-parallel exchange holds
 
 struct TpExchange {
-  uint32_t flag[kMaxTp][32];            // flag[src]: last sequence number src published (own 128-B line)
+  uint32_t flag[kMaxTp][32];            // flag[src]: last argmax-exchange sequence number src published (own 128-B line)
   TpArg arg[kMaxTp][4];                 // argmax partial of each rank per batch row
   // [set][src][n][b]: rank src's fp32 partial of output row n, batch row b, in
   // the low half of the word and the sequence number of its phase in the high
