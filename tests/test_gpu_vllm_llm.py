@@ -53,11 +53,15 @@ def test_llm_generate_through_the_resident_engine(cuda_ok, tmp_path, monkeypatch
               block_size=TINY.block_size, max_num_seqs=4, async_scheduling=False, enforce_eager=True,
               dtype="bfloat16", worker_cls="cruise_b200.worker.ResidentEpochWorker",
               scheduler_cls="cruise_b200.scheduler.ResidentEpochScheduler")
-    prompts = [11, 108, 205]
-    params = SamplingParams(temperature=0.0, max_tokens=7, detokenize=False)
-    outputs = llm.generate([{"prompt_token_ids": [t]} for t in prompts], params)
+    try:
+        prompts = [11, 108, 205]
+        params = SamplingParams(temperature=0.0, max_tokens=7, detokenize=False)
+        outputs = llm.generate([{"prompt_token_ids": [t]} for t in prompts], params)
+    finally:
+        # the executor's shutdown reaches the worker, which closes the engine
+        # (one bridge engine per process: later tests create their own)
+        llm.llm_engine.engine_core.shutdown()
     for prompt, output in zip(prompts, outputs):
         got = list(output.outputs[0].token_ids)
         want = _oracle_greedy(prompt, 7)
         assert got == want[: len(got)] and (len(got) == 7 or got[-1] == TINY.configured_eos), (prompt, got, want)
-    del llm
