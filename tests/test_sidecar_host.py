@@ -191,3 +191,53 @@ def test_transport_errors_keep_the_commit_state():
     with pytest.raises(ResidentEpochExecutionError) as caught:
         engine.execute(plan)
     assert caught.value.status == 12 and caught.value.commit_state == EpochCommitState.PREPARED
+
+
+@pytest.fixture(scope="module")
+def sanitized_server(server, tmp_path_factory) -> Path:
+    """The sidecar server built with AddressSanitizer and UBSan (host code only;
+    the engine library it links is the regular build)."""
+    import shutil
+
+    from cruise_b200.build import PACKAGE, SERVER_SOURCES
+
+    cxx = shutil.which("g++")
+    if cxx is None:
+        pytest.skip("no g++")
+    out = tmp_path_factory.mktemp("asan") / "cruise_epoch_server_asan"
+    cmd = [cxx, "-O1", "-g", "-std=c++17", "-fsanitize=address,undefined", "-fno-omit-frame-pointer",
+           "-fno-sanitize-recover=undefined", "-o", str(out), *map(str, SERVER_SOURCES), f"-L{PACKAGE}",
+           "-l:libcruise_epoch.so", f"-Wl,-rpath,{PACKAGE}"]
+    if subprocess.run(cmd, capture_output=True).returncode != 0:
+        pytest.skip("sanitizer runtime not available")
+    return out
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="exercises the failed-create path of a GPU-less host")
+def test_server_host_code_is_sanitizer_clean(sanitized_server):
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0:abort_on_error=0", UBSAN_OPTIONS="print_stacktrace=1")
+    usage = subprocess.run([str(sanitized_server)], capture_output=True, env=env)
+    assert usage.returncode == 64
+    path = _shm("asan")
+    proc = subprocess.Popen([str(sanitized_server), str(path), "tiny", "", "", "synthetic:0", ""],
+                            stderr=subprocess.PIPE, env=env)
+    try:
+        deadline = time.monotonic() + 120
+        while not path.exists():
+            assert time.monotonic() < deadline and proc.poll() is None
+            time.sleep(0.01)
+        with socket.socket(socket.AF_UNIX, socket.SOCK_STREAM) as s:
+            s.connect(str(path))
+            data = b""
+            while len(data) < sc.RESPONSE.size:
+                chunk = s.recv(sc.RESPONSE.size - len(data))
+                assert chunk
+                data += chunk
+        assert sc.RESPONSE.unpack(data)[1] == 103
+        _, err = proc.communicate(timeout=120)
+        assert proc.returncode == 103
+        text = err.decode(errors="replace")
+        assert "AddressSanitizer" not in text and "runtime error" not in text, text[-2000:]
+    finally:
+        if proc.poll() is None:
+            proc.kill()
