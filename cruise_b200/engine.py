@@ -44,7 +44,7 @@ def rope_tables(config: ModelConfig) -> tuple[torch.Tensor, torch.Tensor]:
 class EpochOutput:
     history: np.ndarray        # i64 [8, 4] step-major, -1 filled
     control_out: np.ndarray    # i32 [28]
-    logits: np.ndarray | None  # f32 [8, 4, V] when requested
+    logits: np.ndarray | None  # f32 [8, 4, V] when requested (a TP rank fills its vocabulary rows [v0, v0+nv))
     device_us: float           # CUDA-event time of the epoch kernel
 
     @property
@@ -144,6 +144,8 @@ class EpochEngine:
 
     # -- KV cache ------------------------------------------------------------------
     def read_kv(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """The resident K and V caches, bf16 [layers][blocks][block_size][kv
+        heads][head_dim]; a tensor-parallel rank holds (and returns) its KV heads."""
         shape = self.shard.kv_cache_shape(self.config)
         key = np.empty(shape, dtype=np.int16)
         value = np.empty(shape, dtype=np.int16)
