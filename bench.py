@@ -625,26 +625,29 @@ def random_weights(cfg, layers: int, seed: int) -> dict:
 
 def forced_epochs_all_rows(sc, cfg, generation_offset: int):
     """Teacher-forced epochs writing the KV of every prompt token but the last,
-    all rows of the cohort in the same epochs (8 positions per epoch)."""
+    all rows of the cohort in the same epochs.  An epoch runs as many steps as
+    the row with the fewest positions left (at most 8), so no row runs past its
+    prompt; rows that are done drop out."""
     from scenario import BATCH, MAX_STEPS, compute_slot
 
-    longest = max(len(p) for p in sc.prompts)
     eos = next(t for t in range(cfg.vocab - 1, -1, -1) if all(t not in p for p in sc.prompts))
     gens = [g + generation_offset if g else 0 for g in sc.generations]
-    for done in range(0, longest - 1, MAX_STEPS):
+    done = [0] * BATCH
+    while True:
+        left = {r: len(p) - 1 - done[r] for r, p in enumerate(sc.prompts) if p and len(p) - 1 > done[r]}
+        if not left:
+            return
+        steps = min(MAX_STEPS, min(left.values()))
         token = np.zeros(BATCH, dtype=np.int64)
         position = np.zeros(BATCH, dtype=np.int64)
         seq_len = np.zeros(BATCH, dtype=np.int32)
         active = np.zeros(BATCH, dtype=np.int32)
         forced = np.full((MAX_STEPS, BATCH), -1, dtype=np.int64)
-        steps = 0
-        for row, prompt in enumerate(sc.prompts):
-            if len(prompt) - 1 <= done:
-                continue
-            n = min(MAX_STEPS, len(prompt) - 1 - done)
-            steps = max(steps, n)
-            token[row], position[row], seq_len[row], active[row] = prompt[done], done, done + 1, 1
-            forced[:n, row] = prompt[done + 1: done + 1 + n]
+        for row in left:
+            prompt, d = sc.prompts[row], done[row]
+            token[row], position[row], seq_len[row], active[row] = prompt[d], d, d + 1, 1
+            forced[:steps, row] = prompt[d + 1: d + 1 + steps]
+            done[row] += steps
         slot = np.array([compute_slot(sc.block_table, cfg.block_size, r, int(position[r])) for r in range(BATCH)],
                         dtype=np.int32)
         row_gens = [gens[r] if active[r] else 0 for r in range(BATCH)]
