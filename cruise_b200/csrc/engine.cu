@@ -747,8 +747,10 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     e->last_error = "cruise_epoch_prefill: single-GPU engines only (no tensor parallelism)";
     return -4;
   }
-  if (m.bs > prefill::kMaxKeys || (m.d != 64 && m.d != 128) || m.nq / m.nkv * prefill::kAttnChunk > prefill::kMaxKeys) {
-    e->last_error = "cruise_epoch_prefill: needs block size <= 128, head size 64 or 128, <= 8 query heads per KV head";
+  if (m.bs > prefill::kMaxKeys || (m.d != 64 && m.d != 128) || m.nq / m.nkv * prefill::kAttnChunk > prefill::kMaxKeys ||
+      m.I % 4 != 0) {
+    e->last_error = "cruise_epoch_prefill: needs block size <= 128, head size 64 or 128, <= 8 query heads per KV head"
+                    " and an intermediate size divisible by 4";
     return -1;
   }
   std::vector<int64_t> tok;
@@ -808,22 +810,25 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
   bool blas_ok = true;
   if (T > 0) {
     prefill::embed_rows<<<T, 128, 0, e->stream>>>(e->embed, ps->tok, ps->h, H);
+    prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, e->layers[0].w_in, ps->x, H, m.eps);
     for (int l = 0; l < m.L && blas_ok; ++l) {
+      // x holds rms_norm(h) * w_in of this layer
       const LayerWeights &lw = e->layers[l];
       const PrefillLayer &pl = ps->layers[l];
-      prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, lw.w_in, ps->x, H, m.eps);
       blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
       prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, pl.qkv_b, e->rope_cos, e->rope_sin, ps->row, ps->pos,
                                                         ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
+      // the last layer's K/V are its only output the payload holds: its
+      // attention, O projection and MLP would feed no later layer
+      if (l == m.L - 1) break;
       attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(ps->q, payload, spans, ps->attn, l,
                                                                                 m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
       blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, ps->acc, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
-      prefill::add_residual<<<ew, 256, 0, e->stream>>>(ps->acc, ps->h, static_cast<int64_t>(T) * H);
-      prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, lw.w_post, ps->x, H, m.eps);
+      prefill::residual_rms_norm<<<T, 256, 0, e->stream>>>(ps->acc, ps->h, lw.w_post, ps->x, H, m.eps);
       blas_ok &= prefill_gemm(ps->blas, ps->x, pl.gu_w, ps->acc, T, 2 * I, H) == CUBLAS_STATUS_SUCCESS;
       prefill::swiglu<<<ew, 256, 0, e->stream>>>(ps->acc, ps->act, T, I);
       blas_ok &= prefill_gemm(ps->blas, ps->act, pl.down_w, ps->acc, T, H, I) == CUBLAS_STATUS_SUCCESS;
-      prefill::add_residual<<<ew, 256, 0, e->stream>>>(ps->acc, ps->h, static_cast<int64_t>(T) * H);
+      prefill::residual_rms_norm<<<T, 256, 0, e->stream>>>(ps->acc, ps->h, e->layers[l + 1].w_in, ps->x, H, m.eps);
     }
   }
   if (!blas_ok) {

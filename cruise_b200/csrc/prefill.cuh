@@ -73,6 +73,30 @@ __global__ void rms_norm_rows(const bf16 *h, const bf16 *w, bf16 *x, int H, floa
   for (int i = threadIdx.x; i < H; i += blockDim.x) out[i] = b(__fmul_rn(r(__fmul_rn(f(row[i]), inv)), f(w[i])));
 }
 
+// The residual update after the O and down projections followed by the next
+// rms_norm, one CTA per token.  hidden = residual + materialize(mm_t(x, W))
+// (:380-386, :399-403): h[t] = bf16(h + bf16(acc)), the GEMM's fp32 sum
+// rounded to bf16, added to the bf16 residual, rounded again.  Then x[t] =
+// rms_norm(h[t]) * w with the summation order of rms_norm_rows.  A thread
+// reads back only the elements it wrote, so no barrier sits between the two.
+__global__ void residual_rms_norm(const float *acc, bf16 *h, const bf16 *w, bf16 *x, int H, float eps) {
+  __shared__ float scratch[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
+  bf16 *row = h + base;
+  const float *sum = acc + base;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const bf16 nv = b(__fadd_rn(f(row[i]), r(sum[i])));
+    row[i] = nv;
+    const float v = f(nv);
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps)));
+  bf16 *out = x + base;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) out[i] = b(__fmul_rn(r(__fmul_rn(f(row[i]), inv)), f(w[i])));
+}
+
 // QKV epilogue, one CTA per token: q, k, v = bf16(acc + bias) (F.linear: fp32
 // sum plus bias, one rounding), rope on q and k with the token's position
 // (q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16), q to
@@ -308,25 +332,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   }
 }
 
-// hidden = residual + materialize(mm_t(x, W)) (:380-386, :399-403): the GEMM's
-// fp32 sum rounded to bf16, added to the bf16 residual, rounded again.
-__global__ void add_residual(const float *acc, bf16 *h, int64_t count) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    h[i] = b(__fadd_rn(f(h[i]), r(acc[i])));
+// silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398); acc
+// rows are [gate (I) | up (I)] per token.  Four consecutive elements per
+// thread (16-byte loads, 8-byte stores): I % 4 == 0 and T * I < 2^31, both
+// checked by the host.
+__device__ __forceinline__ float swiglu_one(float g, float u) {
+  const float gate = r(g);
+  const float silu = r(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
+  return __fmul_rn(silu, r(u));
 }
 
-// silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398); acc
-// rows are [gate (I) | up (I)] per token.
 __global__ void swiglu(const float *acc, bf16 *act, int T, int I) {
-  const int64_t count = static_cast<int64_t>(T) * I;
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < count;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = e / I, i = e % I;
-    const float gate = r(acc[t * 2 * I + i]);
-    const float up = r(acc[t * 2 * I + I + i]);
-    const float silu = r(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
-    act[e] = b(__fmul_rn(silu, up));
+  const int quads = I >> 2;
+  const int count = T * quads;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
+    const int t = e / quads, i = (e - t * quads) << 2;
+    const float *row = acc + static_cast<int64_t>(t) * 2 * I;
+    const float4 g = *reinterpret_cast<const float4 *>(row + i);
+    const float4 u = *reinterpret_cast<const float4 *>(row + I + i);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(swiglu_one(g.x, u.x), swiglu_one(g.y, u.y));
+    __nv_bfloat162 hi = __floats2bfloat162_rn(swiglu_one(g.z, u.z), swiglu_one(g.w, u.w));
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t *>(&lo);
+    packed.y = *reinterpret_cast<uint32_t *>(&hi);
+    *reinterpret_cast<uint2 *>(act + static_cast<int64_t>(t) * I + i) = packed;
   }
 }
 
