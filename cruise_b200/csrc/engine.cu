@@ -748,9 +748,9 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     return -4;
   }
   if (m.bs > prefill::kMaxKeys || (m.d != 64 && m.d != 128) || m.nq / m.nkv * prefill::kAttnChunk > prefill::kMaxKeys ||
-      m.I % 4 != 0) {
-    e->last_error = "cruise_epoch_prefill: needs block size <= 128, head size 64 or 128, <= 8 query heads per KV head"
-                    " and an intermediate size divisible by 4";
+      m.I % 4 != 0 || m.H % 8 != 0 || m.H > 8 * prefill::kNormThreads * prefill::kNormChunks) {
+    e->last_error = "cruise_epoch_prefill: needs block size <= 128, head size 64 or 128, <= 8 query heads per KV head,"
+                    " an intermediate size divisible by 4 and a hidden size divisible by 8, at most 8192";
     return -1;
   }
   std::vector<int64_t> tok;
@@ -824,11 +824,11 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(ps->q, payload, spans, ps->attn, l,
                                                                                 m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
       blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, ps->acc, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
-      prefill::residual_rms_norm<<<T, 256, 0, e->stream>>>(ps->acc, ps->h, lw.w_post, ps->x, H, m.eps);
+      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(ps->acc, ps->h, lw.w_post, ps->x, H, m.eps);
       blas_ok &= prefill_gemm(ps->blas, ps->x, pl.gu_w, ps->acc, T, 2 * I, H) == CUBLAS_STATUS_SUCCESS;
       prefill::swiglu<<<ew, 256, 0, e->stream>>>(ps->acc, ps->act, T, I);
       blas_ok &= prefill_gemm(ps->blas, ps->act, pl.down_w, ps->acc, T, H, I) == CUBLAS_STATUS_SUCCESS;
-      prefill::residual_rms_norm<<<T, 256, 0, e->stream>>>(ps->acc, ps->h, e->layers[l + 1].w_in, ps->x, H, m.eps);
+      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(ps->acc, ps->h, e->layers[l + 1].w_in, ps->x, H, m.eps);
     }
   }
   if (!blas_ok) {

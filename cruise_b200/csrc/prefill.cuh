@@ -74,61 +74,141 @@ __global__ void rms_norm_rows(const bf16 *h, const bf16 *w, bf16 *x, int H, floa
 }
 
 // The residual update after the O and down projections followed by the next
-// rms_norm, one CTA per token.  hidden = residual + materialize(mm_t(x, W))
-// (:380-386, :399-403): h[t] = bf16(h + bf16(acc)), the GEMM's fp32 sum
-// rounded to bf16, added to the bf16 residual, rounded again.  Then x[t] =
-// rms_norm(h[t]) * w with the summation order of rms_norm_rows.  A thread
-// reads back only the elements it wrote, so no barrier sits between the two.
-__global__ void residual_rms_norm(const float *acc, bf16 *h, const bf16 *w, bf16 *x, int H, float eps) {
+// rms_norm, one CTA of kNormThreads per token.  hidden = residual +
+// materialize(mm_t(x, W)) (:380-386, :399-403): h[t] = bf16(h + bf16(acc)),
+// the GEMM's fp32 sum rounded to bf16, added to the bf16 residual, rounded
+// again.  Then x[t] = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w).  Each thread
+// owns chunks of 8 consecutive elements (16-byte h and w loads, two 16-byte
+// acc loads), issues all its loads before the first store, and keeps the
+// updated h in registers for the norm.  H % 8 == 0 and H <= 8 *
+// kNormThreads * kNormChunks, both checked by the host.
+constexpr int kNormThreads = 256;
+constexpr int kNormChunks = 4;
+
+__device__ __forceinline__ void unpack8(const uint4 &u, float (&v)[8]) {
+  const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = __low2float(p[k]);
+    v[2 * k + 1] = __high2float(p[k]);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 u;
+  uint32_t *w = reinterpret_cast<uint32_t *>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    __nv_bfloat162 pair = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    w[k] = *reinterpret_cast<uint32_t *>(&pair);
+  }
+  return u;
+}
+
+__global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const float *acc, bf16 *h, const bf16 *w, bf16 *x,
+                                                                   int H, float eps) {
   __shared__ float scratch[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
-  bf16 *row = h + base;
-  const float *sum = acc + base;
+  const int chunks = H >> 3;
+  uint4 old[kNormChunks];
+  float4 sum_lo[kNormChunks], sum_hi[kNormChunks];
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < chunks) {
+      old[j] = *reinterpret_cast<const uint4 *>(h + base + c * 8);
+      sum_lo[j] = *reinterpret_cast<const float4 *>(acc + base + c * 8);
+      sum_hi[j] = *reinterpret_cast<const float4 *>(acc + base + c * 8 + 4);
+    }
+  }
+  float hv[kNormChunks][8];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const bf16 nv = b(__fadd_rn(f(row[i]), r(sum[i])));
-    row[i] = nv;
-    const float v = f(nv);
-    ss = __fadd_rn(ss, __fmul_rn(v, v));
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < chunks) {
+      float prev[8];
+      unpack8(old[j], prev);
+      const float a[8] = {sum_lo[j].x, sum_lo[j].y, sum_lo[j].z, sum_lo[j].w,
+                          sum_hi[j].x, sum_hi[j].y, sum_hi[j].z, sum_hi[j].w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        hv[j][k] = r(__fadd_rn(prev[k], r(a[k])));
+        ss = __fadd_rn(ss, __fmul_rn(hv[j][k], hv[j][k]));
+      }
+      *reinterpret_cast<uint4 *>(h + base + c * 8) = pack8(hv[j]);
+    }
   }
   const float total = block_sum(ss, scratch);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps)));
-  bf16 *out = x + base;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) out[i] = b(__fmul_rn(r(__fmul_rn(f(row[i]), inv)), f(w[i])));
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < chunks) {
+      float wv[8], out[8];
+      unpack8(*reinterpret_cast<const uint4 *>(w + c * 8), wv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) out[k] = __fmul_rn(r(__fmul_rn(hv[j][k], inv)), wv[k]);
+      *reinterpret_cast<uint4 *>(x + base + c * 8) = pack8(out);
+    }
+  }
 }
 
 // QKV epilogue, one CTA per token: q, k, v = bf16(acc + bias) (F.linear: fp32
 // sum plus bias, one rounding), rope on q and k with the token's position
 // (q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16), q to
-// `q_out` [T][Hq], k and v into the payload at (row, position).
+// `q_out` [T][Hq], k and v into the payload at (row, position).  A thread
+// takes one unit: for q and k, the element pairs (i, i+1) of a head and their
+// rotation partners (i+half, i+half+1), so each partner is loaded once; for v,
+// two consecutive elements.  d is even and half = d/2 is even (d = 64 or 128).
+__device__ __forceinline__ uint32_t bf2_bits(float lo, float hi) {
+  __nv_bfloat162 pair = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&pair);
+}
+
 __global__ void qkv_rope_store(const float *acc, const bf16 *bias, const bf16 *cos, const bf16 *sin,
                                const int32_t *tok_row, const int32_t *tok_pos, bf16 *q_out, bf16 *payload,
                                int layer, int L, int nq, int nkv, int d, int bs) {
   const int t = blockIdx.x;
   const int Hq = nq * d, kvw = nkv * d, N = Hq + 2 * kvw;
-  const int row = tok_row[t], pos = tok_pos[t], half = d / 2;
+  const int row = tok_row[t], pos = tok_pos[t], half = d / 2, quarter = d / 4;
   const float *a = acc + static_cast<int64_t>(t) * N;
   const bf16 *cs = cos + static_cast<int64_t>(pos) * d;
   const bf16 *sn = sin + static_cast<int64_t>(pos) * d;
   const int64_t block_elems = static_cast<int64_t>(bs) * kvw;
   const int64_t slot_off = (static_cast<int64_t>(layer) * kBatch + row) * block_elems + static_cast<int64_t>(pos) * kvw;
   const int64_t v_base = static_cast<int64_t>(L) * kBatch * block_elems;   // V half of the payload
-  for (int n = threadIdx.x; n < N; n += blockDim.x) {
-    const float x = r(__fadd_rn(a[n], f(bias[n])));
-    if (n >= Hq + kvw) {   // v
-      payload[v_base + slot_off + (n - Hq - kvw)] = b(x);
+  const int rope_units = (nq + nkv) * quarter, units = rope_units + kvw / 2;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    if (u >= rope_units) {   // v: two elements
+      const int n = Hq + kvw + 2 * (u - rope_units);
+      const float2 s2 = *reinterpret_cast<const float2 *>(a + n);
+      const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162 *>(bias + n);
+      *reinterpret_cast<uint32_t *>(payload + v_base + slot_off + (n - Hq - kvw)) =
+          bf2_bits(__fadd_rn(s2.x, __low2float(b2)), __fadd_rn(s2.y, __high2float(b2)));
       continue;
     }
-    const int base = n - n % d, i = n % d;
-    const int pn = base + (i < half ? i + half : i - half);
-    const float partner = r(__fadd_rn(a[pn], f(bias[pn])));
-    const float rot = i < half ? -partner : partner;
-    const float roped = r(__fadd_rn(r(__fmul_rn(x, f(cs[i]))), r(__fmul_rn(rot, f(sn[i])))));
-    if (n < Hq) {
-      q_out[static_cast<int64_t>(t) * Hq + n] = b(roped);
-    } else {
-      payload[slot_off + (n - Hq)] = b(roped);
-    }
+    const int head = u / quarter, i = 2 * (u - head * quarter);   // q heads, then k heads
+    const int n_lo = head * d + i, n_hi = n_lo + half;
+    const float2 s_lo = *reinterpret_cast<const float2 *>(a + n_lo);
+    const float2 s_hi = *reinterpret_cast<const float2 *>(a + n_hi);
+    const __nv_bfloat162 b_lo = *reinterpret_cast<const __nv_bfloat162 *>(bias + n_lo);
+    const __nv_bfloat162 b_hi = *reinterpret_cast<const __nv_bfloat162 *>(bias + n_hi);
+    const __nv_bfloat162 c_lo = *reinterpret_cast<const __nv_bfloat162 *>(cs + i);
+    const __nv_bfloat162 c_hi = *reinterpret_cast<const __nv_bfloat162 *>(cs + i + half);
+    const __nv_bfloat162 z_lo = *reinterpret_cast<const __nv_bfloat162 *>(sn + i);
+    const __nv_bfloat162 z_hi = *reinterpret_cast<const __nv_bfloat162 *>(sn + i + half);
+    const float x0 = r(__fadd_rn(s_lo.x, __low2float(b_lo))), x1 = r(__fadd_rn(s_lo.y, __high2float(b_lo)));
+    const float y0 = r(__fadd_rn(s_hi.x, __low2float(b_hi))), y1 = r(__fadd_rn(s_hi.y, __high2float(b_hi)));
+    // rotate_half: element i pairs with -(i+half), element i+half with +(i)
+    const float lo0 = r(__fadd_rn(r(__fmul_rn(x0, __low2float(c_lo))), r(__fmul_rn(-y0, __low2float(z_lo)))));
+    const float lo1 = r(__fadd_rn(r(__fmul_rn(x1, __high2float(c_lo))), r(__fmul_rn(-y1, __high2float(z_lo)))));
+    const float hi0 = r(__fadd_rn(r(__fmul_rn(y0, __low2float(c_hi))), r(__fmul_rn(x0, __low2float(z_hi)))));
+    const float hi1 = r(__fadd_rn(r(__fmul_rn(y1, __high2float(c_hi))), r(__fmul_rn(x1, __high2float(z_hi)))));
+    // a head lies wholly in q or wholly in k
+    bf16 *dst = n_lo < Hq ? q_out + static_cast<int64_t>(t) * Hq + n_lo : payload + slot_off + (n_lo - Hq);
+    *reinterpret_cast<uint32_t *>(dst) = bf2_bits(lo0, lo1);
+    *reinterpret_cast<uint32_t *>(dst + half) = bf2_bits(hi0, hi1);
   }
 }
 
