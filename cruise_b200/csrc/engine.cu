@@ -665,10 +665,13 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
 int64_t import_payload_bytes(const Engine *e);
 
 // y[T][N] (fp32) = x[T][K] . W[N][K]^T, both bf16 row-major (cuBLAS is column-major: y^T = W x^T).
-cublasStatus_t prefill_gemm(cublasHandle_t blas, const bf16 *x, const bf16 *w, float *y, int T, int N, int K) {
+// y[T][N] = x[T][K] W[N][K]^T with fp32 accumulation; y is fp32, or bf16 (the
+// fp32 sum rounded once, as the decoder's materialize(mm_t(x, W))).
+cublasStatus_t prefill_gemm(cublasHandle_t blas, const bf16 *x, const bf16 *w, void *y, cudaDataType_t y_type, int T,
+                            int N, int K) {
   const float one = 1.0f, zero = 0.0f;
   return cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16BF, K, x, CUDA_R_16BF, K, &zero, y,
-                      CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+                      y_type, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
 }
 
 // Builds the untiled weights (once) and buffers for kBatch * block_size tokens.
@@ -815,7 +818,7 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       // x holds rms_norm(h) * w_in of this layer
       const LayerWeights &lw = e->layers[l];
       const PrefillLayer &pl = ps->layers[l];
-      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
+      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, CUDA_R_32F, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
       prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, pl.qkv_b, e->rope_cos, e->rope_sin, ps->row, ps->pos,
                                                         ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
       // the last layer's K/V are its only output the payload holds: its
@@ -823,12 +826,15 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       if (l == m.L - 1) break;
       attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(ps->q, payload, spans, ps->attn, l,
                                                                                 m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
-      blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, ps->acc, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
-      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(ps->acc, ps->h, lw.w_post, ps->x, H, m.eps);
-      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.gu_w, ps->acc, T, 2 * I, H) == CUBLAS_STATUS_SUCCESS;
-      prefill::swiglu<<<ew, 256, 0, e->stream>>>(ps->acc, ps->act, T, I);
-      blas_ok &= prefill_gemm(ps->blas, ps->act, pl.down_w, ps->acc, T, H, I) == CUBLAS_STATUS_SUCCESS;
-      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(ps->acc, ps->h, e->layers[l + 1].w_in, ps->x, H, m.eps);
+      // O, gate/up and down results rounded to bf16 by the GEMM itself
+      bf16 *out = reinterpret_cast<bf16 *>(ps->acc);
+      blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, out, CUDA_R_16BF, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
+      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(out, ps->h, lw.w_post, ps->x, H, m.eps);
+      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.gu_w, out, CUDA_R_16BF, T, 2 * I, H) == CUBLAS_STATUS_SUCCESS;
+      prefill::swiglu<<<ew, 256, 0, e->stream>>>(out, ps->act, T, I);
+      blas_ok &= prefill_gemm(ps->blas, ps->act, pl.down_w, out, CUDA_R_16BF, T, H, I) == CUBLAS_STATUS_SUCCESS;
+      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(out, ps->h, e->layers[l + 1].w_in, ps->x,
+                                                                              H, m.eps);
     }
   }
   if (!blas_ok) {

@@ -4,11 +4,13 @@
 // [K|V][layer][row][block_size][kv_heads][head_dim] -- the one-shot import
 // format of the epoch controller -- at the token's position in its row's first
 // block.  The projections are plain row-major bf16 GEMMs (cuBLAS, fp32
-// accumulation, fp32 output); these kernels do everything between them with
-// the decoder step's rounding points (batched_decoder_step.py:224-229 norm,
-// :305-313 QKV, :231-240 rope, :356-377 scores/softmax, :380-403 residuals and
-// SwiGLU), token by token, so a prefilled token's K/V equal the single-token
-// step's up to fp32 summation order.
+// accumulation; fp32 output for QKV, whose bias joins the fp32 sum before its
+// one rounding, bf16 output for the others).  These kernels do everything
+// between them with the decoder step's rounding points
+// (batched_decoder_step.py:224-229 norm, :305-313 QKV, :231-240 rope,
+// :356-377 scores/softmax, :380-403 residuals and SwiGLU), token by token, so
+// a prefilled token's K/V equal the single-token step's up to fp32 summation
+// order.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -75,11 +77,11 @@ __global__ void rms_norm_rows(const bf16 *h, const bf16 *w, bf16 *x, int H, floa
 
 // The residual update after the O and down projections followed by the next
 // rms_norm, one CTA of kNormThreads per token.  hidden = residual +
-// materialize(mm_t(x, W)) (:380-386, :399-403): h[t] = bf16(h + bf16(acc)),
-// the GEMM's fp32 sum rounded to bf16, added to the bf16 residual, rounded
-// again.  Then x[t] = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w).  Each thread
-// owns chunks of 8 consecutive elements (16-byte h and w loads, two 16-byte
-// acc loads), issues all its loads before the first store, and keeps the
+// materialize(mm_t(x, W)) (:380-386, :399-403): h[t] = bf16(h + y), y the
+// GEMM's fp32 sum already rounded to bf16 by the GEMM, added to the bf16
+// residual, rounded again.  Then x[t] = bf16(bf16(h * rsqrt(mean(h^2) + eps)) *
+// w).  Each thread owns chunks of 8 consecutive elements (16-byte loads of h,
+// y and w), issues all its loads before the first store, and keeps the
 // updated h in registers for the norm.  H % 8 == 0 and H <= 8 *
 // kNormThreads * kNormChunks, both checked by the host.
 constexpr int kNormThreads = 256;
@@ -105,20 +107,18 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return u;
 }
 
-__global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const float *acc, bf16 *h, const bf16 *w, bf16 *x,
+__global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const bf16 *y, bf16 *h, const bf16 *w, bf16 *x,
                                                                    int H, float eps) {
   __shared__ float scratch[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
   const int chunks = H >> 3;
-  uint4 old[kNormChunks];
-  float4 sum_lo[kNormChunks], sum_hi[kNormChunks];
+  uint4 old[kNormChunks], sum[kNormChunks];
 #pragma unroll
   for (int j = 0; j < kNormChunks; ++j) {
     const int c = threadIdx.x + j * kNormThreads;
     if (c < chunks) {
       old[j] = *reinterpret_cast<const uint4 *>(h + base + c * 8);
-      sum_lo[j] = *reinterpret_cast<const float4 *>(acc + base + c * 8);
-      sum_hi[j] = *reinterpret_cast<const float4 *>(acc + base + c * 8 + 4);
+      sum[j] = *reinterpret_cast<const uint4 *>(y + base + c * 8);
     }
   }
   float hv[kNormChunks][8];
@@ -127,13 +127,12 @@ __global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const float *a
   for (int j = 0; j < kNormChunks; ++j) {
     const int c = threadIdx.x + j * kNormThreads;
     if (c < chunks) {
-      float prev[8];
+      float prev[8], a[8];
       unpack8(old[j], prev);
-      const float a[8] = {sum_lo[j].x, sum_lo[j].y, sum_lo[j].z, sum_lo[j].w,
-                          sum_hi[j].x, sum_hi[j].y, sum_hi[j].z, sum_hi[j].w};
+      unpack8(sum[j], a);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        hv[j][k] = r(__fadd_rn(prev[k], r(a[k])));
+        hv[j][k] = r(__fadd_rn(prev[k], a[k]));
         ss = __fadd_rn(ss, __fmul_rn(hv[j][k], hv[j][k]));
       }
       *reinterpret_cast<uint4 *>(h + base + c * 8) = pack8(hv[j]);
@@ -412,26 +411,29 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   }
 }
 
-// silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398); acc
-// rows are [gate (I) | up (I)] per token.  Four consecutive elements per
-// thread (16-byte loads, 8-byte stores): I % 4 == 0 and T * I < 2^31, both
-// checked by the host.
-__device__ __forceinline__ float swiglu_one(float g, float u) {
-  const float gate = r(g);
+// silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398); y
+// rows are [gate (I) | up (I)] per token, the GEMM's fp32 sums already
+// rounded to bf16 by the GEMM.  Four consecutive elements per thread (8-byte
+// loads and stores): I % 4 == 0 and T * I < 2^31, both checked by the host.
+__device__ __forceinline__ float swiglu_one(float gate, float up) {
   const float silu = r(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
-  return __fmul_rn(silu, r(u));
+  return __fmul_rn(silu, up);
 }
 
-__global__ void swiglu(const float *acc, bf16 *act, int T, int I) {
+__global__ void swiglu(const bf16 *y, bf16 *act, int T, int I) {
   const int quads = I >> 2;
   const int count = T * quads;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
     const int t = e / quads, i = (e - t * quads) << 2;
-    const float *row = acc + static_cast<int64_t>(t) * 2 * I;
-    const float4 g = *reinterpret_cast<const float4 *>(row + i);
-    const float4 u = *reinterpret_cast<const float4 *>(row + I + i);
-    __nv_bfloat162 lo = __floats2bfloat162_rn(swiglu_one(g.x, u.x), swiglu_one(g.y, u.y));
-    __nv_bfloat162 hi = __floats2bfloat162_rn(swiglu_one(g.z, u.z), swiglu_one(g.w, u.w));
+    const bf16 *row = y + static_cast<int64_t>(t) * 2 * I;
+    const uint2 gq = *reinterpret_cast<const uint2 *>(row + i);
+    const uint2 uq = *reinterpret_cast<const uint2 *>(row + I + i);
+    const __nv_bfloat162 *g2 = reinterpret_cast<const __nv_bfloat162 *>(&gq);
+    const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&uq);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(swiglu_one(__low2float(g2[0]), __low2float(u2[0])),
+                                              swiglu_one(__high2float(g2[0]), __high2float(u2[0])));
+    __nv_bfloat162 hi = __floats2bfloat162_rn(swiglu_one(__low2float(g2[1]), __low2float(u2[1])),
+                                              swiglu_one(__high2float(g2[1]), __high2float(u2[1])));
     uint2 packed;
     packed.x = *reinterpret_cast<uint32_t *>(&lo);
     packed.y = *reinterpret_cast<uint32_t *>(&hi);
