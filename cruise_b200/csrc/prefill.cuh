@@ -234,6 +234,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// 16-byte asynchronous global -> shared copy; `src_bytes` 0 writes zeros and
+// reads nothing.  Both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -294,28 +303,27 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   const int64_t block_elems = static_cast<int64_t>(bs) * kvw;
   const bf16 *kg = payload + (static_cast<int64_t>(layer) * kBatch + row) * block_elems + kvh * D;
   const bf16 *vg = kg + static_cast<int64_t>(L) * kBatch * block_elems;
-  // stage K / V rows [0, keys) (zero beyond p1) and Q rows [0, 16 * ceil(rows / 16)) (zero beyond rows)
+  // stage K / V rows [0, keys) (zero beyond p1) and Q rows [0, 16 * ceil(rows / 16)) (zero beyond rows):
+  // every copy of the thread is issued before the one wait
   constexpr int U = D / 8;   // 16-byte units per row
   for (int i = threadIdx.x; i < keys * U; i += blockDim.x) {
     const int j = i / U, u = i % U;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (j < p1) {
-      kv = *reinterpret_cast<const uint4 *>(kg + static_cast<int64_t>(j) * kvw + u * 8);
-      vv = *reinterpret_cast<const uint4 *>(vg + static_cast<int64_t>(j) * kvw + u * 8);
-    }
-    *reinterpret_cast<uint4 *>(ks + j * S + u * 8) = kv;
-    *reinterpret_cast<uint4 *>(vs + j * S + u * 8) = vv;
+    const int64_t off = j < p1 ? static_cast<int64_t>(j) * kvw + u * 8 : 0;
+    cp_async16(ks + j * S + u * 8, kg + off, j < p1 ? 16 : 0);
+    cp_async16(vs + j * S + u * 8, vg + off, j < p1 ? 16 : 0);
   }
   const int qrows = (rows + 15) & ~15;
+  const bf16 *q_first = q + static_cast<int64_t>(spans.start[row] + p0) * nq * D + kvh * groups * D;
   for (int i = threadIdx.x; i < qrows * U; i += blockDim.x) {
     const int r = i / U, u = i % U;
-    uint4 v = make_uint4(0, 0, 0, 0);
+    const bf16 *src = q_first;
     if (r < rows) {
       const int t = spans.start[row] + p0 + r / groups, h = kvh * groups + r % groups;
-      v = *reinterpret_cast<const uint4 *>(q + static_cast<int64_t>(t) * nq * D + h * D + u * 8);
+      src = q + static_cast<int64_t>(t) * nq * D + h * D + u * 8;
     }
-    *reinterpret_cast<uint4 *>(qs + r * S + u * 8) = v;
+    cp_async16(qs + r * S + u * 8, src, r < rows ? 16 : 0);
   }
+  cp_async_wait_all();
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = warp * 16;
