@@ -219,15 +219,24 @@ struct RowSpans {
 };
 
 constexpr int kAttnChunk = 16;     // query positions per CTA
-constexpr int kAttnWarps = 8;
+constexpr int kAttnWarps = 16;     // 8 pairs; a pair takes 16 query rows
 constexpr int kMaxKeys = 128;      // block_size bound: keys (and query rows) per CTA
+constexpr int kAttnPairs = kAttnWarps / 2;
+constexpr int kHalfKeys = kMaxKeys / 2;   // keys per warp of a pair in S = Q K^T
 
 __host__ __device__ inline int attention_row_stride(int d) { return d + 8; }   // bf16; 16-byte pad per row
+
+// Shared memory of causal_attention_mma: Q, K and V rows (kMaxKeys each,
+// padded stride), each pair's bf16 probabilities P [16][kMaxKeys + 8], and the
+// pairs' per-row partial maxima and sums.
+__host__ __device__ inline int attention_p_stride() { return kMaxKeys + 8; }
 
 __host__ __device__ inline size_t attention_smem_bytes(int bs, int d, int groups) {
   (void)bs;
   (void)groups;
-  return static_cast<size_t>(3) * kMaxKeys * attention_row_stride(d) * 2;   // Q rows, K rows, V rows
+  return static_cast<size_t>(3) * kMaxKeys * attention_row_stride(d) * 2 +
+         static_cast<size_t>(kAttnPairs) * 16 * attention_p_stride() * 2 +
+         static_cast<size_t>(2) * kAttnPairs * 2 * 16 * 4;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -275,24 +284,31 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 // Causal attention of the query heads sharing one KV head, for a chunk of a
 // row's prompt positions, on the tensor cores: grid (chunks, kv heads, rows),
-// kAttnWarps warps.  The chunk's query rows (position-major, head-minor), the
-// row's K and V up to the chunk's last position are staged in shared memory;
-// warp w takes query rows [16w, 16w + 16) through
-//   S = Q K^T (m16n8k16 bf16 MMAs, fp32 sums) -> scores bf16(bf16(S) / sqrt(d))
-//   with the causal mask (:356-367) -> softmax in fp32 rounded to bf16
-//   (:368-377) -> O = P V (the probabilities feed the second MMA straight from
-//   the accumulator layout) -> bf16(O).
+// kAttnWarps warps in kAttnPairs pairs.  The chunk's query rows
+// (position-major, head-minor) and the row's K and V up to the chunk's last
+// position are staged in shared memory.  Pair p takes query rows
+// [16p, 16p + 16):
+//   S = Q K^T (m16n8k16 bf16 MMAs, fp32 sums), warp h of the pair over keys
+//   [64h, 64h + 64) -> scores bf16(bf16(S) / sqrt(d)) with the causal mask
+//   (:356-367) -> softmax in fp32 rounded to bf16 (:368-377): each warp's row
+//   maxima and sums of exponentials meet through shared memory, so every
+//   probability is exp(s - row max) / row sum over all the row's keys ->
+//   P in shared memory -> O = P V, warp h of the pair over output dimensions
+//   [h D/2, (h + 1) D/2) and all keys -> bf16(O).
+// Every warp reaches every __syncthreads (pairs without rows skip the math).
 // Requires block_size <= 128 and d in {64, 128}.
 template <int D>
-__global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
+__global__ void __launch_bounds__(kAttnWarps * 32, 1) causal_attention_mma(
     const bf16 *q, const bf16 *payload, RowSpans spans, bf16 *out, int layer, int L, int nq, int nkv, int bs,
     float sqrt_d) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int S = D + 8;   // shared-memory row stride (bf16)
+  constexpr int SP = kMaxKeys + 8;   // probability row stride (bf16)
+  constexpr int DT = D / 16;         // output 8-column tiles per warp in O = P V
   const int chunk = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int count = spans.count[row];
   const int p0 = chunk * kAttnChunk;
-  if (p0 >= count) return;
+  if (p0 >= count) return;   // uniform over the CTA
   const int p1 = min(count, p0 + kAttnChunk);   // positions [p0, p1) query keys [0, p1)
   const int groups = nq / nkv, kvw = nkv * D;
   const int rows = (p1 - p0) * groups;          // query rows of this CTA
@@ -300,6 +316,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   bf16 *qs = reinterpret_cast<bf16 *>(smem);
   bf16 *ks = qs + kMaxKeys * S;
   bf16 *vs = ks + kMaxKeys * S;
+  bf16 *ps = vs + kMaxKeys * S;                                     // [pair][16][SP]
+  float *red_max = reinterpret_cast<float *>(ps + kAttnPairs * 16 * SP);   // [pair][half][16]
+  float *red_sum = red_max + kAttnPairs * 2 * 16;                   // [pair][half][16]
   const int64_t block_elems = static_cast<int64_t>(bs) * kvw;
   const bf16 *kg = payload + (static_cast<int64_t>(layer) * kBatch + row) * block_elems + kvh * D;
   const bf16 *vg = kg + static_cast<int64_t>(L) * kBatch * block_elems;
@@ -326,37 +345,41 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   cp_async_wait_all();
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = warp * 16;
-  if (m0 >= rows) return;
+  const int pair = warp >> 1, half = warp & 1;
+  const int m0 = pair * 16;
+  const bool busy = m0 < rows;
   const int g = lane >> 2, tq = lane & 3;
-  // S = Q K^T: 16 query rows x up to 128 keys (16 n-tiles of 8)
-  float sc[16][4];
+  const int rA = m0 + g, rB = rA + 8;
+  const int posA = rA < rows ? p0 + rA / groups : -1, posB = rB < rows ? p0 + rB / groups : -1;
+  const int ntiles = keys / 8;           // 8-key tiles holding keys
+  const int nt0 = half * (kHalfKeys / 8);  // this warp's first key tile
+  // S = Q K^T over this warp's 64 keys (8 n-tiles of 8)
+  float sc[kHalfKeys / 8][4];
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-  const int ntiles = keys / 8;
+  for (int nt = 0; nt < kHalfKeys / 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+  if (busy) {
 #pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    uint32_t a[4];
-    ldsm_x4(a, qs + (m0 + (lane & 15)) * S + kk * 16 + (lane >> 4) * 8);
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, qs + (m0 + (lane & 15)) * S + kk * 16 + (lane >> 4) * 8);
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      if (nt < ntiles) {
-        uint32_t bfrag[2];
-        ldsm_x2(bfrag, ks + (nt * 8 + (lane & 7)) * S + kk * 16 + ((lane >> 3) & 1) * 8);
-        mma16816(sc[nt], a, bfrag);
+      for (int nt = 0; nt < kHalfKeys / 8; ++nt) {
+        if (nt0 + nt < ntiles) {
+          uint32_t bfrag[2];
+          ldsm_x2(bfrag, ks + ((nt0 + nt) * 8 + (lane & 7)) * S + kk * 16 + ((lane >> 3) & 1) * 8);
+          mma16816(sc[nt], a, bfrag);
+        }
       }
     }
   }
-  // scores, causal mask, softmax per query row (rows g and g + 8 of the warp's tile)
-  const int rA = m0 + g, rB = rA + 8;
-  const int posA = rA < rows ? p0 + rA / groups : -1, posB = rB < rows ? p0 + rB / groups : -1;
+  // scores and causal mask; this warp's row maxima
   float mxA = -INFINITY, mxB = -INFINITY;
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
+  for (int nt = 0; nt < kHalfKeys / 8; ++nt) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const int key = nt * 8 + tq * 2 + j;
-      const bool inA = nt < ntiles && key <= posA, inB = nt < ntiles && key <= posB;
+      const int key = (nt0 + nt) * 8 + tq * 2 + j;
+      const bool inA = nt0 + nt < ntiles && key <= posA, inB = nt0 + nt < ntiles && key <= posB;
       sc[nt][j] = inA ? r(__fdiv_rn(r(sc[nt][j]), sqrt_d)) : -INFINITY;
       sc[nt][2 + j] = inB ? r(__fdiv_rn(r(sc[nt][2 + j]), sqrt_d)) : -INFINITY;
       mxA = fmaxf(mxA, sc[nt][j]);
@@ -367,11 +390,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
   mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
   mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+  float *my_max = red_max + (pair * 2 + half) * 16, *my_sum = red_sum + (pair * 2 + half) * 16;
+  const float *other_max = red_max + (pair * 2 + (half ^ 1)) * 16;
+  const float *other_sum = red_sum + (pair * 2 + (half ^ 1)) * 16;
+  if (tq == 0) {
+    my_max[g] = mxA;
+    my_max[g + 8] = mxB;
+  }
+  __syncthreads();
+  // the row maximum over all keys (max is exact in any order)
+  mxA = fmaxf(mxA, other_max[g]);
+  mxB = fmaxf(mxB, other_max[g + 8]);
   if (posA < 0) mxA = 0.f;   // padding rows: no keys, all probabilities 0
   if (posB < 0) mxB = 0.f;
   float sumA = 0.f, sumB = 0.f;
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
+  for (int nt = 0; nt < kHalfKeys / 8; ++nt) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       sc[nt][j] = sc[nt][j] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][j], mxA));
@@ -384,24 +418,48 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
   sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
   sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+  if (tq == 0) {
+    my_sum[g] = sumA;
+    my_sum[g + 8] = sumB;
+  }
+  __syncthreads();
+  // both halves in the same order on both warps: keys [0, 64) then [64, 128)
+  {
+    const float lowA = half == 0 ? sumA : other_sum[g], highA = half == 0 ? other_sum[g] : sumA;
+    const float lowB = half == 0 ? sumB : other_sum[g + 8], highB = half == 0 ? other_sum[g + 8] : sumB;
+    sumA = lowA + highA;
+    sumB = lowB + highB;
+  }
   if (posA < 0) sumA = 1.f;
   if (posB < 0) sumB = 1.f;
-  // O = P V: P (16 x keys) as the A operand straight from the accumulator tiles
-  float o[D / 8][4];
+  // P = bf16(e / sum) into the pair's probability rows (this warp's keys)
+  bf16 *prow = ps + pair * 16 * SP;
 #pragma unroll
-  for (int nt = 0; nt < D / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  for (int nt = 0; nt < kHalfKeys / 8; ++nt) {
+    if (busy && nt0 + nt < ntiles) {
+      const int key = (nt0 + nt) * 8 + tq * 2;
+      *reinterpret_cast<uint32_t *>(prow + g * SP + key) =
+          pack_bf16(r(__fdiv_rn(sc[nt][0], sumA)), r(__fdiv_rn(sc[nt][1], sumA)));
+      *reinterpret_cast<uint32_t *>(prow + (g + 8) * SP + key) =
+          pack_bf16(r(__fdiv_rn(sc[nt][2], sumB)), r(__fdiv_rn(sc[nt][3], sumB)));
+    }
+  }
+  __syncthreads();
+  if (!busy) return;
+  // O = P V over all keys, this warp's output columns [half * D / 2, (half + 1) * D / 2)
+  float o[DT][4];
 #pragma unroll
-  for (int kj = 0; kj < 8; ++kj) {
+  for (int nt = 0; nt < DT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  const int dt0 = half * DT;
+#pragma unroll
+  for (int kj = 0; kj < kMaxKeys / 16; ++kj) {
     if (kj * 16 < keys) {
       uint32_t a[4];
-      a[0] = pack_bf16(r(__fdiv_rn(sc[2 * kj][0], sumA)), r(__fdiv_rn(sc[2 * kj][1], sumA)));
-      a[1] = pack_bf16(r(__fdiv_rn(sc[2 * kj][2], sumB)), r(__fdiv_rn(sc[2 * kj][3], sumB)));
-      a[2] = pack_bf16(r(__fdiv_rn(sc[2 * kj + 1][0], sumA)), r(__fdiv_rn(sc[2 * kj + 1][1], sumA)));
-      a[3] = pack_bf16(r(__fdiv_rn(sc[2 * kj + 1][2], sumB)), r(__fdiv_rn(sc[2 * kj + 1][3], sumB)));
+      ldsm_x4(a, prow + (lane & 15) * SP + kj * 16 + (lane >> 4) * 8);
 #pragma unroll
-      for (int nt = 0; nt < D / 8; ++nt) {
+      for (int nt = 0; nt < DT; ++nt) {
         uint32_t bfrag[2];
-        ldsm_x2_trans(bfrag, vs + (kj * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * S + nt * 8);
+        ldsm_x2_trans(bfrag, vs + (kj * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * S + (dt0 + nt) * 8);
         mma16816(o[nt], a, bfrag);
       }
     }
@@ -410,8 +468,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) causal_attention_mma(
   const int64_t tA = spans.start[row] + posA, tB = spans.start[row] + posB;
   const int hA = kvh * groups + rA % groups, hB = kvh * groups + rB % groups;
 #pragma unroll
-  for (int nt = 0; nt < D / 8; ++nt) {
-    const int dim = nt * 8 + tq * 2;
+  for (int nt = 0; nt < DT; ++nt) {
+    const int dim = (dt0 + nt) * 8 + tq * 2;
     if (posA >= 0)
       *reinterpret_cast<__nv_bfloat162 *>(out + tA * nq * D + hA * D + dim) = __floats2bfloat162_rn(o[nt][0], o[nt][1]);
     if (posB >= 0)
