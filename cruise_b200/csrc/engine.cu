@@ -751,9 +751,9 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     return -4;
   }
   if (m.bs > prefill::kMaxKeys || (m.d != 64 && m.d != 128) || m.nq / m.nkv * prefill::kAttnChunk > prefill::kMaxKeys ||
-      m.I % 4 != 0 || m.H % 8 != 0 || m.H > 8 * prefill::kNormThreads * prefill::kNormChunks) {
+      m.I % 8 != 0 || m.H % 8 != 0 || m.H > 8 * prefill::kNormThreads * prefill::kNormChunks) {
     e->last_error = "cruise_epoch_prefill: needs block size <= 128, head size 64 or 128, <= 8 query heads per KV head,"
-                    " an intermediate size divisible by 4 and a hidden size divisible by 8, at most 8192";
+                    " an intermediate size divisible by 8 and a hidden size divisible by 8, at most 8192";
     return -1;
   }
   std::vector<int64_t> tok;

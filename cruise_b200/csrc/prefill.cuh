@@ -479,31 +479,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) causal_attention_mma(
 
 // silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398); y
 // rows are [gate (I) | up (I)] per token, the GEMM's fp32 sums already
-// rounded to bf16 by the GEMM.  Four consecutive elements per thread (8-byte
-// loads and stores): I % 4 == 0 and T * I < 2^31, both checked by the host.
+// rounded to bf16 by the GEMM.  Eight consecutive elements per thread
+// (16-byte loads and stores): I % 8 == 0 and T * I < 2^31, both checked by
+// the host.
 __device__ __forceinline__ float swiglu_one(float gate, float up) {
   const float silu = r(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
   return __fmul_rn(silu, up);
 }
 
 __global__ void swiglu(const bf16 *y, bf16 *act, int T, int I) {
-  const int quads = I >> 2;
-  const int count = T * quads;
+  const int octs = I >> 3;
+  const int count = T * octs;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
-    const int t = e / quads, i = (e - t * quads) << 2;
+    const int t = e / octs, i = (e - t * octs) << 3;
     const bf16 *row = y + static_cast<int64_t>(t) * 2 * I;
-    const uint2 gq = *reinterpret_cast<const uint2 *>(row + i);
-    const uint2 uq = *reinterpret_cast<const uint2 *>(row + I + i);
-    const __nv_bfloat162 *g2 = reinterpret_cast<const __nv_bfloat162 *>(&gq);
-    const __nv_bfloat162 *u2 = reinterpret_cast<const __nv_bfloat162 *>(&uq);
-    __nv_bfloat162 lo = __floats2bfloat162_rn(swiglu_one(__low2float(g2[0]), __low2float(u2[0])),
-                                              swiglu_one(__high2float(g2[0]), __high2float(u2[0])));
-    __nv_bfloat162 hi = __floats2bfloat162_rn(swiglu_one(__low2float(g2[1]), __low2float(u2[1])),
-                                              swiglu_one(__high2float(g2[1]), __high2float(u2[1])));
-    uint2 packed;
-    packed.x = *reinterpret_cast<uint32_t *>(&lo);
-    packed.y = *reinterpret_cast<uint32_t *>(&hi);
-    *reinterpret_cast<uint2 *>(act + static_cast<int64_t>(t) * I + i) = packed;
+    float g[8], u[8], v[8];
+    unpack8(*reinterpret_cast<const uint4 *>(row + i), g);
+    unpack8(*reinterpret_cast<const uint4 *>(row + I + i), u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = swiglu_one(g[k], u[k]);
+    *reinterpret_cast<uint4 *>(act + static_cast<int64_t>(t) * I + i) = pack8(v);
   }
 }
 
