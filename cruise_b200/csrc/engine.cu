@@ -360,6 +360,8 @@ void default_rope(const Engine *e, std::vector<uint16_t> &cos_t, std::vector<uin
   }
 }
 
+void prefill_release(Engine *e);
+
 void destroy_engine(Engine *e) {
   if (e == nullptr) return;
   cudaSetDevice(e->device);
@@ -373,12 +375,7 @@ void destroy_engine(Engine *e) {
   cudaFree(e->xchg);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->h_stream) cudaFreeHost(e->h_stream);
-  if (e->prefill != nullptr) {
-    if (e->prefill->blas != nullptr) cublasDestroy(e->prefill->blas);
-    cudaFree(e->prefill->weights);
-    cudaFree(e->prefill->work);
-    delete e->prefill;
-  }
+  prefill_release(e);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -674,7 +671,21 @@ cublasStatus_t prefill_gemm(cublasHandle_t blas, const bf16 *x, const bf16 *w, v
                       y_type, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
 }
 
+// Frees the prefill state (cuBLAS handle, untiled weights, buffers), whole or
+// partly built; cudaFree waits for the work queued on them.
+void prefill_release(Engine *e) {
+  PrefillState *ps = e->prefill;
+  if (ps == nullptr) return;
+  if (ps->blas != nullptr) cublasDestroy(ps->blas);
+  cudaFree(ps->weights);
+  cudaFree(ps->work);
+  delete ps;
+  e->prefill = nullptr;
+}
+
 // Builds the untiled weights (once) and buffers for kBatch * block_size tokens.
+// A failure leaves the state partly built; the caller releases it, so the next
+// call starts over instead of using it.
 int32_t prefill_prepare(Engine *e) {
   if (e->prefill != nullptr) return 0;
   const ModelDims &m = e->m;
@@ -775,7 +786,10 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     }
   }
   int32_t rc = prefill_prepare(e);
-  if (rc != 0) return rc;
+  if (rc != 0) {
+    prefill_release(e);
+    return rc;
+  }
   PrefillState *ps = e->prefill;
   const size_t payload_bytes = static_cast<size_t>(import_payload_bytes(e));
   cudaError_t err = cudaSuccess;
