@@ -19,7 +19,9 @@ Contents
              and the host bridge ``native/resident_epoch_bridge.cpp:424-649``.
 
 Parity pin: ``tests/golden/make_golden.py`` imports the reference's own
-``PagedQwenDecoderStep`` (tiny constants patched in, the documented CPU op
-bodies registered) and records its outputs; ``tests/test_oracle_golden.py``
-checks this oracle bit-exactly against those fixtures.
+``PagedQwenDecoderStep`` (geometry constants patched in, the documented CPU op
+bodies registered) and records its outputs.  The geometries are tiny and a
+1-layer shape with the 7B model's attention (7 query heads per KV head, head
+size 128).  ``tests/test_oracle_golden.py`` checks this oracle bit-exactly
+against those fixtures.
 """

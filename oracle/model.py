@@ -64,6 +64,13 @@ QWEN25_7B = OracleConfig(
     num_layers=28, hidden=3584, num_heads=28, num_kv_heads=4, head_dim=128,
     intermediate=18944, vocab=152064, block_size=128,
 )
+# the 7B model's attention shape -- 7 query heads per KV head, head size 128,
+# rope theta 1e6 -- at a size the reference module runs in about a second on
+# the CPU (golden fixture tests/golden/decoder_gqa7_d128.npz)
+GQA7_D128 = OracleConfig(
+    num_layers=1, hidden=1792, num_heads=14, num_kv_heads=2, head_dim=128,
+    intermediate=1024, vocab=4096, block_size=16,
+)
 
 
 def tensor_shapes(cfg: OracleConfig) -> dict[str, tuple[int, ...]]:

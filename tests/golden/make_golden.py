@@ -3,14 +3,21 @@
 
 Run in the container that holds the reference checkout (default path below):
 
-    python tests/golden/make_golden.py --reference /path/to/Cruise
+    python tests/golden/make_golden.py --reference /path/to/Cruise [--geometry tiny|gqa7]
 
 It imports ``PagedQwenDecoderStep`` from
 ``history/attempts/g4c-attempt69c-b4-air/batched_decoder_step.py`` unmodified,
-overrides its module-level geometry constants with the tiny configuration
-(2 layers, hidden 256, 4/2 heads of 64, intermediate 688, vocab 4096, block 16,
-logical capacity 32), and registers for the CPU the bodies its custom ops are
-documented to compute:
+overrides its module-level geometry constants with one of two configurations,
+and registers for the CPU the bodies its custom ops are documented to
+compute.  The configurations:
+
+* ``tiny``: 2 layers, hidden 256, 4/2 heads of 64, intermediate 688, vocab
+  4096, block 16, logical capacity 32 -> ``decoder_tiny.npz``;
+* ``gqa7``: the 7B model's attention shape at a small size, 1 layer, hidden
+  1792, 14/2 heads of 128 (7 query heads per KV head), intermediate 1024,
+  vocab 4096, block 16 -> ``decoder_gqa7_d128.npz``.
+
+The custom-op bodies:
 
 * ``g4a_linear_t::mm_t``          = ``torch.mm(x, W.T)``   (``g4a_linear_t.py:17-18``)
 * ``g4a_linear_t_bias::linear``   = ``F.linear(x, W, b)``  (``g4a_linear_t_bias.py:18-21``)
@@ -20,7 +27,7 @@ documented to compute:
                                     (``bf16-barrier/bf16_barrier.cpp:47-50``)
 
 Weights come from the seeded generator (seed 0); caches and step inputs from a
-seeded torch generator.  Outputs go to ``tests/golden/decoder_tiny.npz``.
+seeded torch generator.
 """
 
 from __future__ import annotations
@@ -37,9 +44,10 @@ import torch.nn.functional as F
 REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO))
 
-from oracle.model import TINY, seeded_weights  # noqa: E402
+from oracle.model import GQA7_D128, TINY, seeded_weights  # noqa: E402
 
 MODULE = "history/attempts/g4c-attempt69c-b4-air/batched_decoder_step.py"
+GEOMETRIES = {"tiny": (TINY, "decoder_tiny.npz"), "gqa7": (GQA7_D128, "decoder_gqa7_d128.npz")}
 
 
 def register_cpu_ops() -> None:
@@ -65,11 +73,10 @@ def register_cpu_ops() -> None:
     register_cpu_ops.libs = libs  # keep the registrations alive
 
 
-def load_reference(reference: Path):
+def load_reference(reference: Path, cfg):
     spec = importlib.util.spec_from_file_location("ref_batched_decoder_step", reference / MODULE)
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
-    cfg = TINY
     module.NUM_LAYERS = cfg.num_layers
     module.HIDDEN_SIZE = cfg.hidden
     module.INTERMEDIATE_SIZE = cfg.intermediate
@@ -95,12 +102,14 @@ def bits(t: torch.Tensor) -> np.ndarray:
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", type=Path, required=True, help="checkout of the reference project")
-    parser.add_argument("--output", type=Path, default=REPO / "tests/golden/decoder_tiny.npz")
+    parser.add_argument("--geometry", choices=sorted(GEOMETRIES), default="tiny")
+    parser.add_argument("--output", type=Path, default=None)
     args = parser.parse_args()
+    cfg, name = GEOMETRIES[args.geometry]
+    output = args.output or REPO / "tests/golden" / name
     torch.set_num_threads(8)
     register_cpu_ops()
-    ref = load_reference(args.reference)
-    cfg = TINY
+    ref = load_reference(args.reference, cfg)
     weights = seeded_weights(cfg, seed=0)
     model = ref.PagedQwenDecoderStep(dict(weights), batch_size=cfg.batch, physical_blocks=cfg.num_blocks)
 
@@ -126,7 +135,7 @@ def main() -> None:
             token, position, seq_len, block_table, slot, key_cache, value_cache, tiling, active
         )
     np.savez_compressed(
-        args.output,
+        output,
         seed=np.int64(0),
         token=token.numpy(),
         position=position.numpy(),
@@ -141,7 +150,7 @@ def main() -> None:
         value_cache_out=bits(new_value),
         next_position=next_position.numpy(),
     )
-    print(f"wrote {args.output}: argmax per row {logits.reshape(cfg.batch, -1).argmax(-1).tolist()}")
+    print(f"wrote {output}: argmax per row {logits.reshape(cfg.batch, -1).argmax(-1).tolist()}")
 
 
 if __name__ == "__main__":
