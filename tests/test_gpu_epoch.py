@@ -159,3 +159,28 @@ def test_recovery_statuses_preserve_inputs(cuda_ok, tiny_weights, mutate, status
     assert torch.equal(key0.view(torch.int16), key1.view(torch.int16))
     assert torch.equal(value0.view(torch.int16), value1.view(torch.int16))
     engine.close()
+
+
+def test_non_finite_logits_mid_epoch_fall_back(cuda_ok, tiny_weights):
+    """Status 209 on the device (controller :555-556): with a NaN embedding row
+    for the token row 0 emits at the first step, the second step's logits of
+    row 0 are non-finite.  The device must stop the epoch exactly where the
+    oracle does: same history (first step kept), model calls 2, executed
+    counts, FALLBACK reasons and status -- the whole control output."""
+    from test_oracle_epoch import _poisoned_scenario
+
+    _, bad, _ = _poisoned_scenario(tiny_weights)
+    engine = new_engine(weights=bad)
+    oracle = OracleEpochController(OracleDecoder(ORACLE_TINY, bad))
+    sc = make_scenario(vocab=ORACLE_TINY.vocab, seed=6, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    for inputs in prefill_epochs(sc, ORACLE_TINY.block_size, ORACLE_TINY.vocab):
+        assert engine.run(**inputs).status == 0
+        oracle.run(**inputs)
+    inputs = decode_inputs(sc, ORACLE_TINY.block_size)
+    inputs["control"][0] = 4
+    want_history, want_out = oracle.run(**inputs)
+    got = engine.run(**inputs)
+    engine.close()
+    assert want_out[3] == 209
+    np.testing.assert_array_equal(got.history, want_history)
+    np.testing.assert_array_equal(got.control_out, want_out)

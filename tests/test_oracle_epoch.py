@@ -150,3 +150,40 @@ def test_bridge_statuses(weights):
     ok = bridge_execute(ctl, 1, 2, configured_eos=4095, **base)
     assert ok.ret == 0 and ok.commit_state == 2 and ok.device_status == 0 and ok.executed[0] == 2
     assert ok.declared_input_bytes == 260 and ok.declared_output_bytes == 368
+
+
+def _poisoned_scenario(weights, seed=6):
+    """Seeded cohort (rows 0-2 active) whose row 0 emits, at the first step of a
+    K=4 epoch, a token that is in no prompt; returns that token and weights
+    whose embedding row for it is NaN."""
+    sc, probe = prefilled(weights, seed=seed, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    inputs = decode_inputs(sc, TINY.block_size)
+    inputs["control"][0] = 4
+    history, out = probe.run(**inputs)
+    assert out[3] == 0 and out[4] == 4
+    poison = int(history[0, 0])
+    assert all(poison not in p for p in sc.prompts) and poison not in history[0, 1:3].tolist()
+    bad = dict(weights)
+    embed = weights["model.embed_tokens.weight"].clone()
+    embed[poison] = float("nan")
+    bad["model.embed_tokens.weight"] = embed
+    return poison, bad, history
+
+
+def test_non_finite_logits_mid_epoch_fall_back(weights):
+    """209 (controller :555-556): the second step's logits of row 0 are NaN.  The
+    epoch stops there: the first step's tokens stay in the history, model
+    calls = 2, executed = 1 per active row, every row finishes with FALLBACK,
+    and the resident state does not advance (:599-614 is not reached)."""
+    poison, bad, clean_history = _poisoned_scenario(weights)
+    sc, ctl = prefilled(bad, seed=6, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    res_position = list(ctl.res_position)
+    inputs = decode_inputs(sc, TINY.block_size)
+    inputs["control"][0] = 4
+    history, out = ctl.run(**inputs)
+    assert out[3] == 209 and out[4] == 2
+    assert history[0, :3].tolist() == clean_history[0, :3].tolist() and history[0, 0] == poison
+    assert (history[1:] == -1).all() and history[0, 3] == -1
+    assert list(out[14:18]) == [1, 1, 1, 0]           # executed
+    assert list(out[18:22]) == [3, 3, 3, 3]           # every row finishes with FALLBACK
+    assert list(ctl.res_position) == res_position
