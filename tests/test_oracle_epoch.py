@@ -187,3 +187,20 @@ def test_non_finite_logits_mid_epoch_fall_back(weights):
     assert list(out[14:18]) == [1, 1, 1, 0]           # executed
     assert list(out[18:22]) == [3, 3, 3, 3]           # every row finishes with FALLBACK
     assert list(ctl.res_position) == res_position
+
+
+def test_replay_after_a_mid_epoch_fallback_matches_a_clean_run(weights):
+    """After a mid-epoch fallback the resident state has not moved (:599-614 is
+    not reached), so the same inputs -- same generations -- pass continuity on
+    replay; the replay rewrites the KV slots the failed epoch touched and emits
+    the tokens of a run that never failed."""
+    _, bad, clean_history = _poisoned_scenario(weights)
+    sc, ctl = prefilled(bad, seed=6, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    inputs = decode_inputs(sc, TINY.block_size)
+    inputs["control"][0] = 4
+    _, out = ctl.run(**inputs)
+    assert out[3] == 209
+    ctl.decoder = OracleDecoder(TINY, weights)        # the fault is gone
+    history, out = ctl.run(**inputs)
+    assert out[3] == 0 and out[4] == 4
+    np.testing.assert_array_equal(history, clean_history)
