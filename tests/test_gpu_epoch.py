@@ -184,3 +184,30 @@ def test_non_finite_logits_mid_epoch_fall_back(cuda_ok, tiny_weights):
     assert want_out[3] == 209
     np.testing.assert_array_equal(got.history, want_history)
     np.testing.assert_array_equal(got.control_out, want_out)
+
+
+def test_replay_after_a_mid_epoch_fallback(cuda_ok, tiny_weights):
+    """After the device's 209 the resident state has not moved: with the fault
+    removed (the embedding row restored), the same inputs are accepted and the
+    device emits what the oracle emits on the same replay."""
+    from test_oracle_epoch import _poisoned_scenario
+
+    _, bad, _ = _poisoned_scenario(tiny_weights)
+    engine = new_engine(weights=bad)
+    oracle = OracleEpochController(OracleDecoder(ORACLE_TINY, bad))
+    sc = make_scenario(vocab=ORACLE_TINY.vocab, seed=6, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    for inputs in prefill_epochs(sc, ORACLE_TINY.block_size, ORACLE_TINY.vocab):
+        assert engine.run(**inputs).status == 0
+        oracle.run(**inputs)
+    inputs = decode_inputs(sc, ORACLE_TINY.block_size)
+    inputs["control"][0] = 4
+    assert engine.run(**inputs).status == 209
+    oracle.run(**inputs)
+    engine.set_weight("model.embed_tokens.weight", tiny_weights["model.embed_tokens.weight"])
+    oracle.decoder = OracleDecoder(ORACLE_TINY, tiny_weights)
+    want_history, want_out = oracle.run(**inputs)
+    got = engine.run(**inputs)
+    engine.close()
+    assert want_out[3] == 0
+    np.testing.assert_array_equal(got.history, want_history)
+    np.testing.assert_array_equal(got.control_out, want_out)
