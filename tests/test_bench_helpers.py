@@ -33,3 +33,42 @@ def test_all_rows_forcing_matches_row_by_row_prefill():
     h2, c2 = batched.run(**decode_inputs(sc, TINY.block_size))
     np.testing.assert_array_equal(h1, h2)
     np.testing.assert_array_equal(c1, c2)
+
+
+def test_roofline_numerator_matches_the_checkpoint_tensor_sizes():
+    """The bench's algorithmic bytes per decode step: every 7B tensor but the
+    embedding table streams once (14,141,238,272 B, counted independently from
+    the checkpoint map), 57,344 B of K/V per context position per active row,
+    and one 7,168-byte embedding row per active row."""
+    from cruise_b200.model_config import QWEN25_7B
+    from oracle.model import QWEN25_7B as ORACLE_7B, tensor_shapes
+
+    streamed = sum(int(np.prod(shape)) * 2 for name, shape in tensor_shapes(ORACLE_7B).items()
+                   if name != "model.embed_tokens.weight")
+    assert bench.weight_bytes_per_step(QWEN25_7B) == streamed == 14_141_238_272
+    contexts = [3, 4, 5, 6]
+    kv_token = 2 * 28 * 4 * 128 * 2
+    assert kv_token == 57_344
+    assert bench.step_bytes(QWEN25_7B, contexts) == streamed + kv_token * (sum(contexts) + 4) + 4 * 7_168
+
+
+def test_tensor_parallel_shards_cover_the_step_once():
+    """Summed over the ranks, the shards stream every weight once, except the
+    norms, which each rank keeps whole, and the KV heads replicated when there
+    are more ranks than KV heads (TP = 8 over 4 heads)."""
+    from cruise_b200.model_config import QWEN25_7B, TpShard
+
+    cfg = QWEN25_7B
+    contexts = [10, 20, 30, 40]
+    single = bench.step_bytes(cfg, contexts)
+    assert bench.shard_step_bytes(cfg, TpShard.of(cfg, 0, 1), contexts) == single
+    norms = 2 * (2 * cfg.num_layers * cfg.hidden + cfg.hidden)
+    embed_rows = len(contexts) * cfg.hidden * 2
+    for world in (2, 4, 8):
+        total = sum(bench.shard_step_bytes(cfg, TpShard.of(cfg, r, world), contexts) for r in range(world))
+        extra_kv_heads = max(world, cfg.num_kv_heads) - cfg.num_kv_heads
+        kv_extra = 2 * cfg.num_layers * extra_kv_heads * cfg.head_dim * 2 * (sum(contexts) + len(contexts))
+        qkv_extra = 2 * cfg.num_layers * extra_kv_heads * cfg.head_dim * (cfg.hidden + 1) * 2
+        pad = sum(TpShard.of(cfg, r, world).ni for r in range(world)) - cfg.intermediate
+        mlp_pad = 2 * cfg.num_layers * 3 * pad * cfg.hidden
+        assert total == single + (world - 1) * (norms + embed_rows) + kv_extra + qkv_extra + mlp_pad, world
