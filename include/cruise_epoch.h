@@ -256,8 +256,12 @@ int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,
  * token prompt[len-1].  The projections run as cuBLAS bf16 GEMMs on an
  * untiled copy of the layer weights made on the first call (kept until
  * destroy); attention, norms, rope and SwiGLU follow the decoder step's
- * rounding points.  0, -1 bad arguments, -2 library failure, -4 tensor-
- * parallel engine, or a CUDA error code. */
+ * rounding points.  Geometry limits: block_size <= 128, head size 64 or
+ * 128, at most 8 query heads per KV head, intermediate and hidden sizes
+ * divisible by 8, hidden size at most 8192 (others return -1 with the reason
+ * in cruise_epoch_last_error).  0, -1 bad arguments, -2 library failure, -4
+ * tensor-parallel engine, or a CUDA error code; after a failure in the first
+ * call's set-up the next call starts the set-up over. */
 int32_t cruise_epoch_prefill(void *engine, const int64_t *prompt_tokens,
                              const int32_t *prompt_lens, int32_t stride);
 
