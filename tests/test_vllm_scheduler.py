@@ -323,3 +323,27 @@ def test_eos_from_a_single_stop_token_without_tokenizer(tmp_path):
     none = Request(request_id="n", client_index=0, prompt_token_ids=[6], pooling_params=None,
                    sampling_params=SamplingParams(temperature=0.0, max_tokens=4))
     assert request_rejection_reason(none) == "missing-eos"
+
+
+def test_resident_rows_reuse_freed_rows_with_fresh_generations():
+    """Row bookkeeping (the reference's scheduler.py:62-86): a request keeps its
+    row while it stays in the batch; a request that leaves frees its row and
+    its device ownership; a new request takes the lowest free row and a
+    generation never used before; more requests than rows, or an exhausted
+    32-bit generation space, are errors rather than silent reuse."""
+    from cruise_b200.scheduler import ResidentRows
+
+    rows = ResidentRows()
+    rows.assign(("a", "b", "c"), 4)
+    assert rows.rows == {"a": 0, "b": 1, "c": 2} and rows.generations == {"a": 1, "b": 2, "c": 3}
+    rows.device_owned.update({"a", "b"})
+    rows.assign(("a", "c", "d", "e"), 4)               # b leaves; d takes its row, e the last one
+    assert rows.rows == {"a": 0, "c": 2, "d": 1, "e": 3}
+    assert rows.generations["d"] == 4 and rows.generations["e"] == 5 and rows.device_owned == {"a"}
+    with pytest.raises(RuntimeError, match="exhausted"):
+        rows.assign(("a", "c", "d", "e", "f"), 4)
+    late = ResidentRows(next_generation=2**31 - 1)
+    late.assign(("x",), 4)
+    assert late.generations == {"x": 2**31 - 1}
+    with pytest.raises(RuntimeError, match="generation space"):
+        late.assign(("x", "y"), 4)
