@@ -30,6 +30,7 @@ from vllm.v1.core.sched.scheduler import Scheduler
 from vllm.v1.outputs import ModelRunnerOutput
 
 from .config import ResidentEpochConfig, epoch_steps
+from .benchmark_metrics import ResidentEpochBenchmarkMetrics
 from .contract import CONTRACT_VERSION, ResidentEpochPlan, ResidentEpochRequest, attach_plan, get_plan, get_result
 from .eligibility import effective_eos, request_rejection_reason
 from .model_config import PRESETS
@@ -89,6 +90,7 @@ class ResidentEpochScheduler(Scheduler):
         self.last_rejection: str | None = None
         self.last_plan: ResidentEpochPlan | None = None
         self.last_result: Any | None = None
+        self.benchmark_metrics = ResidentEpochBenchmarkMetrics.from_env()
         if self.vllm_config.speculative_config is not None:
             raise ValueError("resident epoch scheduler cannot be combined with speculative decoding")
         if self.scheduler_config.async_scheduling:
@@ -110,6 +112,7 @@ class ResidentEpochScheduler(Scheduler):
         scheduler.last_rejection = None
         scheduler.last_plan = None
         scheduler.last_result = None
+        scheduler.benchmark_metrics = ResidentEpochBenchmarkMetrics.from_env()
         return scheduler
 
     # -- host isolation (scheduler.py:102-162) ------------------------------------------
@@ -165,6 +168,7 @@ class ResidentEpochScheduler(Scheduler):
                 raise RuntimeError("isolated host lane created a resident plan")
             rejection = lane_reason
         self.last_rejection, self.last_plan, self.last_result = rejection, plan, None
+        self.benchmark_metrics.record_schedule(plan, rejection)
         if plan is not None:
             attach_plan(output, plan)
         else:
@@ -253,6 +257,7 @@ class ResidentEpochScheduler(Scheduler):
         if result is None:
             raise RuntimeError("resident epoch plan did not receive execution metadata")
         self.last_result = result
+        self.benchmark_metrics.record_result(result)
         sampled = {r: list(model_runner_output.sampled_token_ids[model_runner_output.req_id_to_index[r]])
                    for r in plan.req_ids}
         result.validate_against(plan, sampled)
