@@ -204,3 +204,62 @@ def test_replay_after_a_mid_epoch_fallback_matches_a_clean_run(weights):
     history, out = ctl.run(**inputs)
     assert out[3] == 0 and out[4] == 4
     np.testing.assert_array_equal(history, clean_history)
+
+
+# The reference's epoch case matrix (g4c-attempt69e-r5-*/prepare_inputs.py:12-26):
+# K, and per row A(ctive) / E(mpty: never admitted) / F(inished: inactive with
+# its length at position + 1).
+CASE_MATRIX = [
+    ("k1-heterogeneous", 1, "AAAA"),
+    ("k2-heterogeneous", 2, "AAAA"),
+    ("k4-heterogeneous", 4, "AAAA"),
+    ("k8-all-active", 8, "AAAA"),
+    ("active-empty-alternating", 4, "AEAE"),
+    ("finished-active-empty-active", 4, "FAEA"),
+    ("independent-early-eos", 4, "AAAA"),
+]
+
+
+@pytest.mark.parametrize("name, k, pattern", CASE_MATRIX, ids=[c[0] for c in CASE_MATRIX])
+def test_epoch_case_matrix(weights, name, k, pattern):
+    """Per row: an active row runs until its own EOS or K steps (reason EOS 1 or
+    MAX_STEPS 2) and its resident state advances by what it ran; an empty row
+    finishes EMPTY (4), a finished row ALREADY_FINISHED (5), and neither
+    emits, runs or touches its blocks.  Model calls are the longest row's
+    steps; the control output counts the initially and finally active rows."""
+    active_rows = tuple(1 if c == "A" else 0 for c in pattern)
+    sc, ctl = prefilled(weights, seed=11, active_rows=active_rows, k=k, budget=(8, 8))
+    inputs = decode_inputs(sc, TINY.block_size)
+    for r, c in enumerate(pattern):
+        if c == "F":
+            inputs["token"][r], inputs["position"][r], inputs["seq_len"][r] = 7, 3, 4
+            inputs["slot"][r] = compute_slot(TINY, inputs["block_table"], r, 3)
+        if c != "A":
+            assert inputs["control"][7 + r] == 0
+    if name == "independent-early-eos":
+        # row r's EOS is the token it emits at step r: the rows stop one after another
+        _, probe = prefilled(weights, seed=11, active_rows=active_rows, k=k, budget=(8, 8))
+        clean, _ = probe.run(**inputs)
+        for r in range(4):
+            inputs["control"][1 + r] = int(clean[r, r])
+    eos = [int(inputs["control"][1 + r]) for r in range(4)]
+    key0 = ctl.key.clone()
+    history, out = ctl.run(**inputs)
+    assert out[3] == 0 and out[0] == k
+    executed, reasons = list(out[14:18]), list(out[18:22])
+    for r, c in enumerate(pattern):
+        column = [int(t) for t in history[:, r]]
+        if c != "A":
+            assert column == [-1] * 8 and executed[r] == 0 and reasons[r] == (4 if c == "E" else 5)
+            for block in sc.block_table[r]:
+                assert torch.equal(ctl.key[:, int(block)], key0[:, int(block)])
+            continue
+        emitted = [t for t in column if t >= 0]
+        stop = next((i + 1 for i, t in enumerate(emitted) if t == eos[r]), None)
+        assert len(emitted) == executed[r] == (stop or k) and column[executed[r]:] == [-1] * (8 - executed[r])
+        assert reasons[r] == (1 if stop else 2)
+        assert ctl.res_position[r] == len(sc.prompts[r]) - 1 + executed[r]
+        if name == "independent-early-eos":
+            assert executed[r] == r + 1
+    assert out[4] == max(executed)
+    assert out[22] == pattern.count("A") and out[23] == sum(1 for r in range(4) if reasons[r] == 2)
