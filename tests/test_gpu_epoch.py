@@ -211,3 +211,30 @@ def test_replay_after_a_mid_epoch_fallback(cuda_ok, tiny_weights):
     assert want_out[3] == 0
     np.testing.assert_array_equal(got.history, want_history)
     np.testing.assert_array_equal(got.control_out, want_out)
+
+
+def _case_matrix():
+    from test_oracle_epoch import CASE_MATRIX
+
+    return CASE_MATRIX
+
+
+@pytest.mark.parametrize("name, k, pattern", _case_matrix(), ids=[c[0] for c in _case_matrix()])
+def test_epoch_case_matrix_on_device(cuda_ok, tiny_weights, name, k, pattern):
+    """The reference's epoch case matrix (K 1/2/4/8; active, empty and finished
+    rows; independent early EOS) on the device: token history and the whole
+    control output equal the oracle's."""
+    from test_oracle_epoch import case_matrix_inputs
+
+    sc, inputs = case_matrix_inputs(tiny_weights, name, k, pattern)
+    engine = new_engine(synthetic_seed=0)
+    oracle = OracleEpochController(OracleDecoder(ORACLE_TINY, tiny_weights))
+    for prefill in prefill_epochs(sc, ORACLE_TINY.block_size, ORACLE_TINY.vocab):
+        assert engine.run(**prefill).status == 0
+        oracle.run(**prefill)
+    want_history, want_out = oracle.run(**inputs)
+    got = engine.run(**inputs)
+    engine.close()
+    assert want_out[3] == 0
+    np.testing.assert_array_equal(got.history, want_history)
+    np.testing.assert_array_equal(got.control_out, want_out)

@@ -220,15 +220,11 @@ CASE_MATRIX = [
 ]
 
 
-@pytest.mark.parametrize("name, k, pattern", CASE_MATRIX, ids=[c[0] for c in CASE_MATRIX])
-def test_epoch_case_matrix(weights, name, k, pattern):
-    """Per row: an active row runs until its own EOS or K steps (reason EOS 1 or
-    MAX_STEPS 2) and its resident state advances by what it ran; an empty row
-    finishes EMPTY (4), a finished row ALREADY_FINISHED (5), and neither
-    emits, runs or touches its blocks.  Model calls are the longest row's
-    steps; the control output counts the initially and finally active rows."""
+def case_matrix_inputs(weights, name, k, pattern):
+    """The seeded cohort of one case and the inputs of its decode epoch (after
+    the cohort's prefill epochs)."""
     active_rows = tuple(1 if c == "A" else 0 for c in pattern)
-    sc, ctl = prefilled(weights, seed=11, active_rows=active_rows, k=k, budget=(8, 8))
+    sc = make_scenario(vocab=TINY.vocab, seed=11, active_rows=active_rows, k=k, budget=(8, 8))
     inputs = decode_inputs(sc, TINY.block_size)
     for r, c in enumerate(pattern):
         if c == "F":
@@ -242,6 +238,20 @@ def test_epoch_case_matrix(weights, name, k, pattern):
         clean, _ = probe.run(**inputs)
         for r in range(4):
             inputs["control"][1 + r] = int(clean[r, r])
+    return sc, inputs
+
+
+@pytest.mark.parametrize("name, k, pattern", CASE_MATRIX, ids=[c[0] for c in CASE_MATRIX])
+def test_epoch_case_matrix(weights, name, k, pattern):
+    """Per row: an active row runs until its own EOS or K steps (reason EOS 1 or
+    MAX_STEPS 2) and its resident state advances by what it ran; an empty row
+    finishes EMPTY (4), a finished row ALREADY_FINISHED (5), and neither
+    emits, runs or touches its blocks.  Model calls are the longest row's
+    steps; the control output counts the initially and finally active rows."""
+    sc, inputs = case_matrix_inputs(weights, name, k, pattern)
+    ctl = controller(weights)
+    for prefill in prefill_epochs(sc, TINY.block_size, TINY.vocab):
+        assert ctl.run(**prefill)[1][3] == 0
     eos = [int(inputs["control"][1 + r]) for r in range(4)]
     key0 = ctl.key.clone()
     history, out = ctl.run(**inputs)
