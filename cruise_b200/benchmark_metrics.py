@@ -66,6 +66,7 @@ class ResidentEpochBenchmarkMetrics:
         self.epoch_steps: Counter[int] = Counter()
         self._journal: int | None = None
         if path is not None:
+            path.parent.mkdir(parents=True, exist_ok=True)
             journal = path.with_name(f"{path.stem}.events.jsonl")
             self._journal = os.open(journal, os.O_WRONLY | os.O_CREAT | os.O_APPEND, 0o600)
 

@@ -55,6 +55,14 @@ def test_disabled_by_default_and_flush_once(tmp_path):
     assert not any(p.name.endswith(".tmp") for p in tmp_path.iterdir())
 
 
+def test_missing_directories_are_created(tmp_path):
+    output = tmp_path / "new" / "dir" / "metrics.json"
+    metrics = ResidentEpochBenchmarkMetrics(output)
+    metrics.record_schedule(None, "x")
+    metrics.flush()
+    assert json.loads(output.read_text())["rejections"] == {"x": 1}
+
+
 def test_journal_survives_a_process_that_never_flushes(tmp_path):
     """Events are on disk as they happen: a second writer appends, and the
     replay counts both even though neither wrote its summary."""
