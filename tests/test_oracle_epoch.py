@@ -273,3 +273,33 @@ def test_epoch_case_matrix(weights, name, k, pattern):
             assert executed[r] == r + 1
     assert out[4] == max(executed)
     assert out[22] == pattern.count("A") and out[23] == sum(1 for r in range(4) if reasons[r] == 2)
+
+
+def test_k_step_epoch_equals_k_single_step_epochs(weights):
+    """The reference's host-loop route (g4c_b4_epoch_runner.cpp:245-382: one
+    decoder call per token, the host feeding each token back) and one resident
+    epoch of K steps compute the same thing: tokens, KV cache and resident
+    state after K = 4 single-step epochs equal those after one 4-step epoch."""
+    sc, resident = prefilled(weights, seed=5, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    _, host_loop = prefilled(weights, seed=5, active_rows=(1, 1, 1, 0), budget=(8, 8))
+    inputs = decode_inputs(sc, TINY.block_size)
+    inputs["control"][0] = 4
+    history, out = resident.run(**inputs)
+    assert out[3] == 0 and out[4] == 4
+    step_inputs = {k: np.array(v, copy=True) for k, v in inputs.items()}
+    step_inputs["control"][0] = 1
+    tokens = []
+    for _ in range(4):
+        h, o = host_loop.run(**step_inputs)
+        assert o[3] == 0 and o[4] == 1
+        tokens.append(h[0].copy())
+        for r in range(4):
+            if step_inputs["active"][r] and h[0, r] >= 0:
+                step_inputs["token"][r] = h[0, r]
+                step_inputs["position"][r] += 1
+                step_inputs["seq_len"][r] += 1
+                step_inputs["slot"][r] = compute_slot(TINY, step_inputs["block_table"], r, int(step_inputs["position"][r]))
+    np.testing.assert_array_equal(np.stack(tokens), history[:4])
+    assert torch.equal(resident.key, host_loop.key) and torch.equal(resident.value, host_loop.value)
+    assert list(resident.res_position) == list(host_loop.res_position)
+    assert list(resident.res_token) == list(host_loop.res_token)
