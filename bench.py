@@ -11,22 +11,27 @@ host-to-device KV import (the import epoch is the first K=2 epoch), and then
 K=2 greedy epochs keep decoding.  A "step" of this benchmark is one epoch.
 
 value    decode tokens/s over the timed epochs, device time (CUDA events around
-         the epoch kernel on its own stream), max over ranks, all ranks summed.
+         the epoch kernel on its own stream), max over ranks.
 e2e      the same through the C-ABI call with host buffers: H2D of the epoch
          inputs and D2H of the token history + control output inside the timed
          wall-clock region.
---impl reference  times the CPU oracle (a port of the reference's torch decode
-         step and controller, the reference path itself needs Ascend hardware)
-         on the host cores on a bounded sample of the same workload.
+cpu_baseline / --impl reference
+         whole greedy epochs of the CPU oracle (a port of the reference's torch
+         decode step and epoch controller; the reference path itself needs
+         Ascend hardware), all 28 layers, on the host cores: the same seeded
+         weights (the C restatement of the generator), the same cohort,
+         prefilled and imported the same way, perf_counter around each epoch.
 
-Multi-GPU (torchrun): each rank runs an independent B=4 cohort on its own GPU
-(data-parallel replicas, no collective on the data path); the process group is
-only used for the start/stop barrier and the max-over-ranks timing.
-With --tp the N ranks instead form one tensor-parallel group decoding a single
-B=4 cohort (strong scaling): each GPU streams its 1/N of the weights and the
-epoch kernel exchanges the O / down partials and the vocabulary argmax over
-NVLink peer memory; value counts the cohort's tokens once, and the roofline
-compares the group's shard bytes with N x the per-GPU HBM peak.
+Multi-GPU (torchrun, N ranks): the headline is one tensor-parallel group over
+the N GPUs decoding the same single B=4 cohort as N=1 (strong scaling): each GPU
+streams its 1/N of the weights and the epoch kernel exchanges the O / down
+partials and the vocabulary argmax over NVLink peer memory; value counts the
+cohort's tokens once, and the roofline compares the group's shard bytes with N
+x the per-GPU HBM peak.  tp_check compares the group's tokens with a single-GPU
+engine's on the untimed epochs.  The line's "dp" key is the data-parallel
+layout measured in the same run: every rank an independent B=4 cohort on its
+own full-model engine (weak scaling, tokens summed).  --dp makes that layout
+the headline instead.
 
 Other options: --k (epoch length), --prompt-max (longest seeded prompt; the
 box-scale variant uses 120), --trace (per-phase CTA-0 timeline of one extra
@@ -44,6 +49,7 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
@@ -229,7 +235,7 @@ def gather_kv_shards(engine, key, value):
     return full_k, full_v
 
 
-def setup_cohort(engine, cfg, seed: int, k: int, prompt_max: int = 5):
+def setup_cohort(engine, cfg, seed: int, k: int, prompt_max: int = 5, want_logits: bool = False):
     """Device prefill of a seeded B=4 cohort, then the one-shot import epoch."""
     from scenario import decode_inputs, import_payload, make_scenario, prefill_epochs
 
@@ -243,7 +249,7 @@ def setup_cohort(engine, cfg, seed: int, k: int, prompt_max: int = 5):
         key, value = gather_kv_shards(engine, key, value)
     payload = import_payload(key, value, sc)
     inputs = decode_inputs(sc, cfg.block_size, importing=True)
-    out = engine.run(**inputs, import_payload=payload)
+    out = engine.run(**inputs, import_payload=payload, want_logits=want_logits)
     assert out.status == 0, f"import epoch status {out.status}"
     return sc, out
 
@@ -277,9 +283,9 @@ class Cohort:
         return dict(token=self.token.copy(), position=self.position.copy(), seq_len=seq_len, slot=slot,
                     active=np.ones(4, dtype=np.int32), block_table=sc.block_table.reshape(-1), control=control)
 
-    def step(self):
+    def step(self, want_logits: bool = False):
         inputs = self.inputs()
-        out = self.engine.run(**inputs)
+        out = self.engine.run(**inputs, want_logits=want_logits) if want_logits else self.engine.run(**inputs)
         if out.status != 0:
             raise RuntimeError(f"epoch status {out.status}")
         self._advance(out)
@@ -289,7 +295,7 @@ class Cohort:
         return int(self.cfg.capacity - self.position.max() - 1)
 
 
-def reduce_over_ranks(dev_s: float, tokens: int, wall_s: float, device,
+def reduce_over_ranks(dev_s: float, tokens: int, wall: float, device,
                       sum_tokens: bool = True) -> tuple[float, float, float]:
     """(max device seconds, total tokens, max wall seconds) over the ranks of
     the default process group (identity without one).  A tensor-parallel group
@@ -298,13 +304,146 @@ def reduce_over_ranks(dev_s: float, tokens: int, wall_s: float, device,
     import torch.distributed as dist
 
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
-        return dev_s, float(tokens), wall_s
+        return dev_s, float(tokens), wall
     where = f"cuda:{device}" if device is not None else "cpu"
-    times = torch.tensor([dev_s, wall_s], dtype=torch.float64, device=where)
+    times = torch.tensor([dev_s, wall], dtype=torch.float64, device=where)
     total = torch.tensor([float(tokens)], dtype=torch.float64, device=where)
     dist.all_reduce(times, op=dist.ReduceOp.MAX)
     dist.all_reduce(total, op=dist.ReduceOp.SUM if sum_tokens else dist.ReduceOp.MAX)
     return float(times[0]), float(total[0]), float(times[1])
+
+
+def top2_margins(logits: np.ndarray) -> list[list[float]]:
+    """[steps][rows] relative gap between the two largest logits of each row
+    (the near-tie rule's measure), from f32 [steps, 4, V] logits."""
+    top = np.sort(np.partition(logits, -2, axis=-1)[..., -2:], axis=-1)
+    scale = np.maximum(np.abs(top[..., 1]), 1e-6)
+    return ((top[..., 1] - top[..., 0]) / scale).tolist()
+
+
+def tp_token_check(group_outs, single_outs, tol: float = 2e-2) -> dict:
+    """The tensor-parallel group's token histories against a single-GPU
+    engine's on the same cohort and epochs: a row may differ only at a step
+    where the single-GPU logits' top-2 margin is below ``tol`` (the near-tie
+    rule); a row that differed is not compared in later epochs."""
+    from scenario import find_divergence
+
+    done: dict[int, tuple[int, int]] = {}
+    compared = 0
+    for epoch, (g, o) in enumerate(zip(group_outs, single_outs)):
+        calls = o.model_calls
+        margins = top2_margins(o.logits[:calls])
+        gh, oh = g.history.copy(), o.history.copy()
+        for row in done:   # rows that differed earlier: excluded from here on
+            gh[:, row] = oh[:, row]
+        try:
+            diverged = find_divergence(gh, oh, margins, tol)
+        except AssertionError as exc:
+            return {"ok": False, "epochs": epoch + 1, "error": str(exc)}
+        for row, step in diverged.items():
+            done[row] = (epoch, step)
+        compared += sum(1 for r in range(4) if r not in done)
+    return {"ok": True, "epochs": len(single_outs), "rows_compared": compared,
+            "near_tie_divergences": {str(r): {"epoch": e, "step": s} for r, (e, s) in done.items()}}
+
+
+def timed_epochs(cohort, cfg, steps: int, device: int, world: int, tp: bool, barrier) -> dict:
+    """`steps` epochs of `cohort`, bracketed by barriers, with the SM clocks
+    sampled during the timed region.  Device time is the CUDA-event time of
+    each epoch kernel; wall time covers the whole C-ABI call with host buffers."""
+    engine = cohort.engine
+    barrier()
+    tokens = 0
+    device_us = []
+    step_bytes_total = 0
+    model_calls = 0
+    with ClockSampler(device) as clocks:
+        wall0 = time.perf_counter()
+        for _ in range(steps):
+            out, inputs = cohort.step()
+            executed = out.control_out[6 + 8: 6 + 12]
+            tokens += int(executed.sum())
+            device_us.append(out.device_us)
+            model_calls += out.model_calls
+            contexts0 = [int(p) for p in inputs["position"]]
+            for s in range(out.model_calls):
+                ctx = [c + s for c, e in zip(contexts0, executed) if e > s]
+                step_bytes_total += shard_step_bytes(cfg, engine.shard, ctx) * world if tp else step_bytes(cfg, ctx)
+        wall = time.perf_counter() - wall0
+    barrier()
+    return {"tokens": tokens, "dev_s": sum(device_us) / 1e6, "wall": wall, "bytes": step_bytes_total,
+            "model_calls": model_calls, "clocks": clocks.summary()}
+
+
+def host_loop_comparison(engine, cohort, cfg, ks=(2, 4, 8), reps: int = 3) -> dict | None:
+    """The reference's central comparison on this engine: a K-step resident
+    epoch (one C-ABI call, one kernel) against the host-loop route (K
+    decoder-ABI calls, logits copied to pinned host memory and argmaxed there,
+    cruise_b200.host_loop), wall clock around each, K = 2/4/8, median of
+    `reps`.  The epochs run first and the host loops continue from where they
+    ended (a host loop leaves the engine's resident row state behind)."""
+    import torch
+
+    from cruise_b200.host_loop import host_loop_epoch
+
+    if cohort.room() < 2 * reps * sum(ks):
+        return None
+    epoch_s = {k: [] for k in ks}
+    loop_s = {k: [] for k in ks}
+    loop_dev = {k: [] for k in ks}
+    for k in ks:
+        for _ in range(reps):
+            inputs = cohort.inputs()
+            inputs["control"][0] = k
+            t0 = time.perf_counter()
+            out = engine.run(**inputs)
+            epoch_s[k].append(time.perf_counter() - t0)
+            assert out.status == 0, out.status
+            cohort._advance(out)
+    logits = torch.empty((4, cfg.vocab), dtype=torch.float32, pin_memory=True).numpy()
+    device_us = []
+
+    def step(*a):
+        result = engine.decoder_step(*a, logits_out=logits)
+        device_us.append(engine.last_timing()[0])
+        return result
+
+    for k in ks:
+        for _ in range(reps):
+            inputs = cohort.inputs()
+            inputs["control"][0] = k
+            device_us.clear()
+            t0 = time.perf_counter()
+            history, control = host_loop_epoch(step, inputs, cfg.block_size, cfg.capacity)
+            loop_s[k].append(time.perf_counter() - t0)
+            loop_dev[k].append(sum(device_us) / 1e6)
+            cohort._advance(OracleOutput(history, control, None, 0.0))
+    result = {}
+    for k in ks:
+        e, h = statistics.median(epoch_s[k]), statistics.median(loop_s[k])
+        result[f"k{k}"] = {"epoch_ms": round(e * 1e3, 3), "host_loop_ms": round(h * 1e3, 3),
+                           "host_loop_kernel_ms": round(statistics.median(loop_dev[k]) * 1e3, 3),
+                           "speedup": round(h / e, 3)}
+    result["note"] = ("wall clock per epoch through the C ABI with host buffers; the host loop keeps K/V on the "
+                      "device and copies 4 x V f32 logits per step to pinned host memory (the reference's runner "
+                      "also copies both caches out per step)")
+    return result
+
+
+def workload_config(args, world: int, tp: bool) -> dict:
+    """The `config` object of both arms' lines (the reference arm times the
+    same workload on the CPU)."""
+    return {
+        "workload": "configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
+                    "one-shot H2D KV import of the prefilled prompts (2-%d tokens)" % (args.k, args.prompt_max),
+        "model": "Qwen2.5-7B architecture (28 layers, hidden 3584, 28/4 heads x 128, I 18944, V 152064)",
+        "global_batch": 4 if (tp or world == 1) else 4 * world,
+        "epoch_k": args.k,
+        "kv": "paged, block 128, 2 blocks per row",
+        "parallelism": (f"tp{world} (one cohort sharded over {world} GPUs)" if tp else
+                        f"dp{world} (independent cohorts)" if world > 1 else "single GPU"),
+        "l2": "no flush: every step streams 14.1 GB of weights, > 126 MB L2",
+    }
 
 
 def run_gpu(args) -> None:
@@ -326,64 +465,65 @@ def run_gpu(args) -> None:
         # reduced geometry for profiler captures only (never a bench line)
         cfg = cfg.with_(num_layers=args.layers or cfg.num_layers, vocab=args.vocab or cfg.vocab,
                         configured_eos=(args.vocab or cfg.vocab) - 1)
-    tp = args.tp and world > 1
-    if tp:
-        # one cohort sharded over all ranks (one GPU each); the kernel exchanges
-        # the row-parallel partials and the vocabulary argmax over peer memory
-        from cruise_b200.tp import create_tp_engine
-
-        engine = create_tp_engine(cfg, device=device)
-    else:
-        engine = EpochEngine(cfg, device=device)
-    t0 = time.perf_counter()
-    engine.init_synthetic(seed=0)
-    synth_s = time.perf_counter() - t0
-    sc, first = setup_cohort(engine, cfg, seed=1000 + (0 if tp else rank), k=args.k, prompt_max=args.prompt_max)
-    cohort = Cohort(engine, cfg, sc, first)
-    need = (args.warmup + args.steps + (1 if args.trace else 0)) * args.k
-    if cohort.room() < need:
-        raise RuntimeError(f"capacity {cfg.capacity} too small for {need} more positions")
-    for _ in range(args.warmup):
-        cohort.step()
+    tp = world > 1 and not args.dp
 
     def barrier():
         torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
 
-    # ---- timed region: device-resident epochs (value) ----
-    barrier()
-    tokens = 0
-    device_us = []
-    step_bytes_total = 0
-    with ClockSampler(device) as clocks:
-        wall0 = time.perf_counter()
-        for _ in range(args.steps):
-            out, inputs = cohort.step()
-            executed = out.control_out[6 + 8 : 6 + 12]
-            tokens += int(executed.sum())
-            device_us.append(out.device_us)
-            contexts0 = [int(p) for p in inputs["position"]]
-            for s in range(out.model_calls):
-                ctx = [c + s for c, e in zip(contexts0, executed) if e > s]
-                step_bytes_total += shard_step_bytes(cfg, engine.shard, ctx) * world if tp else step_bytes(cfg, ctx)
-        wall = time.perf_counter() - wall0
-    barrier()
-    dev_s = sum(device_us) / 1e6
-    model_calls = args.steps * args.k
-    t_max, tok_total, e2e_wall = reduce_over_ranks(dev_s, tokens, wall, device=device if world > 1 else None,
-                                                   sum_tokens=not tp)
-    value = tok_total / t_max
-    e2e_tokens = tok_total
+    t0 = time.perf_counter()
+    group = None
+    if tp:
+        # one cohort sharded over all ranks (one GPU each); the kernel exchanges
+        # the row-parallel partials and the vocabulary argmax over peer memory
+        from cruise_b200.tp import create_tp_engine
+
+        group = create_tp_engine(cfg, device=device)
+        group.init_synthetic(seed=0)
+    single = EpochEngine(cfg, device=device)
+    single.init_synthetic(seed=0)
+    synth_s = time.perf_counter() - t0
+    need = (args.warmup + args.steps + (1 if args.trace else 0)) * args.k
+
+    # the single-GPU cohort of this rank (seed 1000 + rank; rank 0's is the tensor-parallel cohort)
+    check_logits = tp and rank == 0
+    sc, first_single = setup_cohort(single, cfg, seed=1000 + rank, k=args.k, prompt_max=args.prompt_max,
+                                    want_logits=check_logits)
+    single_cohort = Cohort(single, cfg, sc, first_single)
+    if single_cohort.room() < need:
+        raise RuntimeError(f"capacity {cfg.capacity} too small for {need} more positions")
+    single_warm = [single_cohort.step(want_logits=check_logits)[0] for _ in range(args.warmup)]
+    if tp:
+        sc_tp, first_tp = setup_cohort(group, cfg, seed=1000, k=args.k, prompt_max=args.prompt_max)
+        tp_cohort = Cohort(group, cfg, sc_tp, first_tp)
+        tp_warm = [tp_cohort.step()[0] for _ in range(args.warmup)]
+
+    # ---- timed regions: device-resident epochs ----
+    runs = {}
+    if tp:
+        runs["tp"] = timed_epochs(tp_cohort, cfg, args.steps, device, world, True, barrier)
+    runs["single"] = timed_epochs(single_cohort, cfg, args.steps, device, world, False, barrier)
+    head = runs["tp"] if tp else runs["single"]
+    t_max, tok_total, e2e_wall = reduce_over_ranks(head["dev_s"], head["tokens"], head["wall"],
+                                                   device=device if world > 1 else None, sum_tokens=not tp)
     if args.trace and (rank == 0 or tp):
         # a tensor-parallel group runs the traced epoch on every rank
-        print_trace(engine, cohort, cfg, args.k, show=rank == 0)
+        print_trace(group if tp else single, tp_cohort if tp else single_cohort, cfg, args.k, show=rank == 0)
+    dp = None
+    if tp:
+        d = runs["single"]
+        dp_t, dp_tok, dp_wall = reduce_over_ranks(d["dev_s"], d["tokens"], d["wall"], device=device)
+        dp = {"value": round(dp_tok / dp_t, 2), "unit": "tok/s", "scaling": "weak",
+              "ms_per_step": round(dp_t * 1e3 / args.steps, 4), "global_batch": 4 * world,
+              "e2e_value": round(dp_tok / dp_wall, 2),
+              "note": "every rank an independent B=4 cohort on its own full-model engine, tokens summed"}
     peak, peak_kind = hbm_peak()
     per_epoch_us = t_max * 1e6 / args.steps
-    achieved_gbs = step_bytes_total / (t_max if tp else dev_s) / 1e9
+    achieved_gbs = head["bytes"] / (t_max if tp else head["dev_s"]) / 1e9
     if tp:
         peak = peak * world   # the group's aggregate HBM bandwidth
-    clock = clocks.summary()
+    value = tok_total / t_max
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -399,18 +539,7 @@ def run_gpu(args) -> None:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded random-init weights generated on the device; seeded prompts)",
-            "config": {
-                "workload": "configs[1]: Qwen2.5-7B arch, B=4 all active, K=%d greedy epochs after the "
-                            "one-shot H2D KV import of the device-prefilled prompts (2-%d tokens)"
-                            % (args.k, args.prompt_max),
-                "model": "Qwen2.5-7B architecture (28 layers, hidden 3584, 28/4 heads x 128, I 18944, V 152064)",
-                "global_batch": 4 if tp else 4 * world,
-                "epoch_k": args.k,
-                "kv": "paged, block 128, 2 blocks per row",
-                "parallelism": (f"tp{world} (one cohort sharded over {world} GPUs)" if tp else
-                                f"dp{world} (independent cohorts)" if world > 1 else "single GPU"),
-                "l2": "no flush: every step streams 14.1 GB of weights, > 126 MB L2",
-            },
+            "config": workload_config(args, world, tp),
             "roofline": {
                 "bound": "hbm",
                 "achieved": round(achieved_gbs, 1),
@@ -423,23 +552,31 @@ def run_gpu(args) -> None:
                             else None),
                 "traffic_unit": "bytes per decode step (ncu dram read + write)",
                 "kernel": "resident_epoch_kernel",
-                "bytes_per_decode_step": step_bytes_total // model_calls,
+                "bytes_per_decode_step": head["bytes"] // max(head["model_calls"], 1),
             },
             "e2e": {
-                "value": round(e2e_tokens / e2e_wall, 2),
+                "value": round(tok_total / e2e_wall, 2),
                 "unit": "tok/s",
                 "h2d_bytes_per_step": EPOCH_H2D_BYTES,
                 "d2h_bytes_per_step": EPOCH_D2H_BYTES,
-                "host_control_ms_per_epoch": round(wall * 1e3 / args.steps, 4),
+                "host_control_ms_per_epoch": round(e2e_wall * 1e3 / args.steps, 4),
             },
             "gpu_launches": args.steps * world,   # one epoch kernel per step on every rank
-            "clocks": clock,
+            "clocks": head["clocks"],
             "setup": {"weight_synthesis_s": round(synth_s, 2)},
         }
-        if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(engine, cfg)
+        if tp:
+            line["tp_check"] = tp_token_check([first_tp, *tp_warm], [first_single, *single_warm])
+            line["dp"] = dp
+    if tp:
+        group.close()
+    if rank == 0 and world == 1 and not args.no_host_loop and not (args.layers or args.vocab):
+        line["host_loop"] = host_loop_comparison(single, single_cohort, cfg)
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(cfg, args, first_single)
+    if rank == 0:
         print(json.dumps(line), flush=True)
-    engine.close()
+    single.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -495,132 +632,116 @@ def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
               f"{a[6]:7.1f}   {bw:6.0f}", file=sys.stderr)
 
 
-SAMPLE_LAYERS = (1, 5)
+@dataclass
+class OracleOutput:
+    history: np.ndarray
+    control_out: np.ndarray
+    logits: None
+    device_us: float   # wall-clock time of the oracle epoch
+
+    @property
+    def status(self) -> int:
+        return int(self.control_out[3])
+
+    @property
+    def model_calls(self) -> int:
+        return int(self.control_out[4])
 
 
-def cpu_oracle_step_time(weights: dict, cfg, threads: int) -> tuple[float, str]:
-    """Seconds of one 7B decode step of the CPU oracle (bf16 torch ops, the
-    reference's own arithmetic), from a bounded sample: steps of the same
-    geometry truncated to 1 and 5 layers give the per-layer and the fixed
-    (embedding, final norm, lm_head) costs, extrapolated to all layers."""
-    import torch
+class OracleEngine:
+    """The CPU oracle (the reference's decode step and epoch controller, ported
+    to torch CPU) behind the engine's run / read_kv surface, with the engine's
+    seeded weights at full depth.  Used by the CPU legs of this benchmark only."""
 
-    from oracle.decoder import OracleDecoder
-    from oracle.model import OracleConfig
+    def __init__(self, cfg, threads: int) -> None:
+        import torch
 
-    torch.set_num_threads(threads)
-    times = {}
-    for layers in SAMPLE_LAYERS:
-        ocfg = OracleConfig(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
-                            num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
-                            intermediate=cfg.intermediate, vocab=cfg.vocab, block_size=cfg.block_size)
-        decoder = OracleDecoder(ocfg, weights)   # a truncation reads layers 0..layers-1 only
-        shape = (layers, ocfg.num_blocks, ocfg.block_size, ocfg.num_kv_heads, ocfg.head_dim)
-        key = torch.zeros(shape, dtype=torch.bfloat16)
-        value = torch.zeros(shape, dtype=torch.bfloat16)
-        token = torch.tensor([11, 12, 13, 14], dtype=torch.int64)
-        position = torch.tensor([4, 4, 4, 4], dtype=torch.int64)
-        seq_len = torch.tensor([5, 5, 5, 5], dtype=torch.int32)
-        bt = torch.arange(8, dtype=torch.int32).reshape(4, 2)
-        slot = torch.tensor([4, 260, 516, 772], dtype=torch.int32)
-        active = torch.ones(4, dtype=torch.int32)
-        decoder.step(token, position, seq_len, bt, slot, key, value, active)   # warm-up
-        samples = []
-        for _ in range(3):
-            t = time.perf_counter()
-            decoder.step(token, position, seq_len, bt, slot, key, value, active)
-            samples.append(time.perf_counter() - t)
-        times[layers] = min(samples)
-    lo, hi = SAMPLE_LAYERS
-    per_layer = max((times[hi] - times[lo]) / (hi - lo), 1e-9)
-    fixed = max(times[lo] - lo * per_layer, 0.0)
-    return fixed + cfg.num_layers * per_layer, (
-        f"{lo}- and {hi}-layer truncations of the 7B decode step (B=4, ctx 5, {threads} threads), best of 3, "
-        f"extrapolated to {cfg.num_layers} layers: {times[lo]*1e3:.0f} / {times[hi]*1e3:.0f} ms"
-    )
+        from cruise_b200.model_config import TpShard
+        from oracle.decoder import OracleDecoder
+        from oracle.epoch import OracleEpochController
+        from oracle.model import OracleConfig, seeded_weights
+
+        torch.set_num_threads(threads)
+        self.config = cfg
+        self.shard = TpShard.of(cfg, 0, 1)
+        ocfg = OracleConfig(num_layers=cfg.num_layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
+                            num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, intermediate=cfg.intermediate,
+                            vocab=cfg.vocab, block_size=cfg.block_size, blocks_per_row=cfg.blocks_per_row,
+                            num_blocks=cfg.num_blocks)
+        t0 = time.perf_counter()
+        weights = seeded_weights(ocfg, seed=0, use_c=True)
+        self.synth_s = time.perf_counter() - t0
+        self.controller = OracleEpochController(OracleDecoder(ocfg, weights))
+
+    def run(self, import_payload=None, forced=None, want_logits=False, **inputs) -> OracleOutput:
+        t0 = time.perf_counter()
+        history, control = self.controller.run(**inputs, import_payload=import_payload, forced=forced)
+        return OracleOutput(history, control, None, (time.perf_counter() - t0) * 1e6)
+
+    def read_kv(self):
+        return self.controller.key, self.controller.value
 
 
-def engine_weights_fn(engine):
-    import torch
-
-    from oracle.model import LAYER_KEYS
-
-    cfg = engine.config
-
-    def weights(layers: int):
-        shapes = {"model.embed_tokens.weight": (cfg.vocab, cfg.hidden), "model.norm.weight": (cfg.hidden,),
-                  "lm_head.weight": (cfg.vocab, cfg.hidden)}
-        h, kv, i = cfg.hidden, cfg.kv_width, cfg.intermediate
-        per = {"input_layernorm.weight": (h,), "post_attention_layernorm.weight": (h,),
-               "self_attn.q_proj.weight": (h, h), "self_attn.q_proj.bias": (h,),
-               "self_attn.k_proj.weight": (kv, h), "self_attn.k_proj.bias": (kv,),
-               "self_attn.v_proj.weight": (kv, h), "self_attn.v_proj.bias": (kv,),
-               "self_attn.o_proj.weight": (h, h), "mlp.gate_proj.weight": (i, h),
-               "mlp.up_proj.weight": (i, h), "mlp.down_proj.weight": (h, i)}
-        out = {name: engine.get_weight(name, shape) for name, shape in shapes.items()}
-        for layer in range(layers):
-            for key in LAYER_KEYS:
-                out[f"model.layers.{layer}.{key}"] = engine.get_weight(f"model.layers.{layer}.{key}", per[key])
-        return out
-
-    return weights
+def oracle_epochs(cfg, k: int, prompt_max: int, warmup: int, steps: int, threads: int) -> dict:
+    """Whole greedy epochs of the CPU oracle on the benchmark's cohort (seed
+    1000): prefill and the import epoch untimed, `warmup` untimed epochs, then
+    `steps` epochs each timed with perf_counter around the whole controller."""
+    engine = OracleEngine(cfg, threads)
+    sc, first = setup_cohort(engine, cfg, seed=1000, k=k, prompt_max=prompt_max)
+    cohort = Cohort(engine, cfg, sc, first)
+    for _ in range(warmup):
+        cohort.step()
+    tokens, seconds, calls = 0, 0.0, 0
+    for _ in range(steps):
+        out, _ = cohort.step()
+        tokens += int(out.control_out[6 + 8: 6 + 12].sum())
+        seconds += out.device_us / 1e6
+        calls += out.model_calls
+    return {"tokens": tokens, "seconds": seconds, "model_calls": calls, "import_history": first.history,
+            "synth_s": engine.synth_s}
 
 
-def cpu_baseline(engine, cfg) -> dict:
+def cpu_baseline(cfg, args, gpu_first) -> dict:
+    """The oracle on the GPU box's host cores, a bounded sample of the same
+    workload: 1 warm-up epoch and 3 timed epochs after the import epoch."""
     threads = len(os.sched_getaffinity(0))
-    step_s, sample = cpu_oracle_step_time(engine_weights_fn(engine)(SAMPLE_LAYERS[-1]), cfg, threads)
-    return {"value": round(4 / step_s, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": sample, "us_per_decode_step": round(step_s * 1e6, 1)}
+    r = oracle_epochs(cfg, args.k, args.prompt_max, warmup=1, steps=3, threads=threads)
+    return {"value": round(r["tokens"] / r["seconds"], 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"3 whole K={args.k} epochs of the 28-layer oracle (torch CPU, bf16) after the import "
+                      f"epoch and 1 warm-up epoch, same seeded weights and cohort, {threads} threads",
+            "ms_per_epoch": round(r["seconds"] * 1e3 / 3, 1),
+            "us_per_decode_step": round(r["seconds"] * 1e6 / max(r["model_calls"], 1), 1),
+            "import_epoch_tokens_equal_gpu": bool(np.array_equal(r["import_history"], gpu_first.history))}
 
 
 def run_reference(args) -> None:
-    """CPU arm: the oracle port of the reference path on the host cores."""
+    """CPU arm: the oracle port of the reference path on the host cores, whole
+    epochs of the same workload (rank 0 only under torchrun)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import torch
-
     from cruise_b200.model_config import QWEN25_7B
 
     cfg = QWEN25_7B
     threads = len(os.sched_getaffinity(0))
-
-    weights = random_weights(cfg, layers=SAMPLE_LAYERS[-1], seed=0)
-    samples = []
-    sample_desc = ""
-    for _ in range(args.warmup + args.steps):
-        step_s, sample_desc = cpu_oracle_step_time(weights, cfg, threads)
-        samples.append(step_s)
-    timed = samples[args.warmup:]
-    step_s = sum(timed) / len(timed)
-    value = 4 / step_s
+    r = oracle_epochs(cfg, args.k, args.prompt_max, warmup=args.warmup, steps=args.steps, threads=threads)
+    value = r["tokens"] / r["seconds"]
+    sample = (f"{args.steps} whole K={args.k} epochs of the 28-layer oracle (torch CPU, bf16) after the import "
+              f"epoch and {args.warmup} warm-up epochs, {threads} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": 0,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * args.k * 1e3, 2),
-        "us_per_decode_step": round(step_s * 1e6, 1), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "configs[1] decode steps (B=4, 7B arch) on the host cores",
-                   "epoch_k": args.k},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["seconds"] * 1e3 / args.steps, 2),
+        "us_per_decode_step": round(r["seconds"] * 1e6 / max(r["model_calls"], 1), 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, the GPU arm's; seeded prompts)",
+        "config": workload_config(args, int(os.environ.get("WORLD_SIZE", "1")),
+                                  int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.dp),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": sample_desc},
+                         "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup": {"weight_synthesis_s": round(r["synth_s"], 2)},
     }
     print(json.dumps(line), flush=True)
-
-
-def random_weights(cfg, layers: int, seed: int) -> dict:
-    """N(0, 0.02) bf16 weights of the 7B geometry truncated to `layers` layers
-    (CPU timing does not depend on the values; torch's generator is fast)."""
-    import torch
-
-    from oracle.model import OracleConfig, tensor_shapes
-
-    ocfg = OracleConfig(num_layers=layers, hidden=cfg.hidden, num_heads=cfg.num_heads,
-                        num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
-                        intermediate=cfg.intermediate, vocab=cfg.vocab, block_size=cfg.block_size)
-    gen = torch.Generator().manual_seed(seed)
-    return {name: torch.empty(shape, dtype=torch.bfloat16).normal_(0.0, 0.02, generator=gen)
-            for name, shape in tensor_shapes(ocfg).items()}
 
 
 def forced_epochs_all_rows(sc, cfg, generation_offset: int):
@@ -714,11 +835,15 @@ def main() -> None:
     parser.add_argument("--k", type=int, default=2, choices=(1, 2, 4, 8))
     parser.add_argument("--impl", default="cruise", choices=("cruise", "reference"))
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-host-loop", action="store_true",
+                        help="skip the resident-epoch vs host-loop comparison (N=1)")
     parser.add_argument("--trace", action="store_true", help="per-phase timing of one extra epoch (stderr)")
     parser.add_argument("--layers", type=int, default=0, help="profiling only: truncate the model to N layers")
     parser.add_argument("--vocab", type=int, default=0, help="profiling only: vocabulary size")
     parser.add_argument("--tp", action="store_true",
-                        help="under torchrun: the ranks form one tensor-parallel group decoding one cohort")
+                        help="under torchrun: the ranks form one tensor-parallel group (the default)")
+    parser.add_argument("--dp", action="store_true",
+                        help="under torchrun: headline = independent data-parallel cohorts, no tensor parallelism")
     parser.add_argument("--prompt-max", type=int, default=5,
                         help="longest prompt of the seeded cohort (2..block_size; configs[4] uses 120)")
     parser.add_argument("--prefill", action="store_true",

@@ -76,6 +76,10 @@ SIGNATURES = {
     "cruise_epoch_run_noalloc": (
         ctypes.c_int32, [ctypes.c_void_p, i64p, i64p, i32p, i32p, i32p, i32p, i32p, i64p, i32p],
     ),
+    "cruise_decoder_step": (
+        ctypes.c_int32,
+        [ctypes.c_void_p, i64p, i64p, i32p, ctypes.c_void_p, i32p, i32p, i32p, ctypes.c_void_p, u8p, f32p, i64p],
+    ),
     "cruise_epoch_last_timing": (
         ctypes.c_int32, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), i32p]
     ),

@@ -917,6 +917,41 @@ int64_t import_payload_bytes(const Engine *e) {
   return 2LL * e->m.L * kBatch * e->m.bs * e->m.nkv_all * e->m.d * 2;   // every KV head of the model
 }
 
+// Launch parameters of a regular (engine-allocated) launch: the model, the
+// resident caches and state, the engine's scratch, the launch geometry.
+EpochParams engine_params(const Engine *e) {
+  EpochParams p{};
+  p.m = e->m;
+  p.layers = e->d_layers;
+  p.embed = e->embed;
+  p.final_norm = e->final_norm;
+  p.lm_head = e->lm_head;
+  p.rope_cos = e->rope_cos;
+  p.rope_sin = e->rope_sin;
+  p.key_cache = e->key_cache;
+  p.value_cache = e->value_cache;
+  p.h = e->h;
+  p.qkv = e->qkv;
+  p.attn = e->attn;
+  p.act = e->act;
+  p.partials = e->partials;
+  p.arg_val = e->arg_val;
+  p.arg_idx = e->arg_idx;
+  p.arg_bad = e->arg_bad;
+  p.io = e->d_io;
+  p.res = e->d_res;
+  p.work = e->d_work;
+  p.sync = e->d_sync;
+  p.grid = e->sms;
+  p.stages = e->stages;
+  p.xs_stride = e->xs_stride;
+  p.down_xglobal = e->down_xglobal;
+  p.trace = e->trace_on ? e->trace : nullptr;
+  p.l2_ahead = e->l2_ahead;
+  p.mode = kModeEpoch;
+  return p;
+}
+
 // One epoch: H2D of the 8 inputs (+ optional import payload), one cooperative
 // launch, D2H of the 2 outputs.
 int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, const int32_t *seq_len,
@@ -970,41 +1005,14 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sizeof(SyncState), e->stream);
   if (err != cudaSuccess) return set_err(e, err, "epoch inputs");
 
-  EpochParams p{};
-  p.m = e->m;
-  p.layers = e->d_layers;
-  p.embed = e->embed;
-  p.final_norm = e->final_norm;
-  p.lm_head = e->lm_head;
-  p.rope_cos = e->rope_cos;
-  p.rope_sin = e->rope_sin;
-  p.key_cache = e->key_cache;
-  p.value_cache = e->value_cache;
-  p.h = e->h;
-  p.qkv = e->qkv;
-  p.attn = e->attn;
-  p.act = e->act;
-  p.partials = e->partials;
-  p.arg_val = e->arg_val;
-  p.arg_idx = e->arg_idx;
-  p.arg_bad = e->arg_bad;
+  EpochParams p = engine_params(e);
   p.logits = logits_out != nullptr ? e->logits : nullptr;
   p.import_payload = payload_on_device ? static_cast<const uint8_t *>(payload) : e->d_payload;
-  p.io = e->d_io;
-  p.res = e->d_res;
-  p.work = e->d_work;
-  p.sync = e->d_sync;
-  p.grid = e->sms;
-  p.stages = e->stages;
-  p.xs_stride = e->xs_stride;
-  p.down_xglobal = e->down_xglobal;
-  p.trace = e->trace_on ? e->trace : nullptr;
   if (e->trace_on) cudaMemsetAsync(e->trace, 0, kTraceSeries * kTraceMax * sizeof(uint64_t), e->stream);
   // every device-side wait gives up after 2 s; under tensor parallelism after
   // 20 s by default (CRUISE_TP_TIMEOUT_MS at creation), since a rank's first
   // wait also covers the other ranks' launch skew
   p.timeout_ns = e->tp_size > 1 ? e->tp_timeout_ns : 2000000000ull;
-  p.l2_ahead = e->l2_ahead;
   p.tp_size = e->tp_size;
   p.tp_rank = e->tp_rank;
   if (e->tp_size > 1) {
@@ -1046,6 +1054,92 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
     if (copy_sync(e, words, &e->d_sync->error, sizeof(words), cudaMemcpyDeviceToHost) == cudaSuccess && words[0])
       e->last_error = "epoch ended by a device-side wait that gave up (site " + std::to_string(words[1]) + ")";
   }
+  return 0;
+}
+
+// One decoder call of the 9-input / 4-output decoder ABI (config/graph_config.json:6-16):
+// H2D of the row inputs, one cooperative launch in decoder-step mode, D2H of
+// the logits [4][V] and the next positions.  The caches are the engine's
+// resident K/V, or device buffers of the caller in the same layout.
+int32_t run_decoder_step(Engine *e, const int64_t *token, const int64_t *position, const int32_t *seq_len,
+                         void *key_cache, const int32_t *slot, const int32_t *active, const int32_t *block_table,
+                         void *value_cache, float *logits_out, int64_t *next_position_out) {
+  const ModelDims &m = e->m;
+  cudaSetDevice(e->device);
+  if (e->tp_size > 1) {
+    e->last_error = "cruise_decoder_step: single-GPU engines only (no tensor parallelism)";
+    return -4;
+  }
+  auto reject = [&](const std::string &why) {
+    e->last_error = "cruise_decoder_step: " + why;
+    return -1;
+  };
+  for (int i = 0; i < kBatch * m.bpr; ++i)
+    if (block_table[i] < 0 || block_table[i] >= m.NB) return reject("block table entry outside the cache");
+  for (int b = 0; b < kBatch; ++b) {
+    // every row's embedding row is gathered, so every token must exist
+    if (token[b] < 0 || token[b] >= m.V) return reject("token id outside the vocabulary");
+    if (active[b] != 0 && active[b] != 1) return reject("active flags must be 0 or 1");
+    if (seq_len[b] < 0 || seq_len[b] > m.C) return reject("sequence length outside [0, capacity]");
+    if (active[b] == 0) continue;
+    if (position[b] < 0 || position[b] >= m.C) return reject("position of an active row outside [0, capacity)");
+    // the new K/V are written at slot[row] and read back at the row's position:
+    // the two must be the same cache slot (what the reference's callers pass)
+    const int64_t logical = position[b] / m.bs;
+    const int64_t expect = static_cast<int64_t>(block_table[b * m.bpr + logical]) * m.bs + position[b] % m.bs;
+    if (slot[b] != expect) return reject("slot of an active row is not its position's block-table slot");
+  }
+  for (void *cache : {key_cache, value_cache}) {
+    if (cache == nullptr) continue;
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, cache) != cudaSuccess || attr.type != cudaMemoryTypeDevice ||
+        attr.device != e->device || (reinterpret_cast<uintptr_t>(cache) & 15) != 0) {
+      cudaGetLastError();
+      return reject("caches must be 16-byte aligned device memory on the engine's device");
+    }
+  }
+  if ((key_cache == nullptr) != (value_cache == nullptr)) return reject("pass both caches or neither");
+  EpochIO *io = e->h_io;
+  std::memset(io, 0, sizeof(EpochIO));
+  std::memcpy(io->token, token, sizeof(io->token));
+  std::memcpy(io->position, position, sizeof(io->position));
+  std::memcpy(io->seq_len, seq_len, sizeof(io->seq_len));
+  std::memcpy(io->slot, slot, sizeof(io->slot));
+  std::memcpy(io->active, active, sizeof(io->active));
+  std::memcpy(io->block_table, block_table, sizeof(int32_t) * kBatch * m.bpr);
+  cudaError_t err = cudaMemcpyAsync(e->d_io, io, offsetof(EpochIO, history), cudaMemcpyHostToDevice, e->stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sizeof(SyncState), e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "decoder step inputs");
+  EpochParams p = engine_params(e);
+  p.mode = kModeDecoderStep;
+  p.trace = nullptr;
+  p.logits = e->logits;
+  if (key_cache != nullptr) {
+    p.key_cache = static_cast<bf16 *>(key_cache);
+    p.value_cache = static_cast<bf16 *>(value_cache);
+  }
+  p.timeout_ns = 2000000000ull;
+  p.tp_size = 1;
+  p.launch_id = ++e->launches;
+  void *args[] = {&p};
+  cudaEventRecord(e->ev0, e->stream);
+  err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
+                                    dim3(kThreads), args, e->smem, e->stream);
+  cudaEventRecord(e->ev1, e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "decoder step launch");
+  err = cudaMemcpyAsync(&io->history, &e->d_io->history, sizeof(EpochIO) - offsetof(EpochIO, history),
+                        cudaMemcpyDeviceToHost, e->stream);
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(logits_out, e->logits, sizeof(float) * kBatch * m.V, cudaMemcpyDeviceToHost, e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return set_err(e, err, "decoder step completion");
+  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  e->last_launches = 1;
+  if (io->control_out[3] != kOk) {
+    e->last_error = "cruise_decoder_step: a device-side wait gave up (status " + std::to_string(io->control_out[3]) + ")";
+    return -3;
+  }
+  std::memcpy(next_position_out, io->history, sizeof(int64_t) * kBatch);
   return 0;
 }
 
@@ -1223,7 +1317,10 @@ std::mutex g_noalloc_mutex;
 void *g_noalloc_base[kNoAllocMaxDevices] = {};
 
 // Device address of the static scratch on `device`, which must be current.  The
-// lookup runs once per device, on that device's first allocation-free call.
+// lookup runs once per device, on that device's first allocation-free call, and
+// the address is kept for the life of the process: after a cudaDeviceReset
+// (which creates a new primary context) the allocation-free call must not be
+// used again in this process.
 cudaError_t noalloc_base(int device, void **base) {
   if (device < 0 || device >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
@@ -1343,15 +1440,26 @@ int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *positi
   p.l2_ahead = e->l2_ahead;
   p.tp_size = 1;
   void *args[] = {&p};
+  cudaEventRecord(e->ev0, e->stream);
   err = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(resident_epoch_kernel), dim3(e->sms),
                                     dim3(kThreads), args, e->smem, e->stream);
+  cudaEventRecord(e->ev1, e->stream);
   if (err != cudaSuccess) return set_err(e, err, "noalloc epoch launch");
   err = cudaMemcpyAsync(&io.history, sb + l.io + offsetof(EpochIO, history),
                         sizeof(EpochIO) - offsetof(EpochIO, history), cudaMemcpyDeviceToHost, e->stream);
+  // the error word and the site of the wait that gave up, for a 207 status
+  uint32_t words[2] = {0, 0};
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(words, sb + l.sync + offsetof(SyncState, error), sizeof(words), cudaMemcpyDeviceToHost,
+                          e->stream);
   if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
   if (err != cudaSuccess) return set_err(e, err, "noalloc epoch completion");
+  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  e->last_launches = 1;
   std::memcpy(history, io.history, sizeof(io.history));
   std::memcpy(control_out, io.control_out, sizeof(io.control_out));
+  if (control_out[3] == kModelError && words[0])
+    e->last_error = "epoch ended by a device-side wait that gave up (site " + std::to_string(words[1]) + ")";
   return 0;
 }
 
@@ -1522,6 +1630,20 @@ int32_t cruise_epoch_run_noalloc(void *engine, const int64_t *token, const int64
   std::lock_guard<std::mutex> lock(e->execute_mutex);
   return cruise::run_epoch_noalloc(e, token, position, seq_len, slot, active, block_table, control, history,
                                    control_out);
+}
+
+int32_t cruise_decoder_step(void *engine, const int64_t *token, const int64_t *position, const int32_t *seq_len,
+                            void *key_cache, const int32_t *slot, const int32_t *active,
+                            const int32_t *block_table, void *value_cache, const uint8_t *tiling,
+                            float *logits_out, int64_t *next_position_out) {
+  (void)tiling;   // the ABI's 72-byte tiling blob: accepted, not needed
+  if (engine == nullptr || token == nullptr || position == nullptr || seq_len == nullptr || slot == nullptr ||
+      active == nullptr || block_table == nullptr || logits_out == nullptr || next_position_out == nullptr)
+    return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  return cruise::run_decoder_step(e, token, position, seq_len, key_cache, slot, active, block_table, value_cache,
+                                  logits_out, next_position_out);
 }
 
 int32_t cruise_epoch_last_timing(void *engine, double *device_us, int32_t *kernel_launches) {

@@ -1379,6 +1379,39 @@ __device__ void adler_block(const uint8_t *data, int n, uint64_t &S1, uint64_t &
   named_sync(1, kConsumerThreads);
 }
 
+// ---- consumer: decoder-step prologue (CTA 0, thread 0) ------------------------------------------------
+// One call of the 9-in / 4-out decoder ABI: the inputs become the working row
+// state of a single step with no controller checks (the host validated the
+// ranges the kernel indexes with), no import and no continuity.
+__device__ void decoder_step_setup(const EpochParams &p) {
+  EpochWork *w = p.work;
+  EpochIO *io = p.io;
+  w->importing = 0;
+  w->variant = 0;
+  w->sampling = 0;
+  w->max_steps = 1;
+  w->import_rows = 0;
+  w->checksum = 0;
+  w->model_calls = 0;
+  for (int b = 0; b < kBatch; ++b) {
+    w->eos[b] = -1;
+    w->generation[b] = 0;
+    w->token[b] = io->token[b];
+    w->position[b] = io->position[b];
+    w->length[b] = io->seq_len[b];
+    w->slot[b] = io->slot[b];
+    w->active[b] = io->active[b];
+    w->active0[b] = io->active[b];
+    w->executed[b] = 0;
+    w->reason[b] = kNone;
+    w->new_gen[b] = 0;
+  }
+  for (int i = 0; i < kBatch * p.m.bpr; ++i) w->bt[i] = io->block_table[i];
+  for (int i = 0; i < kMaxSteps * kBatch; ++i) io->history[i] = -1;
+  w->status = kOk;
+  w->stop = 0;
+}
+
 // ---- the kernel ---------------------------------------------------------------------------------------
 // The register file is split over the SM's four sub-partitions (16K registers each) and ten warps put
 // three warps on two of them, so one CTA of 320 threads fits only at <= 168 registers per thread; the
@@ -1424,8 +1457,11 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
   const size_t payload_block_elems = static_cast<size_t>(m.bs) * m.nkv_all * m.d;
   const size_t layer_elems = static_cast<size_t>(m.NB) * block_elems;
 
+  const bool step_mode = p.mode == kModeDecoderStep;
   // 1. validation (CTA 0)
-  if (blockIdx.x == 0 && tid == 0) {
+  if (blockIdx.x == 0 && tid == 0 && step_mode) {
+    decoder_step_setup(p);
+  } else if (blockIdx.x == 0 && tid == 0) {
     int32_t st = validate_inputs(p);
     if (st < 0) {   // an imported row failed its check after earlier rows were imported
       w->status = -st;
@@ -1516,7 +1552,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
   }
 
   // 3. generation continuity (:448-473), then clear the rows of new generations
-  if (ok && blockIdx.x == 0 && tid == 0 && w->status == kOk) {
+  if (ok && !step_mode && blockIdx.x == 0 && tid == 0 && w->status == kOk) {
     for (int b = 0; b < kBatch && w->status == kOk; ++b) {
       if (w->active0[b] == 0) continue;
       if (p.res->generation[b] == w->generation[b]) {
@@ -1578,6 +1614,14 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
         done_parity ^= 1u;
       } else if (ph < 5 * L) {
         attention_phase(p, s, ph / 5);
+      } else if (blockIdx.x == 0 && step_mode) {
+        // the decoder ABI's fourth output: next_position = where(active, pos + 1, pos)
+        // (batched_decoder_step.py:409-411), in the history words
+        if (tid == 0) {
+          w->model_calls = 1;
+          for (int b = 0; b < kBatch; ++b) io->history[b] = w->active[b] ? w->position[b] + 1 : w->position[b];
+          w->stop = 1;
+        }
       } else if (blockIdx.x == 0) {
         // control: two-pass argmax (pass 2 over the per-CTA partials), then the
         // per-row bookkeeping of the reference K-loop body (:537-591)
@@ -1705,8 +1749,12 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
   }
   if (tid == 0) *s.prod_ctl = -1;   // producer: no more steps
 
-  // 5. finish (:593-614) and emit (:296-324), CTA 0
-  if (blockIdx.x == 0 && tid == 0) {
+  // 5. finish (:593-614) and emit (:296-324), CTA 0; a decoder step reports
+  //    only its status and call count and leaves the resident state alone
+  if (blockIdx.x == 0 && tid == 0 && step_mode) {
+    io->control_out[3] = (!ok || aborted(p)) ? kModelError : w->status;
+    io->control_out[4] = w->model_calls;
+  } else if (blockIdx.x == 0 && tid == 0) {
     int32_t status = w->status;
     if (!ok || aborted(p)) status = kModelError;
     const bool good = status == kOk;

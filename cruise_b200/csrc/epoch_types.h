@@ -49,6 +49,11 @@ enum Status : int32_t {
 };
 enum Finish : int32_t { kNone = 0, kEos = 1, kMaxStepsReason = 2, kFallback = 3, kEmpty = 4, kAlreadyFinished = 5 };
 
+// What one launch runs: a resident epoch (the controller and up to K decoder
+// steps), or one decoder step of the 9-in / 4-out decoder ABI (logits and the
+// next positions out, K/V updated in place, no controller and no resident state).
+enum LaunchMode : int32_t { kModeEpoch = 0, kModeDecoderStep = 1 };
+
 // Per-rank geometry.  Without tensor parallelism the rank holds the whole
 // model; with it (tp ranks) the rank holds query heads [q0, q0 + nq), KV heads
 // [kv0, kv0 + nkv) of nkv_all, intermediate rows [i0, i0 + I) and vocabulary
@@ -210,7 +215,7 @@ struct EpochParams {
   uint32_t tp_seq_base;        // launch-unique base of the exchange sequence numbers
   uint32_t launch_id;          // epochs launched by this engine, this one included
   StreamRing *stream;          // device view of the host-mapped egress ring (nullptr: off)
-  uint32_t pad3;
+  int32_t mode;                // kModeEpoch, or kModeDecoderStep: one decoder call, no controller
 };
 
 }  // namespace cruise

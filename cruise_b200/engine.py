@@ -219,6 +219,44 @@ class EpochEngine:
         self.lib.cruise_epoch_last_timing(self.handle, ctypes.byref(device_us), ctypes.byref(launches))
         return EpochOutput(history, control_out, logits, float(device_us.value))
 
+    # -- one decoder step (9-in / 4-out decoder ABI) ---------------------------------
+    def decoder_step(self, token, position, seq_len, slot, active, block_table, key: torch.Tensor | None = None,
+                     value: torch.Tensor | None = None, logits_out: np.ndarray | None = None
+                     ) -> tuple[np.ndarray, np.ndarray]:
+        """One decoder call, no controller (``cruise_decoder_step``): returns the
+        f32 logits [4, V] and the next positions [4].  ``key`` / ``value`` are
+        caller-held bf16 CUDA caches in the engine's layout (updated in place),
+        or None for the engine's resident caches.  ``logits_out`` may be a
+        preallocated f32 [4, V] array (for example a view of pinned memory)."""
+        cfg = self.config
+        token = np.ascontiguousarray(np.asarray(token, dtype=np.int64).reshape(BATCH))
+        position = np.ascontiguousarray(np.asarray(position, dtype=np.int64).reshape(BATCH))
+        seq_len = np.ascontiguousarray(np.asarray(seq_len, dtype=np.int32).reshape(BATCH))
+        slot = np.ascontiguousarray(np.asarray(slot, dtype=np.int32).reshape(BATCH))
+        active = np.ascontiguousarray(np.asarray(active, dtype=np.int32).reshape(BATCH))
+        block_table = np.ascontiguousarray(
+            np.asarray(block_table, dtype=np.int32).reshape(BATCH * cfg.blocks_per_row))
+        logits = np.empty((BATCH, cfg.vocab), dtype=np.float32) if logits_out is None else logits_out
+        if logits.shape != (BATCH, cfg.vocab) or logits.dtype != np.float32 or not logits.flags.c_contiguous:
+            raise ValueError(f"logits_out must be a contiguous float32 [{BATCH}, {cfg.vocab}] array")
+        next_position = np.empty(BATCH, dtype=np.int64)
+        caches = []
+        for cache in (key, value):
+            if cache is None:
+                caches.append(None)
+                continue
+            if (not cache.is_cuda or cache.dtype != torch.bfloat16 or not cache.is_contiguous()
+                    or tuple(cache.shape) != self.shard.kv_cache_shape(cfg)):
+                raise ValueError(f"caches must be contiguous bf16 CUDA tensors of shape {self.shard.kv_cache_shape(cfg)}")
+            caches.append(ctypes.c_void_p(cache.data_ptr()))
+        rc = self.lib.cruise_decoder_step(
+            self.handle, _ptr(token, ctypes.c_int64), _ptr(position, ctypes.c_int64), _ptr(seq_len, ctypes.c_int32),
+            caches[0], _ptr(slot, ctypes.c_int32), _ptr(active, ctypes.c_int32), _ptr(block_table, ctypes.c_int32),
+            caches[1], None, _ptr(logits, ctypes.c_float), _ptr(next_position, ctypes.c_int64),
+        )
+        self._check(rc, "cruise_decoder_step")
+        return logits, next_position
+
     # -- batched device prefill -------------------------------------------------------
     def prefill(self, prompts) -> None:
         """Runs up to four prompts (row r <- prompts[r]; an empty prompt leaves the

@@ -207,10 +207,14 @@ int32_t cruise_epoch_run(void *engine, const int64_t *token,
  * Arguments mean what they mean for cruise_epoch_run (host arrays; no tiling,
  * forced tokens or logits).  KV imports are not accepted here.
  * The first call on a device looks up the array's device address (once per
- * device); make that first call before any stream capture.  Every call, on
- * every engine of the process, shares the one array and clears it first:
- * calls that overlap in time (two threads, two engines on one GPU) race and
- * must be serialised by the caller.
+ * device) and keeps it for the life of the process, so the call must not be
+ * used after a cudaDeviceReset of that device; make that first call before
+ * any stream capture.  The call returns after the epoch completed (it waits
+ * for the engine's stream).  Every call, on every engine of the process,
+ * shares the one array and clears it first: calls that overlap in time (two
+ * threads, two engines on one GPU) race and must be serialised by the caller.
+ * cruise_epoch_last_timing reports this call like cruise_epoch_run, and a
+ * device status 207 names the wait that gave up in cruise_epoch_last_error.
  * Returns 0 when the epoch ran (device status in control_out[3]), -1 for a
  * NULL argument, -2 when the model's scratch exceeds the 1 MiB array, -3 for
  * an import request, -4 for a tensor-parallel engine, or a CUDA error code;
@@ -223,8 +227,44 @@ int32_t cruise_epoch_run_noalloc(void *engine, const int64_t *token,
                                  const int32_t *control, int64_t *history,
                                  int32_t *control_out);
 
-/* Device time of the last epoch in microseconds (CUDA events around the
- * epoch kernel) and the number of kernels it launched. */
+/* One decoder step through the 9-input / 4-output decoder ABI of the
+ * reference's decode graph (config/graph_config.json:6-16; the call the
+ * device controller makes once per step, controller/g4c_b4_resident_epoch.cpp
+ * :485-498, and the host-loop runner K times per epoch,
+ * g4c_b4_epoch_runner.cpp:245-382).  No controller runs: the caller decides
+ * tokens, termination and slots between calls.
+ * Inputs, in the ABI's order (host arrays): token i64[4] (the ABI's [4,1]),
+ * position i64[4], seq_len i32[4] ([4,1]), key_cache, slot i32[4], active
+ * i32[4], block_table i32[4*blocks_per_row], value_cache, tiling u8[72]
+ * (may be NULL; accepted and unused).
+ * key_cache / value_cache: device bf16 [layers][num_blocks][block_size]
+ * [kv_heads][head_dim] on the engine's device, 16-byte aligned, updated in
+ * place (the ABI's K and V outputs); both NULL for the engine's resident
+ * caches.
+ * Outputs (host): logits_out f32 [4][vocab], next_position_out i64[4] =
+ * position + 1 for active rows, position otherwise.
+ * For active rows the step computes exactly what the reference decoder does
+ * (batched_decoder_step.py:277-417): the new K/V are written at slot[row]
+ * and attention covers positions < seq_len.  Rows with active 0 write no K/V
+ * and keep their position; their logits are not computed from attention and
+ * must not be used (the reference's callers never read them, controller
+ * :547-552).
+ * Returns 0, -1 for invalid arguments (a token outside the vocabulary, an
+ * active row whose position is outside the capacity or whose slot is not its
+ * position's block-table slot, a block-table entry outside the cache, a
+ * sequence length above the capacity, caches that are not device memory of
+ * the engine's device), -3 when a device-side wait gave up, -4 for a
+ * tensor-parallel engine, or a CUDA error code; cruise_epoch_last_error
+ * explains -1, -3 and -4. */
+int32_t cruise_decoder_step(void *engine, const int64_t *token,
+                            const int64_t *position, const int32_t *seq_len,
+                            void *key_cache, const int32_t *slot,
+                            const int32_t *active, const int32_t *block_table,
+                            void *value_cache, const uint8_t *tiling,
+                            float *logits_out, int64_t *next_position_out);
+
+/* Device time of the last epoch (or decoder step) in microseconds (CUDA
+ * events around the epoch kernel) and the number of kernels it launched. */
 int32_t cruise_epoch_last_timing(void *engine, double *device_us,
                                  int32_t *kernel_launches);
 

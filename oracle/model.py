@@ -12,7 +12,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .synth import synth_bf16_bits
+from .synth import synth_bf16_bits, synth_bf16_bits_c
 
 LAYER_KEYS = (
     "input_layernorm.weight",
@@ -112,13 +112,19 @@ def tensor_id(cfg: OracleConfig, name: str) -> int:
 
 
 def seeded_weights(
-    cfg: OracleConfig, seed: int, std: float = 0.02, dtype: torch.dtype = torch.bfloat16
+    cfg: OracleConfig, seed: int, std: float = 0.02, dtype: torch.dtype = torch.bfloat16,
+    use_c: bool = False,
 ) -> dict[str, torch.Tensor]:
-    """All weights of the model as CPU tensors with the generator's bf16 values."""
+    """All weights of the model as CPU tensors with the generator's bf16 values.
+    ``use_c`` computes them with oracle/csynth.c on every host core (the same
+    bits; a full 7B model in seconds instead of minutes)."""
     weights = {}
     for name, shape in tensor_shapes(cfg).items():
         count = int(np.prod(shape))
-        bits = synth_bf16_bits(seed, tensor_id(cfg, name), count, std)
-        value = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+        if use_c:
+            bits = synth_bf16_bits_c(seed, tensor_id(cfg, name), count, std)
+        else:
+            bits = synth_bf16_bits(seed, tensor_id(cfg, name), count, std)
+        value = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
         weights[name] = value.reshape(shape).to(dtype)
     return weights

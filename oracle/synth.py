@@ -74,3 +74,49 @@ def synth_bf16_bits(
     ).astype(np.int64)
     centred = (2 * lanes - CENTER).astype(np.float32)
     return f32_to_bf16_bits(centred * scale_f32(std))
+
+
+# -- the same generator in C (oracle/csynth.c), for full-depth models ----------
+_CSYNTH = None
+
+
+def csynth_library():
+    """oracle/libcsynth.so, compiled with gcc (OpenMP) when missing or older
+    than its source.  Raises when no C compiler is available."""
+    global _CSYNTH
+    if _CSYNTH is not None:
+        return _CSYNTH
+    import ctypes
+    import os
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent
+    src, lib = here / "csynth.c", here / "libcsynth.so"
+    if not lib.exists() or lib.stat().st_mtime < src.stat().st_mtime:
+        cc = shutil.which("gcc") or shutil.which("cc")
+        if cc is None:
+            raise RuntimeError("oracle/csynth.c needs a C compiler (gcc)")
+        tmp = lib.with_name(f"libcsynth.so.tmp{os.getpid()}")
+        subprocess.run([cc, "-O3", "-fopenmp", "-shared", "-fPIC", "-o", str(tmp), str(src)], check=True)
+        os.replace(tmp, lib)
+    handle = ctypes.CDLL(str(lib))
+    handle.cruise_oracle_synth.argtypes = [ctypes.c_uint64, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_float, ctypes.c_void_p, ctypes.c_int32]
+    handle.cruise_oracle_synth.restype = None
+    _CSYNTH = handle
+    return handle
+
+
+def synth_bf16_bits_c(seed: int, tensor_id: int, count: int, std: float = 0.02, start: int = 0,
+                      threads: int | None = None) -> np.ndarray:
+    """:func:`synth_bf16_bits` computed by oracle/csynth.c on ``threads`` host
+    threads (default: every core this process may use)."""
+    import os
+
+    out = np.empty(count, dtype=np.uint16)
+    n = threads or len(os.sched_getaffinity(0))
+    csynth_library().cruise_oracle_synth(seed, tensor_id, start, count, float(scale_f32(std)),
+                                         out.ctypes.data, n)
+    return out

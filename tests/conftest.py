@@ -19,3 +19,20 @@ def cuda_ok():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return True
+
+
+def pytest_terminal_summary(terminalreporter):
+    """How many engine epochs were compared with the oracle, and every
+    permitted near-tie divergence among them (row: step)."""
+    try:
+        from scenario import EPOCH_LOG
+    except ImportError:
+        return
+    if not EPOCH_LOG:
+        return
+    rows = sum(n for _, n, _ in EPOCH_LOG)
+    diverged = [(label, d) for label, _, d in EPOCH_LOG if d]
+    count = sum(len(d) for _, d in diverged)
+    terminalreporter.write_line(
+        f"oracle parity: {len(EPOCH_LOG)} epochs, {rows} active rows compared, "
+        f"{count} permitted near-tie divergence(s)" + (f": {diverged}" if diverged else ""))

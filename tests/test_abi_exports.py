@@ -12,7 +12,7 @@ def declared_functions() -> set[str]:
     names = set()
     for header in INCLUDE.glob("*.h"):
         text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
-        names.update(re.findall(r"\b((?:resident|cruise)_epoch_\w+)\s*\(", text))
+        names.update(re.findall(r"\b((?:resident_epoch|cruise_epoch|cruise_decoder)_\w+)\s*\(", text))
     return names
 
 

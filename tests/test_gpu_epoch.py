@@ -17,9 +17,7 @@ from oracle.decoder import OracleDecoder
 from oracle.epoch import EpochTrace, OracleEpochController
 from oracle.model import TINY as ORACLE_TINY
 from oracle.model import seeded_weights, tensor_shapes
-from scenario import (
-    compare_histories, decode_inputs, import_payload, make_scenario, prefill_epochs,
-)
+from scenario import check_epoch, decode_inputs, import_payload, make_scenario, prefill_epochs
 
 pytestmark = pytest.mark.gpu
 
@@ -94,15 +92,9 @@ def test_prefill_then_decode_epoch(cuda_ok, tiny_weights, seed):
     out = engine.run(**inputs, want_logits=True)
     history, control = oracle.run(**inputs, trace=trace)
     assert out.status == int(control[3]) == 0
-    diverged = compare_histories(out.history, history, trace.margins)
-    for step, logits in enumerate(trace.logits):
-        for row in range(4):
-            if trace.active[step][row] and row not in diverged:
-                err = rel_err(torch.from_numpy(out.logits[step, row]), logits[row])
-                assert err <= TOL, f"step {step} row {row}: logits rel err {err:.3g}"
-    if not diverged:
-        np.testing.assert_array_equal(out.control_out, control)
-        assert_kv_close(engine, oracle, owned)
+    key, value = engine.read_kv()
+    check_epoch(out, history, control, trace, inputs, kv=(key, value, oracle.key, oracle.value),
+                block_size=ORACLE_TINY.block_size, label=f"tiny decode seed {seed}")
     engine.close()
 
 
@@ -122,9 +114,9 @@ def test_import_then_decode_epoch(cuda_ok, tiny_weights):
     history, control = oracle.run(**inputs, import_payload=payload, trace=trace)
     assert out.status == int(control[3]) == 0
     assert int(out.control_out[5]) == int(control[5]) != 0   # Adler-32 of the imported blocks
-    diverged = compare_histories(out.history, history, trace.margins)
-    if not diverged:
-        np.testing.assert_array_equal(out.control_out, control)
+    key, value = engine.read_kv()
+    check_epoch(out, history, control, trace, inputs, kv=(key, value, oracle.key, oracle.value),
+                block_size=ORACLE_TINY.block_size, label="tiny import")
     engine.close()
 
 
