@@ -30,9 +30,11 @@ def pytest_terminal_summary(terminalreporter):
         return
     if not EPOCH_LOG:
         return
-    rows = sum(n for _, n, _ in EPOCH_LOG)
-    diverged = [(label, d) for label, _, d in EPOCH_LOG if d]
+    rows = sum(entry[1] for entry in EPOCH_LOG)
+    near = sum(entry[3] for entry in EPOCH_LOG)
+    diverged = [(entry[0], entry[2]) for entry in EPOCH_LOG if entry[2]]
     count = sum(len(d) for _, d in diverged)
     terminalreporter.write_line(
-        f"oracle parity: {len(EPOCH_LOG)} epochs, {rows} active rows compared, "
-        f"{count} permitted near-tie divergence(s)" + (f": {diverged}" if diverged else ""))
+        f"oracle parity: {len(EPOCH_LOG)} epochs, {rows} active rows compared, {near} near-tie row-steps "
+        f"(oracle top-2 margin < 2e-2), {count} permitted near-tie divergence(s)"
+        + (f": {diverged}" if diverged else ""))
