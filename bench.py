@@ -484,7 +484,7 @@ def run_gpu(args) -> None:
     single = EpochEngine(cfg, device=device)
     single.init_synthetic(seed=0)
     synth_s = time.perf_counter() - t0
-    need = (args.warmup + args.steps + (1 if args.trace else 0)) * args.k
+    need = (args.warmup + args.steps + (1 if args.trace else 0) + (1 if args.trace_cta else 0)) * args.k
 
     # the single-GPU cohort of this rank (seed 1000 + rank; rank 0's is the tensor-parallel cohort)
     check_logits = tp and rank == 0
@@ -510,6 +510,8 @@ def run_gpu(args) -> None:
     if args.trace and (rank == 0 or tp):
         # a tensor-parallel group runs the traced epoch on every rank
         print_trace(group if tp else single, tp_cohort if tp else single_cohort, cfg, args.k, show=rank == 0)
+    if args.trace_cta and (rank == 0 or tp):
+        print_trace_cta(group if tp else single, tp_cohort if tp else single_cohort, cfg, show=rank == 0)
     dp = None
     if tp:
         d = runs["single"]
@@ -582,6 +584,71 @@ def run_gpu(args) -> None:
 
 
 PHASE_NAMES = ("qkv", "attention", "o_proj", "gate_up", "down")
+
+
+def print_trace_cta(engine, cohort, cfg, show: bool = True) -> None:
+    """One traced epoch with every CTA's phase marks: per phase kind, summed
+    over layers and steps (us per decode step), the medians over CTAs of
+    activation staging, tile stream and epilogue, the spread of the arrivals
+    (last CTA minus median), the release (first and last CTA out minus last
+    in), and the CTAs that arrived last most often."""
+    engine.set_trace(2)
+    out, _ = cohort.step()
+    engine.set_trace(False)
+    L = cfg.num_layers
+    phases = 5 * L + 2
+    count = 2 + out.model_calls * phases + 1
+    raw = engine.read_trace_cta(count).astype(np.int64)
+    # unwrap the 32-bit stamps against barrier 1's exit of CTA 0
+    base = raw[1, 0, 0]
+    t = np.where(raw == 0, 0, (raw - base) % (1 << 32))
+    first = 2
+    acc, last_cta = {}, {}
+    for step in range(out.model_calls):
+        for ph in range(phases):
+            j = first + step * phases + ph + 1
+            name = "lm_head" if ph == 5 * L else "control" if ph > 5 * L else PHASE_NAMES[ph % 5]
+            a = acc.setdefault(name, np.zeros(15))
+            start, staged, tiles, arrive = t[j - 1, :, 0], t[j, :, 1], t[j, :, 2], t[j, :, 3]
+            e_start, e_done, e_fenced = t[j, :, 4], t[j, :, 6], t[j, :, 7]
+            if e_done.any():
+                last_flush, warps_done = t[j, :, 8], t[j, :, 9]
+                a[12] += np.median(warps_done - tiles)
+                a[13] += np.median(last_flush - warps_done)
+                a[14] += np.median(e_done - last_flush)
+                a[8] += np.median(e_start - start)
+                a[9] += np.median(raw[j, :, 5])
+                a[10] += np.median(e_done - tiles)
+                a[11] += np.median(e_fenced - e_done)
+            exit_ = t[j, :, 0]
+            a[0] += np.median(exit_) - np.median(start)
+            if staged.any():
+                a[1] += np.median(staged - start)
+                a[2] += np.median(tiles - staged)
+                a[3] += np.median(arrive - tiles)
+            else:
+                a[3] += np.median(arrive - start)
+            a[4] += arrive.max() - np.median(arrive)
+            a[5] += exit_.min() - arrive.max()
+            a[6] += exit_.max() - arrive.max()
+            a[7] += start.max() - start.min()
+            lc = last_cta.setdefault(name, {})
+            c = int(arrive.argmax())
+            lc[c] = lc.get(c, 0) + 1
+    if not show:
+        return
+    calls = out.model_calls
+    print(f"per-CTA trace: epoch {out.device_us:.1f} us, {calls} steps, {raw.shape[1]} CTAs; per step, us "
+          f"[phase | med staging  med tiles  med epilogue | last-arrival lag | release first/last | start skew]"
+          f"  last CTAs\n    epilogue warp, medians over CTAs: [start after phase start | partner wait | "
+          f"last segment after last tile | fence]", file=sys.stderr)
+    for name in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "control"):
+        a = acc.get(name, np.zeros(15)) / calls / 1e3
+        top = sorted(last_cta.get(name, {}).items(), key=lambda kv: -kv[1])[:4]
+        print(f"  {name:9s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} | {a[5]:6.1f} {a[6]:6.1f} "
+              f"| {a[7]:6.1f}  {top}\n  {'':9s} {'':8s}   epilogue warp: {a[8]:7.1f} | {a[9]:7.1f} | {a[10]:7.1f} | "
+              f"{a[11]:7.1f} || slowest consumer warp after warp 0: {a[12]:6.1f}, last flush taken after that: "
+              f"{a[13]:6.1f}, last segment's epilogue: {a[14]:6.1f}", file=sys.stderr)
 
 
 def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
@@ -838,6 +905,8 @@ def main() -> None:
     parser.add_argument("--no-host-loop", action="store_true",
                         help="skip the resident-epoch vs host-loop comparison (N=1)")
     parser.add_argument("--trace", action="store_true", help="per-phase timing of one extra epoch (stderr)")
+    parser.add_argument("--trace-cta", action="store_true",
+                        help="every CTA's phase marks of one extra epoch, summarised (stderr)")
     parser.add_argument("--layers", type=int, default=0, help="profiling only: truncate the model to N layers")
     parser.add_argument("--vocab", type=int, default=0, help="profiling only: vocabulary size")
     parser.add_argument("--tp", action="store_true",

@@ -87,6 +87,9 @@ SIGNATURES = {
     "cruise_epoch_read_trace": (
         ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
     ),
+    "cruise_epoch_read_trace_cta": (
+        ctypes.c_int32, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32, i32p]
+    ),
     "cruise_epoch_last_error": (ctypes.c_char_p, [ctypes.c_void_p]),
     "cruise_epoch_prefill": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]),
     "cruise_epoch_stream_enable": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32]),

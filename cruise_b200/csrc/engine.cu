@@ -28,6 +28,7 @@ namespace cruise {
 namespace {
 
 constexpr long kDefaultL2AheadKb = 128;   // L2 run-ahead of the weight stream per CTA
+constexpr uint32_t kDefaultL2Hints = 1;   // weight copies into the ring mark their L2 lines evict-first
 
 constexpr int kLayerTensors = 12;  // per-layer checkpoint tensors, in id order
 const char *const kLayerKeys[kLayerTensors] = {
@@ -188,9 +189,13 @@ struct Engine {
   int stages = 0;
   int xs_stride = 0;
   uint32_t l2_ahead = 0;   // bytes of L2 run-ahead per CTA (CRUISE_L2_AHEAD_KB)
+  uint32_t l2_hints = 0;   // L2 eviction-priority hints of the weight stream (CRUISE_L2_HINTS)
   int down_xglobal = 0;
+  int o_xglobal = 0;
   uint64_t *trace = nullptr;     // per-launch phase timestamps (optional)
   bool trace_on = false;
+  uint32_t *trace_cta = nullptr; // per-CTA phase timestamps (allocated when first enabled)
+  bool trace_cta_on = false;
   size_t smem = 0;
   // device memory
   void *weights = nullptr;   // one allocation for every weight tensor
@@ -202,7 +207,8 @@ struct Engine {
   bf16 *key_cache = nullptr, *value_cache = nullptr;
   bf16 *rope_cos = nullptr, *rope_sin = nullptr;
   bf16 *h = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr;
-  float *partials = nullptr, *arg_val = nullptr, *logits = nullptr;
+  uint64_t *partials = nullptr;   // tagged split row-group partials, right after d_sync
+  float *arg_val = nullptr, *logits = nullptr;
   int32_t *arg_idx = nullptr, *arg_bad = nullptr;
   EpochIO *d_io = nullptr;
   ResidentState *d_res = nullptr;
@@ -372,6 +378,7 @@ void destroy_engine(Engine *e) {
   cudaFree(e->d_payload);
   for (void *ptr : e->opened) cudaIpcCloseMemHandle(ptr);
   cudaFree(e->d_peers);
+  cudaFree(e->trace_cta);
   cudaFree(e->xchg);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->h_stream) cudaFreeHost(e->h_stream);
@@ -433,6 +440,12 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
   // the projections that stage it there; the down projection reads its input
   // from L2 instead when it runs one 64-wide k-step per consumer warp.
   e->down_xglobal = pick_kc(m.I_pad) == 64 * kConsumerWarps;
+  {
+    // the O projection reads the attention output straight from L2 when it
+    // runs one 64-wide k-step per consumer warp (CRUISE_O_XGLOBAL=0 stages it)
+    const char *env = std::getenv("CRUISE_O_XGLOBAL");
+    e->o_xglobal = pick_kc(m.Hq) == 64 * kConsumerWarps && (env == nullptr || std::strtol(env, nullptr, 10) != 0);
+  }
   const int kmax = e->down_xglobal ? m.H : std::max(m.H, m.I_pad);
   e->xs_stride = kmax + 8;
   if (const char *env = std::getenv("CRUISE_TP_TIMEOUT_MS")) {
@@ -443,6 +456,8 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
     const char *env = std::getenv("CRUISE_L2_AHEAD_KB");
     const long kb = env != nullptr ? std::strtol(env, nullptr, 10) : kDefaultL2AheadKb;
     e->l2_ahead = static_cast<uint32_t>(std::min(std::max(kb, 0L), 4096L)) * 1024u;
+    const char *hints = std::getenv("CRUISE_L2_HINTS");
+    e->l2_hints = static_cast<uint32_t>(hints != nullptr ? std::strtol(hints, nullptr, 10) & 3 : kDefaultL2Hints);
   }
   // the attention unit's scratch aliases the activation rows and the reduction ring
   if (attn_scratch_bytes(m.d, m.C) >
@@ -519,14 +534,13 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
   const size_t o_cos = take2(static_cast<size_t>(m.C) * m.d * 2), o_sin = take2(static_cast<size_t>(m.C) * m.d * 2);
   const size_t o_h = take2(kBatch * H * 2), o_qkv = take2(static_cast<size_t>(kBatch) * m.Nqkv * 2);
   const size_t o_attn = take2(kBatch * H * 2), o_act = take2(static_cast<size_t>(kBatch) * m.I_pad * 2);
-  const size_t o_part = take2(static_cast<size_t>(e->sms) * 64 * 4);
   const size_t o_av = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ai = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_ab = take2(static_cast<size_t>(e->sms) * kBatch * 4);
   const size_t o_lg = take2(static_cast<size_t>(kMaxSteps) * kBatch * m.V * 4);
   const size_t o_trace = take2(kTraceSeries * kTraceMax * sizeof(uint64_t));
   const size_t o_io = take2(sizeof(EpochIO)), o_res = take2(sizeof(ResidentState));
-  const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sizeof(SyncState));
+  const size_t o_work = take2(sizeof(EpochWork)), o_sync = take2(sync_bytes(e->sms));
   if (cudaMalloc(&e->state, st) != cudaSuccess) return fail("state allocation");
   cudaMemsetAsync(e->state, 0, st, e->stream);
   uint8_t *sb = static_cast<uint8_t *>(e->state);
@@ -538,7 +552,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
   e->qkv = reinterpret_cast<bf16 *>(sb + o_qkv);
   e->attn = reinterpret_cast<bf16 *>(sb + o_attn);
   e->act = reinterpret_cast<bf16 *>(sb + o_act);
-  e->partials = reinterpret_cast<float *>(sb + o_part);
+  e->partials = reinterpret_cast<uint64_t *>(sb + o_sync + sizeof(SyncState));
   e->arg_val = reinterpret_cast<float *>(sb + o_av);
   e->arg_idx = reinterpret_cast<int32_t *>(sb + o_ai);
   e->arg_bad = reinterpret_cast<int32_t *>(sb + o_ab);
@@ -946,8 +960,11 @@ EpochParams engine_params(const Engine *e) {
   p.stages = e->stages;
   p.xs_stride = e->xs_stride;
   p.down_xglobal = e->down_xglobal;
+  p.o_xglobal = e->o_xglobal;
   p.trace = e->trace_on ? e->trace : nullptr;
+  p.trace_cta = e->trace_cta_on ? e->trace_cta : nullptr;
   p.l2_ahead = e->l2_ahead;
+  p.l2_hints = e->l2_hints;
   p.mode = kModeEpoch;
   return p;
 }
@@ -1002,13 +1019,15 @@ int32_t run_epoch(Engine *e, const int64_t *token, const int64_t *position, cons
   }
   const size_t in_bytes = offsetof(EpochIO, history);
   err = cudaMemcpyAsync(e->d_io, io, in_bytes, cudaMemcpyHostToDevice, e->stream);
-  if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sizeof(SyncState), e->stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sync_bytes(e->sms), e->stream);
   if (err != cudaSuccess) return set_err(e, err, "epoch inputs");
 
   EpochParams p = engine_params(e);
   p.logits = logits_out != nullptr ? e->logits : nullptr;
   p.import_payload = payload_on_device ? static_cast<const uint8_t *>(payload) : e->d_payload;
   if (e->trace_on) cudaMemsetAsync(e->trace, 0, kTraceSeries * kTraceMax * sizeof(uint64_t), e->stream);
+  if (e->trace_cta_on)
+    cudaMemsetAsync(e->trace_cta, 0, static_cast<size_t>(kTraceMax) * e->sms * kTraceCtaWords * sizeof(uint32_t), e->stream);
   // every device-side wait gives up after 2 s; under tensor parallelism after
   // 20 s by default (CRUISE_TP_TIMEOUT_MS at creation), since a rank's first
   // wait also covers the other ranks' launch skew
@@ -1108,11 +1127,12 @@ int32_t run_decoder_step(Engine *e, const int64_t *token, const int64_t *positio
   std::memcpy(io->active, active, sizeof(io->active));
   std::memcpy(io->block_table, block_table, sizeof(int32_t) * kBatch * m.bpr);
   cudaError_t err = cudaMemcpyAsync(e->d_io, io, offsetof(EpochIO, history), cudaMemcpyHostToDevice, e->stream);
-  if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sizeof(SyncState), e->stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->d_sync, 0, sync_bytes(e->sms), e->stream);
   if (err != cudaSuccess) return set_err(e, err, "decoder step inputs");
   EpochParams p = engine_params(e);
   p.mode = kModeDecoderStep;
   p.trace = nullptr;
+  p.trace_cta = nullptr;
   p.logits = e->logits;
   if (key_cache != nullptr) {
     p.key_cache = static_cast<bf16 *>(key_cache);
@@ -1337,7 +1357,7 @@ cudaError_t noalloc_base(int device, void **base) {
 // Offsets in the static scratch of everything one epoch uses besides the
 // engine's model state (weights, KV cache, RoPE tables, resident row state).
 struct NoAllocLayout {
-  size_t io, work, sync, h, qkv, attn, act, part, av, ai, ab, total;
+  size_t io, work, sync, h, qkv, attn, act, av, ai, ab, total;
 };
 
 NoAllocLayout noalloc_layout(const Engine *e) {
@@ -1351,12 +1371,11 @@ NoAllocLayout noalloc_layout(const Engine *e) {
   };
   l.io = take(sizeof(EpochIO));
   l.work = take(sizeof(EpochWork));
-  l.sync = take(sizeof(SyncState));
+  l.sync = take(sync_bytes(e->sms));   // SyncState, then the tagged partial-sum words
   l.h = take(static_cast<size_t>(kBatch) * m.H * 2);
   l.qkv = take(static_cast<size_t>(kBatch) * m.Nqkv * 2);
   l.attn = take(static_cast<size_t>(kBatch) * m.H * 2);
   l.act = take(static_cast<size_t>(kBatch) * m.I_pad * 2);
-  l.part = take(static_cast<size_t>(e->sms) * 64 * 4);
   l.av = take(static_cast<size_t>(e->sms) * kBatch * 4);
   l.ai = take(static_cast<size_t>(e->sms) * kBatch * 4);
   l.ab = take(static_cast<size_t>(e->sms) * kBatch * 4);
@@ -1421,7 +1440,7 @@ int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *positi
   p.qkv = reinterpret_cast<bf16 *>(sb + l.qkv);
   p.attn = reinterpret_cast<bf16 *>(sb + l.attn);
   p.act = reinterpret_cast<bf16 *>(sb + l.act);
-  p.partials = reinterpret_cast<float *>(sb + l.part);
+  p.partials = reinterpret_cast<uint64_t *>(sb + l.sync + sizeof(SyncState));
   p.arg_val = reinterpret_cast<float *>(sb + l.av);
   p.arg_idx = reinterpret_cast<int32_t *>(sb + l.ai);
   p.arg_bad = reinterpret_cast<int32_t *>(sb + l.ab);
@@ -1435,9 +1454,11 @@ int32_t run_epoch_noalloc(Engine *e, const int64_t *token, const int64_t *positi
   p.stages = e->stages;
   p.xs_stride = e->xs_stride;
   p.down_xglobal = e->down_xglobal;
+  p.o_xglobal = e->o_xglobal;
   p.trace = nullptr;
   p.timeout_ns = 2000000000ull;   // every device-side wait gives up after 2 s
   p.l2_ahead = e->l2_ahead;
+  p.l2_hints = e->l2_hints;
   p.tp_size = 1;
   void *args[] = {&p};
   cudaEventRecord(e->ev0, e->stream);
@@ -1656,8 +1677,35 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us, int32_t *kerne
 
 int32_t cruise_epoch_set_trace(void *engine, int32_t enable) {
   if (engine == nullptr) return -1;
-  static_cast<Engine *>(engine)->trace_on = enable != 0;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  if (enable == 2 && e->trace_cta == nullptr) {
+    cudaSetDevice(e->device);
+    const cudaError_t err = cudaMalloc(&e->trace_cta, static_cast<size_t>(cruise::kTraceMax) * e->sms * cruise::kTraceCtaWords * sizeof(uint32_t));
+    if (err != cudaSuccess) {
+      e->trace_cta = nullptr;
+      return cruise::set_err(e, err, "per-CTA trace buffer");
+    }
+  }
+  e->trace_on = enable != 0;
+  e->trace_cta_on = enable == 2;
   return 0;
+}
+
+int32_t cruise_epoch_read_trace_cta(void *engine, uint32_t *stamps, int32_t barriers, int32_t *ctas) {
+  if (engine == nullptr || ctas == nullptr || barriers < 0 || barriers > cruise::kTraceMax ||
+      (stamps == nullptr && barriers > 0))
+    return -1;
+  Engine *e = static_cast<Engine *>(engine);
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  *ctas = e->sms;
+  if (barriers == 0) return 0;
+  if (e->trace_cta == nullptr) return -1;
+  cudaSetDevice(e->device);
+  const cudaError_t err = cruise::copy_sync(e, stamps, e->trace_cta,
+                                            static_cast<size_t>(barriers) * e->sms * cruise::kTraceCtaWords * sizeof(uint32_t),
+                                            cudaMemcpyDeviceToHost);
+  return cruise::set_err(e, err, "read per-CTA trace");
 }
 
 int32_t cruise_epoch_prefill(void *engine, const int64_t *prompt_tokens, const int32_t *prompt_lens,

@@ -88,7 +88,7 @@ __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int k
         g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = lw.w_in; g.embed_src = layer == 0;
         break;
       case kO:
-        g.W = lw.o_w; g.N = m.H; g.K = m.Hq; g.xmode = kXCopy; g.xsrc = p.attn;
+        g.W = lw.o_w; g.N = m.H; g.K = m.Hq; g.xmode = p.o_xglobal ? kXGlobal : kXCopy; g.xsrc = p.attn;
         g.xsrc_stride = m.Hq;
         break;
       case kGU:
@@ -252,6 +252,8 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
     const int lane = threadIdx.x;
     int ok = 1;
     if (lane == 0) {
+      if (p.trace_cta != nullptr && index < kTraceMax)
+        p.trace_cta[(static_cast<size_t>(index) * p.grid + blockIdx.x) * kTraceCtaWords + 3] = static_cast<uint32_t>(globaltimer());
       if (p.trace != nullptr && index < kTraceMax) {
         if (blockIdx.x == 0) p.trace[kTraceMax + index] = globaltimer();   // CTA 0 finished its share
         atomicMax(reinterpret_cast<unsigned long long *>(&p.trace[4 * kTraceMax + index]),
@@ -288,6 +290,8 @@ __device__ bool grid_barrier(const EpochParams &p, const Smem &s, uint32_t index
     if (lane == 0) {
       if (ok && aborted(p)) ok = 0;
       if (p.trace != nullptr && blockIdx.x == 0 && index < kTraceMax) p.trace[index] = globaltimer();
+      if (p.trace_cta != nullptr && index < kTraceMax)
+        p.trace_cta[(static_cast<size_t>(index) * p.grid + blockIdx.x) * kTraceCtaWords] = static_cast<uint32_t>(globaltimer());
       s.misc[0] = ok;
     }
   }
@@ -307,6 +311,24 @@ __device__ __forceinline__ float tp_recv(const EpochParams &p, const uint64_t *w
       if ((++polls & 15) == 0) {
         if (aborted(p)) return 0.f;
         if (globaltimer() > deadline) { raise_error(p, 300); return 0.f; }
+      }
+    }
+  }
+  return __uint_as_float(static_cast<uint32_t>(v));
+}
+
+// The fp32 value of a tagged partial-sum word once it carries `tag` (the
+// phase's sequence number in the high half).  A wait that runs out raises the
+// epoch error and returns 0, so the kernel winds down.
+__device__ __forceinline__ float tagged_recv(const EpochParams &p, const uint64_t *word, uint32_t tag) {
+  uint64_t v = ld_relaxed_gpu_u64(word);
+  if (static_cast<uint32_t>(v >> 32) != tag) {
+    const uint64_t deadline = globaltimer() + p.timeout_ns;
+    uint32_t polls = 0;
+    while (static_cast<uint32_t>((v = ld_relaxed_gpu_u64(word)) >> 32) != tag) {
+      if ((++polls & 15) == 0) {
+        if (aborted(p)) return 0.f;
+        if (globaltimer() > deadline) { raise_error(p, 1001); return 0.f; }
       }
     }
   }
@@ -379,6 +401,8 @@ struct L2RunAhead {
   const uint8_t *W = nullptr;
   uint64_t bytes = 0;   // issued so far
 
+  uint64_t policy = 0;   // evict-last policy of the prefetched lines (l2_hints bit 1)
+
   __device__ void top_up(const EpochParams &p, uint64_t loaded) {
     const int L = p.m.L;
     const int phases = 5 * L + 2;
@@ -397,7 +421,11 @@ struct L2RunAhead {
       }
       const int64_t per = kStageBytes / tile_bytes;   // one ring stage's worth per prefetch
       const int64_t n = t1 - t < per ? t1 - t : per;
-      prefetch_l2(W + t * tile_bytes, static_cast<uint32_t>(n * tile_bytes));
+      if (p.l2_hints & 2u) {
+        prefetch_l2_hint(W + t * tile_bytes, static_cast<uint32_t>(n * tile_bytes), policy);
+      } else {
+        prefetch_l2(W + t * tile_bytes, static_cast<uint32_t>(n * tile_bytes));
+      }
       t += n;
       bytes += static_cast<uint64_t>(n * tile_bytes);
     }
@@ -412,6 +440,9 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
   uint32_t issued = 0;
   bool stop = false;
   L2RunAhead ahead;
+  if (p.l2_hints & 2u) ahead.policy = l2_policy_evict_last();
+  // weights are read once per step: their lines may leave L2 first once copied
+  const uint64_t copy_policy = (p.l2_hints & 1u) ? l2_policy_evict_first() : 0;
   uint64_t loaded = 0;   // bytes of bulk copies issued into the ring
   for (int step = 0; step < kMaxSteps && !stop; ++step) {
     if (lane == 0) stop = !wait_step(p, s, step);
@@ -434,8 +465,13 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
             const uint32_t bytes = static_cast<uint32_t>(n * tile_elems * 2);
             loaded += bytes;
             mbar_arrive_expect_tx(&s.full[ring.slot], bytes);
-            bulk_g2s(s.ring + static_cast<size_t>(ring.slot) * kStageBytes, g.W + t * tile_elems, bytes,
-                     &s.full[ring.slot]);
+            if (p.l2_hints & 1u) {
+              bulk_g2s_hint(s.ring + static_cast<size_t>(ring.slot) * kStageBytes, g.W + t * tile_elems, bytes,
+                            &s.full[ring.slot], copy_policy);
+            } else {
+              bulk_g2s(s.ring + static_cast<size_t>(ring.slot) * kStageBytes, g.W + t * tile_elems, bytes,
+                       &s.full[ring.slot]);
+            }
           }
         }
         stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
@@ -517,14 +553,18 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
     for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
   }
   named_sync(1, kConsumerThreads);
-  if (tid < kBatch) {
+  // every thread sums the 8 warp partials in the same order and computes the
+  // 4 inverse RMS values itself (no second barrier)
+  float rinv[kBatch];
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
     float total = 0.f;
-    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + tid];
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + b];
     // mean = sum / K; rsqrt = 1 / sqrt(mean + eps), each IEEE-rounded as on the CPU
     const float var = __fdiv_rn(total, static_cast<float>(K));
-    s.nrm[32 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
+    rinv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
   }
-  named_sync(1, kConsumerThreads);
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int k8 = tid + j * kConsumerThreads;
@@ -532,7 +572,7 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
     const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&wv[j]);
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
-      const float r = s.nrm[32 + b];
+      const float r = rinv[b];
       const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&v[j][b]);
       uint4 o;
       __nv_bfloat162 *o2 = reinterpret_cast<__nv_bfloat162 *>(&o);
@@ -790,6 +830,8 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
   if (!xg) load_x(p, s, g);
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
     p.trace[2 * kTraceMax + trace_slot] = globaltimer();   // activations staged
+  if (p.trace_cta != nullptr && tid == 0 && trace_slot < kTraceMax)
+    p.trace_cta[(static_cast<size_t>(trace_slot) * p.grid + blockIdx.x) * kTraceCtaWords + 1] = static_cast<uint32_t>(globaltimer());
   if (g.kc == 64 * kConsumerWarps && kStageBytes / (kRows * g.kc * 2) == 2) {
     gemv_tiles_k512(p, s, g, tr, ring, red);
   } else {
@@ -797,6 +839,11 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
   }
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
     p.trace[3 * kTraceMax + trace_slot] = globaltimer();   // last tile consumed by warp 0
+  if (p.trace_cta != nullptr && tid == 0 && trace_slot < kTraceMax)
+    p.trace_cta[(static_cast<size_t>(trace_slot) * p.grid + blockIdx.x) * kTraceCtaWords + 2] = static_cast<uint32_t>(globaltimer());
+  if (p.trace_cta != nullptr && (tid & 31) == 0 && trace_slot < kTraceMax)   // the last consumer warp done
+    atomicMax(&p.trace_cta[(static_cast<size_t>(trace_slot) * p.grid + blockIdx.x) * kTraceCtaWords + 9],
+              static_cast<uint32_t>(globaltimer()));
 }
 
 // ---- epilogue warp: one projection phase --------------------------------------------------------
@@ -809,6 +856,13 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
   const int lane = threadIdx.x & 31;
   const ModelDims &m = p.m;
   const TileRange tr = tile_range(g, blockIdx.x, p.grid);
+  // per-CTA trace of the epilogue warp: [4] started, [5] ns waited for the
+  // stream-K partner, [6] last segment done, [7] outputs fenced
+  uint32_t *const mark = p.trace_cta != nullptr && trace_slot < kTraceMax
+                             ? p.trace_cta + (static_cast<size_t>(trace_slot) * p.grid + blockIdx.x) * kTraceCtaWords
+                             : nullptr;
+  uint64_t partner_ns = 0;
+  if (mark != nullptr && lane == 0) mark[4] = static_cast<uint32_t>(globaltimer());
   float best = -INFINITY;
   int32_t best_i = INT_MAX, bad = 0;
 
@@ -846,20 +900,15 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
       float part0 = 0.f, part1 = 0.f;
       if (head_seg && !group_end) {
         // finisher: the next CTA publishes the rest of this row group early in
-        // its range; fetch it while the consumers are still streaming
-        if (lane == 0) {
-          const uint64_t deadline = globaltimer() + p.timeout_ns;
-          uint32_t polls = 0;
-          while (ld_acquire_u32(&p.sync->flags[blockIdx.x + 1]) != seq) {
-            if (aborted(p)) break;
-            if ((++polls & 15) == 0 && globaltimer() > deadline) { raise_error(p, 1001); break; }
-          }
-        }
-        __syncwarp();
-        part0 = __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane);
-        part1 = __ldcg(p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane + 32);
+        // its range as tagged words; each lane takes its two once their tag
+        // is this phase's (an aligned 64-bit access is single-copy atomic)
+        const uint64_t wait0 = globaltimer();
+        part0 = tagged_recv(p, p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane, seq);
+        part1 = tagged_recv(p, p.partials + static_cast<size_t>(blockIdx.x + 1) * 64 + lane + 32, seq);
+        if (lane == 0) partner_ns += globaltimer() - wait0;
       }
       wait_bar(p, &s.red_full[red.slot], red.parity, s.prod_ctl, 1003);
+      if (mark != nullptr && lane == 0) mark[8] = static_cast<uint32_t>(globaltimer());
       const float *r = s.red + static_cast<size_t>(red.slot) * kConsumerWarps * 64;
       float v0 = 0.f, v1 = 0.f;
 #pragma unroll
@@ -873,13 +922,10 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
       const bool head = head_seg;   // this CTA holds the group's first tile
       seg_start = t + 1;
       if (!head) {
-        p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane] = v0;
-        p.partials[static_cast<size_t>(blockIdx.x) * 64 + lane + 32] = v1;
-        __syncwarp();
-        if (lane == 0) {
-          __threadfence();
-          st_release_u32(&p.sync->flags[blockIdx.x], seq);
-        }
+        // publish this CTA's part of the row group to the finisher (CTA - 1)
+        const uint64_t tag = static_cast<uint64_t>(seq) << 32;
+        st_relaxed_gpu_u64(p.partials + static_cast<size_t>(blockIdx.x) * 64 + lane, tag | __float_as_uint(v0));
+        st_relaxed_gpu_u64(p.partials + static_cast<size_t>(blockIdx.x) * 64 + lane + 32, tag | __float_as_uint(v1));
       } else {
         if (!group_end) {   // the rest of the row group came from CTA + 1
           v0 += part0;
@@ -1001,10 +1047,17 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
     if (p.trace != nullptr && blockIdx.x == 0 && lane == 0 && trace_slot < kTraceMax)
       p.trace[5 * kTraceMax + trace_slot] = globaltimer() - wait0;
   }
-  // the phase's outputs written by this warp are visible GPU-wide before the
-  // consumers may arrive at the grid barrier
-  __threadfence();
+  if (mark != nullptr && lane == 0) {
+    mark[5] = static_cast<uint32_t>(partner_ns);
+    mark[6] = static_cast<uint32_t>(globaltimer());
+  }
+  // The phase's outputs become visible GPU-wide through the chain: this
+  // warp's writes -> __syncwarp -> lane 0's mbarrier arrive (release, CTA
+  // scope) -> thread 0's wait on it (acquire, CTA scope) -> the consumers'
+  // bar.sync -> thread 0's release add at the grid barrier (GPU scope,
+  // cumulative) -> every other CTA's acquire load of the barrier counter.
   __syncwarp();
+  if (mark != nullptr && lane == 0) mark[7] = static_cast<uint32_t>(globaltimer());
   if (lane == 0) mbar_arrive(s.phase_done);
 }
 
@@ -1027,9 +1080,11 @@ __device__ void epilogue_main(const EpochParams &p, const Smem &s) {
       bool started = true;
       if (lane == 0) {
         const uint64_t deadline = globaltimer() + p.timeout_ns;
-        while (*s.phase_started < seq) {
-          if (*s.prod_ctl == -1 || aborted(p) || globaltimer() > deadline) { started = false; break; }
-          __nanosleep(32);
+        for (uint32_t polls = 1; *s.phase_started < seq; ++polls) {
+          if ((polls & 15) == 0 && (*s.prod_ctl == -1 || aborted(p) || globaltimer() > deadline)) {
+            started = false;
+            break;
+          }
         }
       }
       started = __shfl_sync(0xffffffffu, started ? 1 : 0, 0) != 0;

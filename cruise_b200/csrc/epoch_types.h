@@ -30,6 +30,7 @@ constexpr int kMaxCtas = 1024;
 constexpr int kMaxStages = 8;
 constexpr int kTraceMax = 2048;       // grid barriers recorded per launch
 constexpr int kTraceSeries = 6;      // globaltimer series per grid barrier (see cruise_epoch_read_trace)
+constexpr int kTraceCtaWords = 12;    // per-CTA marks per grid barrier (see cruise_epoch_read_trace_cta)
 
 // statuses and finish reasons of the reference controller (:51-74)
 enum Status : int32_t {
@@ -146,15 +147,20 @@ struct EpochWork {
   uint64_t adler[2 * 64 * kBatch * 2];  // per imported block: (S1, S2)
 };
 
-// Cross-CTA synchronisation words; zeroed by the host before every launch.
+// Cross-CTA synchronisation words; zeroed by the host before every launch,
+// together with the grid's tagged partial-sum words that follow it.
 constexpr int kBarrierLanes = 8;     // arrival counters of the grid barrier
 struct SyncState {
   uint32_t barrier[kBarrierLanes][32];   // CTA c arrives on counter c % 8 (one 128-B line each)
   uint32_t error;              // non-zero: a wait timed out, every CTA leaves
   uint32_t error_where;
   uint32_t pad0[30];
-  uint32_t flags[kMaxCtas];    // split row-group partial published (phase seq)
 };
+// Bytes the host clears before a launch: SyncState, then [grid][64] tagged
+// split row-group partial sums (fp32 value | phase sequence number << 32).
+__host__ __device__ inline size_t sync_bytes(int grid) {
+  return sizeof(SyncState) + static_cast<size_t>(grid) * 64 * sizeof(uint64_t);
+}
 
 // One rank's block of the tensor-parallel exchange, written by its peers over
 // NVLink: the fp32 row-parallel partials of the O and down projections
@@ -190,7 +196,7 @@ struct EpochParams {
   bf16 *qkv;                   // [4][Nqkv]
   bf16 *attn;                  // [4][H]
   bf16 *act;                   // [4][I_pad]
-  float *partials;             // [G][64] split row-group partial sums
+  uint64_t *partials;          // [G][64] split row-group partial sums as tagged words (after SyncState)
   float *arg_val;              // [G][4]
   int32_t *arg_idx;            // [G][4]
   int32_t *arg_bad;            // [G][4]
@@ -204,9 +210,14 @@ struct EpochParams {
   int32_t stages;              // weight ring depth
   int32_t xs_stride;           // activation row stride in smem (elements)
   int32_t down_xglobal;        // 1: the down projection reads its input from L2, not smem
+  int32_t o_xglobal;           // 1: the O projection reads its input (attention output) from L2, not smem
   uint64_t *trace;             // optional: CTA 0 globaltimer at each grid barrier (exit, entry)
+  uint32_t *trace_cta;         // optional: [kTraceMax][grid][kTraceCtaWords] low 32 bits of globaltimer
+                               // per CTA (see cruise_epoch_read_trace_cta)
   uint64_t timeout_ns;         // bound of every spin wait
   uint32_t l2_ahead;           // bytes of weights prefetched into L2 beyond the ring (0: off)
+  uint32_t l2_hints;           // bit 0: weight copies into the ring mark their L2 lines evict-first;
+                               // bit 1: the run-ahead prefetch marks its lines evict-last
   // tensor parallelism (tp_size 1: off).  Every rank's exchange block is
   // mapped into every other rank (peer memory over NVLink); tp_peer[r] is rank r's.
   int32_t tp_size, tp_rank;

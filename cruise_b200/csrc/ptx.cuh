@@ -91,6 +91,30 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, u
       : "memory");
 }
 
+// The same copy with an L2 eviction-priority policy (createpolicy) on the
+// lines it reads.
+__device__ __forceinline__ void bulk_g2s_hint(void *dst_smem, const void *src_gmem, uint32_t bytes,
+                                              uint64_t *bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 eviction-priority policies for the whole accessed range.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 // ---- tensor-core MMA (bf16 in, f32 accumulate) ----------------------------------
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
@@ -116,6 +140,12 @@ __device__ __forceinline__ uint4 lds128(const void *ptr) {
 // Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, multiple of 16).
 __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// The same prefetch with an L2 eviction-priority policy on the fetched lines.
+__device__ __forceinline__ void prefetch_l2_hint(const void *src, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(policy)
+               : "memory");
 }
 
 // 16-byte asynchronous global -> shared copy (L2 only), completed by the
@@ -162,6 +192,17 @@ __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *ptr, uint64_t v) {
 __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *ptr) {
   uint64_t v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// GPU-scope relaxed 64-bit accesses (self-validating tagged words between CTAs).
+__device__ __forceinline__ void st_relaxed_gpu_u64(uint64_t *ptr, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_gpu_u64(const uint64_t *ptr) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
   return v;
 }
 

@@ -314,8 +314,22 @@ class EpochEngine:
             raise result["err"]
         return result["out"]
 
-    def set_trace(self, enable: bool) -> None:
-        self.lib.cruise_epoch_set_trace(self.handle, 1 if enable else 0)
+    def set_trace(self, enable: bool | int) -> None:
+        """True / 1: CTA 0's phase timeline; 2: also every CTA's (read_trace_cta)."""
+        self._check(self.lib.cruise_epoch_set_trace(self.handle, int(enable)), "set_trace")
+
+    def read_trace_cta(self, barriers: int) -> np.ndarray:
+        """[barriers, ctas, 8] low 32 bits of globaltimer ns per CTA (0: not
+        recorded): left barrier j, staged, last tile, arrived at barrier j;
+        the epilogue warp's start, ns it waited for the stream-K partner,
+        last segment done, outputs fenced, last consumer flush received; the
+        last consumer warp's last tile (see cruise_epoch_read_trace_cta)."""
+        ctas = ctypes.c_int32(0)
+        self.lib.cruise_epoch_read_trace_cta(self.handle, None, 0, ctypes.byref(ctas))
+        out = np.zeros((barriers, max(ctas.value, 1), 12), dtype=np.uint32)
+        self._check(self.lib.cruise_epoch_read_trace_cta(self.handle, _ptr(out, ctypes.c_uint32), barriers,
+                                                         ctypes.byref(ctas)), "read_trace_cta")
+        return out
 
     def read_trace(self, count: int) -> np.ndarray:
         """[6, count] globaltimer ns per grid barrier of the last epoch: CTA 0

@@ -279,10 +279,22 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us,
  *   5  not a time stamp: nanoseconds CTA 0's epilogue waited for the other
  *      ranks' partials in phase j (O and down of a tensor-parallel engine;
  *      0 otherwise)
- * cruise_epoch_read_trace copies `count` entries of one series. */
+ * cruise_epoch_read_trace copies `count` entries of one series.
+ * enable = 2 also records, for EVERY CTA and barrier j, eight words, the low
+ * 32 bits of globaltimer unless noted: [0] the CTA left barrier j, [1] it had
+ * staged the activations of the phase ending at j (projection phases), [2] its
+ * warp 0 consumed its last weight tile there, [3] it arrived at barrier j;
+ * its epilogue warp [4] started the phase, [5] waited that many ns for the
+ * stream-K partner's partial sums, [6] finished its last row group, [7] had
+ * fenced its outputs, [8] received the consumers' last partial sums; [9] its
+ * last consumer warp consumed its last weight tile; [10], [11] unused.
+ * cruise_epoch_read_trace_cta copies `barriers` x ctas x 12 words (barrier-
+ * major) and reports the CTA count; 0 = no record. */
 int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
 int32_t cruise_epoch_read_trace(void *engine, int32_t series, uint64_t *ns,
                                 int32_t count);
+int32_t cruise_epoch_read_trace_cta(void *engine, uint32_t *stamps,
+                                    int32_t barriers, int32_t *ctas);
 
 /* Batched device prefill (the reference prefills on the host and imports the
  * KV; here the prompts run through the model on the GPU in one pass per
