@@ -583,7 +583,10 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
-PHASE_NAMES = ("qkv", "attention", "o_proj", "gate_up", "down")
+# grid barriers per layer: QKV and attention share one (attention units wait
+# for their KV head's QKV row groups), then O, gate/up, down
+PHASE_NAMES = ("qkv+attention", "o_proj", "gate_up", "down")
+PHASES_PER_LAYER = len(PHASE_NAMES)
 
 
 def print_trace_cta(engine, cohort, cfg, show: bool = True) -> None:
@@ -596,7 +599,7 @@ def print_trace_cta(engine, cohort, cfg, show: bool = True) -> None:
     out, _ = cohort.step()
     engine.set_trace(False)
     L = cfg.num_layers
-    phases = 5 * L + 2
+    phases = PHASES_PER_LAYER * L + 2
     count = 2 + out.model_calls * phases + 1
     raw = engine.read_trace_cta(count).astype(np.int64)
     # unwrap the 32-bit stamps against barrier 1's exit of CTA 0
@@ -607,8 +610,9 @@ def print_trace_cta(engine, cohort, cfg, show: bool = True) -> None:
     for step in range(out.model_calls):
         for ph in range(phases):
             j = first + step * phases + ph + 1
-            name = "lm_head" if ph == 5 * L else "control" if ph > 5 * L else PHASE_NAMES[ph % 5]
-            a = acc.setdefault(name, np.zeros(15))
+            name = ("lm_head" if ph == PHASES_PER_LAYER * L else "control" if ph > PHASES_PER_LAYER * L
+                    else PHASE_NAMES[ph % PHASES_PER_LAYER])
+            a = acc.setdefault(name, np.zeros(18))
             start, staged, tiles, arrive = t[j - 1, :, 0], t[j, :, 1], t[j, :, 2], t[j, :, 3]
             e_start, e_done, e_fenced = t[j, :, 4], t[j, :, 6], t[j, :, 7]
             if e_done.any():
@@ -623,6 +627,11 @@ def print_trace_cta(engine, cohort, cfg, show: bool = True) -> None:
             exit_ = t[j, :, 0]
             a[0] += np.median(exit_) - np.median(start)
             if staged.any():
+                loaded, shared = t[j, :, 10], t[j, :, 11]
+                if loaded.any():
+                    a[15] += np.median(loaded - start)
+                    a[16] += np.median(shared - loaded)
+                    a[17] += np.median(staged - shared)
                 a[1] += np.median(staged - start)
                 a[2] += np.median(tiles - staged)
                 a[3] += np.median(arrive - tiles)
@@ -642,13 +651,15 @@ def print_trace_cta(engine, cohort, cfg, show: bool = True) -> None:
           f"[phase | med staging  med tiles  med epilogue | last-arrival lag | release first/last | start skew]"
           f"  last CTAs\n    epilogue warp, medians over CTAs: [start after phase start | partner wait | "
           f"last segment after last tile | fence]", file=sys.stderr)
-    for name in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "control"):
-        a = acc.get(name, np.zeros(15)) / calls / 1e3
+    for name in (*PHASE_NAMES, "lm_head", "control"):
+        a = acc.get(name, np.zeros(18)) / calls / 1e3
         top = sorted(last_cta.get(name, {}).items(), key=lambda kv: -kv[1])[:4]
-        print(f"  {name:9s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} | {a[5]:6.1f} {a[6]:6.1f} "
+        print(f"  {name:13s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} | {a[5]:6.1f} {a[6]:6.1f} "
               f"| {a[7]:6.1f}  {top}\n  {'':9s} {'':8s}   epilogue warp: {a[8]:7.1f} | {a[9]:7.1f} | {a[10]:7.1f} | "
               f"{a[11]:7.1f} || slowest consumer warp after warp 0: {a[12]:6.1f}, last flush taken after that: "
-              f"{a[13]:6.1f}, last segment's epilogue: {a[14]:6.1f}", file=sys.stderr)
+              f"{a[13]:6.1f}, last segment's epilogue: {a[14]:6.1f}"
+              + (f"\n  {'':9s} {'':8s}   norm staging: loads {a[15]:6.1f}, sum of squares shared {a[16]:6.1f}, "
+                 f"normalised {a[17]:6.1f}" if a[15] else ""), file=sys.stderr)
 
 
 def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
@@ -660,7 +671,7 @@ def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
     out, _ = cohort.step()
     engine.set_trace(False)
     L = cfg.num_layers
-    phases = 5 * L + 2
+    phases = PHASES_PER_LAYER * L + 2
     count = 2 + out.model_calls * phases + 1
     tr = engine.read_trace(count).astype(np.int64)
     exit_ns, entry_ns, xready, tiles, last, tp_wait = tr
@@ -670,7 +681,8 @@ def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
     for step in range(out.model_calls):
         for ph in range(phases):
             j = first + step * phases + ph + 1
-            name = "lm_head" if ph == 5 * L else "control" if ph > 5 * L else PHASE_NAMES[ph % 5]
+            name = ("lm_head" if ph == PHASES_PER_LAYER * L else "control" if ph > PHASES_PER_LAYER * L
+                    else PHASE_NAMES[ph % PHASES_PER_LAYER])
             a = acc.setdefault(name, np.zeros(7))
             start = end_ns[j - 1]
             a[0] += end_ns[j] - start
@@ -686,16 +698,16 @@ def print_trace(engine, cohort, cfg, k, show: bool = True) -> None:
     if not show:
         return
     sh, h, d = engine.shard, cfg.hidden, cfg.head_dim   # this rank's shard (the whole model on one GPU)
-    wbytes = {"qkv": (sh.nq + 2 * sh.nkv) * d * h * 2 * L, "o_proj": h * sh.nq * d * 2 * L,
+    wbytes = {"qkv+attention": (sh.nq + 2 * sh.nkv) * d * h * 2 * L, "o_proj": h * sh.nq * d * 2 * L,
               "gate_up": 2 * sh.ni * h * 2 * L, "down": h * sh.ni * 2 * L, "lm_head": sh.nv * h * 2}
     calls = out.model_calls
     print(f"trace: epoch {out.device_us:.1f} us, {calls} steps; per step, us "
           f"[total | x-staging  tiles  epilogue | wait-last-CTA  release | epilogue tp-wait] and weight GB/s",
           file=sys.stderr)
-    for name in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "control"):
+    for name in (*PHASE_NAMES, "lm_head", "control"):
         a = acc.get(name, np.zeros(7)) / calls / 1e3
         bw = wbytes.get(name, 0) / (a[0] * 1e3) if name in wbytes and a[0] else 0.0
-        print(f"  {name:9s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} {a[5]:7.1f} "
+        print(f"  {name:13s} {a[0]:8.1f} | {a[1]:7.1f} {a[2]:7.1f} {a[3]:7.1f} | {a[4]:7.1f} {a[5]:7.1f} "
               f"{a[6]:7.1f}   {bw:6.0f}", file=sys.stderr)
 
 

@@ -257,6 +257,7 @@ bool valid_config(const CruiseModelConfig &c) {
   if (c.num_layers < 1 || c.num_layers > 64 || c.hidden < 64 || c.hidden % 64 != 0) return false;
   if (c.hidden > 4096) return false;   // RMSNorm staging: 2 x 8 elements per thread and row
   if (c.num_heads < 1 || c.num_kv_heads < 1 || c.num_heads % c.num_kv_heads != 0) return false;
+  if (c.num_kv_heads > kMaxKvGroups) return false;   // one QKV completion counter per KV head
   if (c.head_dim != 64 && c.head_dim != 128) return false;
   if (c.num_heads * c.head_dim != c.hidden) return false;
   if (c.intermediate < 8 || c.intermediate % 8 != 0) return false;

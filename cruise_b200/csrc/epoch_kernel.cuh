@@ -317,6 +317,21 @@ __device__ __forceinline__ float tp_recv(const EpochParams &p, const uint64_t *w
   return __uint_as_float(static_cast<uint32_t>(v));
 }
 
+// QKV rows are q (heads of this rank) | k | v; every 16-row group lies inside
+// one head (head_dim is a multiple of 16).  The KV head whose attention needs
+// row group `rg`, and how many row groups one KV head's attention needs.
+__device__ __forceinline__ int qkv_group_of(const ModelDims &m, int64_t rg) {
+  const int64_t row = rg * kRows;
+  const int groups = m.nq / m.nkv;
+  if (row < m.Hq) return static_cast<int>(row / m.d) / groups;
+  const int64_t kv = (row - m.Hq) / m.d;   // k heads, then v heads
+  return static_cast<int>(kv < m.nkv ? kv : kv - m.nkv);
+}
+
+__device__ __forceinline__ uint32_t qkv_rows_per_group(const ModelDims &m) {
+  return static_cast<uint32_t>((m.nq / m.nkv + 2) * (m.d / kRows));
+}
+
 // The fp32 value of a tagged partial-sum word once it carries `tag` (the
 // phase's sequence number in the high half).  A wait that runs out raises the
 // epoch error and returns 0, so the kernel winds down.
@@ -497,7 +512,7 @@ __device__ void producer_main(const EpochParams &p, const Smem &s) {
 // ---- consumer: activation prologue ------------------------------------------------------
 // Fills s.xs[4][K] with the projection input: RMSNorm of the residual stream
 // (batched_decoder_step.py:224-229) or a plain copy (attention / SwiGLU output).
-__device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
+__device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g, uint32_t *mark) {
   const int tid = threadIdx.x;
   const int K = g.K;
   const int K8 = K / 8;
@@ -543,6 +558,7 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
     }
   }
   const int warp = tid >> 5, lane = tid & 31;
+  if (mark != nullptr && tid == 0) mark[10] = static_cast<uint32_t>(globaltimer());   // loads returned
 #pragma unroll
   for (int b = 0; b < kBatch; ++b) {
 #pragma unroll
@@ -553,18 +569,22 @@ __device__ void load_x(const EpochParams &p, const Smem &s, const Gemv &g) {
     for (int b = 0; b < kBatch; ++b) s.nrm[warp * 4 + b] = ss[b];
   }
   named_sync(1, kConsumerThreads);
-  // every thread sums the 8 warp partials in the same order and computes the
-  // 4 inverse RMS values itself (no second barrier)
-  float rinv[kBatch];
-#pragma unroll
-  for (int b = 0; b < kBatch; ++b) {
+  if (mark != nullptr && tid == 0) mark[11] = static_cast<uint32_t>(globaltimer());   // sums shared
+  // every warp sums the 8 warp partials in the same order, lane b computing
+  // row b's inverse RMS, and broadcasts the four values by shuffles (no
+  // second barrier; one IEEE divide / square root / divide chain per lane)
+  float mine = 0.f;
+  if (lane < kBatch) {
     float total = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + b];
+    for (int w = 0; w < kConsumerWarps; ++w) total += s.nrm[w * 4 + lane];
     // mean = sum / K; rsqrt = 1 / sqrt(mean + eps), each IEEE-rounded as on the CPU
     const float var = __fdiv_rn(total, static_cast<float>(K));
-    rinv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
+    mine = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.m.eps)));
   }
+  float rinv[kBatch];
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) rinv[b] = __shfl_sync(0xffffffffu, mine, b);
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int k8 = tid + j * kConsumerThreads;
@@ -827,7 +847,11 @@ __device__ void gemv_consume(const EpochParams &p, const Smem &s, const Gemv &g,
   }
   if (tr.t0 >= tr.t1) return;
   const bool xg = g.xmode == kXGlobal;
-  if (!xg) load_x(p, s, g);
+  if (!xg)
+    load_x(p, s, g,
+           p.trace_cta != nullptr && trace_slot < kTraceMax
+               ? p.trace_cta + (static_cast<size_t>(trace_slot) * p.grid + blockIdx.x) * kTraceCtaWords
+               : nullptr);
   if (p.trace != nullptr && blockIdx.x == 0 && tid == 0 && trace_slot < kTraceMax)
     p.trace[2 * kTraceMax + trace_slot] = globaltimer();   // activations staged
   if (p.trace_cta != nullptr && tid == 0 && trace_slot < kTraceMax)
@@ -953,6 +977,10 @@ __device__ void gemv_finish(const EpochParams &p, const Smem &s, const Gemv &g, 
           // F.linear(x, W, b) on bf16: fp32 sum plus fp32 bias, one rounding (:305-313)
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n0] = tobf(__fadd_rn(v0, e0));
           p.qkv[static_cast<size_t>(b) * m.Nqkv + n1] = tobf(__fadd_rn(v1, e1));
+          // the row group is complete: count it for its KV head's attention
+          // (the warp's stores are ordered before lane 0's release add)
+          __syncwarp();
+          if (lane == 0) red_release_add_u32(&p.sync->qkv_done[qkv_group_of(m, rg)][0], 1u);
         } else if (tp_partial) {
           // Row-parallel output under tensor parallelism: every rank's finisher
           // of this row group holds a partial over its K shard.  Publish ours
@@ -1123,8 +1151,27 @@ __host__ __device__ inline size_t attn_scratch_bytes(int D, int C) {
          16 * 4 + static_cast<size_t>(groups) * D * 4;
 }
 
+// Waits (thread 0, bounded) until KV head `kvh`'s QKV row groups of the
+// current QKV phase are all written, then makes them visible to the CTA.
+__device__ __forceinline__ void wait_qkv_group(const EpochParams &p, const Smem &s, int kvh, uint32_t target) {
+  if (threadIdx.x == 0) {
+    const uint32_t *counter = &p.sync->qkv_done[kvh][0];
+    if (static_cast<int32_t>(ld_acquire_u32(counter) - target) < 0) {
+      const uint64_t deadline = globaltimer() + p.timeout_ns;
+      uint32_t polls = 0;
+      while (static_cast<int32_t>(ld_acquire_u32(counter) - target) < 0) {
+        if ((++polls & 15) == 0) {
+          if (aborted(p)) break;
+          if (globaltimer() > deadline) { raise_error(p, 1005); break; }
+        }
+      }
+    }
+  }
+  named_sync(1, kConsumerThreads);
+}
+
 template <int D>
-__device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer) {
+__device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer, uint32_t qkv_target) {
   const ModelDims &m = p.m;
   const int tid = threadIdx.x;
   constexpr int half = D / 2;
@@ -1194,6 +1241,8 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
       }
     }
     cp_async_commit();
+    // the cached rows above do not depend on this layer's projections; q, k, v do
+    wait_qkv_group(p, s, kvh, qkv_target);
     const bf16 *qsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + qh * D;
     const bf16 *ksrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.Hq + kvh * D;
     const bf16 *vsrc = p.qkv + static_cast<size_t>(b) * m.Nqkv + m.Hq + m.nkv * D + kvh * D;
@@ -1311,11 +1360,11 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
   }
 }
 
-__device__ void attention_phase(const EpochParams &p, const Smem &s, int layer) {
+__device__ void attention_phase(const EpochParams &p, const Smem &s, int layer, uint32_t qkv_target) {
   if (p.m.d == 128) {
-    attention_phase_d<128>(p, s, layer);
+    attention_phase_d<128>(p, s, layer, qkv_target);
   } else {
-    attention_phase_d<64>(p, s, layer);
+    attention_phase_d<64>(p, s, layer, qkv_target);
   }
 }
 
@@ -1668,7 +1717,11 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
         if (tid == 0) wait_bar(p, s.phase_done, done_parity, nullptr, 1004);
         done_parity ^= 1u;
       } else if (ph < 5 * L) {
-        attention_phase(p, s, ph / 5);
+        // attention follows QKV without a grid barrier: this CTA's epilogue
+        // warp is done with the shared memory the attention scratch reuses,
+        // and each unit waits for its own KV head's row groups
+        named_sync(1, kConsumerThreads);
+        attention_phase(p, s, ph / 5, qkv_rows_per_group(m) * static_cast<uint32_t>(step * L + ph / 5 + 1));
       } else if (blockIdx.x == 0 && step_mode) {
         // the decoder ABI's fourth output: next_position = where(active, pos + 1, pos)
         // (batched_decoder_step.py:409-411), in the history words
@@ -1799,7 +1852,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_epoch_kernel(const Epoch
           }
         }
       }
-      if (ok) ok = grid_barrier(p, s, ++barrier_index, 100 + ph);
+      if (ok && kind != kQKV) ok = grid_barrier(p, s, ++barrier_index, 100 + ph);
     }
   }
   if (tid == 0) *s.prod_ctl = -1;   // producer: no more steps

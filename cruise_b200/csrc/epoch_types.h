@@ -150,11 +150,16 @@ struct EpochWork {
 // Cross-CTA synchronisation words; zeroed by the host before every launch,
 // together with the grid's tagged partial-sum words that follow it.
 constexpr int kBarrierLanes = 8;     // arrival counters of the grid barrier
+constexpr int kMaxKvGroups = 16;     // KV heads per rank with their own QKV completion counter
 struct SyncState {
   uint32_t barrier[kBarrierLanes][32];   // CTA c arrives on counter c % 8 (one 128-B line each)
   uint32_t error;              // non-zero: a wait timed out, every CTA leaves
   uint32_t error_where;
   uint32_t pad0[30];
+  // QKV row groups finished per KV head (one 128-B line each), over the whole
+  // launch: attention units of a KV head start once its count reaches
+  // (row groups of the head) x (QKV phases so far); no grid barrier between
+  uint32_t qkv_done[kMaxKvGroups][32];
 };
 // Bytes the host clears before a launch: SyncState, then [grid][64] tagged
 // split row-group partial sums (fp32 value | phase sequence number << 32).

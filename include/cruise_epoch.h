@@ -287,7 +287,9 @@ int32_t cruise_epoch_last_timing(void *engine, double *device_us,
  * its epilogue warp [4] started the phase, [5] waited that many ns for the
  * stream-K partner's partial sums, [6] finished its last row group, [7] had
  * fenced its outputs, [8] received the consumers' last partial sums; [9] its
- * last consumer warp consumed its last weight tile; [10], [11] unused.
+ * last consumer warp consumed its last weight tile; RMSNorm staging (QKV,
+ * gate/up, lm_head): [10] the residual rows had arrived, [11] the sums of
+ * squares were shared.
  * cruise_epoch_read_trace_cta copies `barriers` x ctas x 12 words (barrier-
  * major) and reports the CTA count; 0 = no record. */
 int32_t cruise_epoch_set_trace(void *engine, int32_t enable);
