@@ -572,6 +572,15 @@ def run_gpu(args) -> None:
             line["dp"] = dp
     if tp:
         group.close()
+    if rank == 0 and world == 1 and args.k != 8 and not (args.layers or args.vocab) and single_cohort.room() >= 40:
+        # the same cohort in five K=8 epochs: the north star's epoch length
+        k_default, single_cohort.sc.k = single_cohort.sc.k, 8
+        r8 = timed_epochs(single_cohort, cfg, 5, device, 1, False, barrier)
+        single_cohort.sc.k = k_default
+        gbs8 = r8["bytes"] / r8["dev_s"] / 1e9
+        line["k8"] = {"value": round(r8["tokens"] / r8["dev_s"], 2), "unit": "tok/s", "epochs": 5,
+                      "us_per_decode_step": round(r8["dev_s"] * 1e6 / max(r8["model_calls"], 1), 2),
+                      "roofline_frac": round(gbs8 / peak, 4), "e2e_value": round(r8["tokens"] / r8["wall"], 2)}
     if rank == 0 and world == 1 and not args.no_host_loop and not (args.layers or args.vocab):
         line["host_loop"] = host_loop_comparison(single, single_cohort, cfg)
     if rank == 0 and not args.no_cpu_baseline and world == 1:
