@@ -59,9 +59,9 @@ def build_server() -> Path:
 
 
 def link_flags() -> list[str]:
-    """cuBLAS (the prefill GEMMs) from the toolkit next to nvcc, found there at run time."""
-    lib = Path(nvcc()).resolve().parent.parent / "lib64"
-    return [f"-L{lib}", "-lcublas", "-Xlinker", f"-rpath={lib}"]
+    """No library beyond the CUDA runtime (linked statically by nvcc); the
+    driver's tensor-map encoder is found at run time through the runtime."""
+    return []
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:

@@ -2,7 +2,8 @@
 // (include/cruise_epoch.h): device memory, seeded weight synthesis, weight
 // loading, the one-launch epoch, and the reference-compatible bridge
 // resident_epoch_create / _execute / _destroy.
-#include <cublas_v2.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -23,6 +24,7 @@
 #include "../../include/cruise_epoch.h"
 #include "epoch_kernel.cuh"
 #include "prefill.cuh"
+#include "prefill_gemm.cuh"
 
 namespace cruise {
 namespace {
@@ -162,21 +164,18 @@ struct Region {
   int64_t elems = 0;
 };
 
-// Untiled projection weights and activation buffers of the batched prefill,
-// built on the first cruise_epoch_prefill (the decode epoch never needs them).
-struct PrefillLayer {
-  const bf16 *qkv_w, *qkv_b, *o_w, *gu_w, *down_w;   // [Nqkv][H], [Nqkv], [H][Hq], [2I][H], [H][I]
-};
+// Activation buffers of the batched prefill, built on the first
+// cruise_epoch_prefill (the decode epoch never needs them).  The projections
+// read the engine's own tiled weights.
 struct PrefillState {
-  cublasHandle_t blas = nullptr;
-  void *weights = nullptr;
-  std::vector<PrefillLayer> layers;
   void *work = nullptr;
   int max_tokens = 0;
   bf16 *h = nullptr, *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
-  float *acc = nullptr;
+  float *acc = nullptr;        // fp32 k-range partial sums [split][T][N]
   int64_t *tok = nullptr;
   int32_t *row = nullptr, *pos = nullptr;
+  uint32_t *error = nullptr;   // site of a tensor-core GEMM wait that ran out (0: none)
+  bool gemm_attr = false;      // the GEMM's shared-memory limit has been raised
 };
 
 struct Engine {
@@ -676,84 +675,132 @@ int32_t copy_tensor(Engine *e, const std::string &name, void *host, uint64_t byt
 // ---- batched device prefill ---------------------------------------------------------------------
 int64_t import_payload_bytes(const Engine *e);
 
-// y[T][N] (fp32) = x[T][K] . W[N][K]^T, both bf16 row-major (cuBLAS is column-major: y^T = W x^T).
-// y[T][N] = x[T][K] W[N][K]^T with fp32 accumulation; y is fp32, or bf16 (the
-// fp32 sum rounded once, as the decoder's materialize(mm_t(x, W))).
-cublasStatus_t prefill_gemm(cublasHandle_t blas, const bf16 *x, const bf16 *w, void *y, cudaDataType_t y_type, int T,
-                            int N, int K) {
-  const float one = 1.0f, zero = 0.0f;
-  return cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, N, T, K, &one, w, CUDA_R_16BF, K, x, CUDA_R_16BF, K, &zero, y,
-                      y_type, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+// ---- tensor-core GEMMs of the batched prefill (prefill_gemm.cuh) --------------------------
+PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled fn = [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled>(ptr);
+  }();
+  return fn;
 }
 
-// Frees the prefill state (cuBLAS handle, untiled weights, buffers), whole or
-// partly built; cudaFree waits for the work queued on them.
+// A tiled projection [N][K] (tiles of 16 rows x kc, stream order [row group][k
+// tile]) as the 5-D tensor (element in a 128-byte segment, segment, row in
+// tile, k tile, row group); a box is 16 row groups x 16 rows of one segment.
+bool weight_map(CUtensorMap *map, const bf16 *W, int N, int K, int kc) {
+  const PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(kc / 64), 16, static_cast<cuuint64_t>(K / kc),
+                              static_cast<cuuint64_t>(N / 16)};
+  const cuuint64_t strides[4] = {128, static_cast<cuuint64_t>(kc) * 2, static_cast<cuuint64_t>(kc) * 32,
+                                 static_cast<cuuint64_t>(K / kc) * kc * 32};
+  const cuuint32_t box[5] = {64, 1, 16, 1, tcgemm::kRows / 16};
+  const cuuint32_t elem[5] = {1, 1, 1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<bf16 *>(W), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Row-major activations [T][width] (row pitch `pitch` elements) in boxes of
+// 64 columns x 256 tokens with the 128-byte swizzle; out-of-range reads zero.
+bool activation_map(CUtensorMap *map, const bf16 *X, int T, int width, int pitch) {
+  const PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch) * 2};
+  const cuuint32_t box[2] = {64, 256};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16 *>(X), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// k-range splits of a projection for T tokens: enough (256-row tile, token
+// half) pairs x splits to cover the SMs once, at most one split per k chunk.
+int gemm_splits(const Engine *e, int N, int K, int T) {
+  const int tiles = (N + tcgemm::kRows - 1) / tcgemm::kRows * (T > tcgemm::kTokHalf ? 2 : 1);
+  const int chunks = K / tcgemm::kKChunk;
+  return std::max(1, std::min(chunks, e->sms / tiles));
+}
+
+// Y = X . W^T on the tensor cores.  mode 0: fp32 partials [nsplit][T][N] into
+// ps->acc; mode 1 (the interleaved gate/up projection): the SwiGLU activation
+// [T][N / 2] into ps->act.  Returns false when a tensor map cannot be made or
+// the launch fails.
+bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, int x_width, int mode, int nsplit) {
+  PrefillState *ps = e->prefill;
+  CUtensorMap wmap, xmap;
+  if (!weight_map(&wmap, W, N, K, pick_kc(K)) || !activation_map(&xmap, X, T, x_width, x_width)) return false;
+  tcgemm::Args a{};
+  a.T = T;
+  a.N = N;
+  a.chunks = K / tcgemm::kKChunk;
+  a.kc = pick_kc(K);
+  a.nsplit = nsplit;
+  a.mode = mode;
+  a.halves = T > tcgemm::kTokHalf ? 2 : 1;
+  a.stages = tcgemm::kMaxStages;
+  a.tiles = (N + tcgemm::kRows - 1) / tcgemm::kRows * a.halves * nsplit;
+  a.partials = ps->acc;
+  a.act = ps->act;
+  a.act_stride = N / 2;
+  a.error = ps->error;
+  const size_t smem = tcgemm::smem_bytes(a.stages);
+  if (!ps->gemm_attr) {
+    if (cudaFuncSetAttribute(tcgemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return false;
+    ps->gemm_attr = true;
+  }
+  tcgemm::gemm_kernel<<<std::min(a.tiles, e->sms), tcgemm::kThreads, smem, e->stream>>>(wmap, xmap, a);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+// Frees the prefill buffers, whole or partly built; cudaFree waits for the
+// work queued on them.
 void prefill_release(Engine *e) {
   PrefillState *ps = e->prefill;
   if (ps == nullptr) return;
-  if (ps->blas != nullptr) cublasDestroy(ps->blas);
-  cudaFree(ps->weights);
   cudaFree(ps->work);
   delete ps;
   e->prefill = nullptr;
 }
 
-// Builds the untiled weights (once) and buffers for kBatch * block_size tokens.
-// A failure leaves the state partly built; the caller releases it, so the next
-// call starts over instead of using it.
+// Buffers for kBatch * block_size tokens.  A failure leaves the state partly
+// built; the caller releases it, so the next call starts over instead of using it.
 int32_t prefill_prepare(Engine *e) {
   if (e->prefill != nullptr) return 0;
   const ModelDims &m = e->m;
-  const int64_t H = m.H, kv = static_cast<int64_t>(m.nkv) * m.d, Hq = m.Hq, I = m.I, N = m.Nqkv;
+  const int64_t H = m.H, Hq = m.Hq, I = m.I, N = m.Nqkv;
   auto *ps = new PrefillState();
   e->prefill = ps;
-  if (cublasCreate(&ps->blas) != CUBLAS_STATUS_SUCCESS) {
-    ps->blas = nullptr;
-    e->last_error = "prefill: cublasCreate failed";
+  if (tensor_map_encoder() == nullptr) {
+    e->last_error = "prefill: the driver has no cuTensorMapEncodeTiled";
     return -2;
-  }
-  cublasSetStream(ps->blas, e->stream);
-  const int64_t per_layer = N * H + N + H * Hq + 2 * I * H + H * I;
-  cudaError_t err = cudaMalloc(&ps->weights, static_cast<size_t>(per_layer) * m.L * 2);
-  if (err != cudaSuccess) return set_err(e, err, "prefill weights");
-  bf16 *w = static_cast<bf16 *>(ps->weights);
-  auto untile = [&](const std::string &name, bf16 *dst) -> bool {
-    TensorPlace tp;
-    if (!locate(e, name, tp)) return false;
-    if (!tp.tiled) {
-      return cudaMemcpyAsync(dst, tp.base + tp.offset, static_cast<size_t>(tp.rows * tp.cols) * 2,
-                             cudaMemcpyDeviceToDevice, e->stream) == cudaSuccess;
-    }
-    const int64_t count = tp.rows * tp.cols;
-    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148LL * 64));
-    tile_copy_kernel<<<blocks, 256, 0, e->stream>>>(reinterpret_cast<uint16_t *>(tp.base),
-                                                    reinterpret_cast<uint16_t *>(dst), tp.rows, tp.cols,
-                                                    tp.row_map, tp.offset, tp.K, pick_kc(static_cast<int>(tp.K)), 0);
-    return cudaGetLastError() == cudaSuccess;
-  };
-  for (int l = 0; l < m.L; ++l) {
-    const std::string p = "model.layers." + std::to_string(l) + ".";
-    bf16 *qkv_w = w, *qkv_b = qkv_w + N * H, *o_w = qkv_b + N, *gu_w = o_w + H * Hq, *down_w = gu_w + 2 * I * H;
-    w = down_w + H * I;
-    const bool ok = untile(p + "self_attn.q_proj.weight", qkv_w) && untile(p + "self_attn.k_proj.weight", qkv_w + Hq * H) &&
-                    untile(p + "self_attn.v_proj.weight", qkv_w + (Hq + kv) * H) &&
-                    untile(p + "self_attn.q_proj.bias", qkv_b) && untile(p + "self_attn.k_proj.bias", qkv_b + Hq) &&
-                    untile(p + "self_attn.v_proj.bias", qkv_b + Hq + kv) && untile(p + "self_attn.o_proj.weight", o_w) &&
-                    untile(p + "mlp.gate_proj.weight", gu_w) && untile(p + "mlp.up_proj.weight", gu_w + I * H) &&
-                    untile(p + "mlp.down_proj.weight", down_w);
-    if (!ok) return set_err(e, cudaErrorInvalidValue, "prefill weight layout");
-    ps->layers.push_back(PrefillLayer{qkv_w, qkv_b, o_w, gu_w, down_w});
   }
   // activations for every prompt token of a cohort: at most block_size per row
   const int T = kBatch * m.bs;
   ps->max_tokens = T;
-  const int64_t widest = std::max<int64_t>(std::max<int64_t>(N, 2 * I), H);
+  // the most fp32 partial sums (splits x outputs x tokens) of QKV, O and down
+  // at any token count: the split counts depend on the token count only
+  // through the number of token halves (one up to 256 tokens, then two), so
+  // the largest count of each side is taken at that side's most tokens
+  int64_t parts = 0;
+  for (const int t : {std::min(T, tcgemm::kTokHalf), T}) {
+    const int64_t widest = std::max<int64_t>(gemm_splits(e, m.Nqkv, m.H, t) * N,
+                                             std::max(gemm_splits(e, m.H, m.Hq, t), gemm_splits(e, m.H, m.I_pad, t)) * H);
+    parts = std::max(parts, widest * t);
+  }
   size_t bytes = 0;
-  auto take = [&](size_t n) { const size_t off = bytes; bytes = align_up(bytes + n, 256); return off; };
+  auto take = [&](size_t n) { const size_t off = bytes; bytes = align_up(bytes + n, 1024); return off; };
   const size_t o_h = take(T * H * 2), o_x = take(T * H * 2), o_q = take(T * Hq * 2), o_attn = take(T * Hq * 2);
-  const size_t o_act = take(T * I * 2), o_acc = take(T * widest * 4), o_tok = take(T * 8), o_row = take(T * 4),
-               o_pos = take(T * 4);
-  err = cudaMalloc(&ps->work, bytes);
+  const size_t o_act = take(T * I * 2), o_acc = take(parts * 4), o_tok = take(T * 8), o_row = take(T * 4),
+               o_pos = take(T * 4), o_err = take(4);
+  cudaError_t err = cudaMalloc(&ps->work, bytes);
   if (err != cudaSuccess) return set_err(e, err, "prefill buffers");
   uint8_t *b = static_cast<uint8_t *>(ps->work);
   ps->h = reinterpret_cast<bf16 *>(b + o_h);
@@ -765,7 +812,10 @@ int32_t prefill_prepare(Engine *e) {
   ps->tok = reinterpret_cast<int64_t *>(b + o_tok);
   ps->row = reinterpret_cast<int32_t *>(b + o_row);
   ps->pos = reinterpret_cast<int32_t *>(b + o_pos);
-  return set_err(e, cudaStreamSynchronize(e->stream), "prefill preparation");
+  ps->error = reinterpret_cast<uint32_t *>(b + o_err);
+  err = cudaMemsetAsync(ps->work, 0, bytes, e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  return set_err(e, err, "prefill preparation");
 }
 
 // The K/V of prompt tokens 0..len-2 of every row (the decode epoch starts at
@@ -838,41 +888,50 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
   if (T > 0 && cudaFuncSetAttribute(attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(attn_smem)) != cudaSuccess)
     return set_err(e, cudaGetLastError(), "prefill attention shared memory");
-  const unsigned ew = 148 * 8;   // grid of the elementwise kernels
-  bool blas_ok = true;
+  bool gemm_ok = true;
   if (T > 0) {
+    const int sq = gemm_splits(e, m.Nqkv, H, T), so = gemm_splits(e, H, m.Hq, T), sd = gemm_splits(e, H, m.I_pad, T);
+    err = cudaMemsetAsync(ps->error, 0, 4, e->stream);
+    if (err != cudaSuccess) return set_err(e, err, "prefill error word");
     prefill::embed_rows<<<T, 128, 0, e->stream>>>(e->embed, ps->tok, ps->h, H);
     prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, e->layers[0].w_in, ps->x, H, m.eps);
-    for (int l = 0; l < m.L && blas_ok; ++l) {
+    for (int l = 0; l < m.L && gemm_ok; ++l) {
       // x holds rms_norm(h) * w_in of this layer
       const LayerWeights &lw = e->layers[l];
-      const PrefillLayer &pl = ps->layers[l];
-      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.qkv_w, ps->acc, CUDA_R_32F, T, m.Nqkv, H) == CUBLAS_STATUS_SUCCESS;
-      prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, pl.qkv_b, e->rope_cos, e->rope_sin, ps->row, ps->pos,
-                                                        ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
+      gemm_ok &= prefill_gemm(e, lw.qkv_w, m.Nqkv, H, ps->x, T, H, 0, sq);
+      prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, sq, T, lw.qkv_b, e->rope_cos, e->rope_sin, ps->row,
+                                                        ps->pos, ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
       // the last layer's K/V are its only output the payload holds: its
       // attention, O projection and MLP would feed no later layer
       if (l == m.L - 1) break;
       attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(ps->q, payload, spans, ps->attn, l,
                                                                                 m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
-      // O, gate/up and down results rounded to bf16 by the GEMM itself
-      bf16 *out = reinterpret_cast<bf16 *>(ps->acc);
-      blas_ok &= prefill_gemm(ps->blas, ps->attn, pl.o_w, out, CUDA_R_16BF, T, H, m.Hq) == CUBLAS_STATUS_SUCCESS;
-      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(out, ps->h, lw.w_post, ps->x, H, m.eps);
-      blas_ok &= prefill_gemm(ps->blas, ps->x, pl.gu_w, out, CUDA_R_16BF, T, 2 * I, H) == CUBLAS_STATUS_SUCCESS;
-      prefill::swiglu<<<ew, 256, 0, e->stream>>>(out, ps->act, T, I);
-      blas_ok &= prefill_gemm(ps->blas, ps->act, pl.down_w, out, CUDA_R_16BF, T, H, I) == CUBLAS_STATUS_SUCCESS;
-      prefill::residual_rms_norm<<<T, prefill::kNormThreads, 0, e->stream>>>(out, ps->h, e->layers[l + 1].w_in, ps->x,
-                                                                              H, m.eps);
+      gemm_ok &= prefill_gemm(e, lw.o_w, H, m.Hq, ps->attn, T, m.Hq, 0, so);
+      prefill::residual_rms_norm_parts<<<T, prefill::kNormThreads, 0, e->stream>>>(ps->acc, so, T, ps->h, lw.w_post,
+                                                                                   ps->x, H, m.eps);
+      // gate/up with the SwiGLU in its epilogue: the activation [T][I]
+      gemm_ok &= prefill_gemm(e, lw.gu_w, 2 * I, H, ps->x, T, H, 1, 1);
+      gemm_ok &= prefill_gemm(e, lw.down_w, H, m.I_pad, ps->act, T, I, 0, sd);
+      prefill::residual_rms_norm_parts<<<T, prefill::kNormThreads, 0, e->stream>>>(
+          ps->acc, sd, T, ps->h, e->layers[l + 1].w_in, ps->x, H, m.eps);
     }
   }
-  if (!blas_ok) {
-    e->last_error = "prefill: cuBLAS GEMM failed";
+  if (!gemm_ok) {
+    e->last_error = "prefill: tensor-core GEMM launch or tensor map failed";
     return -2;
   }
   err = cudaGetLastError();
   if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
   if (err != cudaSuccess) return set_err(e, err, "prefill");
+  if (T > 0) {
+    uint32_t site = 0;
+    err = copy_sync(e, &site, ps->error, 4, cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) return set_err(e, err, "prefill error word");
+    if (site != 0) {
+      e->last_error = "prefill: a tensor-core GEMM wait gave up (site " + std::to_string(site) + ")";
+      return -2;
+    }
+  }
   e->payload_ready = true;
   return 0;
 }

@@ -3,9 +3,9 @@
 // once, and each layer's roped K and V land in the import payload
 // [K|V][layer][row][block_size][kv_heads][head_dim] -- the one-shot import
 // format of the epoch controller -- at the token's position in its row's first
-// block.  The projections are plain row-major bf16 GEMMs (cuBLAS, fp32
-// accumulation; fp32 output for QKV, whose bias joins the fp32 sum before its
-// one rounding, bf16 output for the others).  These kernels do everything
+// block.  The projections run on the tensor cores (prefill_gemm.cuh, fp32
+// accumulation and fp32 k-range partial sums, added in order here; the
+// gate/up projection writes the SwiGLU activation itself).  These kernels do everything
 // between them with the decoder step's rounding points
 // (batched_decoder_step.py:224-229 norm, :305-313 QKV, :231-240 rope,
 // :356-377 scores/softmax, :380-403 residuals and SwiGLU), token by token, so
@@ -153,6 +153,58 @@ __global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const bf16 *y,
   }
 }
 
+// The same residual update and norm from the projection's fp32 k-range
+// partial sums [split][T][H] (tensor-core GEMM): y = bf16(sum of the splits in
+// order) is the decoder's materialize(mm_t(x, W)), then h = bf16(h + y) and
+// x = the next rms_norm, as above.
+__global__ void __launch_bounds__(kNormThreads) residual_rms_norm_parts(const float *parts, int nsplit, int T,
+                                                                         bf16 *h, const bf16 *w, bf16 *x, int H,
+                                                                         float eps) {
+  __shared__ float scratch[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
+  const int64_t split_stride = static_cast<int64_t>(T) * H;
+  const int chunks = H >> 3;
+  float hv[kNormChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < chunks) {
+      float prev[8], y[8];
+      unpack8(*reinterpret_cast<const uint4 *>(h + base + c * 8), prev);
+      const float4 *p0 = reinterpret_cast<const float4 *>(parts + base + c * 8);
+      float4 lo = p0[0], hi = p0[1];
+      for (int k = 1; k < nsplit; ++k) {
+        const float4 *pk = reinterpret_cast<const float4 *>(parts + k * split_stride + base + c * 8);
+        const float4 a = pk[0], b2 = pk[1];
+        lo.x = __fadd_rn(lo.x, a.x); lo.y = __fadd_rn(lo.y, a.y); lo.z = __fadd_rn(lo.z, a.z); lo.w = __fadd_rn(lo.w, a.w);
+        hi.x = __fadd_rn(hi.x, b2.x); hi.y = __fadd_rn(hi.y, b2.y); hi.z = __fadd_rn(hi.z, b2.z); hi.w = __fadd_rn(hi.w, b2.w);
+      }
+      y[0] = r(lo.x); y[1] = r(lo.y); y[2] = r(lo.z); y[3] = r(lo.w);
+      y[4] = r(hi.x); y[5] = r(hi.y); y[6] = r(hi.z); y[7] = r(hi.w);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        hv[j][k] = r(__fadd_rn(prev[k], y[k]));
+        ss = __fadd_rn(ss, __fmul_rn(hv[j][k], hv[j][k]));
+      }
+      *reinterpret_cast<uint4 *>(h + base + c * 8) = pack8(hv[j]);
+    }
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps)));
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < chunks) {
+      float wv[8], out[8];
+      unpack8(*reinterpret_cast<const uint4 *>(w + c * 8), wv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) out[k] = __fmul_rn(r(__fmul_rn(hv[j][k], inv)), wv[k]);
+      *reinterpret_cast<uint4 *>(x + base + c * 8) = pack8(out);
+    }
+  }
+}
+
 // QKV epilogue, one CTA per token: q, k, v = bf16(acc + bias) (F.linear: fp32
 // sum plus bias, one rounding), rope on q and k with the token's position
 // (q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16), q to
@@ -165,13 +217,26 @@ __device__ __forceinline__ uint32_t bf2_bits(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&pair);
 }
 
-__global__ void qkv_rope_store(const float *acc, const bf16 *bias, const bf16 *cos, const bf16 *sin,
-                               const int32_t *tok_row, const int32_t *tok_pos, bf16 *q_out, bf16 *payload,
-                               int layer, int L, int nq, int nkv, int d, int bs) {
+// The projection's fp32 sum of element n of this token: the k-range partial
+// sums [split][T][N] added in split order (deterministic).
+__device__ __forceinline__ float2 split_sum2(const float *acc, int64_t split_stride, int nsplit, int64_t at) {
+  float2 s = *reinterpret_cast<const float2 *>(acc + at);
+  for (int k = 1; k < nsplit; ++k) {
+    const float2 v = *reinterpret_cast<const float2 *>(acc + k * split_stride + at);
+    s.x = __fadd_rn(s.x, v.x);
+    s.y = __fadd_rn(s.y, v.y);
+  }
+  return s;
+}
+
+__global__ void qkv_rope_store(const float *acc, int nsplit, int T, const bf16 *bias, const bf16 *cos,
+                               const bf16 *sin, const int32_t *tok_row, const int32_t *tok_pos, bf16 *q_out,
+                               bf16 *payload, int layer, int L, int nq, int nkv, int d, int bs) {
   const int t = blockIdx.x;
   const int Hq = nq * d, kvw = nkv * d, N = Hq + 2 * kvw;
   const int row = tok_row[t], pos = tok_pos[t], half = d / 2, quarter = d / 4;
-  const float *a = acc + static_cast<int64_t>(t) * N;
+  const int64_t split_stride = static_cast<int64_t>(T) * N;
+  const int64_t a = static_cast<int64_t>(t) * N;
   const bf16 *cs = cos + static_cast<int64_t>(pos) * d;
   const bf16 *sn = sin + static_cast<int64_t>(pos) * d;
   const int64_t block_elems = static_cast<int64_t>(bs) * kvw;
@@ -181,7 +246,7 @@ __global__ void qkv_rope_store(const float *acc, const bf16 *bias, const bf16 *c
   for (int u = threadIdx.x; u < units; u += blockDim.x) {
     if (u >= rope_units) {   // v: two elements
       const int n = Hq + kvw + 2 * (u - rope_units);
-      const float2 s2 = *reinterpret_cast<const float2 *>(a + n);
+      const float2 s2 = split_sum2(acc, split_stride, nsplit, a + n);
       const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162 *>(bias + n);
       *reinterpret_cast<uint32_t *>(payload + v_base + slot_off + (n - Hq - kvw)) =
           bf2_bits(__fadd_rn(s2.x, __low2float(b2)), __fadd_rn(s2.y, __high2float(b2)));
@@ -189,8 +254,8 @@ __global__ void qkv_rope_store(const float *acc, const bf16 *bias, const bf16 *c
     }
     const int head = u / quarter, i = 2 * (u - head * quarter);   // q heads, then k heads
     const int n_lo = head * d + i, n_hi = n_lo + half;
-    const float2 s_lo = *reinterpret_cast<const float2 *>(a + n_lo);
-    const float2 s_hi = *reinterpret_cast<const float2 *>(a + n_hi);
+    const float2 s_lo = split_sum2(acc, split_stride, nsplit, a + n_lo);
+    const float2 s_hi = split_sum2(acc, split_stride, nsplit, a + n_hi);
     const __nv_bfloat162 b_lo = *reinterpret_cast<const __nv_bfloat162 *>(bias + n_lo);
     const __nv_bfloat162 b_hi = *reinterpret_cast<const __nv_bfloat162 *>(bias + n_hi);
     const __nv_bfloat162 c_lo = *reinterpret_cast<const __nv_bfloat162 *>(cs + i);

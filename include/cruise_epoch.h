@@ -307,8 +307,9 @@ int32_t cruise_epoch_read_trace_cta(void *engine, uint32_t *stamps,
  * import payload format -- and keeps it there: the next cruise_epoch_run with
  * the import flag and import_payload NULL / import_bytes 0 imports it (one-shot
  * device import with the Adler-32 proof) and decodes from position len-1 with
- * token prompt[len-1].  The projections run as cuBLAS bf16 GEMMs on an
- * untiled copy of the layer weights made on the first call (kept until
+ * token prompt[len-1].  The projections run as the engine's own tcgen05
+ * GEMMs, reading the resident tiled weights through TMA (no second copy of
+ * the weights; the first call allocates the activation buffers, kept until
  * destroy); attention, norms, rope and SwiGLU follow the decoder step's
  * rounding points.  Geometry limits: block_size <= 128, head size 64 or
  * 128, at most 8 query heads per KV head, intermediate and hidden sizes
