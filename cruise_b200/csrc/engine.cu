@@ -171,11 +171,14 @@ struct PrefillState {
   void *work = nullptr;
   int max_tokens = 0;
   bf16 *h = nullptr, *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+  bf16 *y = nullptr;           // a projection's bf16 output [T][H] (O without k splits)
   float *acc = nullptr;        // fp32 k-range partial sums [split][T][N]
   int64_t *tok = nullptr;
   int32_t *row = nullptr, *pos = nullptr;
   uint32_t *error = nullptr;   // site of a tensor-core GEMM wait that ran out (0: none)
+  bool chain = true;           // kernels launched as programmatic dependents (CRUISE_PREFILL_PDL=0: plain)
   bool gemm_attr = false;      // the GEMM's shared-memory limit has been raised
+  int gemm_pairs = 0;          // resident CTA pairs of the GEMM (0: not yet asked)
 };
 
 struct Engine {
@@ -690,7 +693,7 @@ PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
 
 // A tiled projection [N][K] (tiles of 16 rows x kc, stream order [row group][k
 // tile]) as the 5-D tensor (element in a 128-byte segment, segment, row in
-// tile, k tile, row group); a box is 16 row groups x 16 rows of one segment.
+// tile, k tile, row group); a box is 8 row groups x 16 rows of one segment.
 bool weight_map(CUtensorMap *map, const bf16 *W, int N, int K, int kc) {
   const PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
   if (encode == nullptr) return false;
@@ -698,7 +701,7 @@ bool weight_map(CUtensorMap *map, const bf16 *W, int N, int K, int kc) {
                               static_cast<cuuint64_t>(N / 16)};
   const cuuint64_t strides[4] = {128, static_cast<cuuint64_t>(kc) * 2, static_cast<cuuint64_t>(kc) * 32,
                                  static_cast<cuuint64_t>(K / kc) * kc * 32};
-  const cuuint32_t box[5] = {64, 1, 16, 1, tcgemm::kRows / 16};
+  const cuuint32_t box[5] = {64, 1, 16, 1, tcgemm::kM / 16};
   const cuuint32_t elem[5] = {1, 1, 1, 1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<bf16 *>(W), dims, strides, box, elem,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -706,58 +709,162 @@ bool weight_map(CUtensorMap *map, const bf16 *W, int N, int K, int kc) {
 }
 
 // Row-major activations [T][width] (row pitch `pitch` elements) in boxes of
-// 64 columns x 256 tokens with the 128-byte swizzle; out-of-range reads zero.
-bool activation_map(CUtensorMap *map, const bf16 *X, int T, int width, int pitch) {
+// 64 columns x `rows` tokens with the 128-byte swizzle; out-of-range reads zero.
+bool activation_map(CUtensorMap *map, const bf16 *X, int T, int width, int pitch, int rows) {
   const PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
   if (encode == nullptr) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch) * 2};
-  const cuuint32_t box[2] = {64, 256};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(rows)};
   const cuuint32_t elem[2] = {1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16 *>(X), dims, strides, box, elem,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// k-range splits of a projection for T tokens: enough (256-row tile, token
-// half) pairs x splits to cover the SMs once, at most one split per k chunk.
-int gemm_splits(const Engine *e, int N, int K, int T) {
-  const int tiles = (N + tcgemm::kRows - 1) / tcgemm::kRows * (T > tcgemm::kTokHalf ? 2 : 1);
-  const int chunks = K / tcgemm::kKChunk;
-  return std::max(1, std::min(chunks, e->sms / tiles));
+// CTA pairs of the GEMM that can be resident at once (one CTA per SM).  The
+// first call raises the kernel's shared-memory limit.
+int gemm_pairs(Engine *e) {
+  PrefillState *ps = e->prefill;
+  if (ps->gemm_pairs > 0) return ps->gemm_pairs;
+  if (!ps->gemm_attr) {
+    if (cudaFuncSetAttribute(tcgemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(tcgemm::smem_bytes())) != cudaSuccess) {
+      cudaGetLastError();
+      return e->sms / 2;   // the launch reports the failure
+    }
+    ps->gemm_attr = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (e->sms / 2));
+  cfg.blockDim = dim3(tcgemm::kThreads);
+  cfg.dynamicSmemBytes = tcgemm::smem_bytes();
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, tcgemm::gemm_kernel, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();
+    clusters = e->sms / 2;
+  }
+  ps->gemm_pairs = std::min(clusters, e->sms / 2);
+  return ps->gemm_pairs;
+}
+
+// Launches a prefill kernel as a programmatic dependent of the previous one in
+// the stream (when enabled): it may begin while that one drains and waits for
+// it inside (prefill::chain_enter).
+template <typename... Params, typename... Actual>
+void chain_launch(Engine *e, dim3 grid, dim3 block, size_t smem, void (*kernel)(Params...), Actual &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = e->prefill->chain ? 1 : 0;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e->stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Actual>(args)...);   // errors surface at the stream check
+}
+
+// How a projection is tiled: tokens per pair tile and k-range splits.
+struct GemmPlan {
+  int ttile = 512, ttiles = 1, nsplit = 1;
+};
+
+// k-range splits for `tiles` pair tiles of `chunks` k chunks: tiles x splits
+// run in waves over the resident pairs; the split count minimises waves x
+// chunks per split, plus two chunks' worth per split for the partial sums it
+// adds.
+int gemm_splits(Engine *e, int tiles, int chunks) {
+  const int pairs = gemm_pairs(e);
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int sp = 1; sp <= std::min(chunks, prefill::kMaxSplits); ++sp) {
+    const int64_t waves = (static_cast<int64_t>(tiles) * sp + pairs - 1) / pairs;
+    const int64_t cost = waves * ((chunks + sp - 1) / sp) + 2 * sp;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
+}
+
+// All tokens in one tile (W read once per tile: the copies from L2 set the
+// pace, and 128-token tiles measured slower for QKV and O), k split where
+// the row tiles alone do not fill the pairs.
+GemmPlan gemm_plan(Engine *e, int N, int K, int T) {
+  GemmPlan p;
+  p.ttile = T <= 128 ? 128 : T <= 256 ? 256 : 512;
+  p.ttiles = (T + p.ttile - 1) / p.ttile;
+  p.nsplit = gemm_splits(e, (N + tcgemm::kRows - 1) / tcgemm::kRows * p.ttiles, K / tcgemm::kKChunk);
+  return p;
 }
 
 // Y = X . W^T on the tensor cores.  mode 0: fp32 partials [nsplit][T][N] into
 // ps->acc; mode 1 (the interleaved gate/up projection): the SwiGLU activation
-// [T][N / 2] into ps->act.  Returns false when a tensor map cannot be made or
-// the launch fails.
-bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, int x_width, int mode, int nsplit) {
+// [T][N / 2] into `out`; mode 2 (no k splits): bf16 [T][N] into `out`.
+// Returns false, with the reason in last_error, when a tensor map cannot be
+// made or the launch fails.
+bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, int x_width, int mode,
+                  const GemmPlan &plan, bf16 *out) {
   PrefillState *ps = e->prefill;
-  CUtensorMap wmap, xmap;
-  if (!weight_map(&wmap, W, N, K, pick_kc(K)) || !activation_map(&xmap, X, T, x_width, x_width)) return false;
   tcgemm::Args a{};
   a.T = T;
   a.N = N;
   a.chunks = K / tcgemm::kKChunk;
   a.kc = pick_kc(K);
-  a.nsplit = nsplit;
+  a.nsplit = plan.nsplit;
   a.mode = mode;
-  a.halves = T > tcgemm::kTokHalf ? 2 : 1;
-  a.stages = tcgemm::kMaxStages;
-  a.tiles = (N + tcgemm::kRows - 1) / tcgemm::kRows * a.halves * nsplit;
+  a.ttile = plan.ttile;
+  a.ttiles = plan.ttiles;
+  a.tsub = plan.ttile > tcgemm::kSub ? 2 : 1;
+  a.xrows = std::min(plan.ttile / 2, tcgemm::kSub / 2);
+  a.stages = std::min<int>(tcgemm::kMaxStages, tcgemm::kRingBytes / tcgemm::stage_bytes(a.tsub, a.xrows));
+  a.tiles = (N + tcgemm::kRows - 1) / tcgemm::kRows * plan.ttiles * plan.nsplit;
   a.partials = ps->acc;
-  a.act = ps->act;
-  a.act_stride = N / 2;
+  a.out = out;
+  a.out_stride = mode == 1 ? N / 2 : N;
   a.error = ps->error;
-  const size_t smem = tcgemm::smem_bytes(a.stages);
-  if (!ps->gemm_attr) {
-    if (cudaFuncSetAttribute(tcgemm::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return false;
-    ps->gemm_attr = true;
+  CUtensorMap wmap, xmap;
+  if (!weight_map(&wmap, W, N, K, a.kc) || !activation_map(&xmap, X, T, x_width, x_width, a.xrows)) {
+    e->last_error = "prefill: a GEMM tensor map could not be encoded";
+    return false;
   }
-  tcgemm::gemm_kernel<<<std::min(a.tiles, e->sms), tcgemm::kThreads, smem, e->stream>>>(wmap, xmap, a);
-  return cudaGetLastError() == cudaSuccess;
+  const size_t smem = tcgemm::smem_bytes();
+  const int pairs = gemm_pairs(e);
+  if (!ps->gemm_attr) {
+    e->last_error = "prefill: the GEMM's shared-memory size (" + std::to_string(smem) + " bytes) was refused";
+    return false;
+  }
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[2]{};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = ps->chain ? 1 : 0;
+  cfg.gridDim = dim3(2 * std::min(a.tiles, pairs));
+  cfg.blockDim = dim3(tcgemm::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e->stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, tcgemm::gemm_kernel, wmap, xmap, a);
+  if (err != cudaSuccess) {
+    e->last_error = std::string("prefill: GEMM launch: ") + cudaGetErrorString(err);
+    cudaGetLastError();
+    return false;
+  }
+  return true;
 }
 
 // Frees the prefill buffers, whole or partly built; cudaFree waits for the
@@ -778,6 +885,7 @@ int32_t prefill_prepare(Engine *e) {
   const int64_t H = m.H, Hq = m.Hq, I = m.I, N = m.Nqkv;
   auto *ps = new PrefillState();
   e->prefill = ps;
+  if (const char *env = std::getenv("CRUISE_PREFILL_PDL")) ps->chain = std::atoi(env) != 0;
   if (tensor_map_encoder() == nullptr) {
     e->last_error = "prefill: the driver has no cuTensorMapEncodeTiled";
     return -2;
@@ -786,19 +894,21 @@ int32_t prefill_prepare(Engine *e) {
   const int T = kBatch * m.bs;
   ps->max_tokens = T;
   // the most fp32 partial sums (splits x outputs x tokens) of QKV, O and down
-  // at any token count: the split counts depend on the token count only
-  // through the number of token halves (one up to 256 tokens, then two), so
-  // the largest count of each side is taken at that side's most tokens
+  // at any token count: the plans change only where a 128-token tile fills
+  // up, so each range's largest count stands for it
   int64_t parts = 0;
-  for (const int t : {std::min(T, tcgemm::kTokHalf), T}) {
-    const int64_t widest = std::max<int64_t>(gemm_splits(e, m.Nqkv, m.H, t) * N,
-                                             std::max(gemm_splits(e, m.H, m.Hq, t), gemm_splits(e, m.H, m.I_pad, t)) * H);
-    parts = std::max(parts, widest * t);
+  for (int t = 128;; t += 128) {
+    const int tt = std::min(T, t);
+    const int64_t sq = gemm_plan(e, m.Nqkv, m.H, tt).nsplit, so = gemm_plan(e, m.H, m.Hq, tt).nsplit;
+    const int64_t sd = gemm_plan(e, m.H, m.I_pad, tt).nsplit;
+    parts = std::max(parts, std::max(sq * N, std::max(so, sd) * H) * tt);
+    if (tt == T) break;
   }
   size_t bytes = 0;
   auto take = [&](size_t n) { const size_t off = bytes; bytes = align_up(bytes + n, 1024); return off; };
   const size_t o_h = take(T * H * 2), o_x = take(T * H * 2), o_q = take(T * Hq * 2), o_attn = take(T * Hq * 2);
-  const size_t o_act = take(T * I * 2), o_acc = take(parts * 4), o_tok = take(T * 8), o_row = take(T * 4),
+  const size_t o_act = take(T * I * 2), o_y = take(T * H * 2), o_acc = take(parts * 4), o_tok = take(T * 8),
+               o_row = take(T * 4),
                o_pos = take(T * 4), o_err = take(4);
   cudaError_t err = cudaMalloc(&ps->work, bytes);
   if (err != cudaSuccess) return set_err(e, err, "prefill buffers");
@@ -808,6 +918,7 @@ int32_t prefill_prepare(Engine *e) {
   ps->q = reinterpret_cast<bf16 *>(b + o_q);
   ps->attn = reinterpret_cast<bf16 *>(b + o_attn);
   ps->act = reinterpret_cast<bf16 *>(b + o_act);
+  ps->y = reinterpret_cast<bf16 *>(b + o_y);
   ps->acc = reinterpret_cast<float *>(b + o_acc);
   ps->tok = reinterpret_cast<int64_t *>(b + o_tok);
   ps->row = reinterpret_cast<int32_t *>(b + o_row);
@@ -890,36 +1001,42 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     return set_err(e, cudaGetLastError(), "prefill attention shared memory");
   bool gemm_ok = true;
   if (T > 0) {
-    const int sq = gemm_splits(e, m.Nqkv, H, T), so = gemm_splits(e, H, m.Hq, T), sd = gemm_splits(e, H, m.I_pad, T);
+    const GemmPlan pq = gemm_plan(e, m.Nqkv, H, T), po = gemm_plan(e, H, m.Hq, T);
+    const GemmPlan pg = gemm_plan(e, 2 * I, H, T), pd = gemm_plan(e, H, m.I_pad, T);
     err = cudaMemsetAsync(ps->error, 0, 4, e->stream);
     if (err != cudaSuccess) return set_err(e, err, "prefill error word");
     prefill::embed_rows<<<T, 128, 0, e->stream>>>(e->embed, ps->tok, ps->h, H);
-    prefill::rms_norm_rows<<<T, 256, 0, e->stream>>>(ps->h, e->layers[0].w_in, ps->x, H, m.eps);
+    chain_launch(e, T, 256, 0, prefill::rms_norm_rows, ps->h, e->layers[0].w_in, ps->x, H, m.eps);
     for (int l = 0; l < m.L && gemm_ok; ++l) {
       // x holds rms_norm(h) * w_in of this layer
       const LayerWeights &lw = e->layers[l];
-      gemm_ok &= prefill_gemm(e, lw.qkv_w, m.Nqkv, H, ps->x, T, H, 0, sq);
-      prefill::qkv_rope_store<<<T, 256, 0, e->stream>>>(ps->acc, sq, T, lw.qkv_b, e->rope_cos, e->rope_sin, ps->row,
-                                                        ps->pos, ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
+      gemm_ok &= prefill_gemm(e, lw.qkv_w, m.Nqkv, H, ps->x, T, H, 0, pq, nullptr);
+      chain_launch(e, T, 256, 0, prefill::qkv_rope_store, ps->acc, pq.nsplit, T, lw.qkv_b, e->rope_cos, e->rope_sin,
+                   ps->row, ps->pos, ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
       // the last layer's K/V are its only output the payload holds: its
       // attention, O projection and MLP would feed no later layer
       if (l == m.L - 1) break;
-      attention<<<attn_grid, prefill::kAttnWarps * 32, attn_smem, e->stream>>>(ps->q, payload, spans, ps->attn, l,
-                                                                                m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
-      gemm_ok &= prefill_gemm(e, lw.o_w, H, m.Hq, ps->attn, T, m.Hq, 0, so);
-      prefill::residual_rms_norm_parts<<<T, prefill::kNormThreads, 0, e->stream>>>(ps->acc, so, T, ps->h, lw.w_post,
-                                                                                   ps->x, H, m.eps);
+      chain_launch(e, attn_grid, prefill::kAttnWarps * 32, attn_smem, attention, ps->q, payload, spans, ps->attn, l,
+                   m.L, m.nq, m.nkv, m.bs, m.sqrt_d);
+      if (po.nsplit == 1) {   // bf16 out of the GEMM: the decoder's materialize(mm_t(attn, Wo))
+        gemm_ok &= prefill_gemm(e, lw.o_w, H, m.Hq, ps->attn, T, m.Hq, 2, po, ps->y);
+        chain_launch(e, T, prefill::kNormThreads, 0, prefill::residual_rms_norm, ps->y, ps->h, lw.w_post, ps->x, H,
+                     m.eps);
+      } else {
+        gemm_ok &= prefill_gemm(e, lw.o_w, H, m.Hq, ps->attn, T, m.Hq, 0, po, nullptr);
+        chain_launch(e, T, prefill::kNormThreads, 0, prefill::residual_rms_norm_parts, ps->acc, po.nsplit, T, ps->h,
+                     lw.w_post, ps->x, H, m.eps);
+      }
       // gate/up with the SwiGLU in its epilogue: the activation [T][I]
-      gemm_ok &= prefill_gemm(e, lw.gu_w, 2 * I, H, ps->x, T, H, 1, 1);
-      gemm_ok &= prefill_gemm(e, lw.down_w, H, m.I_pad, ps->act, T, I, 0, sd);
-      prefill::residual_rms_norm_parts<<<T, prefill::kNormThreads, 0, e->stream>>>(
-          ps->acc, sd, T, ps->h, e->layers[l + 1].w_in, ps->x, H, m.eps);
+      GemmPlan pg1 = pg;
+      pg1.nsplit = 1;
+      gemm_ok &= prefill_gemm(e, lw.gu_w, 2 * I, H, ps->x, T, H, 1, pg1, ps->act);
+      gemm_ok &= prefill_gemm(e, lw.down_w, H, m.I_pad, ps->act, T, I, 0, pd, nullptr);
+      chain_launch(e, T, prefill::kNormThreads, 0, prefill::residual_rms_norm_parts, ps->acc, pd.nsplit, T, ps->h,
+                   e->layers[l + 1].w_in, ps->x, H, m.eps);
     }
   }
-  if (!gemm_ok) {
-    e->last_error = "prefill: tensor-core GEMM launch or tensor map failed";
-    return -2;
-  }
+  if (!gemm_ok) return -2;   // prefill_gemm left the reason in last_error
   err = cudaGetLastError();
   if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
   if (err != cudaSuccess) return set_err(e, err, "prefill");

@@ -51,8 +51,19 @@ __device__ __forceinline__ float block_max(float v, float *scratch) {
   return t;
 }
 
+// Programmatic dependent launch: the engine launches each prefill kernel so
+// that it may begin while its predecessor in the stream drains.  A kernel
+// first lets its own successor begin launching, then waits for the
+// predecessor's completion (and its memory) before it reads or writes
+// anything the predecessor touches.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void chain_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // h[t] = embed[token[t]]; one CTA per token.
 __global__ void embed_rows(const bf16 *embed, const int64_t *token, bf16 *h, int H) {
+  chain_enter();
   const int t = blockIdx.x;
   const uint4 *src = reinterpret_cast<const uint4 *>(embed + token[t] * static_cast<int64_t>(H));
   uint4 *dst = reinterpret_cast<uint4 *>(h + static_cast<int64_t>(t) * H);
@@ -62,6 +73,7 @@ __global__ void embed_rows(const bf16 *embed, const int64_t *token, bf16 *h, int
 // x[t] = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w): rms_norm (:224-229); one
 // CTA per token.
 __global__ void rms_norm_rows(const bf16 *h, const bf16 *w, bf16 *x, int H, float eps) {
+  chain_enter();
   __shared__ float scratch[32];
   const bf16 *row = h + static_cast<int64_t>(blockIdx.x) * H;
   float ss = 0.f;
@@ -86,6 +98,7 @@ __global__ void rms_norm_rows(const bf16 *h, const bf16 *w, bf16 *x, int H, floa
 // kNormThreads * kNormChunks, both checked by the host.
 constexpr int kNormThreads = 256;
 constexpr int kNormChunks = 4;
+constexpr int kMaxSplits = 8;   // k-range partial sums a consumer adds (the GEMM's split count is capped here)
 
 __device__ __forceinline__ void unpack8(const uint4 &u, float (&v)[8]) {
   const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(&u);
@@ -109,6 +122,7 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
 
 __global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const bf16 *y, bf16 *h, const bf16 *w, bf16 *x,
                                                                    int H, float eps) {
+  chain_enter();
   __shared__ float scratch[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
   const int chunks = H >> 3;
@@ -160,6 +174,7 @@ __global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const bf16 *y,
 __global__ void __launch_bounds__(kNormThreads) residual_rms_norm_parts(const float *parts, int nsplit, int T,
                                                                          bf16 *h, const bf16 *w, bf16 *x, int H,
                                                                          float eps) {
+  chain_enter();
   __shared__ float scratch[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
   const int64_t split_stride = static_cast<int64_t>(T) * H;
@@ -171,15 +186,25 @@ __global__ void __launch_bounds__(kNormThreads) residual_rms_norm_parts(const fl
     const int c = threadIdx.x + j * kNormThreads;
     if (c < chunks) {
       float prev[8], y[8];
-      unpack8(*reinterpret_cast<const uint4 *>(h + base + c * 8), prev);
-      const float4 *p0 = reinterpret_cast<const float4 *>(parts + base + c * 8);
-      float4 lo = p0[0], hi = p0[1];
-      for (int k = 1; k < nsplit; ++k) {
-        const float4 *pk = reinterpret_cast<const float4 *>(parts + k * split_stride + base + c * 8);
-        const float4 a = pk[0], b2 = pk[1];
-        lo.x = __fadd_rn(lo.x, a.x); lo.y = __fadd_rn(lo.y, a.y); lo.z = __fadd_rn(lo.z, a.z); lo.w = __fadd_rn(lo.w, a.w);
-        hi.x = __fadd_rn(hi.x, b2.x); hi.y = __fadd_rn(hi.y, b2.y); hi.z = __fadd_rn(hi.z, b2.z); hi.w = __fadd_rn(hi.w, b2.w);
-      }
+      const uint4 hraw = *reinterpret_cast<const uint4 *>(h + base + c * 8);
+      // every split's loads in flight before the ordered sum
+      float4 pl[kMaxSplits], ph[kMaxSplits];
+#pragma unroll
+      for (int k = 0; k < kMaxSplits; ++k)
+        if (k < nsplit) {
+          const float4 *pk = reinterpret_cast<const float4 *>(parts + k * split_stride + base + c * 8);
+          pl[k] = pk[0];
+          ph[k] = pk[1];
+        }
+      unpack8(hraw, prev);
+      float4 lo = pl[0], hi = ph[0];
+#pragma unroll
+      for (int k = 1; k < kMaxSplits; ++k)
+        if (k < nsplit) {
+          const float4 a = pl[k], b2 = ph[k];
+          lo.x = __fadd_rn(lo.x, a.x); lo.y = __fadd_rn(lo.y, a.y); lo.z = __fadd_rn(lo.z, a.z); lo.w = __fadd_rn(lo.w, a.w);
+          hi.x = __fadd_rn(hi.x, b2.x); hi.y = __fadd_rn(hi.y, b2.y); hi.z = __fadd_rn(hi.z, b2.z); hi.w = __fadd_rn(hi.w, b2.w);
+        }
       y[0] = r(lo.x); y[1] = r(lo.y); y[2] = r(lo.z); y[3] = r(lo.w);
       y[4] = r(hi.x); y[5] = r(hi.y); y[6] = r(hi.z); y[7] = r(hi.w);
 #pragma unroll
@@ -220,18 +245,24 @@ __device__ __forceinline__ uint32_t bf2_bits(float lo, float hi) {
 // The projection's fp32 sum of element n of this token: the k-range partial
 // sums [split][T][N] added in split order (deterministic).
 __device__ __forceinline__ float2 split_sum2(const float *acc, int64_t split_stride, int nsplit, int64_t at) {
-  float2 s = *reinterpret_cast<const float2 *>(acc + at);
-  for (int k = 1; k < nsplit; ++k) {
-    const float2 v = *reinterpret_cast<const float2 *>(acc + k * split_stride + at);
-    s.x = __fadd_rn(s.x, v.x);
-    s.y = __fadd_rn(s.y, v.y);
-  }
+  float2 v[kMaxSplits];   // every split's load in flight before the ordered sum
+#pragma unroll
+  for (int k = 0; k < kMaxSplits; ++k)
+    if (k < nsplit) v[k] = *reinterpret_cast<const float2 *>(acc + k * split_stride + at);
+  float2 s = v[0];
+#pragma unroll
+  for (int k = 1; k < kMaxSplits; ++k)
+    if (k < nsplit) {
+      s.x = __fadd_rn(s.x, v[k].x);
+      s.y = __fadd_rn(s.y, v[k].y);
+    }
   return s;
 }
 
 __global__ void qkv_rope_store(const float *acc, int nsplit, int T, const bf16 *bias, const bf16 *cos,
                                const bf16 *sin, const int32_t *tok_row, const int32_t *tok_pos, bf16 *q_out,
                                bf16 *payload, int layer, int L, int nq, int nkv, int d, int bs) {
+  chain_enter();
   const int t = blockIdx.x;
   const int Hq = nq * d, kvw = nkv * d, N = Hq + 2 * kvw;
   const int row = tok_row[t], pos = tok_pos[t], half = d / 2, quarter = d / 4;
@@ -366,6 +397,7 @@ template <int D>
 __global__ void __launch_bounds__(kAttnWarps * 32, 1) causal_attention_mma(
     const bf16 *q, const bf16 *payload, RowSpans spans, bf16 *out, int layer, int L, int nq, int nkv, int bs,
     float sqrt_d) {
+  chain_enter();
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int S = D + 8;   // shared-memory row stride (bf16)
   constexpr int SP = kMaxKeys + 8;   // probability row stride (bf16)
@@ -539,31 +571,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) causal_attention_mma(
       *reinterpret_cast<__nv_bfloat162 *>(out + tA * nq * D + hA * D + dim) = __floats2bfloat162_rn(o[nt][0], o[nt][1]);
     if (posB >= 0)
       *reinterpret_cast<__nv_bfloat162 *>(out + tB * nq * D + hB * D + dim) = __floats2bfloat162_rn(o[nt][2], o[nt][3]);
-  }
-}
-
-// silu(bf16(x Wg^T)) * bf16(x Wu^T), each op rounded to bf16 (:391-398); y
-// rows are [gate (I) | up (I)] per token, the GEMM's fp32 sums already
-// rounded to bf16 by the GEMM.  Eight consecutive elements per thread
-// (16-byte loads and stores): I % 8 == 0 and T * I < 2^31, both checked by
-// the host.
-__device__ __forceinline__ float swiglu_one(float gate, float up) {
-  const float silu = r(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
-  return __fmul_rn(silu, up);
-}
-
-__global__ void swiglu(const bf16 *y, bf16 *act, int T, int I) {
-  const int octs = I >> 3;
-  const int count = T * octs;
-  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < count; e += gridDim.x * blockDim.x) {
-    const int t = e / octs, i = (e - t * octs) << 3;
-    const bf16 *row = y + static_cast<int64_t>(t) * 2 * I;
-    float g[8], u[8], v[8];
-    unpack8(*reinterpret_cast<const uint4 *>(row + i), g);
-    unpack8(*reinterpret_cast<const uint4 *>(row + I + i), u);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = swiglu_one(g[k], u[k]);
-    *reinterpret_cast<uint4 *>(act + static_cast<int64_t>(t) * I + i) = pack8(v);
   }
 }
 
