@@ -177,6 +177,8 @@ struct PrefillState {
   int32_t *row = nullptr, *pos = nullptr;
   uint32_t *error = nullptr;   // site of a tensor-core GEMM wait that ran out (0: none)
   bool chain = true;           // kernels launched as programmatic dependents (CRUISE_PREFILL_PDL=0: plain)
+  int narrow_tile = 0;         // token tile cap of QKV, O and down (CRUISE_PREFILL_TTILE; 0: all tokens)
+  int force_split = 0;         // their split count (CRUISE_PREFILL_SPLIT; 0: the cost model's)
   bool gemm_attr = false;      // the GEMM's shared-memory limit has been raised
   int gemm_pairs = 0;          // resident CTA pairs of the GEMM (0: not yet asked)
 };
@@ -799,12 +801,15 @@ int gemm_splits(Engine *e, int tiles, int chunks) {
 
 // All tokens in one tile (W read once per tile: the copies from L2 set the
 // pace, and 128-token tiles measured slower for QKV and O), k split where
-// the row tiles alone do not fill the pairs.
-GemmPlan gemm_plan(Engine *e, int N, int K, int T) {
+// the row tiles alone do not fill the pairs.  `narrow_tile` (0: all tokens)
+// caps the token tile of the split projections.
+GemmPlan gemm_plan(Engine *e, int N, int K, int T, bool splittable = true) {
   GemmPlan p;
   p.ttile = T <= 128 ? 128 : T <= 256 ? 256 : 512;
+  if (splittable && e->prefill->narrow_tile > 0) p.ttile = std::min(p.ttile, e->prefill->narrow_tile);
   p.ttiles = (T + p.ttile - 1) / p.ttile;
-  p.nsplit = gemm_splits(e, (N + tcgemm::kRows - 1) / tcgemm::kRows * p.ttiles, K / tcgemm::kKChunk);
+  p.nsplit = splittable ? gemm_splits(e, (N + tcgemm::kRows - 1) / tcgemm::kRows * p.ttiles, K / tcgemm::kKChunk) : 1;
+  if (splittable && e->prefill->force_split > 0) p.nsplit = std::min(e->prefill->force_split, prefill::kMaxSplits);
   return p;
 }
 
@@ -886,6 +891,11 @@ int32_t prefill_prepare(Engine *e) {
   auto *ps = new PrefillState();
   e->prefill = ps;
   if (const char *env = std::getenv("CRUISE_PREFILL_PDL")) ps->chain = std::atoi(env) != 0;
+  if (const char *env = std::getenv("CRUISE_PREFILL_TTILE")) {
+    const int v = std::atoi(env);
+    ps->narrow_tile = v == 128 || v == 256 || v == 512 ? v : 0;
+  }
+  if (const char *env = std::getenv("CRUISE_PREFILL_SPLIT")) ps->force_split = std::max(0, std::atoi(env));
   if (tensor_map_encoder() == nullptr) {
     e->last_error = "prefill: the driver has no cuTensorMapEncodeTiled";
     return -2;
@@ -1002,7 +1012,10 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
   bool gemm_ok = true;
   if (T > 0) {
     const GemmPlan pq = gemm_plan(e, m.Nqkv, H, T), po = gemm_plan(e, H, m.Hq, T);
-    const GemmPlan pg = gemm_plan(e, 2 * I, H, T), pd = gemm_plan(e, H, m.I_pad, T);
+    const GemmPlan pg = gemm_plan(e, 2 * I, H, T, false), pd = gemm_plan(e, H, m.I_pad, T);
+    // qkv_rope_store: one unit (a rotation pair of q or k elements, or two v elements) per thread
+    const unsigned rope_rows = static_cast<unsigned>(((m.nq + m.nkv) * (m.d / 4) + m.nkv * m.d / 2 + 255) / 256);
+    const unsigned parts_threads = static_cast<unsigned>(prefill::parts_norm_threads(H));
     err = cudaMemsetAsync(ps->error, 0, 4, e->stream);
     if (err != cudaSuccess) return set_err(e, err, "prefill error word");
     prefill::embed_rows<<<T, 128, 0, e->stream>>>(e->embed, ps->tok, ps->h, H);
@@ -1011,8 +1024,8 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       // x holds rms_norm(h) * w_in of this layer
       const LayerWeights &lw = e->layers[l];
       gemm_ok &= prefill_gemm(e, lw.qkv_w, m.Nqkv, H, ps->x, T, H, 0, pq, nullptr);
-      chain_launch(e, T, 256, 0, prefill::qkv_rope_store, ps->acc, pq.nsplit, T, lw.qkv_b, e->rope_cos, e->rope_sin,
-                   ps->row, ps->pos, ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
+      chain_launch(e, dim3(T, rope_rows), 256, 0, prefill::qkv_rope_store, ps->acc, pq.nsplit, T, lw.qkv_b,
+                   e->rope_cos, e->rope_sin, ps->row, ps->pos, ps->q, payload, l, m.L, m.nq, m.nkv, m.d, m.bs);
       // the last layer's K/V are its only output the payload holds: its
       // attention, O projection and MLP would feed no later layer
       if (l == m.L - 1) break;
@@ -1024,15 +1037,13 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
                      m.eps);
       } else {
         gemm_ok &= prefill_gemm(e, lw.o_w, H, m.Hq, ps->attn, T, m.Hq, 0, po, nullptr);
-        chain_launch(e, T, prefill::kNormThreads, 0, prefill::residual_rms_norm_parts, ps->acc, po.nsplit, T, ps->h,
+        chain_launch(e, T, parts_threads, 0, prefill::residual_rms_norm_parts, ps->acc, po.nsplit, T, ps->h,
                      lw.w_post, ps->x, H, m.eps);
       }
-      // gate/up with the SwiGLU in its epilogue: the activation [T][I]
-      GemmPlan pg1 = pg;
-      pg1.nsplit = 1;
-      gemm_ok &= prefill_gemm(e, lw.gu_w, 2 * I, H, ps->x, T, H, 1, pg1, ps->act);
+      // gate/up with the SwiGLU in its epilogue (needs whole sums: no k split): the activation [T][I]
+      gemm_ok &= prefill_gemm(e, lw.gu_w, 2 * I, H, ps->x, T, H, 1, pg, ps->act);
       gemm_ok &= prefill_gemm(e, lw.down_w, H, m.I_pad, ps->act, T, I, 0, pd, nullptr);
-      chain_launch(e, T, prefill::kNormThreads, 0, prefill::residual_rms_norm_parts, ps->acc, pd.nsplit, T, ps->h,
+      chain_launch(e, T, parts_threads, 0, prefill::residual_rms_norm_parts, ps->acc, pd.nsplit, T, ps->h,
                    e->layers[l + 1].w_in, ps->x, H, m.eps);
     }
   }

@@ -170,67 +170,86 @@ __global__ void __launch_bounds__(kNormThreads) residual_rms_norm(const bf16 *y,
 // The same residual update and norm from the projection's fp32 k-range
 // partial sums [split][T][H] (tensor-core GEMM): y = bf16(sum of the splits in
 // order) is the decoder's materialize(mm_t(x, W)), then h = bf16(h + y) and
-// x = the next rms_norm, as above.
-__global__ void __launch_bounds__(kNormThreads) residual_rms_norm_parts(const float *parts, int nsplit, int T,
-                                                                         bf16 *h, const bf16 *w, bf16 *x, int H,
-                                                                         float eps) {
+// x = the next rms_norm, as above.  One CTA per token of H / 16 threads (two
+// 8-element chunks each, so that 4 CTAs fit an SM and all tokens run in one
+// wave); each round loads one split of both chunks.
+constexpr int kPartsChunks = 2;
+
+__host__ __device__ inline int parts_norm_threads(int H) { return ((H / 8 + kPartsChunks - 1) / kPartsChunks + 31) / 32 * 32; }
+
+__global__ void __launch_bounds__(1024) residual_rms_norm_parts(const float *parts, int nsplit, int T, bf16 *h,
+                                                                const bf16 *w, bf16 *x, int H, float eps) {
   chain_enter();
   __shared__ float scratch[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * H;
   const int64_t split_stride = static_cast<int64_t>(T) * H;
   const int chunks = H >> 3;
-  float hv[kNormChunks][8];
+  float acc[kPartsChunks][8];
+  uint4 hraw[kPartsChunks];
+#pragma unroll
+  for (int j = 0; j < kPartsChunks; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
+    if (c < chunks) {
+      hraw[j] = *reinterpret_cast<const uint4 *>(h + base + c * 8);
+      const float4 *p0 = reinterpret_cast<const float4 *>(parts + base + c * 8);
+      const float4 a = p0[0], b2 = p0[1];
+      acc[j][0] = a.x; acc[j][1] = a.y; acc[j][2] = a.z; acc[j][3] = a.w;
+      acc[j][4] = b2.x; acc[j][5] = b2.y; acc[j][6] = b2.z; acc[j][7] = b2.w;
+    }
+  }
+  for (int k = 1; k < nsplit; ++k) {
+    float4 lo[kPartsChunks], hi[kPartsChunks];
+#pragma unroll
+    for (int j = 0; j < kPartsChunks; ++j) {
+      const int c = threadIdx.x + j * blockDim.x;
+      if (c < chunks) {
+        const float4 *pk = reinterpret_cast<const float4 *>(parts + k * split_stride + base + c * 8);
+        lo[j] = pk[0];
+        hi[j] = pk[1];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPartsChunks; ++j) {
+      const int c = threadIdx.x + j * blockDim.x;
+      if (c < chunks) {
+        acc[j][0] = __fadd_rn(acc[j][0], lo[j].x); acc[j][1] = __fadd_rn(acc[j][1], lo[j].y);
+        acc[j][2] = __fadd_rn(acc[j][2], lo[j].z); acc[j][3] = __fadd_rn(acc[j][3], lo[j].w);
+        acc[j][4] = __fadd_rn(acc[j][4], hi[j].x); acc[j][5] = __fadd_rn(acc[j][5], hi[j].y);
+        acc[j][6] = __fadd_rn(acc[j][6], hi[j].z); acc[j][7] = __fadd_rn(acc[j][7], hi[j].w);
+      }
+    }
+  }
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kNormChunks; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+  for (int j = 0; j < kPartsChunks; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
     if (c < chunks) {
-      float prev[8], y[8];
-      const uint4 hraw = *reinterpret_cast<const uint4 *>(h + base + c * 8);
-      // every split's loads in flight before the ordered sum
-      float4 pl[kMaxSplits], ph[kMaxSplits];
-#pragma unroll
-      for (int k = 0; k < kMaxSplits; ++k)
-        if (k < nsplit) {
-          const float4 *pk = reinterpret_cast<const float4 *>(parts + k * split_stride + base + c * 8);
-          pl[k] = pk[0];
-          ph[k] = pk[1];
-        }
-      unpack8(hraw, prev);
-      float4 lo = pl[0], hi = ph[0];
-#pragma unroll
-      for (int k = 1; k < kMaxSplits; ++k)
-        if (k < nsplit) {
-          const float4 a = pl[k], b2 = ph[k];
-          lo.x = __fadd_rn(lo.x, a.x); lo.y = __fadd_rn(lo.y, a.y); lo.z = __fadd_rn(lo.z, a.z); lo.w = __fadd_rn(lo.w, a.w);
-          hi.x = __fadd_rn(hi.x, b2.x); hi.y = __fadd_rn(hi.y, b2.y); hi.z = __fadd_rn(hi.z, b2.z); hi.w = __fadd_rn(hi.w, b2.w);
-        }
-      y[0] = r(lo.x); y[1] = r(lo.y); y[2] = r(lo.z); y[3] = r(lo.w);
-      y[4] = r(hi.x); y[5] = r(hi.y); y[6] = r(hi.z); y[7] = r(hi.w);
+      float prev[8];
+      unpack8(hraw[j], prev);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        hv[j][k] = r(__fadd_rn(prev[k], y[k]));
-        ss = __fadd_rn(ss, __fmul_rn(hv[j][k], hv[j][k]));
+        acc[j][k] = r(__fadd_rn(prev[k], r(acc[j][k])));   // h + bf16(y), rounded
+        ss = __fadd_rn(ss, __fmul_rn(acc[j][k], acc[j][k]));
       }
-      *reinterpret_cast<uint4 *>(h + base + c * 8) = pack8(hv[j]);
+      *reinterpret_cast<uint4 *>(h + base + c * 8) = pack8(acc[j]);
     }
   }
   const float total = block_sum(ss, scratch);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps)));
 #pragma unroll
-  for (int j = 0; j < kNormChunks; ++j) {
-    const int c = threadIdx.x + j * kNormThreads;
+  for (int j = 0; j < kPartsChunks; ++j) {
+    const int c = threadIdx.x + j * blockDim.x;
     if (c < chunks) {
       float wv[8], out[8];
       unpack8(*reinterpret_cast<const uint4 *>(w + c * 8), wv);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) out[k] = __fmul_rn(r(__fmul_rn(hv[j][k], inv)), wv[k]);
+      for (int k = 0; k < 8; ++k) out[k] = __fmul_rn(r(__fmul_rn(acc[j][k], inv)), wv[k]);
       *reinterpret_cast<uint4 *>(x + base + c * 8) = pack8(out);
     }
   }
 }
 
-// QKV epilogue, one CTA per token: q, k, v = bf16(acc + bias) (F.linear: fp32
+// QKV epilogue, a row of CTAs per token (one unit per thread): q, k, v = bf16(acc + bias) (F.linear: fp32
 // sum plus bias, one rounding), rope on q and k with the token's position
 // (q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16), q to
 // `q_out` [T][Hq], k and v into the payload at (row, position).  A thread
@@ -274,14 +293,15 @@ __global__ void qkv_rope_store(const float *acc, int nsplit, int T, const bf16 *
   const int64_t slot_off = (static_cast<int64_t>(layer) * kBatch + row) * block_elems + static_cast<int64_t>(pos) * kvw;
   const int64_t v_base = static_cast<int64_t>(L) * kBatch * block_elems;   // V half of the payload
   const int rope_units = (nq + nkv) * quarter, units = rope_units + kvw / 2;
-  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+  const int u = blockIdx.y * blockDim.x + threadIdx.x;   // one unit per thread
+  if (u < units) {
     if (u >= rope_units) {   // v: two elements
       const int n = Hq + kvw + 2 * (u - rope_units);
       const float2 s2 = split_sum2(acc, split_stride, nsplit, a + n);
       const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162 *>(bias + n);
       *reinterpret_cast<uint32_t *>(payload + v_base + slot_off + (n - Hq - kvw)) =
           bf2_bits(__fadd_rn(s2.x, __low2float(b2)), __fadd_rn(s2.y, __high2float(b2)));
-      continue;
+      return;
     }
     const int head = u / quarter, i = 2 * (u - head * quarter);   // q heads, then k heads
     const int n_lo = head * d + i, n_hi = n_lo + half;

@@ -77,7 +77,8 @@ def test_tiny_prefill(cuda_ok, seed, rows):
     _compare(TINY, ORACLE_TINY, weights, sc)
 
 
-def test_qwen7b_geometry_prefill_long_prompts(cuda_ok):
+@pytest.fixture(scope="module")
+def qwen7b_2l():
     from cruise_b200.engine import EpochEngine
     from cruise_b200.model_config import QWEN25_7B
 
@@ -89,6 +90,23 @@ def test_qwen7b_geometry_prefill_long_prompts(cuda_ok):
     engine.init_synthetic(0)
     weights = {name: engine.get_weight(name, shape) for name, shape in tensor_shapes(ocfg).items()}
     engine.close()
-    sc = make_scenario(vocab=cfg.vocab, seed=3, active_rows=(1, 1, 1, 0), prompt_len=(60, 120), k=4,
+    return cfg, ocfg, weights
+
+
+# The cohort's prompt tokens (all rows, the last token of each excluded) set
+# how the tensor-core GEMMs tile the tokens: up to 128 tokens one 128-token
+# tile, up to 256 one 256-token tile, beyond that two 256-token sub-tiles
+# (the last partly filled), 508 at most (4 rows x 127).
+@pytest.mark.parametrize("seed, rows, prompt_len", [
+    (3, (1, 1, 1, 0), (60, 120)),    # 177..357 tokens
+    (4, (1, 1, 1, 1), (2, 33)),      # at most 128 tokens
+    (5, (1, 0, 1, 1), (45, 86)),     # 132..255 tokens
+    (6, (1, 1, 1, 1), (128, 128)),   # 508 tokens: every row's whole first block
+])
+def test_qwen7b_geometry_prefill(cuda_ok, qwen7b_2l, seed, rows, prompt_len):
+    cfg, ocfg, weights = qwen7b_2l
+    sc = make_scenario(vocab=cfg.vocab, seed=seed, active_rows=rows, prompt_len=prompt_len, k=4,
                        budget=(4, 4), token_high=151643)
+    tokens = sum(len(p) - 1 for p in sc.prompts if p)
+    assert prompt_len[0] * sum(rows) - sum(rows) <= tokens <= (prompt_len[1] - 1) * sum(rows)
     _compare(cfg, ocfg, weights, sc)
