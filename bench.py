@@ -235,12 +235,16 @@ def gather_kv_shards(engine, key, value):
     return full_k, full_v
 
 
-def setup_cohort(engine, cfg, seed: int, k: int, prompt_max: int = 5, want_logits: bool = False):
-    """Device prefill of a seeded B=4 cohort, then the one-shot import epoch."""
+def setup_cohort(engine, cfg, seed: int, k: int, prompt_max: int = 5, want_logits: bool = False,
+                 generation_offset: int = 0):
+    """Device prefill of a seeded B=4 cohort, then the one-shot import epoch.
+    `generation_offset` moves the rows' generations, so a second cohort can
+    take over rows that an earlier one left behind."""
     from scenario import decode_inputs, import_payload, make_scenario, prefill_epochs
 
     sc = make_scenario(vocab=cfg.vocab, seed=seed, active_rows=(1, 1, 1, 1), prompt_len=(2, prompt_max),
                        budget=(2, 8), k=k, eos=cfg.configured_eos, token_high=min(151643, cfg.vocab - 1))
+    sc.generations = [g + generation_offset for g in sc.generations]
     for inputs in prefill_epochs(sc, cfg.block_size, cfg.vocab):
         out = engine.run(**inputs)
         assert out.status == 0, f"prefill epoch status {out.status}"
@@ -373,6 +377,35 @@ def timed_epochs(cohort, cfg, steps: int, device: int, world: int, tp: bool, bar
     barrier()
     return {"tokens": tokens, "dev_s": sum(device_us) / 1e6, "wall": wall, "bytes": step_bytes_total,
             "model_calls": model_calls, "clocks": clocks.summary()}
+
+
+BOX_SCALE_PROMPT_MAX = 120
+
+
+def box_scale_epochs(engine, cfg, seed: int, device: int, world: int, tp: bool, barrier, epochs: int = 3) -> dict:
+    """configs[4], the box-scale variant: a fresh B=4 cohort (prompts of 2-120
+    tokens, new generations on the engine's rows) decoded in K=8 greedy epochs,
+    one warm-up epoch then `epochs` timed ones; the same timing as the
+    headline (device time of each epoch kernel, max over ranks)."""
+    sc, first = setup_cohort(engine, cfg, seed=seed, k=8, prompt_max=BOX_SCALE_PROMPT_MAX, generation_offset=100)
+    cohort = Cohort(engine, cfg, sc, first)
+    if cohort.room() < 8 * (epochs + 1):
+        raise RuntimeError("box-scale cohort: not enough KV capacity")
+    cohort.step()
+    return timed_epochs(cohort, cfg, epochs, device, world, tp, barrier)
+
+
+def box_scale_summary(r: dict, device, world: int, tp: bool, peak: float) -> dict:
+    """Whole-box decode tok/s, µs per decode step and HBM fraction of one
+    box-scale run (tokens counted once for a tensor-parallel group, summed
+    over independent cohorts)."""
+    t_max, tok, wall = reduce_over_ranks(r["dev_s"], r["tokens"], r["wall"], device=device if world > 1 else None,
+                                         sum_tokens=not tp)
+    calls = max(r["model_calls"], 1)
+    gbs = r["bytes"] / t_max / 1e9
+    return {"value": round(tok / t_max, 2), "unit": "tok/s", "us_per_decode_step": round(t_max * 1e6 / calls, 2),
+            "e2e_value": round(tok / wall, 2), "epochs": 3,
+            "roofline_frac": round(gbs / (peak * (world if tp else 1)), 4)}
 
 
 def host_loop_comparison(engine, cohort, cfg, ks=(2, 4, 8), reps: int = 3) -> dict | None:
@@ -570,6 +603,17 @@ def run_gpu(args) -> None:
         if tp:
             line["tp_check"] = tp_token_check([first_tp, *tp_warm], [first_single, *single_warm])
             line["dp"] = dp
+    # configs[4] on the same GPUs: K=8, prompts of 2-120 tokens; a
+    # tensor-parallel group decodes one cohort, the single-GPU engines one
+    # cohort each (the data-parallel layout).  New cohorts take over the
+    # engines' rows, so this runs after everything that continues the
+    # headline cohorts.
+    box_scale = not (args.layers or args.vocab or args.no_box_scale)
+    box = {"workload": "configs[4]: B=4 per cohort, K=8 greedy epochs after prompts of 2-%d tokens"
+                       % BOX_SCALE_PROMPT_MAX}
+    if tp and box_scale:
+        r = box_scale_epochs(group, cfg, 3000, device, world, True, barrier)
+        box["tp"] = box_scale_summary(r, device, world, True, hbm_peak()[0])
     if tp:
         group.close()
     if rank == 0 and world == 1 and args.k != 8 and not (args.layers or args.vocab) and single_cohort.room() >= 40:
@@ -583,6 +627,11 @@ def run_gpu(args) -> None:
                       "roofline_frac": round(gbs8 / peak, 4), "e2e_value": round(r8["tokens"] / r8["wall"], 2)}
     if rank == 0 and world == 1 and not args.no_host_loop and not (args.layers or args.vocab):
         line["host_loop"] = host_loop_comparison(single, single_cohort, cfg)
+    if box_scale:
+        r = box_scale_epochs(single, cfg, 3000 + rank, device, world, False, barrier)
+        box["dp" if world > 1 else "single"] = box_scale_summary(r, device, world, False, hbm_peak()[0])
+        if rank == 0:
+            line["box_scale"] = box
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args, first_single)
     if rank == 0:
@@ -927,6 +976,8 @@ def main() -> None:
     parser.add_argument("--k", type=int, default=2, choices=(1, 2, 4, 8))
     parser.add_argument("--impl", default="cruise", choices=("cruise", "reference"))
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-box-scale", action="store_true",
+                        help="skip the configs[4] figure (K=8 epochs after prompts of 2-120 tokens)")
     parser.add_argument("--no-host-loop", action="store_true",
                         help="skip the resident-epoch vs host-loop comparison (N=1)")
     parser.add_argument("--trace", action="store_true", help="per-phase timing of one extra epoch (stderr)")

@@ -179,9 +179,17 @@ struct PrefillState {
   bool chain = true;           // kernels launched as programmatic dependents (CRUISE_PREFILL_PDL=0: plain)
   int narrow_tile = 0;         // token tile cap of QKV, O and down (CRUISE_PREFILL_TTILE; 0: all tokens)
   int force_split = 0;         // their split count (CRUISE_PREFILL_SPLIT; 0: the cost model's)
+  bool w_evict_first = true;   // GEMM weight copies evict-first in L2 (CRUISE_PREFILL_WHINT=0: no hint)
+  int stage_cap = 0;           // ring depth cap of the GEMM (CRUISE_PREFILL_STAGES; 0: as many as fit)
   bool gemm_attr = false;      // the GEMM's shared-memory limit has been raised
   int gemm_pairs = 0;          // resident CTA pairs of the GEMM (0: not yet asked)
+  // profiling (CRUISE_PREFILL_TRACE=1): %globaltimer marks of the first
+  // kTraceLaunches GEMM launches of a prefill, summarised on stderr
+  uint64_t *trace = nullptr;
+  int trace_calls = 0;
+  int trace_grid[8] = {};
 };
+constexpr int kTraceLaunches = 8;
 
 struct Engine {
   CruiseModelConfig cfg{};
@@ -833,11 +841,19 @@ bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, 
   a.tsub = plan.ttile > tcgemm::kSub ? 2 : 1;
   a.xrows = std::min(plan.ttile / 2, tcgemm::kSub / 2);
   a.stages = std::min<int>(tcgemm::kMaxStages, tcgemm::kRingBytes / tcgemm::stage_bytes(a.tsub, a.xrows));
+  if (ps->stage_cap >= 2) a.stages = std::min(a.stages, ps->stage_cap);
   a.tiles = (N + tcgemm::kRows - 1) / tcgemm::kRows * plan.ttiles * plan.nsplit;
   a.partials = ps->acc;
   a.out = out;
   a.out_stride = mode == 1 ? N / 2 : N;
   a.error = ps->error;
+  a.w_evict_first = ps->w_evict_first ? 1 : 0;
+  a.trace = nullptr;
+  const int pairs_now = gemm_pairs(e);
+  if (ps->trace != nullptr && ps->trace_calls < kTraceLaunches) {
+    ps->trace_grid[ps->trace_calls] = 2 * std::min(a.tiles, pairs_now);
+    a.trace = ps->trace + static_cast<size_t>(ps->trace_calls++) * e->sms * tcgemm::kTraceMarks;
+  }
   CUtensorMap wmap, xmap;
   if (!weight_map(&wmap, W, N, K, a.kc) || !activation_map(&xmap, X, T, x_width, x_width, a.xrows)) {
     e->last_error = "prefill: a GEMM tensor map could not be encoded";
@@ -872,12 +888,50 @@ bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, 
   return true;
 }
 
+// Profiling summary of the traced GEMM launches (stderr), in µs after the
+// moment the launch's predecessor had completed (the earliest "predecessor
+// complete" mark): per launch the CTA medians of entry, first load issued,
+// first stage landed and last MMA committed (leaders), first accumulators
+// ready, epilogue done, and the median and last exit.
+void print_gemm_trace(Engine *e) {
+  PrefillState *ps = e->prefill;
+  const int per = e->sms * tcgemm::kTraceMarks;
+  std::vector<uint64_t> h(static_cast<size_t>(kTraceLaunches) * per);
+  if (copy_sync(e, h.data(), ps->trace, h.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+  static const char *names[kTraceLaunches] = {"qkv", "o", "gate_up", "down", "qkv", "o", "gate_up", "down"};
+  std::fprintf(stderr, "prefill GEMM trace (us after predecessor done): launch grid | entry first_load first_stage "
+                       "last_mma(leaders) first_acc epi_done | exit_median exit_last\n");
+  for (int i = 0; i < ps->trace_calls; ++i) {
+    const uint64_t *t = h.data() + static_cast<size_t>(i) * per;
+    const int grid = ps->trace_grid[i];
+    uint64_t base = UINT64_MAX;
+    for (int c = 0; c < grid; ++c)
+      if (t[c * tcgemm::kTraceMarks + 1] != 0) base = std::min(base, t[c * tcgemm::kTraceMarks + 1]);
+    if (base == UINT64_MAX) continue;
+    auto median = [&](int mark, bool leaders_only, bool last) {
+      std::vector<double> v;
+      for (int c = 0; c < grid; ++c) {
+        if (leaders_only && (c & 1)) continue;
+        const uint64_t x = t[c * tcgemm::kTraceMarks + mark];
+        if (x != 0) v.push_back((static_cast<double>(x) - static_cast<double>(base)) / 1e3);
+      }
+      if (v.empty()) return 0.0;
+      std::sort(v.begin(), v.end());
+      return last ? v.back() : v[v.size() / 2];
+    };
+    std::fprintf(stderr, "  L%d %-8s %4d | %7.2f %7.2f %7.2f %7.2f %7.2f %7.2f | %7.2f %7.2f\n", i / 4, names[i], grid,
+                 median(0, false, false), median(2, false, false), median(3, true, false), median(4, true, false),
+                 median(5, false, false), median(6, false, false), median(7, false, false), median(7, false, true));
+  }
+}
+
 // Frees the prefill buffers, whole or partly built; cudaFree waits for the
 // work queued on them.
 void prefill_release(Engine *e) {
   PrefillState *ps = e->prefill;
   if (ps == nullptr) return;
   cudaFree(ps->work);
+  if (ps->trace != nullptr) cudaFree(ps->trace);
   delete ps;
   e->prefill = nullptr;
 }
@@ -896,6 +950,8 @@ int32_t prefill_prepare(Engine *e) {
     ps->narrow_tile = v == 128 || v == 256 || v == 512 ? v : 0;
   }
   if (const char *env = std::getenv("CRUISE_PREFILL_SPLIT")) ps->force_split = std::max(0, std::atoi(env));
+  if (const char *env = std::getenv("CRUISE_PREFILL_WHINT")) ps->w_evict_first = std::atoi(env) != 0;
+  if (const char *env = std::getenv("CRUISE_PREFILL_STAGES")) ps->stage_cap = std::max(0, std::atoi(env));
   if (tensor_map_encoder() == nullptr) {
     e->last_error = "prefill: the driver has no cuTensorMapEncodeTiled";
     return -2;
@@ -935,6 +991,11 @@ int32_t prefill_prepare(Engine *e) {
   ps->pos = reinterpret_cast<int32_t *>(b + o_pos);
   ps->error = reinterpret_cast<uint32_t *>(b + o_err);
   err = cudaMemsetAsync(ps->work, 0, bytes, e->stream);
+  if (err == cudaSuccess) {
+    const char *env = std::getenv("CRUISE_PREFILL_TRACE");
+    if (env != nullptr && std::atoi(env) != 0)
+      err = cudaMalloc(&ps->trace, sizeof(uint64_t) * kTraceLaunches * e->sms * tcgemm::kTraceMarks);
+  }
   if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
   return set_err(e, err, "prefill preparation");
 }
@@ -1017,6 +1078,10 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
     const unsigned rope_rows = static_cast<unsigned>(((m.nq + m.nkv) * (m.d / 4) + m.nkv * m.d / 2 + 255) / 256);
     const unsigned parts_threads = static_cast<unsigned>(prefill::parts_norm_threads(H));
     err = cudaMemsetAsync(ps->error, 0, 4, e->stream);
+    ps->trace_calls = 0;
+    if (err == cudaSuccess && ps->trace != nullptr)
+      err = cudaMemsetAsync(ps->trace, 0, sizeof(uint64_t) * kTraceLaunches * e->sms * tcgemm::kTraceMarks,
+                            e->stream);
     if (err != cudaSuccess) return set_err(e, err, "prefill error word");
     prefill::embed_rows<<<T, 128, 0, e->stream>>>(e->embed, ps->tok, ps->h, H);
     chain_launch(e, T, 256, 0, prefill::rms_norm_rows, ps->h, e->layers[0].w_in, ps->x, H, m.eps);
@@ -1059,6 +1124,7 @@ int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32
       e->last_error = "prefill: a tensor-core GEMM wait gave up (site " + std::to_string(site) + ")";
       return -2;
     }
+    if (ps->trace != nullptr) print_gemm_trace(e);
   }
   e->payload_ready = true;
   return 0;

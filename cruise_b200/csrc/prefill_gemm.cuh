@@ -95,7 +95,14 @@ struct Args {
   bf16 *out;         // mode 1: the activation [T][out_stride] (out_stride = N / 2); mode 2: [T][out_stride]
   int out_stride;
   uint32_t *error;   // set to the failing site when a wait ran out
+  int w_evict_first; // W copies mark their L2 lines evict-first (W is read once; X and the partials stay)
+  uint64_t *trace;   // profiling: [CTA][kTraceMarks] %globaltimer marks (null: off)
 };
+
+// Trace marks of one CTA: entry, predecessor complete, first load issued,
+// first stage landed (leader), last MMA committed (leader), first
+// accumulators ready (epilogue warp 2), epilogue warp 2 done, exit.
+constexpr int kTraceMarks = 8;
 
 __device__ __forceinline__ uint64_t now_ns() {
   uint64_t t;
@@ -133,6 +140,10 @@ __device__ __forceinline__ bool wait_phase_cluster(uint64_t *bar, uint32_t parit
     if (mbar_try_cluster(bar, parity)) return true;
     if (now_ns() > deadline) return false;
   }
+}
+
+__device__ __forceinline__ void mark(const Args &a, int i) {
+  if (a.trace != nullptr) a.trace[blockIdx.x * kTraceMarks + i] = now_ns();
 }
 
 __device__ __forceinline__ void settle() {
@@ -187,6 +198,21 @@ __device__ __forceinline__ void tma_load_5d_pair(void *dst, const CUtensorMap *m
       "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar_cluster)
       : "memory");
+}
+
+// The same W copy with an L2 eviction-priority policy on its lines.
+__device__ __forceinline__ void tma_load_5d_pair_hint(void *dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                                      int c3, int c4, uint32_t bar_cluster, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar_cluster),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int c0, int c1,
@@ -383,6 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // launched as a dependent of the previous prefill kernel: let the next one
   // begin launching; the set-up below touches nothing the predecessor does
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tid == 0) mark(a, 0);
 
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
@@ -404,37 +431,54 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after_sync();
   const uint32_t tmem = b->tmem_base;
-  // the predecessor's outputs (this GEMM's X) are complete and visible
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the predecessor's outputs (this GEMM's X) are complete and visible; the
+  // producer thread waits inside its role, after its first W copies
+  if (!(warp == 0 && lane == 0)) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 32) mark(a, 1);
 
   if (warp == 0) {
     // ---- producer (both CTAs): chunk c is segment c % segs of k tile c / segs
     if (lane == 0) {
       const int segs = a.kc / kKChunk;
+      const uint64_t policy = l2_policy_evict_first();
+      prefetch_tensormap(&wmap);
+      prefetch_tensormap(&xmap);
       int issued = 0;
       bool ok = true;
-      for (int t = pair; ok && t < a.tiles; t += npairs) {
-        const Tile x = tile_of(a, t);
+      auto load_w = [&](uint8_t *sa, int c, int mt, uint32_t bar) {
+        // W: (element, segment, row in tile, k tile, row group); 8 row groups = this CTA's 128 rows
+        const int rg = mt * (kRows / 16) + static_cast<int>(rank) * 8;
+        if (a.w_evict_first)
+          tma_load_5d_pair_hint(sa, &wmap, 0, c % segs, 0, c / segs, rg, bar, policy);
+        else
+          tma_load_5d_pair(sa, &wmap, 0, c % segs, 0, c / segs, rg, bar);
+      };
+      auto nsub_of = [&](const Tile &x) {
         int nsub = 0;   // sub-tiles with tokens
         for (int s = 0; s < a.tsub; ++s) nsub += sub_tokens(a, x.tq, s) > 0 ? 1 : 0;
+        return nsub;
+      };
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int t = pair; ok && t < a.tiles; t += npairs) {
+        const Tile x = tile_of(a, t);
+        const int nsub = nsub_of(x);
         for (int c = x.c0; c < x.c1; ++c) {
           const int st = issued % S;
           const uint32_t round = static_cast<uint32_t>(issued / S);
+          uint8_t *sa = ring + static_cast<size_t>(st) * sbytes;
+          const uint32_t bar = peer_addr(&b->full[st], 0);
           if (aborted(b) || !wait_phase(&b->empty[st], (round & 1u) ^ 1u)) {
             if (!aborted(b)) fail(a, b, rank, 1u);
             ok = false;
             break;
           }
-          uint8_t *sa = ring + static_cast<size_t>(st) * sbytes;
           if (leader) mbar_arrive_expect_tx(&b->full[st], 2 * (kWBytes + static_cast<uint32_t>(nsub) * xbytes));
-          const uint32_t bar = peer_addr(&b->full[st], 0);
-          // W: (element, segment, row in tile, k tile, row group); 8 row groups = this CTA's 128 rows
-          tma_load_5d_pair(sa, &wmap, 0, c % segs, 0, c / segs, x.mt * (kRows / 16) + static_cast<int>(rank) * 8,
-                           bar);
+          load_w(sa, c, x.mt, bar);
           // X: (k, token); of each sub-tile, this CTA's N / 2 tokens (rows past T read as zeros)
           for (int s = 0; s < nsub; ++s)
             tma_load_2d_pair(sa + kWBytes + s * xbytes, &xmap, c * kKChunk,
                              sub_first(a, x.tq, s) + static_cast<int>(rank) * (sub_n(a, x.tq, s) / 2), bar);
+          if (issued == 0) mark(a, 2);
           ++issued;
         }
       }
@@ -474,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after_sync();
+          if (used == 0) mark(a, 3);
           const uint32_t sw = smem_u32(ring + static_cast<size_t>(st) * sbytes);
 #pragma unroll
           for (int j = 0; j < kKChunk / 16; ++j) {
@@ -488,6 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         commit_pair(&b->acc_full);   // with no k chunks: completes at once, the epilogue writes zeros
       }
+      mark(a, 4);
       // every MMA this thread issued has completed once `drain` fires
       commit_local(&b->drain);
       wait_phase(&b->drain, 0);
@@ -509,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after_sync();
+      if (local == 0 && warp == kEpilogueWarp0 && lane == 0) mark(a, 5);
       const bool zero = x.c1 <= x.c0;
       const int row = x.mt * kRows + static_cast<int>(rank) * kM + quad * 32 + lane;   // this thread's W row
       if (a.mode != 1) {
@@ -613,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (warp == kEpilogueWarp0 && lane == 0) mark(a, 6);
   // after a failure, copies and commits still in flight get time to land
   // before the pair meets for the last time and frees its tensor memory
   if (aborted(b)) settle();
@@ -620,6 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after_sync();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (tid == 0) mark(a, 7);
 }
 
 }  // namespace tcgemm
