@@ -181,6 +181,7 @@ struct PrefillState {
   int force_split = 0;         // their split count (CRUISE_PREFILL_SPLIT; 0: the cost model's)
   bool w_evict_first = true;   // GEMM weight copies evict-first in L2 (CRUISE_PREFILL_WHINT=0: no hint)
   int stage_cap = 0;           // ring depth cap of the GEMM (CRUISE_PREFILL_STAGES; 0: as many as fit)
+  bool p_evict_last = true;    // partial sums stored evict-last in L2 (CRUISE_PREFILL_PHINT=0: no hint)
   bool gemm_attr = false;      // the GEMM's shared-memory limit has been raised
   int gemm_pairs = 0;          // resident CTA pairs of the GEMM (0: not yet asked)
   // profiling (CRUISE_PREFILL_TRACE=1): %globaltimer marks of the first
@@ -732,6 +733,21 @@ bool activation_map(CUtensorMap *map, const bf16 *X, int T, int width, int pitch
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The GEMM's fp32 partial sums [split][T][N] as a 3-D tensor (row, token,
+// split) for its tensor stores: boxes of 32 rows x 8 tokens.
+bool partial_map(CUtensorMap *map, float *P, int N, int T, int nsplit) {
+  const PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(T),
+                              static_cast<cuuint64_t>(nsplit)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N) * 4, static_cast<cuuint64_t>(N) * T * 4};
+  const cuuint32_t box[3] = {32, static_cast<cuuint32_t>(tcgemm::kStoreTokens), 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, P, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // CTA pairs of the GEMM that can be resident at once (one CTA per SM).  The
 // first call raises the kernel's shared-memory limit.
 int gemm_pairs(Engine *e) {
@@ -848,14 +864,18 @@ bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, 
   a.out_stride = mode == 1 ? N / 2 : N;
   a.error = ps->error;
   a.w_evict_first = ps->w_evict_first ? 1 : 0;
+  a.p_evict_last = ps->p_evict_last ? 1 : 0;
   a.trace = nullptr;
   const int pairs_now = gemm_pairs(e);
   if (ps->trace != nullptr && ps->trace_calls < kTraceLaunches) {
     ps->trace_grid[ps->trace_calls] = 2 * std::min(a.tiles, pairs_now);
     a.trace = ps->trace + static_cast<size_t>(ps->trace_calls++) * e->sms * tcgemm::kTraceMarks;
   }
-  CUtensorMap wmap, xmap;
-  if (!weight_map(&wmap, W, N, K, a.kc) || !activation_map(&xmap, X, T, x_width, x_width, a.xrows)) {
+  CUtensorMap wmap, xmap, pmap;
+  // modes 1 and 2 store no partial sums: a small placeholder map
+  const bool parts = mode == 0;
+  if (!weight_map(&wmap, W, N, K, a.kc) || !activation_map(&xmap, X, T, x_width, x_width, a.xrows) ||
+      !partial_map(&pmap, ps->acc, parts ? N : 32, parts ? T : 8, parts ? plan.nsplit : 1)) {
     e->last_error = "prefill: a GEMM tensor map could not be encoded";
     return false;
   }
@@ -879,7 +899,7 @@ bool prefill_gemm(Engine *e, const bf16 *W, int N, int K, const bf16 *X, int T, 
   cfg.stream = e->stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, tcgemm::gemm_kernel, wmap, xmap, a);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, tcgemm::gemm_kernel, wmap, xmap, pmap, a);
   if (err != cudaSuccess) {
     e->last_error = std::string("prefill: GEMM launch: ") + cudaGetErrorString(err);
     cudaGetLastError();
@@ -952,6 +972,7 @@ int32_t prefill_prepare(Engine *e) {
   if (const char *env = std::getenv("CRUISE_PREFILL_SPLIT")) ps->force_split = std::max(0, std::atoi(env));
   if (const char *env = std::getenv("CRUISE_PREFILL_WHINT")) ps->w_evict_first = std::atoi(env) != 0;
   if (const char *env = std::getenv("CRUISE_PREFILL_STAGES")) ps->stage_cap = std::max(0, std::atoi(env));
+  if (const char *env = std::getenv("CRUISE_PREFILL_PHINT")) ps->p_evict_last = std::atoi(env) != 0;
   if (tensor_map_encoder() == nullptr) {
     e->last_error = "prefill: the driver has no cuTensorMapEncodeTiled";
     return -2;

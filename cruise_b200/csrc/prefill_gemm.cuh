@@ -96,6 +96,7 @@ struct Args {
   int out_stride;
   uint32_t *error;   // set to the failing site when a wait ran out
   int w_evict_first; // W copies mark their L2 lines evict-first (W is read once; X and the partials stay)
+  int p_evict_last;  // partial-sum stores mark their lines evict-last (the next kernel reads them)
   uint64_t *trace;   // profiling: [CTA][kTraceMarks] %globaltimer marks (null: off)
 };
 
@@ -347,7 +348,46 @@ struct Bars {
 constexpr int kStashWords = 16;
 constexpr size_t kStashBytes = static_cast<size_t>(kStashWords) * kEpilogueWarps * 32 * 4;
 
-__host__ __device__ inline size_t smem_bytes() { return 1024 + kRingBytes + sizeof(Bars) + kStashBytes; }
+// The barriers get a 1 KB slot after the ring, so the stash starts 1 KB
+// aligned (the fp32 epilogue's tensor stores read it).
+constexpr size_t kBarsSlot = 1024;
+static_assert(sizeof(Bars) <= kBarsSlot, "barrier slot");
+__host__ __device__ inline size_t smem_bytes() { return 1024 + kRingBytes + kBarsSlot + kStashBytes; }
+
+// The fp32 epilogue stages 8 tokens x 32 W rows (1 KB) per tensor store, two
+// such buffers per epilogue warp in its 2 KB of the stash.
+constexpr int kStoreTokens = 8;
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Tensor store of a 32-row x 8-token fp32 box from shared memory into the
+// partial sums [split][T][N] (coordinates: row, token, split; the parts of
+// the box past N or T are not written).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+               : "memory");
+}
+
+// The same store with an L2 eviction-priority policy on the written lines.
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap *map, const void *src, int c0, int c1, int c2,
+                                                  uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2, %3}], [%4], %5;" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src)), "l"(policy)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// At most one of this thread's bulk stores still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// All of this thread's bulk stores complete (written to global memory).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Shared-memory bytes of one stage per CTA: its W rows and its share of each sub-tile's tokens.
 __host__ __device__ inline uint32_t stage_bytes(int tsub, int xrows) {
@@ -395,11 +435,12 @@ __device__ __forceinline__ void fail(const Args &a, Bars *b, uint32_t rank, uint
 __device__ __forceinline__ bool aborted(Bars *b) { return *reinterpret_cast<volatile int *>(&b->abort) != 0; }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Args a) {
+    gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                const __grid_constant__ CUtensorMap pmap, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars *b = reinterpret_cast<Bars *>(ring + kRingBytes);
-  uint32_t *stash = reinterpret_cast<uint32_t *>(b + 1);
+  uint32_t *stash = reinterpret_cast<uint32_t *>(ring + kRingBytes + kBarsSlot);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
@@ -558,7 +599,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (local == 0 && warp == kEpilogueWarp0 && lane == 0) mark(a, 5);
       const bool zero = x.c1 <= x.c0;
       const int row = x.mt * kRows + static_cast<int>(rank) * kM + quad * 32 + lane;   // this thread's W row
-      if (a.mode != 1) {
+      if (a.mode == 0) {
+        // fp32 partial sums through tensor stores: the warp writes 8 tokens
+        // of its 32 rows into one of its two 1 KB stash buffers, lane 0
+        // stores the box; the other buffer's store may still be reading
+        float *slice = reinterpret_cast<float *>(stash) + (warp - kEpilogueWarp0) * (2 * kStoreTokens * 32);
+        const int row0 = x.mt * kRows + static_cast<int>(rank) * kM + quad * 32;
+        const uint64_t keep = l2_policy_evict_last();
+        int stores = 0;
+        for (int s = 0; s < a.tsub; ++s) {
+          const int ntok = sub_tokens(a, x.tq, s), first = sub_first(a, x.tq, s);
+          const uint32_t acc = lane_addr + static_cast<uint32_t>(s) * kAccCols;
+          for (int t0 = 32 * group; t0 < ntok; t0 += 32 * kEpilogueGroups) {
+            float v[32];
+            if (!zero) {
+              tmem_ld32(acc + static_cast<uint32_t>(t0), v);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 32; ++q) v[q] = 0.f;
+            }
+#pragma unroll
+            for (int h = 0; h < 32 / kStoreTokens; ++h) {
+              if (t0 + h * kStoreTokens < ntok) {
+                float *buf = slice + (stores & 1) * (kStoreTokens * 32);
+                if (lane == 0 && stores >= 2) bulk_wait_read1();
+                __syncwarp();
+#pragma unroll
+                for (int q = 0; q < kStoreTokens; ++q) buf[q * 32 + lane] = v[h * kStoreTokens + q];
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {   // boxes reaching past N or T are clipped; one wholly past N is skipped
+                  if (row0 < a.N) {
+                    if (a.p_evict_last)
+                      tma_store_3d_hint(&pmap, buf, row0, first + t0 + h * kStoreTokens, x.split, keep);
+                    else
+                      tma_store_3d(&pmap, buf, row0, first + t0 + h * kStoreTokens, x.split);
+                  }
+                  bulk_commit();
+                }
+                ++stores;
+              }
+            }
+          }
+        }
+        // the stores are complete before the kernel (and the caller's next
+        // kernel) can end; the stash buffers are free for the next tile
+        if (lane == 0) bulk_wait_all();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(leader_empty);
+      } else if (a.mode == 2) {
         for (int s = 0; s < a.tsub; ++s) {
           const int ntok = sub_tokens(a, x.tq, s), first = sub_first(a, x.tq, s);
           const uint32_t acc = lane_addr + static_cast<uint32_t>(s) * kAccCols;
@@ -571,17 +661,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int q = 0; q < 32; ++q) v[q] = 0.f;
             }
             if (row < a.N) {
-              if (a.mode == 0) {
-                float *dst = a.partials + (static_cast<int64_t>(x.split) * a.T + first + t0) * a.N + row;
+              bf16 *dst = a.out + static_cast<int64_t>(first + t0) * a.out_stride + row;
 #pragma unroll
-                for (int q = 0; q < 32; ++q)
-                  if (t0 + q < ntok) dst[static_cast<int64_t>(q) * a.N] = v[q];
-              } else {
-                bf16 *dst = a.out + static_cast<int64_t>(first + t0) * a.out_stride + row;
-#pragma unroll
-                for (int q = 0; q < 32; ++q)
-                  if (t0 + q < ntok) dst[static_cast<int64_t>(q) * a.out_stride] = __float2bfloat16_rn(v[q]);
-              }
+              for (int q = 0; q < 32; ++q)
+                if (t0 + q < ntok) dst[static_cast<int64_t>(q) * a.out_stride] = __float2bfloat16_rn(v[q]);
             }
           }
         }
