@@ -938,11 +938,12 @@ def run_prefill(args) -> None:
     tokens = sum(len(p) - 1 for p in sc.prompts)
     engine.prefill(sc.prompts)   # first call allocates the activation buffers
     batched = []
-    for _ in range(max(3, args.steps)):
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        engine.prefill(sc.prompts)
-        batched.append((time.perf_counter() - t0) * 1e3)
+    with ClockSampler(0) as clocks:
+        for _ in range(max(3, args.steps)):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            engine.prefill(sc.prompts)
+            batched.append((time.perf_counter() - t0) * 1e3)
     out = engine.run(**decode_inputs(sc, cfg.block_size, importing=True))
     assert out.status == 0, out.status
     # the same prompts again as teacher-forced epochs (all four rows together,
@@ -965,6 +966,7 @@ def run_prefill(args) -> None:
         "teacher_forced_epochs": epochs, "teacher_forced_device_ms": round(forced_dev, 3),
         "teacher_forced_wall_ms": round(forced_wall, 3), "speedup_vs_teacher_forced": round(forced_wall / ms, 1),
         "batched_includes": "host token upload, all layers (tcgen05 GEMMs + prefill kernels), sync",
+        "clocks": clocks.summary(),
     }), flush=True)
 
 

@@ -98,6 +98,30 @@ def test_prefill_then_decode_epoch(cuda_ok, tiny_weights, seed):
     engine.close()
 
 
+def test_configuration1_against_the_fp32_oracle(cuda_ok, tiny_weights):
+    """configs[0] names torch fp32 for the tiny model.  The engine computes in
+    bf16 (fp32 accumulation); against the fp32 oracle on the same seeded
+    weights it stays within the parity rule: tokens, statuses and control
+    words equal (near-ties excepted), logits and KV within 2e-2 per vector."""
+    sc = make_scenario(vocab=ORACLE_TINY.vocab, seed=0)
+    engine = new_engine(tiny_weights)
+    oracle = OracleEpochController(OracleDecoder(ORACLE_TINY, tiny_weights, torch.float32))
+    for inputs in prefill_epochs(sc, ORACLE_TINY.block_size, ORACLE_TINY.vocab):
+        out = engine.run(**inputs)
+        history, control = oracle.run(**inputs)
+        assert out.status == int(control[3]) == 0
+        np.testing.assert_array_equal(out.history, history)
+    inputs = decode_inputs(sc, ORACLE_TINY.block_size)
+    trace = EpochTrace()
+    out = engine.run(**inputs, want_logits=True)
+    history, control = oracle.run(**inputs, trace=trace)
+    assert out.status == int(control[3]) == 0
+    key, value = engine.read_kv()
+    check_epoch(out, history, control, trace, inputs, kv=(key, value, oracle.key, oracle.value),
+                block_size=ORACLE_TINY.block_size, label="tiny decode vs fp32 oracle")
+    engine.close()
+
+
 def test_import_then_decode_epoch(cuda_ok, tiny_weights):
     sc = make_scenario(vocab=ORACLE_TINY.vocab, seed=0)
     # prefill on the oracle only: it stands for the stock prefill whose KV is imported
