@@ -582,6 +582,10 @@ def run_gpu(args) -> None:
                 "peak_kind": f"{peak_kind}, x{world} GPUs (aggregate)" if tp else peak_kind,
                 "unit": "GB/s",
                 "frac": round(achieved_gbs / peak, 4),
+                # the second denominator the north star asks for: nominal 8 TB/s per GPU
+                "frac_of_nominal_8tbs": round(achieved_gbs / (8000.0 * (world if tp else 1)), 4),
+                "logits": "not materialised (argmax fused into the lm_head phase): 0 of the 4 x V x 4 B = "
+                          "2,433,024 B per step a materialising step would add",
                 "traffic": (PROFILED_TRAFFIC["bytes_per_launch"] // PROFILED_TRAFFIC["steps_per_launch"]
                             if args.k == PROFILED_TRAFFIC["k"] and not args.layers and not args.vocab and not tp
                             else None),
