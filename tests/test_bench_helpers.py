@@ -72,3 +72,25 @@ def test_tensor_parallel_shards_cover_the_step_once():
         pad = sum(TpShard.of(cfg, r, world).ni for r in range(world)) - cfg.intermediate
         mlp_pad = 2 * cfg.num_layers * 3 * pad * cfg.hidden
         assert total == single + (world - 1) * (norms + embed_rows) + kv_extra + qkv_extra + mlp_pad, world
+
+
+def test_second_cohort_takes_over_the_rows_under_new_generations():
+    """The configs[4] figure (box_scale) prefills a fresh cohort on rows an
+    earlier cohort still holds: with its generations moved, every epoch of the
+    new cohort passes the controller's continuity check and decodes (CPU
+    oracle, tiny model); the summary counts tokens per device second."""
+    from cruise_b200.model_config import TINY
+
+    engine = bench.OracleEngine(TINY, threads=1)
+    sc, first = bench.setup_cohort(engine, TINY, seed=11, k=2, prompt_max=5)
+    cohort = bench.Cohort(engine, TINY, sc, first)
+    cohort.step()
+    sc2, first2 = bench.setup_cohort(engine, TINY, seed=12, k=8, prompt_max=12, generation_offset=100)
+    assert first2.status == 0 and sc2.generations == [g + 100 for g in sc.generations]
+    second = bench.Cohort(engine, TINY, sc2, first2)
+    out, _ = second.step()
+    assert out.status == 0 and out.model_calls > 0
+    summary = bench.box_scale_summary({"dev_s": 0.5, "tokens": 100, "wall": 0.6, "bytes": 10 ** 12,
+                                       "model_calls": 25}, device=None, world=1, tp=False, peak=4000.0)
+    assert summary["value"] == 200.0 and summary["us_per_decode_step"] == 20000.0
+    assert summary["roofline_frac"] == 0.5 and summary["e2e_value"] == round(100 / 0.6, 2)
