@@ -39,6 +39,7 @@ SIGNATURES = {
         ],
     ),
     "resident_epoch_destroy": (None, [ctypes.c_void_p]),
+    "resident_epoch_prefill": (ctypes.c_int32, [ctypes.c_void_p, i64p, i32p, ctypes.c_int32]),
     "cruise_epoch_preset": (ctypes.c_int32, [ctypes.c_char_p, ctypes.POINTER(CruiseModelConfigC)]),
     "cruise_epoch_create": (ctypes.c_void_p, [ctypes.POINTER(CruiseModelConfigC), ctypes.c_int32, i32p]),
     "cruise_epoch_destroy": (None, [ctypes.c_void_p]),

@@ -74,6 +74,11 @@ class NativeEpochEngine(Protocol):
         self, plan: ResidentEpochPlan, transfer: DeviceKVTransfer
     ) -> NativeEpochOutput: ...
 
+    # Optional (no reference counterpart): prefill the plan's prompts
+    # (requests with prompt_token_ids) on the device, then run the epoch that
+    # imports them.
+    def execute_with_device_prefill(self, plan: ResidentEpochPlan) -> NativeEpochOutput: ...
+
 
 def _model_runner_output(req_ids: list[str], sampled: list[list[int]]) -> Any:
     try:
@@ -109,6 +114,13 @@ class ResidentEpochBackend:
             close()
 
     def _run_native(self, plan, snapshot, device_transfer) -> NativeEpochOutput:
+        if any(r.prompt_token_ids for r in plan.requests):
+            run = getattr(self.engine, "execute_with_device_prefill", None)
+            if not callable(run) or snapshot is not None or device_transfer is not None:
+                raise ResidentEpochExecutionError(
+                    "resident backend cannot prefill on the device", commit_state=EpochCommitState.PREPARED
+                )
+            return run(plan)
         if device_transfer is not None:
             run = getattr(self.engine, "execute_with_device_transfer", None)
             if not callable(run):
@@ -167,6 +179,11 @@ class ResidentEpochBackend:
             raise ResidentEpochExecutionError(
                 "direct Device KV transfer did not return an import checksum", commit_state=committed
             )
+        device_prefill = any(r.prompt_token_ids for r in plan.requests)
+        if device_prefill and (not native.kv_imported or native.kv_import_checksum == 0):
+            raise ResidentEpochExecutionError(
+                "device prefill did not return an import checksum", commit_state=committed
+            )
         if set(native.token_ids) != set(plan.req_ids):
             raise ResidentEpochExecutionError(
                 "native resident epoch returned the wrong request set", commit_state=committed
@@ -193,7 +210,8 @@ class ResidentEpochBackend:
             kv_import_checksum=native.kv_import_checksum,
             kv_snapshot_checksum=snapshot.checksum if snapshot is not None else 0,
             kv_transfer_mode=(
-                "device_ipc" if device_transfer is not None else "host_snapshot" if snapshot is not None else "none"
+                "device_ipc" if device_transfer is not None else "host_snapshot" if snapshot is not None
+                else "device_prefill" if device_prefill else "none"
             ),
         )
         try:

@@ -6,6 +6,8 @@ Environment names are the reference's operator surface:
 reference fixes capacity at 8 tokens; here it defaults to the paged layout's
 ``blocks_per_row * block_size`` of the served preset
 (``VLLM_ASCEND_RESIDENT_EPOCH_MODEL``; 256 for the 7B preset).
+``VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL`` (1: prefill new prompts on the
+device) extends the reference's surface.
 """
 
 from __future__ import annotations
@@ -34,6 +36,10 @@ class ResidentEpochConfig:
     blocks_per_request: int = 2
     block_size: int = 128
     max_batch_size: int = 4
+    # VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL=1 (no reference counterpart):
+    # new prompts of 2..block_size tokens are prefilled by the engine on the
+    # device inside their first epoch instead of on the host lane
+    device_prefill: bool = False
 
     @classmethod
     def from_env(cls) -> "ResidentEpochConfig":
@@ -48,6 +54,7 @@ class ResidentEpochConfig:
             physical_blocks=preset.num_blocks,
             blocks_per_request=preset.blocks_per_row,
             block_size=preset.block_size,
+            device_prefill=_env_int("VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL", 0) != 0,
         )
         config.validate()
         return config

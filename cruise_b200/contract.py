@@ -56,6 +56,11 @@ class ResidentEpochRequest:
     device_block_ids: tuple[int, int]
     state_owner: Literal["host", "device"] = "host"
     kv_import_required: bool = False
+    # Device prefill (no reference counterpart; the reference prefills on the
+    # host): the whole prompt, whose K/V at positions 0..len-2 the engine
+    # computes and imports before this epoch decodes from position len-1.
+    # Empty for a request whose KV already exists.
+    prompt_token_ids: tuple[int, ...] = ()
 
 
 def _fail(message: str) -> None:
@@ -122,6 +127,13 @@ class ResidentEpochPlan:
                 _fail("KV import requires Host-owned request state")
             if r.position + self.max_steps > self.logical_capacity:
                 _fail("epoch exceeds logical capacity")
+            if r.prompt_token_ids:
+                if len(r.prompt_token_ids) < 2:
+                    _fail("a device prefill needs a prompt of at least two tokens")
+                if not r.kv_import_required or r.state_owner != "host":
+                    _fail("a device prefill imports Host-owned request state")
+                if r.position != len(r.prompt_token_ids) - 1 or r.token_id != r.prompt_token_ids[-1]:
+                    _fail("a device prefill decodes from the last prompt token")
         if tuple(expected) != tuple(self.active_mask):
             _fail("active mask does not match resident rows")
 
@@ -147,7 +159,7 @@ class ResidentEpochResult:
     kv_imported: bool = False
     kv_import_checksum: int = 0
     kv_snapshot_checksum: int = 0
-    kv_transfer_mode: Literal["none", "host_snapshot", "device_ipc"] = "none"
+    kv_transfer_mode: Literal["none", "host_snapshot", "device_ipc", "device_prefill"] = "none"
 
     def _check_device_route(self, plan: ResidentEpochPlan) -> None:
         if self.status != 0:
@@ -164,7 +176,7 @@ class ResidentEpochResult:
     def _check_transfer(self) -> None:
         mode = "host_snapshot" if self.kv_imported and self.kv_transfer_mode == "none" else self.kv_transfer_mode
         if self.kv_imported:
-            if self.kv_import_checksum == 0 or mode not in ("host_snapshot", "device_ipc"):
+            if self.kv_import_checksum == 0 or mode not in ("host_snapshot", "device_ipc", "device_prefill"):
                 _fail("device result did not prove an imported KV transfer")
             if mode == "host_snapshot" and (
                 self.kv_snapshot_checksum == 0 or self.kv_import_checksum != self.kv_snapshot_checksum

@@ -1463,6 +1463,7 @@ bool g_bridge_active = false;
 struct BridgeEngine {
   Engine *engine = nullptr;
   std::map<std::string, void *> ipc_imports;
+  int32_t prefill_mask = 0;   // rows resident_epoch_prefill left in the device staging for the next execute
 };
 
 bool read_transfer(const Engine *e, const char *path, uint64_t transfer_id, const int32_t *gens,
@@ -2130,7 +2131,9 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   if (output_commit_state == nullptr) return 10;
   *output_commit_state = CRUISE_EPOCH_PREPARED;
   const bool device_import = ipc_metadata != nullptr;
-  const bool importing = transfer_path != nullptr || device_import;
+  // no file and no IPC metadata but a transfer id: the rows resident_epoch_prefill computed
+  const bool prefill_import = transfer_path == nullptr && !device_import && transfer_id != 0;
+  const bool importing = transfer_path != nullptr || device_import || prefill_import;
   if (opaque == nullptr || request_count < 1 || request_count > kBatch || max_steps < 1 || max_steps > kMaxSteps ||
       input_token_ids == nullptr || input_positions == nullptr || input_sequence_lengths == nullptr ||
       input_eos_token_ids == nullptr || input_row_generations == nullptr || output_token_ids == nullptr ||
@@ -2149,14 +2152,24 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   std::vector<uint8_t> payload;
   int32_t import_mask = 0;
   uint32_t expected_checksum = 0;
-  if (importing && !device_import &&
+  if (importing && !device_import && !prefill_import &&
       !cruise::read_transfer(e, transfer_path, transfer_id, input_row_generations, payload, import_mask,
                              expected_checksum))
     return 13;
   if (device_import) {
+    // the IPC copy overwrites the staging buffer a pending prefill left
+    be->prefill_mask = 0;
+    e->payload_ready = false;
     if (!cruise::validate_ipc(e, ipc_metadata, input_row_generations) || !cruise::prepare_ipc_payload(be, ipc_metadata))
       return 35;
     import_mask = static_cast<int32_t>(ipc_metadata->import_mask);
+  }
+  if (prefill_import) {
+    // every prefilled row is imported, and only into a row this epoch runs
+    if (be->prefill_mask == 0 || !e->payload_ready) return 13;
+    for (int r = 0; r < kBatch; ++r)
+      if (((be->prefill_mask >> r) & 1) != 0 && input_row_generations[r] == 0) return 13;
+    import_mask = be->prefill_mask;
   }
   *output_model_calls = 0;
   *output_device_status = -1;
@@ -2166,8 +2179,9 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   *output_wall_us = 0;
   *output_native_cpu_us = 0;
   const int64_t payload_bytes = cruise::import_payload_bytes(e);
-  *output_declared_input_bytes = device_import ? CRUISE_SIDECAR_REQUEST_BYTES + CRUISE_RESIDENT_IPC_METADATA_BYTES
-                                               : (importing ? payload_bytes + 244 : 260);
+  *output_declared_input_bytes = device_import    ? CRUISE_SIDECAR_REQUEST_BYTES + CRUISE_RESIDENT_IPC_METADATA_BYTES
+                                 : prefill_import ? 260
+                                 : (importing ? payload_bytes + 244 : 260);
   *output_declared_output_bytes = 368;
   const int64_t cpu_start = cruise::process_cpu_us();
   std::fill(output_token_ids, output_token_ids + kBatch * kMaxSteps, -1);
@@ -2212,10 +2226,13 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   int32_t out[cruise::kControlOut];
   const auto wall_start = std::chrono::steady_clock::now();
   *output_commit_state = CRUISE_EPOCH_EXECUTING;
+  // a prefill import passes no payload: run_epoch takes the prefilled device staging
+  if (prefill_import) be->prefill_mask = 0;
   const int32_t rc = cruise::run_epoch(
       e, tokens, positions, lengths, slots, active, blocks.data(), e->tiling.data(), control,
-      device_import ? static_cast<const void *>(e->d_payload) : (importing ? payload.data() : nullptr),
-      importing ? static_cast<uint64_t>(payload_bytes) : 0, history, out, nullptr, nullptr, device_import);
+      device_import ? static_cast<const void *>(e->d_payload) : (importing && !prefill_import ? payload.data() : nullptr),
+      importing && !prefill_import ? static_cast<uint64_t>(payload_bytes) : 0, history, out, nullptr, nullptr,
+      device_import);
   const auto wall_end = std::chrono::steady_clock::now();
   *output_feed_calls = 1;
   if (rc != 0) return 30;
@@ -2225,8 +2242,9 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   *output_model_calls = out[4];
   *output_kv_import_checksum = out[5];
   if (*output_device_status == 0) {
-    if (device_import && *output_kv_import_checksum == 0) return 34;
-    if (importing && !device_import && static_cast<uint32_t>(*output_kv_import_checksum) != expected_checksum)
+    if ((device_import || prefill_import) && *output_kv_import_checksum == 0) return 34;
+    if (importing && !device_import && !prefill_import &&
+        static_cast<uint32_t>(*output_kv_import_checksum) != expected_checksum)
       return 34;
   }
   for (int r = 0; r < kBatch; ++r) {
@@ -2239,6 +2257,27 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   const int64_t cpu_end = cruise::process_cpu_us();
   if (cpu_start >= 0 && cpu_end >= cpu_start) *output_native_cpu_us = cpu_end - cpu_start;
   *output_commit_state = CRUISE_EPOCH_COMMITTED;
+  return 0;
+}
+
+int32_t resident_epoch_prefill(void *opaque, const int64_t *prompt_tokens, const int32_t *prompt_lens,
+                               int32_t stride) {
+  if (opaque == nullptr || prompt_tokens == nullptr || prompt_lens == nullptr || stride < 1) return 10;
+  auto *be = static_cast<BridgeEngine *>(opaque);
+  Engine *e = be->engine;
+  std::lock_guard<std::mutex> lock(e->execute_mutex);
+  cudaSetDevice(e->device);
+  be->prefill_mask = 0;
+  int32_t mask = 0;
+  for (int r = 0; r < kBatch; ++r) {
+    if (prompt_lens[r] < 0 || prompt_lens[r] > stride) return 10;
+    if (prompt_lens[r] >= 2) mask |= 1 << r;   // a 1-token prompt has no K/V before its decode position
+  }
+  if (mask == 0) return 10;
+  const int32_t rc = cruise::prefill_run(e, prompt_tokens, prompt_lens, stride);
+  if (rc == -1) return 11;   // a prompt longer than a block or a token outside the vocabulary
+  if (rc != 0) return 30;
+  be->prefill_mask = mask;
   return 0;
 }
 

@@ -39,6 +39,7 @@ class CudaEpochEngine:
         self.config = PRESETS[self.model]
         weights = weights or os.getenv("VLLM_ASCEND_RESIDENT_EPOCH_EXTERNAL_WEIGHTS", "synthetic:0")
         tiling = tiling or os.getenv("VLLM_ASCEND_RESIDENT_EPOCH_TILING")
+        self.prefill_transfers = 0   # transfer ids of device-prefill imports
         self.library = _lib.load()
         status = ctypes.c_int32(-1)
         self.handle = self.library.resident_epoch_create(
@@ -78,6 +79,34 @@ class CudaEpochEngine:
         transfer.validate()
         metadata = ctypes.create_string_buffer(transfer.wire_bytes())
         return self._execute(plan, transfer_path=None, transfer_id=transfer.transfer_id, ipc=metadata)
+
+    def execute_with_device_prefill(self, plan: ResidentEpochPlan) -> NativeEpochOutput:
+        """The plan's prompts (its requests with ``prompt_token_ids``) run
+        through the engine's batched device prefill, then the epoch imports
+        their K/V from the device and decodes from each last prompt token
+        (``resident_epoch_prefill``, then ``resident_epoch_execute`` with a
+        transfer id and neither a file nor IPC metadata)."""
+        stride = self.config.block_size
+        tokens = (ctypes.c_int64 * (4 * stride))()
+        lengths = (ctypes.c_int32 * 4)()
+        for r in plan.requests:
+            if not r.prompt_token_ids:
+                continue
+            if len(r.prompt_token_ids) > stride:
+                raise ResidentEpochExecutionError(
+                    f"a device prefill takes at most {stride} prompt tokens per row",
+                    commit_state=EpochCommitState.PREPARED,
+                )
+            for i, token in enumerate(r.prompt_token_ids):
+                tokens[r.row * stride + i] = int(token)
+            lengths[r.row] = len(r.prompt_token_ids)
+        ret = self.library.resident_epoch_prefill(self.handle, tokens, lengths, stride)
+        if ret != 0:
+            raise ResidentEpochExecutionError(
+                f"resident_epoch_prefill failed with status {ret}", commit_state=EpochCommitState.PREPARED, status=ret
+            )
+        self.prefill_transfers += 1
+        return self._execute(plan, transfer_path=None, transfer_id=self.prefill_transfers, ipc=None, prefill=True)
 
     def close(self) -> None:
         if getattr(self, "handle", None):
@@ -126,7 +155,7 @@ class CudaEpochEngine:
                       row_generations=tuple(out_gens))
         return result
 
-    def _execute(self, plan: ResidentEpochPlan, *, transfer_path, transfer_id, ipc) -> NativeEpochOutput:
+    def _execute(self, plan: ResidentEpochPlan, *, transfer_path, transfer_id, ipc, prefill=False) -> NativeEpochOutput:
         if plan.graph_batch_size != 4:
             raise ValueError("the CUDA engine serves the static B=4 epoch")
         tokens, positions, lengths = [0] * 4, [0] * 4, [0] * 4
@@ -159,9 +188,10 @@ class CudaEpochEngine:
             feed_calls=out["feed_calls"], fetch_calls=out["fetch_calls"], wall_us=out["wall_us"],
             native_cpu_us=out["native_cpu_us"], declared_input_bytes=out["declared_input_bytes"],
             declared_output_bytes=out["declared_output_bytes"],
-            kv_imported=transfer_path is not None or ipc is not None,
+            kv_imported=transfer_path is not None or ipc is not None or prefill,
             kv_import_checksum=out["kv_import_checksum"] & 0xFFFFFFFF,
-            kv_transfer_mode="device_ipc" if ipc is not None else "host_snapshot" if transfer_path else "none",
+            kv_transfer_mode=("device_ipc" if ipc is not None else "host_snapshot" if transfer_path
+                              else "device_prefill" if prefill else "none"),
         )
 
 

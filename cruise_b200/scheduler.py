@@ -19,6 +19,14 @@ vLLM's token accounting by the K - 1 extra steps.
   with the device-owned requests paused.
 * Rejection reasons: every schedule without a plan records why in
   ``last_rejection`` (vocabulary of the reference).
+* Device prefill (``VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL=1``; the
+  reference has no such mode): a fresh greedy prompt of 2..block_size tokens
+  that vLLM schedules whole goes into the plan at once with its prompt
+  (``prompt_token_ids``).  The engine prefills it on the device, imports its
+  K/V and decodes from its last prompt token in the same epoch, beside the
+  device-owned rows, so such prompts need no host lane.  vLLM's accounting
+  counts the prompt as scheduled and the epoch's K - 1 further positions as
+  computed.
 """
 
 from __future__ import annotations
@@ -115,6 +123,15 @@ class ResidentEpochScheduler(Scheduler):
         scheduler.benchmark_metrics = ResidentEpochBenchmarkMetrics.from_env()
         return scheduler
 
+    def _device_prefill_eligible(self, request: Any) -> bool:
+        """A fresh request whose whole prompt the engine can prefill on the
+        device inside its first epoch (device_prefill mode only): supported
+        sampling, no output yet, 2..block_size prompt tokens."""
+        cfg = self.resident_config
+        return (cfg.device_prefill and request.num_output_tokens == 0
+                and 2 <= request.num_prompt_tokens <= cfg.block_size
+                and request_rejection_reason(request) is None)
+
     # -- host isolation (scheduler.py:102-162) ------------------------------------------
     def _host_lane_reason(self, device_running: tuple[Any, ...]) -> str | None:
         """Why the host must run something while device-owned requests wait."""
@@ -126,7 +143,8 @@ class ResidentEpochScheduler(Scheduler):
         if any(r.num_computed_tokens < r.num_prompt_tokens for r in host_running):
             return "host-prefill-admission"
         waiting = list(self.waiting) + list(getattr(self, "skipped_waiting", ()))
-        needs_host = any(r.num_prompt_tokens > 1 or request_rejection_reason(r) is not None for r in waiting)
+        needs_host = any((r.num_prompt_tokens > 1 and not self._device_prefill_eligible(r))
+                         or request_rejection_reason(r) is not None for r in waiting)
         if needs_host and len(self.running) < self.max_num_running_reqs:
             return "host-prefill-admission"
         return None
@@ -178,10 +196,14 @@ class ResidentEpochScheduler(Scheduler):
     def _make_plan(self, output: Any) -> tuple[ResidentEpochPlan | None, str | None]:
         cfg = self.resident_config
         req_ids = tuple(output.num_scheduled_tokens)
+        # device_prefill mode: a fresh prompt scheduled whole in this step is
+        # prefilled on the device inside the epoch (the engine's K/V import)
+        prefill = {r for r in req_ids if self._device_prefill_eligible(self.requests[r])
+                   and output.num_scheduled_tokens[r] == self.requests[r].num_prompt_tokens}
         gates = (
             (not req_ids, "empty-schedule"),
             (len(req_ids) > cfg.max_batch_size, "batch-too-large"),
-            (any(output.num_scheduled_tokens[r] != 1 for r in req_ids), "not-single-token-decode"),
+            (any(output.num_scheduled_tokens[r] != 1 for r in req_ids if r not in prefill), "not-single-token-decode"),
             (bool(output.scheduled_spec_decode_tokens), "speculative-decode"),
             (bool(output.scheduled_encoder_inputs), "encoder-input"),
             (bool(output.preempted_req_ids), "preemption"),
@@ -202,7 +224,7 @@ class ResidentEpochScheduler(Scheduler):
             owned = request.request_id in self.resident.device_owned
             if request.num_prompt_tokens > cfg.logical_capacity:
                 return None, "prompt-exceeds-resident-capacity"
-            if request.num_prompt_tokens > 1 and request.num_output_tokens == 0:
+            if request.num_prompt_tokens > 1 and request.num_output_tokens == 0 and request.request_id not in prefill:
                 return None, "host-prefill-in-progress"
             if request.num_prompt_tokens > 1 and not owned and len(self._block_ids(request)) != 1:
                 return None, "multiple-kv-cache-groups"
@@ -235,6 +257,8 @@ class ResidentEpochScheduler(Scheduler):
                 device_block_ids=(row * cfg.blocks_per_request, row * cfg.blocks_per_request + 1),
                 state_owner="device" if owned else "host",
                 kv_import_required=request.num_prompt_tokens > 1 and not owned,
+                prompt_token_ids=(tuple(int(t) for t in request.prompt_token_ids)
+                                  if request.request_id in prefill else ()),
             ))
             mask[row] = 1
         plan = ResidentEpochPlan(version=CONTRACT_VERSION, graph_batch_size=cfg.max_batch_size, max_steps=steps,
@@ -264,9 +288,12 @@ class ResidentEpochScheduler(Scheduler):
         # vLLM counts one computed token per scheduled token; an epoch computed
         # `steps` of them: credit the rest before vLLM appends the outputs
         extra = {}
+        prefilled = {r.req_id for r in plan.requests if r.prompt_token_ids}
         for req_id, steps in result.computed_steps.items():
             request = self.requests[req_id]
-            more = steps - scheduler_output.num_scheduled_tokens[req_id]
+            # a device prefill was scheduled as its whole prompt, computed with
+            # the epoch's first step; a decode request as one token
+            more = steps - (1 if req_id in prefilled else scheduler_output.num_scheduled_tokens[req_id])
             if more < 0:
                 raise RuntimeError("resident epoch computed fewer than scheduled tokens")
             if request.num_computed_tokens + more > request.num_tokens + len(sampled[req_id]):

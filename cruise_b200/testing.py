@@ -13,7 +13,9 @@ match on:
   8-in / 2-out byte ledger of the epoch ABI (260 bytes in, 368 out);
 * an import epoch declares its payload plus a 212-byte header and reports the
   snapshot's checksum; a device transfer reports checksum 1 and the
-  ``device_ipc`` transfer mode.
+  ``device_ipc`` transfer mode, a device prefill checksum 1 and the
+  ``device_prefill`` mode (the last has no counterpart in the reference's
+  double).
 """
 
 from __future__ import annotations
@@ -46,6 +48,7 @@ class DeterministicTestEngine:
     def __init__(self) -> None:
         self.warmup_calls = 0
         self.execute_calls = 0
+        self.prefill_calls = 0
 
     def warm_up(self) -> NativeWarmupOutput:
         self.warmup_calls += 1
@@ -79,6 +82,10 @@ class DeterministicTestEngine:
     def execute_with_device_transfer(self, plan: ResidentEpochPlan, transfer: DeviceKVTransfer) -> NativeEpochOutput:
         transfer.validate()
         return self._epoch(plan, kv_imported=True, kv_import_checksum=1, kv_transfer_mode="device_ipc")
+
+    def execute_with_device_prefill(self, plan: ResidentEpochPlan) -> NativeEpochOutput:
+        self.prefill_calls += 1
+        return self._epoch(plan, kv_imported=True, kv_import_checksum=1, kv_transfer_mode="device_prefill")
 
 
 def create_test_engine() -> DeterministicTestEngine:

@@ -65,7 +65,9 @@ void *resident_epoch_create(const char *air_path, const char *graph_config,
  * 34 import checksum, 35 device IPC import) and the same commit-state moves
  * (0 -> 1 before submission -> 2 after a valid completion).  Row r owns the
  * blocks r*blocks_per_row + j, as in the reference bridge (:524-532).
- * output_token_ids is [4][8] row-major ([row][step]). */
+ * output_token_ids is [4][8] row-major ([row][step]).  One addition: a
+ * nonzero transfer_id with neither a transfer path nor IPC metadata imports
+ * the rows of the last resident_epoch_prefill (13 when none is pending). */
 int32_t resident_epoch_execute(
     void *opaque, int32_t request_count, int32_t max_steps,
     const int64_t *input_token_ids, const int64_t *input_positions,
@@ -82,6 +84,22 @@ int32_t resident_epoch_execute(
 
 /* Replaces resident_epoch_destroy (native/resident_epoch_bridge.cpp:651-670). */
 void resident_epoch_destroy(void *opaque);
+
+/* No reference counterpart: the device route for what the reference does as
+ * a host prefill plus a one-shot KV import.  Runs cruise_epoch_prefill on the
+ * bridge's engine for the prompts in prompt_tokens [4][stride] (row-major),
+ * prompt_lens[r] in [0, min(stride, block_size)].  Rows with at least 2
+ * tokens are then pending: the next resident_epoch_execute on this handle
+ * called with transfer_path NULL, ipc_metadata NULL and a nonzero transfer_id
+ * imports them from the device (Adler-32 proof in output_kv_import_checksum)
+ * and decodes each from position len-1 with token prompt[len-1].  Every
+ * pending row must run in that epoch (nonzero generation), else it returns 13;
+ * without a pending prefill it returns 13 too.  Another import (a transfer
+ * file or device IPC) discards the pending rows.  Returns 0, 10 bad
+ * arguments (no row with 2 or more tokens), 11 a prompt longer than the
+ * block size or a token outside the vocabulary, 30 a device failure. */
+int32_t resident_epoch_prefill(void *opaque, const int64_t *prompt_tokens,
+                               const int32_t *prompt_lens, int32_t stride);
 
 /* ---- engine API ---------------------------------------------------------- */
 

@@ -121,3 +121,36 @@ def test_epoch_steps_and_config():
     ResidentEpochConfig().validate()
     with pytest.raises(ValueError):
         ResidentEpochConfig(max_steps=3).validate()
+
+
+def prefill_plan(prompt, **request_overrides) -> ResidentEpochPlan:
+    fields = dict(req_id="r0", row=0, generation=1, token_id=prompt[-1], position=len(prompt) - 1,
+                  sequence_length=len(prompt), eos_token_id=9, scheduler_block_ids=(17,), device_block_ids=(0, 1),
+                  state_owner="host", kv_import_required=True, prompt_token_ids=tuple(prompt))
+    fields.update(request_overrides)
+    return ResidentEpochPlan(version=CONTRACT_VERSION, graph_batch_size=1, max_steps=4, logical_capacity=256,
+                             requests=(ResidentEpochRequest(**fields),), active_mask=(1,))
+
+
+def test_device_prefill_request_rules():
+    """A device-prefilled request (an extension over the reference) carries its
+    whole prompt, imports Host-owned state and decodes from the last prompt
+    token; its result proves the import like a device transfer does."""
+    plan = prefill_plan([5, 6, 7])
+    plan.validate()
+    for bad, message in (
+        (prefill_plan([5]), "at least two tokens"),
+        (prefill_plan([5, 6, 7], kv_import_required=False), "imports Host-owned"),
+        (prefill_plan([5, 6, 7], state_owner="device", kv_import_required=False), "imports Host-owned"),
+        (prefill_plan([5, 6, 7], token_id=6), "last prompt token"),
+        (prefill_plan([5, 6, 7], position=1, sequence_length=2), "last prompt token"),
+    ):
+        with pytest.raises(ValueError, match=message):
+            bad.validate()
+    good = device_result(plan, 4, kv_imported=True, kv_import_checksum=7, kv_transfer_mode="device_prefill")
+    good.validate_against(plan, {"r0": [1, 2, 3, 4]})
+    with pytest.raises(ValueError, match="did not commit the requested KV import"):
+        device_result(plan, 4).validate_against(plan, {"r0": [1, 2, 3, 4]})
+    with pytest.raises(ValueError, match="did not prove an imported KV transfer"):
+        device_result(plan, 4, kv_imported=True, kv_transfer_mode="device_prefill").validate_against(
+            plan, {"r0": [1, 2, 3, 4]})

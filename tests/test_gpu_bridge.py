@@ -105,3 +105,86 @@ def test_host_snapshot_import_through_backend(engines):
     result = get_result(out)
     assert result.kv_imported and result.kv_import_checksum == snapshot.checksum
     assert result.kv_transfer_mode == "host_snapshot" and result.model_calls == 2
+
+
+def _oracle_prefill_decode(oracle, prompts, generations, steps, eos=4095):
+    """The oracle's token-by-token prefill of ``prompts`` (rows own blocks
+    2r, 2r+1 as in the bridge) and the K-step epoch after it: (history, trace)."""
+    from oracle.epoch import EpochTrace
+    from scenario import Scenario, decode_inputs, prefill_epochs
+
+    sc = Scenario(block_table=np.arange(8, dtype=np.int32).reshape(4, 2), prompts=prompts, budgets=[8] * 4,
+                  generations=generations, eos=[eos] * 4, k=steps)
+    for inputs in prefill_epochs(sc, TINY.block_size, TINY.vocab):
+        oracle.run(**inputs)
+    trace = EpochTrace()
+    history, control = oracle.run(**decode_inputs(sc, TINY.block_size), trace=trace)
+    return history, control, trace
+
+
+def test_device_prefill_through_the_bridge(engines):
+    """resident_epoch_prefill + the import epoch (no reference counterpart):
+    two rows prefilled on the device, a third starting from a one-token
+    prompt, one row empty; tokens equal the oracle's token-by-token prefill and
+    decode (near-ties excepted), the import proof is nonzero, and a following
+    epoch continues the device-owned rows."""
+    engine, oracle = engines
+    from cruise_b200.backend import ResidentEpochBackend
+    from cruise_b200.contract import CONTRACT_VERSION, ResidentEpochPlan, ResidentEpochRequest, get_result
+    from scenario import find_divergence
+
+    prompts = [[11, 12, 13, 14, 15], [301], [], [7, 8, 9, 10, 11, 12, 13, 14, 15]]
+    generations = [5, 6, 0, 7]
+    reqs = tuple(
+        ResidentEpochRequest(req_id=f"r{row}", row=row, generation=generations[row], token_id=p[-1],
+                             position=len(p) - 1, sequence_length=len(p), eos_token_id=4095,
+                             scheduler_block_ids=(row,), device_block_ids=(2 * row, 2 * row + 1),
+                             kv_import_required=len(p) > 1, prompt_token_ids=tuple(p) if len(p) > 1 else ())
+        for row, p in enumerate(prompts) if p)
+    plan = ResidentEpochPlan(version=CONTRACT_VERSION, graph_batch_size=4, max_steps=4, logical_capacity=32,
+                             requests=reqs, active_mask=(1, 1, 0, 1))
+    out = ResidentEpochBackend(engine).execute(plan)
+    result = get_result(out)
+    assert result.kv_imported and result.kv_transfer_mode == "device_prefill" and result.kv_import_checksum != 0
+    history, control, trace = _oracle_prefill_decode(oracle, prompts, generations, 4)
+    got = np.full((8, 4), -1, dtype=np.int64)
+    for q in plan.requests:
+        tokens = out.sampled_token_ids[out.req_id_to_index[q.req_id]]
+        got[:len(tokens), q.row] = tokens
+    diverged = find_divergence(got, history, trace.margins)
+    assert len(diverged) <= 1, diverged
+
+    # the rows are device-owned now: the next epoch continues the rows that ran
+    # all four steps without an import
+    going = [q for q in plan.requests if got[3, q.row] >= 0 and 4095 not in got[:4, q.row]]
+    if going:
+        follow = ResidentEpochPlan(
+            version=CONTRACT_VERSION, graph_batch_size=4, max_steps=2, logical_capacity=32,
+            requests=tuple(ResidentEpochRequest(
+                req_id=q.req_id, row=q.row, generation=q.generation, token_id=int(got[3, q.row]),
+                position=q.position + 4, sequence_length=q.position + 5, eos_token_id=4095,
+                scheduler_block_ids=q.scheduler_block_ids, device_block_ids=q.device_block_ids, state_owner="device")
+                for q in going),
+            active_mask=tuple(1 if r in {q.row for q in going} else 0 for r in range(4)))
+        assert not get_result(ResidentEpochBackend(engine).execute(follow)).kv_imported
+
+
+def test_prefill_import_needs_a_pending_prefill(engines):
+    engine, _ = engines
+    out = engine._call(request_count=1, max_steps=1, tokens=[5, 0, 0, 0], positions=[2, 0, 0, 0],
+                       lengths=[3, 0, 0, 0], eos=[4095] * 4, generations=[9, 0, 0, 0], transfer_id=3)
+    assert out["ret"] == 13
+    tokens = (np.arange(4 * TINY.block_size, dtype=np.int64) % 100).copy()
+    lens = np.array([3, 0, 4, 0], dtype=np.int32)
+    lib = engine.library
+    import ctypes
+    assert lib.resident_epoch_prefill(engine.handle, tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                      lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), TINY.block_size) == 0
+    # row 2 was prefilled but does not run in this epoch
+    out = engine._call(request_count=1, max_steps=1, tokens=[2, 0, 0, 0], positions=[2, 0, 0, 0],
+                       lengths=[3, 0, 0, 0], eos=[4095] * 4, generations=[9, 0, 0, 0], transfer_id=4)
+    assert out["ret"] == 13
+    too_long = np.array([TINY.block_size + 1, 0, 0, 0], dtype=np.int32)
+    assert lib.resident_epoch_prefill(engine.handle, tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                      too_long.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                      TINY.block_size) == 10

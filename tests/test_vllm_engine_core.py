@@ -180,3 +180,44 @@ def test_engine_core_dynamic_cohort_on_the_test_engine(cuda_device_type, tmp_pat
     finally:
         core.shutdown()
     assert not torch.distributed.is_initialized()
+
+
+def test_engine_core_device_prefill_on_the_test_engine(cuda_device_type, tmp_path, monkeypatch):
+    """VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL=1: multi-token prompts go
+    straight into the first resident epoch (the engine prefills them on the
+    device); the stand-in counts on from each last prompt token."""
+    import time as _time
+
+    from vllm import SamplingParams
+    from vllm.v1.engine import EngineCoreRequest
+
+    from cruise_b200.model_config import QWEN25_7B
+
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_BACKEND_FACTORY", "cruise_b200.testing:create_test_engine")
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_MODEL", QWEN25_7B.name)
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_STEPS", "4")
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL", "1")
+    monkeypatch.setenv("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    core = make_engine_core(hf_config_dir(tmp_path, QWEN25_7B), QWEN25_7B, 256)
+    try:
+        recorder = PlanRecorder(core.scheduler)
+        prompts = {"p": [9707, 11, 358, 374], "q": [500, 501]}
+        for client, (req_id, prompt) in enumerate(prompts.items()):
+            params = SamplingParams(temperature=0.0, max_tokens=6, detokenize=False)
+            params.update_from_generation_config({}, QWEN25_7B.configured_eos)
+            req, wave = core.preprocess_add_request(EngineCoreRequest(
+                request_id=req_id, prompt_token_ids=prompt, mm_features=None, sampling_params=params,
+                pooling_params=None, arrival_time=_time.time(), lora_request=None, cache_salt=None,
+                data_parallel_rank=None, client_index=client))
+            core.add_request(req, wave)
+        first = epoch(core)
+        assert first == {"p": [375, 376, 377, 378], "q": [502, 503, 504, 505]}
+        plan = recorder.plans[0]
+        assert {r.req_id: r.prompt_token_ids for r in plan.requests} == {k: tuple(v) for k, v in prompts.items()}
+        assert core.model_executor.driver_worker.worker.backend.engine.prefill_calls == 1
+        second = epoch(core)
+        assert second == {"p": [379, 380], "q": [506, 507]}
+        assert all(not r.prompt_token_ids and r.state_owner == "device" for r in recorder.plans[1].requests)
+        assert epoch(core) == {} and not core.scheduler.has_requests()
+    finally:
+        core.shutdown()

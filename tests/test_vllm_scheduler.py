@@ -42,7 +42,8 @@ def hf_config_dir(tmp_path, preset=QWEN25_7B):
     return path
 
 
-def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_model_len=256, adopt=True):
+def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_model_len=256, adopt=True,
+                   prefix_caching=True):
     """vLLM's own V1 scheduler for the preset, turned into the resident one."""
     from vllm.config import CacheConfig, DeviceConfig, ModelConfig, SchedulerConfig, VllmConfig
     from vllm.v1.core.sched.scheduler import Scheduler
@@ -54,7 +55,7 @@ def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_mode
 
     model = ModelConfig(model=str(hf_config_dir(tmp_path, preset)), skip_tokenizer_init=True,
                         max_model_len=max_model_len, dtype="bfloat16")
-    cache = CacheConfig(block_size=preset.block_size)
+    cache = CacheConfig(block_size=preset.block_size, enable_prefix_caching=prefix_caching)
     cache.num_gpu_blocks = 16
     sched = SchedulerConfig(max_num_seqs=batch_size, max_num_batched_tokens=512, max_model_len=max_model_len,
                             is_encoder_decoder=False, async_scheduling=False)
@@ -347,3 +348,85 @@ def test_resident_rows_reuse_freed_rows_with_fresh_generations():
     assert late.generations == {"x": 2**31 - 1}
     with pytest.raises(RuntimeError, match="generation space"):
         late.assign(("x", "y"), 4)
+
+
+def device_prefill_config(**kw):
+    return ResidentEpochConfig(logical_capacity=256, block_size=QWEN25_7B.block_size, device_prefill=True, **kw)
+
+
+def test_device_prefill_puts_a_fresh_prompt_in_its_first_epoch(tmp_path):
+    """device_prefill mode: a fresh prompt scheduled whole becomes a plan at
+    once (no host step): the epoch prefills it on the device, imports its K/V
+    and decodes from the last prompt token; vLLM's accounting then counts the
+    prompt plus the K - 1 decoded positions as computed."""
+    scheduler = make_scheduler(tmp_path, 1, device_prefill_config(max_steps=4))
+    r = request("0", [5, 6, 7], max_tokens=6)
+    scheduler.add_request(r)
+    first = scheduler.schedule()
+    plan = get_plan(first)
+    assert plan is not None and first.num_scheduled_tokens == {"0": 3} and plan.max_steps == 4
+    q = plan.requests[0]
+    assert (q.position, q.sequence_length, q.token_id, q.state_owner, q.kv_import_required) == (2, 3, 7, "host", True)
+    assert q.prompt_token_ids == (5, 6, 7)
+    commit_device_epoch(scheduler, first, {"0": [101, 102, 103, 104]})
+    assert (r.num_computed_tokens, r.num_tokens, r.num_output_tokens) == (6, 7, 4)
+    assert "0" in scheduler.resident.device_owned
+    nxt = scheduler.schedule()
+    follow = get_plan(nxt)
+    assert follow.max_steps == 2 and nxt.num_scheduled_tokens == {"0": 1}
+    f = follow.requests[0]
+    assert (f.position, f.token_id, f.state_owner, f.kv_import_required, f.prompt_token_ids) == (
+        6, 104, "device", False, ())
+    commit_device_epoch(scheduler, nxt, {"0": [105, 106]})
+    assert r.status == RequestStatus.FINISHED_LENGTH_CAPPED
+
+
+def test_device_prefill_joins_a_device_owned_request_without_a_host_lane(tmp_path):
+    scheduler = make_scheduler(tmp_path, 2, device_prefill_config(max_steps=2))
+    scheduler.add_request(request("A", [9707, 11], max_tokens=7))
+    plan_a = commit_device_epoch(scheduler, scheduler.schedule(), {"A": [101, 102]})
+    assert plan_a.requests[0].prompt_token_ids == (9707, 11)
+    scheduler.add_request(request("B", [9707, 11, 358], max_tokens=3))
+    out = scheduler.schedule()
+    plan = get_plan(out)
+    assert plan is not None and out.num_scheduled_tokens == {"A": 1, "B": 3}
+    assert [(q.req_id, q.state_owner, q.prompt_token_ids) for q in plan.requests] == [
+        ("A", "device", ()), ("B", "host", (9707, 11, 358))]
+    commit_device_epoch(scheduler, out, {"A": [103, 104], "B": [201, 202]})
+    assert scheduler.resident.device_owned == {"A", "B"}
+
+
+def test_device_prefill_leaves_long_and_unsupported_prompts_to_the_host(tmp_path):
+    # (prompts of a full block or more need the prefix cache's block hashes, which these bare requests lack)
+    scheduler = make_scheduler(tmp_path, 1, device_prefill_config(), prefix_caching=False)
+    scheduler.add_request(request("long", list(range(1, QWEN25_7B.block_size + 2)), max_tokens=2))
+    out = scheduler.schedule()
+    assert get_plan(out) is None and scheduler.last_rejection == "not-single-token-decode"
+    sampled = make_scheduler(tmp_path, 1, device_prefill_config())
+    sampled.add_request(request("t", [5, 6], max_tokens=2, temperature=0.8))
+    assert get_plan(sampled.schedule()) is None and sampled.last_rejection == "not-single-token-decode"
+
+
+def test_device_prefill_through_the_dedicated_worker(tmp_path, monkeypatch):
+    from cruise_b200.worker import ResidentEpochWorker
+
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_BACKEND_FACTORY", "cruise_b200.testing:create_test_engine")
+    scheduler = make_scheduler(tmp_path, 2, device_prefill_config(max_steps=4))
+    reqs = [request("0", [5, 6, 7, 8], max_tokens=4), request("1", [9], max_tokens=4)]
+    for r in reqs:
+        scheduler.add_request(r)
+    output = scheduler.schedule()
+    plan = get_plan(output)
+    assert [q.prompt_token_ids for q in plan.requests] == [(5, 6, 7, 8), ()]
+    worker = ResidentEpochWorker(vllm_config=scheduler.vllm_config, local_rank=0, rank=0,
+                                 distributed_init_method="tcp://127.0.0.1:1", is_driver_worker=True)
+    worker.load_model()
+    worker.compile_or_warm_up_model()
+    runner = worker.execute_model(output)
+    engine = worker._loaded_backend().engine
+    assert engine.prefill_calls == 1
+    scheduler.update_from_output(output, runner)
+    assert scheduler.last_result.kv_transfer_mode == "device_prefill" and scheduler.last_result.kv_imported
+    # the stand-in counts on from the last prompt token
+    assert list(reqs[0].output_token_ids) == [9, 10, 11, 12] and list(reqs[1].output_token_ids) == [10, 11, 12, 13]
+    worker.shutdown()
