@@ -974,6 +974,73 @@ def run_prefill(args) -> None:
     }), flush=True)
 
 
+def run_serve(args) -> None:
+    """Serving through vLLM's own front end (``LLM.generate``, engine core in
+    this process) with the resident epoch scheduler, the dedicated worker and
+    the 7B engine, device prefill on: B = 4 requests with seeded prompts of
+    2-120 tokens, greedy, ``max_tokens`` each, all submitted together.  One
+    warm-up generate, then ``--steps`` timed ones (at least 3).  Prints one
+    JSON line: output tokens per second of wall time around ``generate``
+    (prefill, every epoch and vLLM's own scheduling and output processing
+    included) and the wall time per output step.  Not part of the default
+    decode benchmark."""
+    import tempfile
+
+    for name, value in (("VLLM_ASCEND_RESIDENT_EPOCH_BACKEND_FACTORY", "cruise_b200.cuda_backend:create_cuda_engine"),
+                        ("VLLM_ASCEND_RESIDENT_EPOCH_MODEL", "qwen2.5-7b"),
+                        ("VLLM_ASCEND_RESIDENT_EPOCH_EXTERNAL_WEIGHTS", "synthetic:0"),
+                        ("VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL", "1"),
+                        ("VLLM_ENABLE_V1_MULTIPROCESSING", "0")):
+        os.environ[name] = value
+    from vllm import LLM, SamplingParams
+
+    from cruise_b200.model_config import QWEN25_7B
+
+    cfg = QWEN25_7B
+    model_dir = Path(tempfile.mkdtemp(prefix="cruise-serve-"))
+    (model_dir / "config.json").write_text(json.dumps({
+        "architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2", "hidden_size": cfg.hidden,
+        "intermediate_size": cfg.intermediate, "num_hidden_layers": cfg.num_layers,
+        "num_attention_heads": cfg.num_heads, "num_key_value_heads": cfg.num_kv_heads,
+        "vocab_size": cfg.vocab, "max_position_embeddings": 32768, "rms_norm_eps": 1e-6,
+        "rope_theta": 1000000.0, "torch_dtype": "bfloat16", "tie_word_embeddings": False,
+        "hidden_act": "silu", "eos_token_id": cfg.configured_eos,
+    }))
+    (model_dir / "generation_config.json").write_text(json.dumps({"eos_token_id": cfg.configured_eos}))
+    rng = np.random.default_rng(2026)
+    prompts = [rng.integers(0, 151643, size=int(rng.integers(2, 121))).tolist() for _ in range(4)]
+    max_tokens = 128
+    t0 = time.perf_counter()
+    llm = LLM(model=str(model_dir), skip_tokenizer_init=True, max_model_len=cfg.capacity,
+              block_size=cfg.block_size, max_num_seqs=4, async_scheduling=False, enforce_eager=True,
+              dtype="bfloat16", enable_prefix_caching=False, worker_cls="cruise_b200.worker.ResidentEpochWorker",
+              scheduler_cls="cruise_b200.scheduler.ResidentEpochScheduler")
+    setup_s = time.perf_counter() - t0
+    try:
+        params = SamplingParams(temperature=0.0, max_tokens=max_tokens, detokenize=False)
+        llm.generate([{"prompt_token_ids": p[:8]} for p in prompts], SamplingParams(
+            temperature=0.0, max_tokens=16, detokenize=False), use_tqdm=False)
+        walls, tokens = [], []
+        for _ in range(max(3, args.steps)):
+            t0 = time.perf_counter()
+            outs = llm.generate([{"prompt_token_ids": p} for p in prompts], params, use_tqdm=False)
+            walls.append(time.perf_counter() - t0)
+            tokens.append(sum(len(o.outputs[0].token_ids) for o in outs))
+    finally:
+        llm.llm_engine.engine_core.shutdown()
+    wall = statistics.median(walls)
+    produced = tokens[walls.index(wall)] if wall in walls else tokens[-1]
+    print(json.dumps({
+        "metric": "vLLM LLM.generate on the resident engine (7B arch, B=4, greedy), output tok/s", "unit": "tok/s",
+        "higher_is_better": True, "data": "synthetic (seeded weights and prompts)", "dtype": "bf16",
+        "value": round(produced / wall, 1), "wall_ms": round(wall * 1e3, 2), "output_tokens": produced,
+        "ms_per_output_step": round(wall * 1e3 / max_tokens, 3), "requests": 4, "max_tokens": max_tokens,
+        "prompt_tokens": [len(p) for p in prompts], "repeats": len(walls), "engine_setup_s": round(setup_s, 1),
+        "path": "LLM.generate -> ResidentEpochScheduler (device prefill, K<=8 epochs) -> ResidentEpochWorker -> "
+                "resident_epoch_prefill / resident_epoch_execute",
+    }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -999,10 +1066,14 @@ def main() -> None:
                         help="longest prompt of the seeded cohort (2..block_size; configs[4] uses 120)")
     parser.add_argument("--prefill", action="store_true",
                         help="measure the batched device prefill instead of the decode epochs")
+    parser.add_argument("--serve", action="store_true",
+                        help="measure serving through vLLM's LLM.generate (device prefill + resident epochs)")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.prefill:
+    if args.serve:
+        run_serve(args)
+    elif args.prefill:
         run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -62,8 +62,13 @@ class ResidentKVLayout:
         return self.layer_spec().page_size_bytes * self.model.num_layers
 
     def capacity_bytes(self) -> int:
-        # what the scheduler may allocate: the engine's blocks and nothing more
-        return self.physical_blocks * self.bytes_per_block()
+        """What the scheduler may allocate: the engine's blocks plus one.
+        vLLM's block pool keeps one block back as its null block, and every
+        row must be able to hold its blocks_per_row blocks at once, else vLLM
+        preempts a device-owned request once all rows have grown.  The
+        scheduler's block ids never address device memory (a row's blocks are
+        fixed by its row), so the extra block costs nothing."""
+        return (self.physical_blocks + 1) * self.bytes_per_block()
 
     def check(self, config: KVCacheConfig) -> None:
         """Raises unless the scheduler's KV configuration maps onto the engine's cache."""

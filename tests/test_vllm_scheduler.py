@@ -43,7 +43,7 @@ def hf_config_dir(tmp_path, preset=QWEN25_7B):
 
 
 def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_model_len=256, adopt=True,
-                   prefix_caching=True):
+                   prefix_caching=True, num_blocks=16):
     """vLLM's own V1 scheduler for the preset, turned into the resident one."""
     from vllm.config import CacheConfig, DeviceConfig, ModelConfig, SchedulerConfig, VllmConfig
     from vllm.v1.core.sched.scheduler import Scheduler
@@ -56,14 +56,14 @@ def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_mode
     model = ModelConfig(model=str(hf_config_dir(tmp_path, preset)), skip_tokenizer_init=True,
                         max_model_len=max_model_len, dtype="bfloat16")
     cache = CacheConfig(block_size=preset.block_size, enable_prefix_caching=prefix_caching)
-    cache.num_gpu_blocks = 16
+    cache.num_gpu_blocks = num_blocks
     sched = SchedulerConfig(max_num_seqs=batch_size, max_num_batched_tokens=512, max_model_len=max_model_len,
                             is_encoder_decoder=False, async_scheduling=False)
     vc = VllmConfig(model_config=model, cache_config=cache, scheduler_config=sched,
                     device_config=DeviceConfig(device="cuda"))
     spec = FullAttentionSpec(block_size=preset.block_size, num_kv_heads=preset.num_kv_heads,
                              head_size=preset.head_dim, dtype=torch.bfloat16)
-    kv = KVCacheConfig(num_blocks=16, kv_cache_tensors=[],
+    kv = KVCacheConfig(num_blocks=num_blocks, kv_cache_tensors=[],
                        kv_cache_groups=[KVCacheGroupSpec([f"model.layers.{i}.self_attn" for i in
                                                           range(preset.num_layers)], spec)])
     cls = Scheduler if adopt else ResidentEpochScheduler
@@ -256,7 +256,8 @@ def test_scheduler_to_dedicated_worker_control_path(tmp_path, monkeypatch):
     assert times.language_model > 0 and worker.warmup_output.model_calls == 1
     assert len(worker.get_kv_cache_spec()) == QWEN25_7B.num_layers
     page = 2 * QWEN25_7B.block_size * QWEN25_7B.num_kv_heads * QWEN25_7B.head_dim * 2
-    assert worker.determine_available_memory() == 8 * QWEN25_7B.num_layers * page
+    # the engine's 8 blocks plus vLLM's null block
+    assert worker.determine_available_memory() == 9 * QWEN25_7B.num_layers * page
     scheduler.update_from_output(output, worker.execute_model(output))
     worker.shutdown()
     for r in reqs:
@@ -430,3 +431,29 @@ def test_device_prefill_through_the_dedicated_worker(tmp_path, monkeypatch):
     # the stand-in counts on from the last prompt token
     assert list(reqs[0].output_token_ids) == [9, 10, 11, 12] and list(reqs[1].output_token_ids) == [10, 11, 12, 13]
     worker.shutdown()
+
+
+def test_four_rows_grow_to_two_blocks_without_preemption(tmp_path):
+    """The dedicated worker offers vLLM the engine's 8 blocks plus one (vLLM
+    keeps a null block), so four rows can all grow into their second block:
+    every step stays a resident plan.  With only the 8 blocks vLLM would
+    preempt a device-owned request."""
+    from cruise_b200.model_config import QWEN25_7B as preset
+    from cruise_b200.worker import ResidentKVLayout
+
+    layout = ResidentKVLayout(preset, preset.block_size, preset.num_blocks)
+    blocks = layout.capacity_bytes() // layout.bytes_per_block()
+    assert blocks == preset.num_blocks + 1
+    scheduler = make_scheduler(tmp_path, 4, device_prefill_config(max_steps=8), prefix_caching=False,
+                               num_blocks=blocks)
+    reqs = [request(str(i), [100 + i] * 120, max_tokens=24) for i in range(4)]
+    for r in reqs:
+        scheduler.add_request(r)
+    steps = 0
+    while not all(r.is_finished() for r in reqs):
+        out = scheduler.schedule()
+        plan = get_plan(out)
+        assert plan is not None, scheduler.last_rejection
+        commit_device_epoch(scheduler, out, {q.req_id: [7] * plan.max_steps for q in plan.requests})
+        steps += 1
+    assert steps == 3 and all(r.num_output_tokens == 24 for r in reqs)
