@@ -109,6 +109,9 @@ class ResidentEpochScheduler(Scheduler):
         reason = native_model_rejection(self.vllm_config.model_config.hf_config)
         if reason is not None:
             raise ValueError(f"resident epoch native graph mismatch: {reason}")
+        if self.resident_config.device_prefill and self.cache_config.enable_prefix_caching:
+            # a cached prefix makes vLLM schedule part of a prompt, which only a host lane could run
+            raise ValueError("resident epoch device prefill needs enable_prefix_caching=False")
 
     @classmethod
     def adopt(cls, scheduler: Scheduler, config: ResidentEpochConfig | None = None) -> "ResidentEpochScheduler":

@@ -457,3 +457,10 @@ def test_four_rows_grow_to_two_blocks_without_preemption(tmp_path):
         commit_device_epoch(scheduler, out, {q.req_id: [7] * plan.max_steps for q in plan.requests})
         steps += 1
     assert steps == 3 and all(r.num_output_tokens == 24 for r in reqs)
+
+
+def test_device_prefill_refuses_prefix_caching(tmp_path, monkeypatch):
+    monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL", "1")
+    with pytest.raises(ValueError, match="enable_prefix_caching=False"):
+        make_scheduler(tmp_path, 1, adopt=False)
+    make_scheduler(tmp_path, 1, adopt=False, prefix_caching=False)
