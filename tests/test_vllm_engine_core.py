@@ -44,15 +44,15 @@ def cuda_device_type(monkeypatch):
     monkeypatch.setattr(DeviceConfig, "__post_init__", resolve)
 
 
-def make_engine_core(model_dir, preset, max_model_len):
+def make_engine_core(model_dir, preset, max_model_len, prefix_caching=True):
     from vllm.engine.arg_utils import EngineArgs
     from vllm.v1.engine.core import EngineCore
     from vllm.v1.executor.uniproc_executor import UniProcExecutor
 
     config = EngineArgs(model=str(model_dir), skip_tokenizer_init=True, max_model_len=max_model_len,
                         block_size=preset.block_size, max_num_seqs=4, async_scheduling=False,
-                        enforce_eager=True, dtype="bfloat16", worker_cls=WORKER,
-                        scheduler_cls=SCHEDULER).create_engine_config()
+                        enforce_eager=True, dtype="bfloat16", worker_cls=WORKER, scheduler_cls=SCHEDULER,
+                        enable_prefix_caching=prefix_caching).create_engine_config()
     return EngineCore(vllm_config=config, executor_class=UniProcExecutor, log_stats=True)
 
 
@@ -198,7 +198,7 @@ def test_engine_core_device_prefill_on_the_test_engine(cuda_device_type, tmp_pat
     monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_STEPS", "4")
     monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL", "1")
     monkeypatch.setenv("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
-    core = make_engine_core(hf_config_dir(tmp_path, QWEN25_7B), QWEN25_7B, 256)
+    core = make_engine_core(hf_config_dir(tmp_path, QWEN25_7B), QWEN25_7B, 256, prefix_caching=False)
     try:
         recorder = PlanRecorder(core.scheduler)
         prompts = {"p": [9707, 11, 358, 374], "q": [500, 501]}
