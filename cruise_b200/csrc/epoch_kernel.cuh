@@ -730,8 +730,7 @@ __device__ void gemv_tiles_k512(const EpochParams &p, const Smem &s, const Gemv 
 }
 
 // General tile loop (any kc): each warp takes the 64-k slices warp, warp + 8,
-// ... of every tile, or for tiles narrower than 8 slices one slice of every
-// groups-th tile (below).
+// ... of every tile.
 __device__ void gemv_tiles_general(const EpochParams &p, const Smem &s, const Gemv &g, const TileRange &tr,
                                    RingCursor &ring, RingCursor &red) {
   const int tid = threadIdx.x;
@@ -764,14 +763,6 @@ __device__ void gemv_tiles_general(const EpochParams &p, const Smem &s, const Ge
   auto next_kk = [&](int v) { return v + 1 == tr.KT ? 0 : v + 1; };
   int kk = static_cast<int>(tr.t0 % tr.KT);
   int kq = kk;   // k-tile of the next prefetch
-  // Tiles narrower than 512 columns (ksteps < 8 k-steps of 64) would leave
-  // warps without work: the warps then form kConsumerWarps / ksteps groups
-  // that take the tiles in turn (tile t to group t % groups), each warp one
-  // k-step of its group's tiles.  Every warp still flushes at every segment
-  // end, so the epilogue's fixed-order sum over the warps covers all tiles.
-  const int groups = (!xg && ksteps < kConsumerWarps) ? kConsumerWarps / ksteps : 1;
-  const int first_ks = groups > 1 ? warp % ksteps : warp;
-  const int my_group = groups > 1 ? warp / ksteps : 0;
   uint4 x00, x01, x10, x11, x20, x21, x30, x31;
   xg_load(tr.t0, kq, x00, x01); kq = next_kk(kq);
   xg_load(tr.t0 + 1, kq, x10, x11); kq = next_kk(kq);
@@ -787,8 +778,7 @@ __device__ void gemv_tiles_general(const EpochParams &p, const Smem &s, const Ge
       xg_load(t + 3, kq, x30, x31);
       kq = next_kk(kq);
       const uint8_t *tile = stage + j * tile_bytes;
-      const bool mine = groups == 1 || static_cast<int>(t % groups) == my_group;
-      for (int ks = first_ks; mine && ks < ksteps; ks += kConsumerWarps) {
+      for (int ks = warp; ks < ksteps; ks += kConsumerWarps) {
         const uint32_t u0 = (static_cast<uint32_t>(ks * 8 + 2 * ci) ^ sw) * 16u;
         const uint32_t u1 = (static_cast<uint32_t>(ks * 8 + 2 * ci + 1) ^ sw) * 16u;
         const uint8_t *rlo = tile + gi * row_bytes;
