@@ -53,17 +53,17 @@ __host__ __device__ inline uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
-enum SynthMode : int32_t { kPlain = 0, kQkvRows = 1, kGateUp = 2, kDownPad = 3, kRowsPad = 4, kColsOff = 5 };
+enum SynthMode : int32_t { kPlain = 0, kQkvRows = 1, kGateUp = 2, kDownPad = 3, kRowsPad = 4 };
 
 struct SynthMap {
   int32_t mode;
   int32_t ids[3];       // tensor ids (q,k,v for kQkvRows; gate,up for kGateUp)
   int64_t cols;         // row length of the canonical tensor(s)
   int64_t rows0, rows1; // q rows / k rows (kQkvRows); valid rows (kRowsPad)
-  int64_t dst_cols;     // packed row length (kDownPad, kColsOff)
+  int64_t dst_cols;     // packed row length (kDownPad: columns [off0, off0 + rows0) of each row, zeros up to it)
   int64_t off0, off1;   // shard offsets into the canonical tensor (tensor parallelism):
                         // q row / k,v row (kQkvRows), intermediate row (kGateUp),
-                        // column (kDownPad, kColsOff), vocabulary row (kRowsPad)
+                        // column (kDownPad), vocabulary row (kRowsPad)
   int32_t tiled;        // destination is a tiled matrix with dst_cols columns
   int32_t kc;           // its tile width
 };
@@ -118,11 +118,6 @@ __global__ void synth_kernel(uint16_t *dst, int64_t count, SynthMap map, uint64_
         const int64_t r = e / map.cols, c = e % map.cols;
         zero = r >= map.rows0;
         idx = (map.off0 + r) * map.cols + c;
-        break;
-      }
-      case kColsOff: {
-        const int64_t r = e / map.dst_cols, c = e % map.dst_cols;
-        idx = r * map.cols + map.off0 + c;
         break;
       }
       default:
@@ -336,6 +331,16 @@ void fill_dims(Engine *e) {
   m.kv0 = g.kv0;
   m.nkv_all = c.num_kv_heads;
   m.Hq = g.nq * c.head_dim;
+  // The O projection's input columns (this rank's query heads) are zero-padded
+  // to a multiple of 512 where that adds at most a third and stays within H:
+  // its tiles are then 512 wide, so all consumer warps multiply and the
+  // attention output is read straight from L2, and at TP = 8 the two ranks
+  // sharing a KV head (4 and 3 query heads) stream O shards of one shape.
+  // One GPU (Hq = H = 3584) is unchanged.
+  {
+    const int32_t kq512 = static_cast<int32_t>(align_up(m.Hq, 512));
+    m.Kq = kq512 <= c.hidden && static_cast<int64_t>(kq512) * 3 <= static_cast<int64_t>(m.Hq) * 4 ? kq512 : m.Hq;
+  }
   m.I = g.ni;
   // intermediate columns zero-padded to a multiple of 512 (the down projection's
   // 512-wide tiles and its activation read straight from L2) when that adds at
@@ -458,7 +463,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
     // the O projection reads the attention output straight from L2 when it
     // runs one 64-wide k-step per consumer warp (CRUISE_O_XGLOBAL=0 stages it)
     const char *env = std::getenv("CRUISE_O_XGLOBAL");
-    e->o_xglobal = pick_kc(m.Hq) == 64 * kConsumerWarps && (env == nullptr || std::strtol(env, nullptr, 10) != 0);
+    e->o_xglobal = pick_kc(m.Kq) == 64 * kConsumerWarps && (env == nullptr || std::strtol(env, nullptr, 10) != 0);
   }
   const int kmax = e->down_xglobal ? m.H : std::max(m.H, m.I_pad);
   e->xs_stride = kmax + 8;
@@ -513,7 +518,7 @@ Engine *create_engine(const CruiseModelConfig &cfg, int device, int32_t *status,
     lo[l].w_post = take(H);
     lo[l].qkv_w = take(static_cast<int64_t>(m.Nqkv) * H);
     lo[l].qkv_b = take(m.Nqkv);
-    lo[l].o_w = take(H * static_cast<int64_t>(m.Hq));
+    lo[l].o_w = take(H * static_cast<int64_t>(m.Kq));
     lo[l].gu_w = take(2LL * m.I * H);
     lo[l].down_w = take(H * m.I_pad);
   }
@@ -641,7 +646,7 @@ bool locate(Engine *e, const std::string &name, TensorPlace &tp) {
   if (key == "self_attn.q_proj.bias") return plain(lw.qkv_b, 1, Hq, 0);
   if (key == "self_attn.k_proj.bias") return plain(lw.qkv_b, 1, kv, Hq);
   if (key == "self_attn.v_proj.bias") return plain(lw.qkv_b, 1, kv, Hq + kv);
-  if (key == "self_attn.o_proj.weight") return tiled(lw.o_w, H, Hq, kRowOffset, 0, Hq);
+  if (key == "self_attn.o_proj.weight") return tiled(lw.o_w, H, Hq, kRowOffset, 0, m.Kq);
   if (key == "mlp.gate_proj.weight") return tiled(lw.gu_w, m.I, H, kRowGate, 0, H);
   if (key == "mlp.up_proj.weight") return tiled(lw.gu_w, m.I, H, kRowUp, 0, H);
   if (key == "mlp.down_proj.weight") return tiled(lw.down_w, H, m.I, kRowOffset, 0, m.I_pad);
@@ -1025,7 +1030,7 @@ int32_t prefill_prepare(Engine *e) {
 // position len-1) into the import staging buffer, layer by layer for all tokens.
 int32_t prefill_run(Engine *e, const int64_t *tokens, const int32_t *lens, int32_t stride) {
   const ModelDims &m = e->m;
-  if (e->tp_size > 1) {
+  if (e->tp_size > 1 || m.Kq != m.Hq) {
     e->last_error = "cruise_epoch_prefill: single-GPU engines only (no tensor parallelism)";
     return -4;
   }
@@ -1180,9 +1185,10 @@ int32_t synth_all(Engine *e, uint64_t seed, double stddev) {
     launch(const_cast<bf16 *>(lw.qkv_w), static_cast<int64_t>(m.Nqkv) * H, tile(q, H));
     launch(const_cast<bf16 *>(lw.qkv_b), m.Nqkv, qb);
     SynthMap o{};
-    o.mode = kColsOff; o.ids[0] = base + 8; o.cols = H; o.dst_cols = m.Hq;
+    // this rank's Hq columns of the canonical [H][H] tensor, zero up to Kq
+    o.mode = kDownPad; o.ids[0] = base + 8; o.cols = H; o.rows0 = m.Hq; o.dst_cols = m.Kq;
     o.off0 = static_cast<int64_t>(m.q0) * m.d;
-    launch(const_cast<bf16 *>(lw.o_w), H * m.Hq, tile(o, m.Hq));
+    launch(const_cast<bf16 *>(lw.o_w), H * m.Kq, tile(o, m.Kq));
     SynthMap gu{};
     gu.mode = kGateUp; gu.ids[0] = base + 9; gu.ids[1] = base + 10; gu.cols = H;
     gu.off0 = static_cast<int64_t>(e->tp_rank) * m.I;

@@ -88,8 +88,8 @@ __device__ __forceinline__ Gemv make_gemv(const EpochParams &p, int layer, int k
         g.xsrc = p.h; g.xsrc_stride = m.H; g.norm_w = lw.w_in; g.embed_src = layer == 0;
         break;
       case kO:
-        g.W = lw.o_w; g.N = m.H; g.K = m.Hq; g.xmode = p.o_xglobal ? kXGlobal : kXCopy; g.xsrc = p.attn;
-        g.xsrc_stride = m.Hq;
+        g.W = lw.o_w; g.N = m.H; g.K = m.Kq; g.xmode = p.o_xglobal ? kXGlobal : kXCopy; g.xsrc = p.attn;
+        g.xsrc_stride = m.Kq;   // attention output rows: Kq wide, columns >= Hq stay zero
         break;
       case kGU:
         g.W = lw.gu_w; g.N = 2 * m.I; g.K = m.H; g.xmode = kXNorm; g.xsrc = p.h;
@@ -1205,7 +1205,7 @@ __device__ void attention_phase_d(const EpochParams &p, const Smem &s, int layer
   const int vslice = tid % kSlices, vgroup = tid / kSlices;
   for (int u = blockIdx.x; u < units; u += p.grid) {
     const int b = u / m.nq, qh = u % m.nq, kvh = qh / groups;
-    bf16 *out = p.attn + static_cast<size_t>(b) * m.Hq + qh * D;
+    bf16 *out = p.attn + static_cast<size_t>(b) * m.Kq + qh * D;
     if (s.row_act[b] == 0) {
       for (int i = tid; i < D; i += kConsumerThreads) out[i] = tobf(0.f);
       continue;

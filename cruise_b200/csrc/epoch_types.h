@@ -62,6 +62,7 @@ enum LaunchMode : int32_t { kModeEpoch = 0, kModeDecoderStep = 1 };
 struct ModelDims {
   int32_t L, H, nq, nkv, d, I, I_pad, V, V_pad, Nqkv;
   int32_t Hq;            // attention output width on this rank (nq * d)
+  int32_t Kq;            // the O projection's input columns: Hq, zero-padded (see fill_dims)
   int32_t Vl;            // lm_head rows on this rank (V without tensor parallelism)
   int32_t v0;            // global id of this rank's first vocabulary row
   int32_t kv0, nkv_all;  // first KV head of this rank, KV heads of the model
@@ -80,7 +81,7 @@ struct LayerWeights {
   const bf16 *w_in, *w_post;   // [H]
   const bf16 *qkv_w;           // tiled [Nqkv][H]   rows: q | k | v
   const bf16 *qkv_b;           // [Nqkv]
-  const bf16 *o_w;             // tiled [H][H]
+  const bf16 *o_w;             // tiled [H][Kq]: columns >= Hq are zero
   const bf16 *gu_w;            // tiled [2I][H]: per 16 rows, 8 gate rows then the 8 matching up rows
   const bf16 *down_w;          // tiled [H][I_pad]  columns >= I are zero
 };
