@@ -1,7 +1,8 @@
 """The C ABI from plain C: a C11 program that includes ``include/cruise_epoch.h``
 and ``include/cruise_protocol.h`` (no C++ in either), links against the
 engine library and calls the entry points that need no GPU -- the presets,
-the tensor-parallel shard query and the thread's last create error.  This is
+the tensor-parallel shard query, the thread's last create error and the
+argument check of the device-prefill bridge call.  This is
 what a cgo, JNI or N-API binding compiles against."""
 
 from __future__ import annotations
@@ -44,6 +45,10 @@ int main(void) {
   if (cruise_epoch_tp_shard(&cfg, 0, 3, s) != -1) return 30;
   const char *why = cruise_epoch_last_error(NULL);
   printf("last_error %s\n", why == NULL ? "null" : "string");
+  /* the device-prefill bridge call rejects a missing handle before any GPU work */
+  int64_t tokens[4] = {1, 2, 3, 4};
+  int32_t lens[4] = {2, 0, 0, 0};
+  if (resident_epoch_prefill(NULL, tokens, lens, 1) != 10) return 40;
   return 0;
 }
 """
