@@ -1470,6 +1470,7 @@ struct BridgeEngine {
   Engine *engine = nullptr;
   std::map<std::string, void *> ipc_imports;
   int32_t prefill_mask = 0;   // rows resident_epoch_prefill left in the device staging for the next execute
+  int32_t prefill_lens[kBatch] = {};   // their prompt lengths: the import epoch decodes from len - 1
 };
 
 bool read_transfer(const Engine *e, const char *path, uint64_t transfer_id, const int32_t *gens,
@@ -2173,8 +2174,11 @@ int32_t resident_epoch_execute(void *opaque, int32_t request_count, int32_t max_
   if (prefill_import) {
     // every prefilled row is imported, and only into a row this epoch runs
     if (be->prefill_mask == 0 || !e->payload_ready) return 13;
-    for (int r = 0; r < kBatch; ++r)
-      if (((be->prefill_mask >> r) & 1) != 0 && input_row_generations[r] == 0) return 13;
+    for (int r = 0; r < kBatch; ++r) {
+      if (((be->prefill_mask >> r) & 1) == 0) continue;
+      if (input_row_generations[r] == 0) return 13;
+      if (input_positions[r] != be->prefill_lens[r] - 1) return 11;   // decodes from the last prompt token
+    }
     import_mask = be->prefill_mask;
   }
   *output_model_calls = 0;
@@ -2284,6 +2288,7 @@ int32_t resident_epoch_prefill(void *opaque, const int64_t *prompt_tokens, const
   if (rc == -1) return 11;   // a prompt longer than a block or a token outside the vocabulary
   if (rc != 0) return 30;
   be->prefill_mask = mask;
+  for (int r = 0; r < kBatch; ++r) be->prefill_lens[r] = prompt_lens[r];
   return 0;
 }
 

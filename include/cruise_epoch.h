@@ -93,8 +93,9 @@ void resident_epoch_destroy(void *opaque);
  * called with transfer_path NULL, ipc_metadata NULL and a nonzero transfer_id
  * imports them from the device (Adler-32 proof in output_kv_import_checksum)
  * and decodes each from position len-1 with token prompt[len-1].  Every
- * pending row must run in that epoch (nonzero generation), else it returns 13;
- * without a pending prefill it returns 13 too.  Another import (a transfer
+ * pending row must run in that epoch (nonzero generation), else it returns 13
+ * (and 11 if its position is not len-1); without a pending prefill it
+ * returns 13 too.  Another import (a transfer
  * file or device IPC) discards the pending rows.  Returns 0, 10 bad
  * arguments (no row with 2 or more tokens), 11 a prompt longer than the
  * block size or a token outside the vocabulary, 30 a device failure. */

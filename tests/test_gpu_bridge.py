@@ -184,6 +184,10 @@ def test_prefill_import_needs_a_pending_prefill(engines):
     out = engine._call(request_count=1, max_steps=1, tokens=[2, 0, 0, 0], positions=[2, 0, 0, 0],
                        lengths=[3, 0, 0, 0], eos=[4095] * 4, generations=[9, 0, 0, 0], transfer_id=4)
     assert out["ret"] == 13
+    # both rows run, but row 2 does not start from its last prompt token (position 3)
+    out = engine._call(request_count=2, max_steps=1, tokens=[2, 0, 5, 0], positions=[2, 0, 1, 0],
+                       lengths=[3, 0, 2, 0], eos=[4095] * 4, generations=[9, 0, 10, 0], transfer_id=5)
+    assert out["ret"] == 11
     too_long = np.array([TINY.block_size + 1, 0, 0, 0], dtype=np.int32)
     assert lib.resident_epoch_prefill(engine.handle, tokens.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
                                       too_long.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
