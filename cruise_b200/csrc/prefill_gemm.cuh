@@ -22,8 +22,10 @@
 // memory holds its 128 rows x the tile's tokens (two accumulators of 256 fp32
 // columns).  Every byte of W is read once per tile and every byte of X once
 // per 256 rows: the tile is as large as the tensor memory allows, which
-// matters more here than overlapping the epilogue with the next tile (the
-// copies from L2, not the MMAs, set the pace).
+// matters more here than overlapping the epilogue with the next tile.  On
+// the large projections the MMAs run close to the tensor pipe's rate at the
+// clock the SMs hold under this load; a shallower ring (three stages) costs
+// a few per cent, so the copies keep up.
 //   warp 0         TMA producer (one thread per CTA): waits for its stage to
 //                  be free, loads its W rows and tokens with the 2-SM form of
 //                  the tensor copy, whose bytes complete on the leader CTA's
@@ -39,7 +41,9 @@
 //                  (W rows), 32 tokens at a time (four warps per lane quadrant
 //                  take every fourth chunk of tokens), then either fp32
 //                  partial sums [split][T][N] (the caller adds the splits in
-//                  order, so the result is deterministic) or, for the
+//                  order, so the result is deterministic), staged 8 tokens x
+//                  32 rows at a time in the warp's 2 KB of shared memory and
+//                  written by tensor stores, or, for the
 //                  interleaved gate/up projection, the SwiGLU of each (gate,
 //                  up) row pair written as the bf16 activation [T][I] (the
 //                  decoder's rounding points: bf16(silu(bf16 g)) * bf16 u,
