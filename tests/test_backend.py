@@ -98,3 +98,41 @@ def test_backend_factory_from_env(monkeypatch):
     monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_BACKEND_FACTORY", "nocolon")
     with pytest.raises(RuntimeError):
         load_backend_from_env()
+
+
+def prefill_plan():
+    return ResidentEpochPlan(
+        version=CONTRACT_VERSION, graph_batch_size=4, max_steps=2, logical_capacity=256,
+        requests=(ResidentEpochRequest(req_id="r0", row=0, generation=1, token_id=7, position=2, sequence_length=3,
+                                       eos_token_id=9, scheduler_block_ids=(4,), device_block_ids=(0, 1),
+                                       kv_import_required=True, prompt_token_ids=(5, 6, 7)),),
+        active_mask=(1, 0, 0, 0),
+    )
+
+
+def test_device_prefill_plans_route_to_the_engine_prefill():
+    """A plan whose requests carry prompts goes to execute_with_device_prefill
+    and must come back with an import proof; an engine without that method
+    (the sidecar's, say) or a second transfer source fails before any device
+    work, so the host may replay."""
+    engine = DeterministicTestEngine()
+    out = ResidentEpochBackend(engine).execute(prefill_plan())
+    result = get_result(out)
+    assert engine.prefill_calls == 1 and engine.execute_calls == 1
+    assert result.kv_imported and result.kv_transfer_mode == "device_prefill"
+    assert out.sampled_token_ids[0] == [8, 9]
+
+    class NoPrefill:
+        def execute(self, plan):
+            raise AssertionError("a prefill plan must not run as a plain epoch")
+
+    with pytest.raises(ResidentEpochExecutionError) as caught:
+        ResidentEpochBackend(NoPrefill()).execute(prefill_plan())
+    assert caught.value.input_preserving
+
+    class NoProof(DeterministicTestEngine):
+        def execute_with_device_prefill(self, plan):
+            return self._epoch(plan)   # no import checksum
+
+    with pytest.raises(ResidentEpochExecutionError, match="import checksum"):
+        ResidentEpochBackend(NoProof()).execute(prefill_plan())
