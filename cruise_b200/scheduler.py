@@ -109,9 +109,20 @@ class ResidentEpochScheduler(Scheduler):
         reason = native_model_rejection(self.vllm_config.model_config.hf_config)
         if reason is not None:
             raise ValueError(f"resident epoch native graph mismatch: {reason}")
-        if self.resident_config.device_prefill and self.cache_config.enable_prefix_caching:
-            # a cached prefix makes vLLM schedule part of a prompt, which only a host lane could run
-            raise ValueError("resident epoch device prefill needs enable_prefix_caching=False")
+        if self.resident_config.device_prefill:
+            # vLLM must schedule every eligible prompt whole: a cached prefix, a
+            # token budget smaller than a full cohort of block-size prompts or a
+            # long-prefill threshold would leave part of a prompt for a host lane
+            cfg, sched = self.resident_config, self.scheduler_config
+            if self.cache_config.enable_prefix_caching:
+                raise ValueError("resident epoch device prefill needs enable_prefix_caching=False")
+            if sched.max_num_batched_tokens < cfg.max_batch_size * cfg.block_size:
+                raise ValueError("resident epoch device prefill needs max_num_batched_tokens >= "
+                                 f"{cfg.max_batch_size * cfg.block_size} (4 prompts of a block each)")
+            threshold = getattr(sched, "long_prefill_token_threshold", 0) or 0
+            if 0 < threshold < cfg.block_size:
+                raise ValueError("resident epoch device prefill needs long_prefill_token_threshold 0 or >= "
+                                 f"{cfg.block_size}")
 
     @classmethod
     def adopt(cls, scheduler: Scheduler, config: ResidentEpochConfig | None = None) -> "ResidentEpochScheduler":

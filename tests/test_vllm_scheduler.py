@@ -43,7 +43,7 @@ def hf_config_dir(tmp_path, preset=QWEN25_7B):
 
 
 def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_model_len=256, adopt=True,
-                   prefix_caching=True, num_blocks=16):
+                   prefix_caching=True, num_blocks=16, max_batched_tokens=512):
     """vLLM's own V1 scheduler for the preset, turned into the resident one."""
     from vllm.config import CacheConfig, DeviceConfig, ModelConfig, SchedulerConfig, VllmConfig
     from vllm.v1.core.sched.scheduler import Scheduler
@@ -57,7 +57,8 @@ def make_scheduler(tmp_path, batch_size, config=None, preset=QWEN25_7B, max_mode
                         max_model_len=max_model_len, dtype="bfloat16")
     cache = CacheConfig(block_size=preset.block_size, enable_prefix_caching=prefix_caching)
     cache.num_gpu_blocks = num_blocks
-    sched = SchedulerConfig(max_num_seqs=batch_size, max_num_batched_tokens=512, max_model_len=max_model_len,
+    sched = SchedulerConfig(max_num_seqs=batch_size, max_num_batched_tokens=max_batched_tokens,
+                            max_model_len=max_model_len,
                             is_encoder_decoder=False, async_scheduling=False)
     vc = VllmConfig(model_config=model, cache_config=cache, scheduler_config=sched,
                     device_config=DeviceConfig(device="cuda"))
@@ -459,8 +460,10 @@ def test_four_rows_grow_to_two_blocks_without_preemption(tmp_path):
     assert steps == 3 and all(r.num_output_tokens == 24 for r in reqs)
 
 
-def test_device_prefill_refuses_prefix_caching(tmp_path, monkeypatch):
+def test_device_prefill_refuses_settings_that_split_prompts(tmp_path, monkeypatch):
     monkeypatch.setenv("VLLM_ASCEND_RESIDENT_EPOCH_DEVICE_PREFILL", "1")
     with pytest.raises(ValueError, match="enable_prefix_caching=False"):
         make_scheduler(tmp_path, 1, adopt=False)
+    with pytest.raises(ValueError, match="max_num_batched_tokens >= 512"):
+        make_scheduler(tmp_path, 1, adopt=False, prefix_caching=False, max_batched_tokens=256)
     make_scheduler(tmp_path, 1, adopt=False, prefix_caching=False)
